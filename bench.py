@@ -1,0 +1,423 @@
+"""Decode throughput of the quantized-weight path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c1] [--impl dz|reference]
+
+A step is one whole job of the workload on each GPU: for C2 (the default),
+64 sequences x (32 prompt tokens prefilled + 32 top-p draws) of the 4-layer
+d128 INT4 model. Sequences are independent: each rank runs its own 64
+(weak scaling, no collective on the data path). Prints one JSON line on rank 0.
+
+value: generated tokens / device time with prompts, seeds and outputs resident
+in HBM (CUDA events on the launching stream, L2 flushed between steps outside
+the events, max over ranks). e2e: the same jobs through the public C ABI
+(dz_cuda_generate) from pinned host buffers, host<->device copies inside the
+events. roofline: the dominant kernel class of one eagerly launched job, timed
+per launch with CUDA events. cpu_baseline: the reference's own C sources
+(oracle/_ref) on this host's cores, sequence-parallel, on the same workload.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "INT4/INT8 decode tokens/s at 1/2/4/8 B200; quant-matvec HBM GB/s vs peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = f"/tmp/dz_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.remove(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU baseline
+
+def cpu_reference(wl, seqs=None, repeats=2):
+    """The reference's own C path (oracle/_ref/libdzref.so: model_forward_token
+    + sample_next_token in the generation loop), sequences spread over all host
+    cores; falls back to the oracle port when the reference build is absent."""
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from dranzer_b200 import workloads as W
+    from _native_oracle import REF_SO, Oracle
+    cores = os.cpu_count() or 1
+    n = wl.batch if seqs is None else seqs
+    prompts, seeds = W.prompts(wl)[:n], W.seeds(wl)[:n]
+    mk = np.array(W.MASKED, np.uint32)
+    out = np.zeros((n, wl.n_new), np.uint32)
+    if os.path.exists(REF_SO):
+        kind = "reference"
+        L = ctypes.CDLL(REF_SO)
+        L.rh_build_bundle.argtypes = [ctypes.c_char_p] + [ctypes.c_size_t] * 5 + [ctypes.c_uint64, ctypes.c_int,
+                                                                                  ctypes.c_int]
+        L.rh_load.restype = ctypes.c_void_p
+        L.rh_load.argtypes = [ctypes.c_char_p]
+        L.rh_free.argtypes = [ctypes.c_void_p]
+        L.rh_set_omp_threads.argtypes = [ctypes.c_int]
+        L.rh_generate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                                  ctypes.c_size_t, ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_float,
+                                  ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                  ctypes.c_void_p]
+        path = f"/tmp/dz_cpu_ref_{os.getpid()}.bin".encode()
+        s = wl.spec
+        assert L.rh_build_bundle(path, s.vocab, s.dim, s.heads, s.layers, s.max_seq, wl.weight_seed, wl.bits, 2) == 0
+        sessions = [L.rh_load(path) for _ in range(cores)]
+        os.remove(path)
+
+        def run(t, lo, hi):
+            L.rh_set_omp_threads(1)
+            p = np.ascontiguousarray(prompts[lo:hi])
+            sd = np.ascontiguousarray(seeds[lo:hi])
+            o = np.zeros((hi - lo, wl.n_new), np.uint32)
+            L.rh_generate(sessions[t], p.ctypes.data, hi - lo, wl.prompt_len, wl.n_new, wl.strategy,
+                          wl.temperature, wl.top_k, wl.top_p, sd.ctypes.data if wl.strategy else None,
+                          mk.ctypes.data, mk.size, o.ctypes.data, None)
+            out[lo:hi] = o
+    else:
+        kind = "port"
+        sys.path.insert(0, os.path.join(ROOT, "tests"))
+        from _models import Spec, quantize_params, synth_params
+        o_ = Oracle()
+        s = wl.spec
+        spec = Spec(s.vocab, s.dim, s.heads, s.layers, s.max_seq)
+        _, flat = quantize_params(o_, spec, synth_params(o_, spec, wl.weight_seed), wl.bits)
+        models = [o_.model(spec, flat) for _ in range(cores)]
+
+        def run(t, lo, hi):
+            toks, _ = models[t].generate(prompts[lo:hi], wl.n_new, wl.strategy, wl.temperature, wl.top_k,
+                                         wl.top_p, seeds[lo:hi] if wl.strategy else None, W.MASKED)
+            out[lo:hi] = toks
+    times = []
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        ths = []
+        for t in range(cores):
+            lo, hi = W.shard(n, t, cores)
+            if hi > lo:
+                ths.append(threading.Thread(target=run, args=(t, lo, hi)))
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        times.append(time.perf_counter() - t0)
+    if kind == "reference":
+        for h in sessions:
+            L.rh_free(h)
+    best = min(times)
+    return {"value": n * wl.n_new / best, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{n} sequences x ({wl.prompt_len} prompt + {wl.n_new} decode), best of {repeats}, "
+                      f"sequences spread over {cores} threads (OMP 1 each)",
+            "seconds": best}, out
+
+
+# ---------------------------------------------------------------- GPU arm
+
+def dist_init():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def quant_matvec_probe(dz, torch, stream, hbm):
+    """C3 rows: K=4096, N=32000, M in {1, 8}, INT8 and INT4; enough weight copies
+    rotated per launch that the weights exceed L2 (126 MB)."""
+    from dranzer_b200 import workloads as W  # noqa: F401
+    res = []
+    st = np.array([dz.rng_stream(3, dz.STREAM_TESTING)], np.uint64)
+    x = dz.synth_gaussian(st, 8 * 4096, 1.0).reshape(8, 4096)
+    w = dz.synth_gaussian(st, 4096 * 32000, 0.02).reshape(4096, 32000)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((8, 32000), dtype=torch.float32, device="cuda")
+    for bits in (8, 4):
+        s, p = dz.quantize_pack(w, bits)
+        copies = 2 if bits == 8 else 4
+        mats = [dz.QuantizedWeightMatrix(s, p, 4096, 32000, bits) for _ in range(copies)]
+        for M in (1, 8):
+            for i in range(6):
+                mats[i % copies].matmul_async(xd.data_ptr(), yd.data_ptr(), M, stream.cuda_stream)
+            reps = 24
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+            torch.cuda.synchronize()
+            for i in range(reps):
+                evs[i][0].record(stream)
+                mats[i % copies].matmul_async(xd.data_ptr(), yd.data_ptr(), M, stream.cuda_stream)
+                evs[i][1].record(stream)
+            torch.cuda.synchronize()
+            ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+            nbytes = 4096 * 32000 * bits / 8 + 32000 * 4 + M * 4096 * 4 + M * 32000 * 4
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            res.append({"bits": bits, "M": M, "K": 4096, "N": 32000, "us": round(ms * 1e3, 2),
+                        "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "bytes": int(nbytes)})
+        for m in mats:
+            m.close()
+    return res
+
+
+def run_dz(args, wl):
+    import torch
+    import dranzer_b200 as dz
+    from dranzer_b200 import _native
+    from dranzer_b200 import workloads as W
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    if not dz.available():
+        raise RuntimeError("no usable B200")
+    hbm, bf16, peak_src = peaks()
+
+    path = f"/tmp/dz_bench_{os.getpid()}_{rank}.bin"
+    W.write_bundle(wl, path)
+    bundle = dz.Bundle(path)
+    model = dz.Model.from_bundle(bundle, device=local)
+    cache = dz.KVCache(model, wl.batch, wl.spec.max_seq)
+    stream = torch.cuda.Stream()
+    cache.set_stream(stream.cuda_stream)
+    samp = wl.sampling()
+
+    prompts = W.prompts(wl, rank)
+    seeds = W.seeds(wl, rank)
+    pd = torch.from_numpy(prompts.astype(np.int32)).cuda()
+    sdv = torch.from_numpy(seeds.astype(np.int64)).cuda()
+    od = torch.zeros((wl.batch, wl.n_new), dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    seeds_ptr = sdv.data_ptr() if wl.strategy else None
+
+    def job():
+        cache.generate_async(pd.data_ptr(), wl.prompt_len, wl.n_new, samp, seeds_ptr, od.data_ptr())
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            job()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as tdist
+            tdist.barrier()
+
+    clocks = ClockSampler(local)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    with torch.cuda.stream(stream):
+        for k in range(args.steps):
+            flush.zero_()
+            evs[k][0].record(stream)
+            job()
+            evs[k][1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    dev_ms = sum(a.elapsed_time(b) for a, b in evs)
+    tokens_local = wl.batch * wl.n_new * args.steps
+    got = od.cpu().numpy().astype(np.uint32)
+
+    # e2e through the public C ABI from pinned host buffers
+    hp = torch.from_numpy(prompts.astype(np.int32)).pin_memory()
+    hs = torch.from_numpy(seeds.astype(np.int64)).pin_memory()
+    ho = torch.zeros((wl.batch, wl.n_new), dtype=torch.int32).pin_memory()
+    L = _native.lib()
+
+    def job_e2e():
+        _native.check(L.dz_cuda_generate(cache.handle, hp.data_ptr(), wl.prompt_len, wl.n_new,
+                                         ctypes.byref(samp.c), hs.data_ptr() if wl.strategy else None,
+                                         ho.data_ptr()), "generate")
+
+    job_e2e()
+    e2e_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    for k in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+            e2e_evs[k][0].record(stream)
+        job_e2e()
+        with torch.cuda.stream(stream):
+            e2e_evs[k][1].record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_evs)
+    assert np.array_equal(ho.numpy().astype(np.uint32), got), "e2e tokens differ from the device-resident run"
+
+    if world > 1:
+        import torch.distributed as tdist
+        t = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device="cuda")
+        tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+        dev_ms, e2e_ms = float(t[0]), float(t[1])
+
+    # per-kernel-class CUDA-event timing of one eager job
+    stats = (_native.DzKernelStat * 5)()
+    _native.check(L.dz_cuda_profile_generate(cache.handle, pd.data_ptr(), wl.prompt_len, wl.n_new,
+                                             ctypes.byref(samp.c), seeds_ptr, od.data_ptr(), stats, 5),
+                  "profile_generate")
+    classes = {}
+    for k, name in enumerate(_native.KERNEL_CLASSES):
+        s = stats[k]
+        if s.launches:
+            classes[name] = {"launches": int(s.launches), "total_ms": round(s.total_ms, 4),
+                             "avg_us": round(1e3 * s.total_ms / s.launches, 3),
+                             "bytes_per_launch": int(s.bytes / s.launches)}
+    dom = max(classes, key=lambda n: classes[n]["total_ms"])
+    d = classes[dom]
+    achieved = d["bytes_per_launch"] / (d["avg_us"] * 1e-6) / 1e9
+    total_prof = sum(c["total_ms"] for c in classes.values())
+    for c in classes.values():
+        c["share"] = round(c["total_ms"] / total_prof, 3)
+
+    launches = cache.generate_launches(wl.prompt_len, wl.n_new, samp) * args.steps
+    out = None
+    if rank == 0:
+        tokens = tokens_local * world
+        value = tokens / (dev_ms * 1e-3)
+        out = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": f"int{wl.bits} weights, fp32 compute",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids; no dataset named)",
+            "config": {"workload": wl.name, "model": f"DRANZER d{wl.spec.dim} h{wl.spec.heads} L{wl.spec.layers} "
+                       f"V{wl.spec.vocab} T{wl.spec.max_seq}", "bits": wl.bits,
+                       "sequences_per_gpu": wl.batch, "global_batch": wl.batch * world,
+                       "prompt_len": wl.prompt_len, "decode_len": wl.n_new, "seq_len": wl.prompt_len + wl.n_new,
+                       "sampling": {"strategy": ["greedy", "top-k", "top-p"][wl.strategy],
+                                    "temperature": wl.temperature, "top_k": wl.top_k, "top_p": wl.top_p},
+                       "parallelism": f"batch-sharded x{world} (independent sequences, no collective)",
+                       "l2": "flushed between steps (256 MiB write on the stream, outside the timed events)",
+                       "step": "prefill prompt token by token + decode, one CUDA graph per job"},
+            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(prompts.nbytes + (seeds.nbytes if wl.strategy else 0)),
+                    "d2h_bytes_per_step": int(wl.batch * wl.n_new * 4)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": peak_src,
+                         "traffic": None,
+                         "note": "all weights and KV of this workload fit in L2; the kernel is latency-bound"},
+            "kernels": classes,
+            "clocks": clk,
+        }
+    if rank == 0 and world == 1:
+        out["quant_matvec"] = quant_matvec_probe(dz, torch, stream, hbm)
+        cpu, cpu_tokens = cpu_reference(wl)
+        out["cpu_baseline"] = {k: v for k, v in cpu.items() if k != "seconds"}
+        out["cpu_baseline"]["tokens_match_gpu"] = bool(np.array_equal(cpu_tokens, got))
+    cache.close()
+    model.close()
+    bundle.close()
+    os.remove(path)
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+        tdist.destroy_process_group()
+    return out
+
+
+def run_reference(args, wl):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    vals = []
+    for _ in range(args.warmup):
+        cpu_reference(wl, repeats=1)
+    for _ in range(args.steps):
+        cpu, _ = cpu_reference(wl, repeats=1)
+        vals.append(cpu["value"])
+    v = statistics.median(vals)
+    return {"metric": METRIC, "value": round(v, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1e3 * wl.batch * wl.n_new / v, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": f"int{wl.bits} weights dequantized to fp32 at load (reference loader), fp32 compute",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids; no dataset named)",
+            "config": {"workload": wl.name, "sequences": wl.batch, "prompt_len": wl.prompt_len,
+                       "decode_len": wl.n_new},
+            "impl": "reference",
+            "cpu_baseline": {"value": round(v, 1), "unit": "tokens/s", "cores": cpu["cores"], "kind": cpu["kind"],
+                             "sample": cpu["sample"]},
+            "e2e": {"value": round(v, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2")
+    ap.add_argument("--impl", default="dz", choices=["dz", "reference"])
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    from dranzer_b200 import workloads as W
+    wl = W.WORKLOADS[args.workload]
+    out = run_reference(args, wl) if args.impl == "reference" else run_dz(args, wl)
+    if out is not None:
+        print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

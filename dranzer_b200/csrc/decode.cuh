@@ -1,0 +1,212 @@
+// Decode-step kernels: ring-slot bookkeeping + embedding, ring-KV causal
+// attention for one new token per sequence, LayerNorm. fp32 throughout, the
+// arithmetic of src/core/transformer.c:686-858 and src/core/tensor_ops.c.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace dz {
+
+// Per-sequence ring state, the fields of model_kv_cache_t
+// (src/include/core/transformer.h:10-31) one entry per sequence.
+struct RingState {
+    int* start;       // physical slot of the oldest token
+    int* length;      // retained tokens (<= capacity)
+    long long* total; // absolute tokens consumed since reset
+    int* slot;        // this step: slot the new K/V row is written to
+    int* ctx;         // this step: context length attended over
+    int* row_off;     // this step: slot * dim (epilogue scatter offset)
+};
+
+// One block per sequence: the ring bookkeeping of model_forward_token
+// (src/core/transformer.c:765-775), then hidden = emb[token] + PE[position]
+// (:780-799, out-of-vocabulary ids map to 0). Positions past the host table
+// are computed as compute_positional_encoding_at (src/core/tensor_ops.c:250-260)
+// in the exp(-x ln 10000) form the host table uses.
+__global__ void dz_step_begin_kernel(RingState rs, const uint32_t* __restrict__ tokens, long long tok_stride,
+                                     const float* __restrict__ emb, const float* __restrict__ pe,
+                                     long long pe_rows, float* __restrict__ hidden, int dim, int vocab,
+                                     int capacity) {
+    const int b = blockIdx.x;
+    const int len = rs.length[b], start = rs.start[b];
+    const long long pos = rs.total[b];
+    int slot, ctx, new_start = start;
+    if (len < capacity) {
+        slot = (start + len) % capacity;
+        ctx = len + 1;
+    } else {
+        slot = start;
+        new_start = (start + 1) % capacity;
+        ctx = capacity;
+    }
+    uint32_t tok = tokens[(long long)b * tok_stride];
+    if (tok >= (uint32_t)vocab) tok = 0;
+    const float* e = emb + (long long)tok * dim;
+    float* h = hidden + (long long)b * dim;
+    if (pos < pe_rows) {
+        const float* p = pe + pos * dim;
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) h[i] = e[i] + p[i];
+    } else {
+        const float ln_base = logf(10000.0f);
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+            const float scale = expf(-((2.0f * (float)i) / (float)dim) * ln_base);
+            const float angle = (float)pos * scale;
+            h[i] = e[i] + ((i % 2 == 0) ? sinf(angle) : cosf(angle));
+        }
+    }
+    __syncthreads();  // every thread has read the old ring state
+    if (threadIdx.x == 0) {
+        rs.slot[b] = slot;
+        rs.ctx[b] = ctx;
+        rs.row_off[b] = slot * dim;
+        rs.start[b] = new_start;
+        rs.length[b] = len < capacity ? len + 1 : len;
+        rs.total[b] = pos + 1;
+    }
+}
+
+constexpr int ATT_THREADS = 128;
+
+// attention_head_forward_token (src/core/transformer.c:686-713) for one
+// (head, sequence): score_j = (q . k_j) / sqrtf(hd) over the logical context
+// j = 0..ctx-1 at physical row (start + j) % capacity, softmax, then
+// o = sum_j p_j v_j. Scores live in shared memory (capacity floats).
+__global__ void __launch_bounds__(ATT_THREADS) dz_attention_decode_kernel(
+    const float* __restrict__ q, const float* __restrict__ keys, const float* __restrict__ values,
+    const int* __restrict__ start_arr, const int* __restrict__ ctx_arr, float* __restrict__ out,
+    int dim, int head_dim, int capacity) {
+    extern __shared__ float smem[];
+    float* scores = smem;                 // [capacity]
+    float* qs = smem + capacity;          // [head_dim]
+    float* part = qs + head_dim;          // [ATT_THREADS]
+    __shared__ float red[ATT_THREADS / 32];
+
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int ctx = ctx_arr[b], start = start_arr[b];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* K = keys + (long long)b * capacity * dim + h * head_dim;
+    const float* V = values + (long long)b * capacity * dim + h * head_dim;
+    for (int e = threadIdx.x; e < head_dim; e += ATT_THREADS) qs[e] = q[(long long)b * dim + h * head_dim + e];
+    __syncthreads();
+
+    const float denom = sqrtf((float)head_dim);
+    for (int j = warp; j < ctx; j += ATT_THREADS / 32) {
+        const int phys = (start + j) % capacity;
+        const float* kr = K + (long long)phys * dim;
+        float s = 0.0f;
+        for (int e = lane; e < head_dim; e += 32) s = fmaf(qs[e], kr[e], s);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        if (lane == 0) scores[j] = s / denom;
+    }
+    __syncthreads();
+
+    // softmax (src/core/tensor_ops.c:55-76): max, exp(x - max), sum, * 1/sum
+    float mx = -3.402823466e38f;
+    for (int j = threadIdx.x; j < ctx; j += ATT_THREADS) mx = fmaxf(mx, scores[j]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < ATT_THREADS / 32; w++) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float sum = 0.0f;
+    for (int j = threadIdx.x; j < ctx; j += ATT_THREADS) {
+        const float ev = expf(scores[j] - mx);
+        scores[j] = ev;
+        sum += ev;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    sum = 0.0f;
+    for (int w = 0; w < ATT_THREADS / 32; w++) sum += red[w];
+    const float inv = 1.0f / sum;
+
+    // o[e] = sum_j p_j v_j[e], p_j = e_j * (1/sum) as the reference's softmax
+    // stores it. Thread (g, e) sums rows j = g, g + G, ...; groups combine in smem.
+    if (head_dim <= ATT_THREADS) {
+        const int groups = ATT_THREADS / head_dim;
+        const int e = threadIdx.x % head_dim, g = threadIdx.x / head_dim;
+        float acc = 0.0f;
+        if (g < groups) {
+            for (int j = g; j < ctx; j += groups) {
+                const int phys = (start + j) % capacity;
+                acc = fmaf(scores[j] * inv, V[(long long)phys * dim + e], acc);
+            }
+        }
+        part[threadIdx.x] = acc;
+        __syncthreads();
+        if (threadIdx.x < head_dim) {
+            float o = 0.0f;
+            for (int gg = 0; gg < groups; gg++) o += part[gg * head_dim + threadIdx.x];
+            out[(long long)b * dim + h * head_dim + threadIdx.x] = o;
+        }
+    } else {
+        for (int e = threadIdx.x; e < head_dim; e += ATT_THREADS) {
+            float acc = 0.0f;
+            for (int j = 0; j < ctx; j++) {
+                const int phys = (start + j) % capacity;
+                acc = fmaf(scores[j] * inv, V[(long long)phys * dim + e], acc);
+            }
+            out[(long long)b * dim + h * head_dim + e] = acc;
+        }
+    }
+}
+
+constexpr int LN_THREADS = 256;
+
+// layer_normalize (src/core/tensor_ops.c:88-111), eps 1e-6: mean, biased
+// variance of (x - mean), sigma = sqrtf(var + eps), y = gamma*((x-mean)/sigma)+beta.
+// One block per row. `residual`, when given, is added to x first (the
+// attention sub-block's attn_raw += hidden, src/core/transformer.c:804-806).
+__global__ void __launch_bounds__(LN_THREADS) dz_layernorm_kernel(
+    const float* __restrict__ x, const float* __restrict__ residual, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float* __restrict__ y, int dim, float eps) {
+    __shared__ float red[LN_THREADS / 32];
+    __shared__ float stat;
+    const int r = blockIdx.x;
+    const float* xr = x + (long long)r * dim;
+    const float* rr = residual ? residual + (long long)r * dim : nullptr;
+    float* yr = y + (long long)r * dim;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += LN_THREADS) s += rr ? xr[i] + rr[i] : xr[i];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < LN_THREADS / 32; w++) t += red[w];
+        stat = t / (float)dim;
+    }
+    __syncthreads();
+    const float mean = stat;
+    float v = 0.0f;
+    for (int i = threadIdx.x; i < dim; i += LN_THREADS) {
+        const float d = (rr ? xr[i] + rr[i] : xr[i]) - mean;
+        v = fmaf(d, d, v);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+        for (int w = 0; w < LN_THREADS / 32; w++) t += red[w];
+        stat = sqrtf(t / (float)dim + eps);
+    }
+    __syncthreads();
+    const float sd = stat;
+    for (int i = threadIdx.x; i < dim; i += LN_THREADS) {
+        const float xv = rr ? xr[i] + rr[i] : xr[i];
+        yr[i] = gamma[i] * ((xv - mean) / sd) + beta[i];
+    }
+}
+
+}  // namespace dz

@@ -1,0 +1,1049 @@
+// dranzer-b200 CUDA shim: handles, device layout, launch plans and the C ABI
+// of include/dz_cuda.h. Kernels live in qmv.cuh, decode.cuh and select.cuh.
+#include "dz_cuda.h"
+#include "dz_host.h"
+
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <new>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "decode.cuh"
+#include "qmv.cuh"
+#include "select.cuh"
+
+using namespace dz;
+
+// ------------------------------------------------------------------ errors
+
+static thread_local int g_status = DZ_OK;
+static thread_local char g_message[512] = "";
+
+static int fail(int status, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_message, sizeof(g_message), fmt, ap);
+    va_end(ap);
+    g_status = status;
+    return status;
+}
+
+#define DZ_CUDA(call)                                                                      \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess)                                                             \
+            return fail(e_ == cudaErrorMemoryAllocation ? DZ_E_NOMEM : DZ_E_DEVICE,        \
+                        "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+    } while (0)
+
+extern "C" int dz_cuda_last_error(char* buf, size_t n) {
+    if (buf && n) {
+        strncpy(buf, g_message, n - 1);
+        buf[n - 1] = 0;
+    }
+    return g_status;
+}
+
+// Switches to a handle's device for the duration of a call.
+struct DeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~DeviceGuard() {
+        int cur;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+extern "C" int dz_cuda_available(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return 0;
+    }
+    for (int d = 0; d < n; d++) {
+        cudaDeviceProp p;
+        if (cudaGetDeviceProperties(&p, d) == cudaSuccess && p.major == 10) return 1;
+    }
+    return 0;
+}
+
+// -------------------------------------------------------- device matrices
+
+struct DevQMat {
+    int K = 0, N = 0, Np = 0, bits = 0, gran = 0, nchunks = 0;
+    uint8_t* codes = nullptr;
+    float* col_scale = nullptr;  // [Np] (COLUMN / TENSOR expanded), zero in padding
+    float* k_scale = nullptr;    // [K] ROW granularity
+    size_t code_bytes = 0, scale_bytes = 0;
+};
+
+static void free_qmat(DevQMat& m) {
+    cudaFree(m.codes);
+    cudaFree(m.col_scale);
+    cudaFree(m.k_scale);
+    m = DevQMat();
+}
+
+static int round_up(int x, int m) { return (x + m - 1) / m * m; }
+
+static int check_blob(const dz_tensor_blob_t* w) {
+    size_t ns = 0, nb = 0;
+    if (!w || !w->scales || !w->packed || w->rows == 0 || w->cols == 0 ||
+        (w->bits != 4 && w->bits != 8) || w->rows > (1u << 30) || w->cols > (1u << 30) ||
+        dz_quantized_scale_count(w->rows, w->cols, w->granularity, &ns) != 0 ||
+        dz_quantized_packed_size(w->rows * w->cols, w->bits, &nb) != 0 || w->scale_count != ns ||
+        w->packed_size != nb)
+        return fail(DZ_E_INVALID, "quantized blob: bad shape, bit width or buffer sizes");
+    return DZ_OK;
+}
+
+// Builds the strip layout of the column concatenation of `srcs` (all with the
+// same K, bits and granularity; every source but the last with N % 4 == 0).
+// Device allocations are recorded in *out as they are made, so the caller's
+// free_qmat(*out) releases them on any failure.
+static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cudaStream_t st, DevQMat& m,
+                          uint8_t*& staging) {
+    const dz_tensor_blob_t* s0 = srcs[0];
+    for (auto* s : srcs) {
+        int rc = check_blob(s);
+        if (rc) return rc;
+        if (s->rows != s0->rows || s->bits != s0->bits || s->granularity != s0->granularity)
+            return fail(DZ_E_INVALID, "concatenated matrices disagree in K, bits or granularity");
+    }
+    if (srcs.size() > 1 && s0->granularity == DZ_GRAN_ROW)
+        return fail(DZ_E_INVALID, "ROW-granularity matrices cannot share one device matrix");
+    m.K = (int)s0->rows;
+    m.bits = s0->bits;
+    m.gran = s0->granularity;
+    int N = 0;
+    for (size_t i = 0; i < srcs.size(); i++) {
+        if (i + 1 < srcs.size() && srcs[i]->cols % 4 != 0)
+            return fail(DZ_E_INVALID, "concatenated matrix width not a multiple of 4");
+        N += (int)srcs[i]->cols;
+    }
+    m.N = N;
+    m.Np = round_up(N, 16);
+    const int KC = m.bits == 8 ? 4 : 8;
+    m.nchunks = round_up(m.K, KC) / KC;
+    m.code_bytes = (size_t)(m.Np / 4) * m.nchunks * 16;
+    DZ_CUDA(cudaMalloc(&m.codes, m.code_bytes));
+    DZ_CUDA(cudaMalloc(&m.col_scale, (size_t)m.Np * sizeof(float)));
+    DZ_CUDA(cudaMemsetAsync(m.col_scale, 0, (size_t)m.Np * sizeof(float), st));
+    m.scale_bytes = (size_t)N * 4;
+    if (m.gran == DZ_GRAN_ROW) {
+        DZ_CUDA(cudaMalloc(&m.k_scale, (size_t)m.K * sizeof(float)));
+        DZ_CUDA(cudaMemcpyAsync(m.k_scale, s0->scales, (size_t)m.K * 4, cudaMemcpyHostToDevice, st));
+        std::vector<float> ones(m.Np, 0.0f);
+        for (int i = 0; i < N; i++) ones[i] = 1.0f;
+        DZ_CUDA(cudaMemcpyAsync(m.col_scale, ones.data(), (size_t)m.Np * 4, cudaMemcpyHostToDevice, st));
+        DZ_CUDA(cudaStreamSynchronize(st));
+        m.scale_bytes = (size_t)m.K * 4;
+    }
+    size_t max_packed = 0;
+    for (auto* s : srcs) max_packed = s->packed_size > max_packed ? s->packed_size : max_packed;
+    DZ_CUDA(cudaMalloc(&staging, max_packed));
+    int col0 = 0;
+    for (auto* s : srcs) {
+        DZ_CUDA(cudaMemcpyAsync(staging, s->packed, s->packed_size, cudaMemcpyHostToDevice, st));
+        const int strips = (int)((s->cols + 3) / 4);
+        const long long nwords = (long long)strips * m.nchunks * 4;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(m.codes) + (long long)(col0 / 4) * m.nchunks * 4;
+        dz_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(staging, dst, m.K, (int)s->cols,
+                                                                          m.bits, m.nchunks, nwords);
+        DZ_CUDA(cudaGetLastError());
+        if (m.gran == DZ_GRAN_COLUMN) {
+            DZ_CUDA(cudaMemcpyAsync(m.col_scale + col0, s->scales, s->cols * 4, cudaMemcpyHostToDevice, st));
+        } else if (m.gran == DZ_GRAN_TENSOR) {
+            std::vector<float> rep(s->cols, s->scales[0]);
+            DZ_CUDA(cudaMemcpyAsync(m.col_scale + col0, rep.data(), s->cols * 4, cudaMemcpyHostToDevice, st));
+            DZ_CUDA(cudaStreamSynchronize(st));
+        }
+        DZ_CUDA(cudaStreamSynchronize(st));  // staging is reused by the next source
+        col0 += (int)s->cols;
+    }
+    // padding strips past the last source: all codes qmax (level 0)
+    const int used_strips = (col0 + 3) / 4;
+    if (used_strips < m.Np / 4) {
+        const long long nwords = (long long)(m.Np / 4 - used_strips) * m.nchunks * 4;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(m.codes) + (long long)used_strips * m.nchunks * 4;
+        dz_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(nullptr, dst, m.K, 0, m.bits,
+                                                                          m.nchunks, nwords);
+        DZ_CUDA(cudaGetLastError());
+    }
+    DZ_CUDA(cudaStreamSynchronize(st));
+    return DZ_OK;
+}
+
+static int make_qmat(const std::vector<const dz_tensor_blob_t*>& srcs, cudaStream_t st, DevQMat* out) {
+    uint8_t* staging = nullptr;
+    int rc = make_qmat_into(srcs, st, *out, staging);
+    cudaFree(staging);
+    return rc;
+}
+
+// ---------------------------------------------------------------- profiler
+
+// Optional per-launch CUDA events (dz_cuda_profile_generate): each launch
+// site brackets its kernel with two events on the launching stream and
+// records the kernel class and its algorithmic bytes / flops.
+struct ProfRec {
+    int kind;
+    double bytes, flops;
+    cudaEvent_t a, b;
+};
+static thread_local std::vector<ProfRec>* g_prof = nullptr;
+
+struct ProfScope {
+    ProfRec rec{};
+    cudaStream_t st;
+    bool on;
+    ProfScope(int kind, double bytes, double flops, cudaStream_t s) : st(s), on(g_prof != nullptr) {
+        if (!on) return;
+        rec.kind = kind;
+        rec.bytes = bytes;
+        rec.flops = flops;
+        cudaEventCreate(&rec.a);
+        cudaEventCreate(&rec.b);
+        cudaEventRecord(rec.a, st);
+    }
+    ~ProfScope() {
+        if (!on) return;
+        cudaEventRecord(rec.b, st);
+        g_prof->push_back(rec);
+    }
+};
+
+// ------------------------------------------------------------- qmv plans
+
+template <int BITS, int MT, int ST>
+static void launch_qmv_t(const QmvArgs& a, bool vec, unsigned grid, cudaStream_t st) {
+    if (vec) dz_qmv_kernel<BITS, MT, ST, true><<<grid, QMV_THREADS, 0, st>>>(a);
+    else dz_qmv_kernel<BITS, MT, ST, false><<<grid, QMV_THREADS, 0, st>>>(a);
+}
+
+template <int BITS>
+static void launch_qmv_bits(const QmvArgs& a, int MT, bool vec, unsigned grid, cudaStream_t st) {
+    switch (MT) {
+        case 1: launch_qmv_t<BITS, 1, 4>(a, vec, grid, st); break;
+        case 2: launch_qmv_t<BITS, 2, 2>(a, vec, grid, st); break;
+        case 4: launch_qmv_t<BITS, 4, 1>(a, vec, grid, st); break;
+        default: launch_qmv_t<BITS, 8, 1>(a, vec, grid, st); break;
+    }
+}
+
+static int g_num_sms = 148;
+
+// Y = epilogue(X . deq(W)) for M rows; returns the number of launches (1).
+static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep,
+                      cudaStream_t st) {
+    QmvArgs a;
+    a.codes = W.codes;
+    a.K = W.K;
+    a.N = W.N;
+    a.nchunks = W.nchunks;
+    a.k_scale = W.k_scale;
+    a.X = X;
+    a.ldx = ldx;
+    a.M = M;
+    a.ep = ep;
+    int MT = M >= 8 ? 8 : M >= 4 ? 4 : M >= 2 ? 2 : 1;
+    const int ST = MT == 1 ? 4 : MT == 2 ? 2 : 1;
+    a.m_tiles = (M + MT - 1) / MT;
+    a.n_groups = W.Np / (4 * ST);
+    const long long units = (long long)a.n_groups * a.m_tiles;
+    const long long target = (long long)g_num_sms * 40;
+    int kp = 1;
+    while (kp < QMV_WARPS && units * kp * 2 <= target && W.nchunks / (kp * 2) >= 64) kp *= 2;
+    a.kparts = kp;
+    a.chunks_per_part = (W.nchunks + kp - 1) / kp;
+    const int units_per_cta = QMV_WARPS / kp;
+    const unsigned grid = (unsigned)((units + units_per_cta - 1) / units_per_cta);
+    const int KC = W.bits == 8 ? 4 : 8;
+    const bool vec = (ldx % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (W.K % KC == 0);
+    ProfScope prof(DZ_KERNEL_QMV,
+                   (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N,
+                   2.0 * M * W.K * W.N, st);
+    if (W.bits == 8) launch_qmv_bits<8>(a, MT, vec, grid, st);
+    else launch_qmv_bits<4>(a, MT, vec, grid, st);
+    return 1;
+}
+
+static QmvEpilogue plain_epilogue(const DevQMat& W, float* Y, long long ldy) {
+    QmvEpilogue e;
+    memset(&e, 0, sizeof(e));
+    e.col_scale = W.col_scale;
+    e.nseg = 1;
+    e.seg_start[0] = 0;
+    e.seg_start[1] = W.N;
+    e.seg_ptr[0] = Y;
+    e.seg_ld[0] = ldy;
+    return e;
+}
+
+// ------------------------------------------------------------- qmatrix API
+
+struct dz_cuda_qmatrix {
+    int device;
+    DevQMat m;
+    cudaStream_t stream;
+};
+
+extern "C" int dz_cuda_qmatrix_create(int device, const dz_tensor_blob_t* w, dz_cuda_qmatrix_t** out) {
+    if (!out) return fail(DZ_E_INVALID, "null output handle");
+    *out = nullptr;
+    DeviceGuard g(device);
+    if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", device);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, device);
+    auto* q = new (std::nothrow) dz_cuda_qmatrix;
+    if (!q) return fail(DZ_E_NOMEM, "host allocation");
+    q->device = device;
+    if (cudaStreamCreateWithFlags(&q->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete q;
+        return fail(DZ_E_DEVICE, "stream creation failed");
+    }
+    int rc = make_qmat({w}, q->stream, &q->m);
+    if (rc) {
+        free_qmat(q->m);
+        cudaStreamDestroy(q->stream);
+        delete q;
+        return rc;
+    }
+    *out = q;
+    return DZ_OK;
+}
+
+extern "C" void dz_cuda_qmatrix_free(dz_cuda_qmatrix_t* q) {
+    if (!q) return;
+    DeviceGuard g(q->device);
+    free_qmat(q->m);
+    cudaStreamDestroy(q->stream);
+    delete q;
+}
+
+extern "C" size_t dz_cuda_qmatrix_bytes(const dz_cuda_qmatrix_t* q) {
+    if (!q) return 0;
+    return (size_t)q->m.K * q->m.N * q->m.bits / 8 + q->m.scale_bytes;
+}
+
+extern "C" int dz_cuda_qmatrix_unpack(const dz_cuda_qmatrix_t* q, float* dst) {
+    if (!q || !dst) return fail(DZ_E_INVALID, "null argument");
+    DeviceGuard g(q->device);
+    const long long total = (long long)q->m.K * q->m.N;
+    float* d = nullptr;
+    DZ_CUDA(cudaMalloc(&d, total * 4));
+    const float* scales = q->m.gran == DZ_GRAN_ROW ? q->m.k_scale : q->m.col_scale;
+    int gran = q->m.gran == DZ_GRAN_TENSOR ? DZ_GRAN_COLUMN : q->m.gran;  // expanded per column
+    dz_dequant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, q->stream>>>(q->m.codes, scales, gran, d, q->m.K,
+                                                                           q->m.N, q->m.bits, q->m.nchunks);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dst, d, total * 4, cudaMemcpyDeviceToHost, q->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(q->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return fail(DZ_E_DEVICE, "unpack: %s", cudaGetErrorString(e));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_qmatrix_codes(const dz_cuda_qmatrix_t* q, uint8_t* packed) {
+    if (!q || !packed) return fail(DZ_E_INVALID, "null argument");
+    DeviceGuard g(q->device);
+    size_t nb = 0;
+    dz_quantized_packed_size((size_t)q->m.K * q->m.N, q->m.bits, &nb);
+    uint8_t* d = nullptr;
+    DZ_CUDA(cudaMalloc(&d, nb));
+    dz_unrepack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, q->stream>>>(q->m.codes, d, q->m.K, q->m.N,
+                                                                        q->m.bits, q->m.nchunks, (long long)nb);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaMemcpyAsync(packed, d, nb, cudaMemcpyDeviceToHost, q->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(q->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return fail(DZ_E_DEVICE, "codes: %s", cudaGetErrorString(e));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_matmul_quantized_async(const float* A, const dz_cuda_qmatrix_t* q, float* C, size_t m,
+                                              size_t k, void* stream) {
+    if (!q || !A || !C || m == 0 || k != (size_t)q->m.K || m > (1u << 24))
+        return fail(DZ_E_INVALID, "matmul_quantized: bad arguments (k must equal the matrix rows)");
+    DeviceGuard g(q->device);
+    QmvEpilogue ep = plain_epilogue(q->m, C, q->m.N);
+    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream);
+    DZ_CUDA(cudaGetLastError());
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_matmul_quantized(const float* A, const dz_cuda_qmatrix_t* q, float* C, size_t m,
+                                        size_t k) {
+    if (!q || !A || !C || m == 0 || k != (size_t)q->m.K)
+        return fail(DZ_E_INVALID, "matmul_quantized: bad arguments (k must equal the matrix rows)");
+    DeviceGuard g(q->device);
+    float *dA = nullptr, *dC = nullptr;
+    const size_t n = (size_t)q->m.N;
+    DZ_CUDA(cudaMalloc(&dA, m * k * 4));
+    if (cudaMalloc(&dC, m * n * 4) != cudaSuccess) {
+        cudaFree(dA);
+        return fail(DZ_E_NOMEM, "device allocation");
+    }
+    cudaError_t e = cudaMemcpyAsync(dA, A, m * k * 4, cudaMemcpyHostToDevice, q->stream);
+    int rc = DZ_OK;
+    if (e == cudaSuccess) rc = dz_cuda_matmul_quantized_async(dA, q, dC, m, k, q->stream);
+    if (e == cudaSuccess && rc == DZ_OK) e = cudaMemcpyAsync(C, dC, m * n * 4, cudaMemcpyDeviceToHost, q->stream);
+    if (e == cudaSuccess && rc == DZ_OK) e = cudaStreamSynchronize(q->stream);
+    cudaFree(dA);
+    cudaFree(dC);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(DZ_E_DEVICE, "matmul_quantized: %s", cudaGetErrorString(e));
+    return DZ_OK;
+}
+
+// ------------------------------------------------------------------ model
+
+struct DevLayer {
+    bool fused_qkv = false;
+    DevQMat qkv, q, k, v, wo, w1, w2;
+    float *g1 = nullptr, *be1 = nullptr, *b1 = nullptr, *b2 = nullptr, *g2 = nullptr, *be2 = nullptr;
+};
+
+struct dz_cuda_model {
+    int device = 0;
+    dz_model_desc_t desc{};
+    std::atomic<int> refs{1};
+    float* emb = nullptr;
+    float* out_bias = nullptr;
+    float* pe = nullptr;
+    long long pe_rows = 0;
+    std::vector<DevLayer> layers;
+    DevQMat head;
+    size_t step_bytes = 0;
+    std::vector<void*> f32_allocs;
+};
+
+static void model_release(dz_cuda_model_t* m) {
+    if (!m || --m->refs > 0) return;
+    DeviceGuard g(m->device);
+    for (auto& L : m->layers) {
+        free_qmat(L.qkv); free_qmat(L.q); free_qmat(L.k); free_qmat(L.v);
+        free_qmat(L.wo); free_qmat(L.w1); free_qmat(L.w2);
+    }
+    free_qmat(m->head);
+    for (void* p : m->f32_allocs) cudaFree(p);
+    delete m;
+}
+
+static int upload_f32(dz_cuda_model_t* m, const dz_tensor_blob_t& t, size_t expect, float** out,
+                      cudaStream_t st) {
+    if (t.bits != 0 || !t.f32 || t.rows * t.cols != expect)
+        return fail(DZ_E_UNSUPPORTED, "tensor expected as float32 (default quantization policy)");
+    float* d = nullptr;
+    DZ_CUDA(cudaMalloc(&d, expect * 4));
+    m->f32_allocs.push_back(d);
+    DZ_CUDA(cudaMemcpyAsync(d, t.f32, expect * 4, cudaMemcpyHostToDevice, st));
+    *out = d;
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor_blob_t* tensors, size_t n,
+                                    int device, dz_cuda_model_t** out) {
+    if (!out) return fail(DZ_E_INVALID, "null output handle");
+    *out = nullptr;
+    if (!desc || !tensors) return fail(DZ_E_INVALID, "null argument");
+    if (desc->architecture_flags != 0)
+        return fail(DZ_E_UNSUPPORTED, "architecture flags 0x%x not supported on the device path",
+                    desc->architecture_flags);
+    const size_t D = desc->embedding_dim, V = desc->vocab_size, H = desc->num_heads, F = 4 * D;
+    if (D == 0 || H == 0 || D % H || V == 0 || desc->num_layers == 0 || desc->max_seq_len == 0)
+        return fail(DZ_E_INVALID, "bad model shape");
+    if (n != dz_model_tensor_layout(desc, nullptr, 0))
+        return fail(DZ_E_INVALID, "tensor count %zu does not match the model", n);
+    std::vector<dz_tensor_blob_t> lay(n);
+    dz_model_tensor_layout(desc, lay.data(), n);
+    for (size_t i = 0; i < n; i++) {
+        if (tensors[i].kind != lay[i].kind || tensors[i].rows != lay[i].rows || tensors[i].cols != lay[i].cols)
+            return fail(DZ_E_INVALID, "tensor %zu kind/shape mismatch", i);
+        if (lay[i].kind == DZ_KIND_PROJECTION && tensors[i].bits == 0)
+            return fail(DZ_E_UNSUPPORTED, "float32 projection %zu: use the CPU path", i);
+    }
+    DeviceGuard g(device);
+    if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", device);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, device);
+    auto* m = new (std::nothrow) dz_cuda_model;
+    if (!m) return fail(DZ_E_NOMEM, "host allocation");
+    m->device = device;
+    m->desc = *desc;
+    cudaStream_t st;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
+        delete m;
+        return fail(DZ_E_DEVICE, "stream creation failed");
+    }
+    int rc = DZ_OK;
+    size_t step = 0;
+    do {
+        const dz_tensor_blob_t* t = tensors;
+        if ((rc = upload_f32(m, t[0], V * D, &m->emb, st))) break;
+        if ((rc = make_qmat({&t[1]}, st, &m->head))) break;
+        if ((rc = upload_f32(m, t[2], V, &m->out_bias, st))) break;
+        step += m->head.code_bytes + m->head.scale_bytes + V * 4 + D * 4;
+        m->layers.resize(desc->num_layers);
+        size_t ti = 3;
+        for (size_t l = 0; l < desc->num_layers && !rc; l++, ti += 12) {
+            DevLayer& L = m->layers[l];
+            const dz_tensor_blob_t *tq = &t[ti], *tk = &t[ti + 1], *tv = &t[ti + 2];
+            L.fused_qkv = tq->granularity != DZ_GRAN_ROW && D % 4 == 0;
+            if (L.fused_qkv) {
+                if ((rc = make_qmat({tq, tk, tv}, st, &L.qkv))) break;
+                step += L.qkv.code_bytes + L.qkv.scale_bytes;
+            } else {
+                if ((rc = make_qmat({tq}, st, &L.q)) || (rc = make_qmat({tk}, st, &L.k)) ||
+                    (rc = make_qmat({tv}, st, &L.v)))
+                    break;
+                step += 3 * (L.q.code_bytes + L.q.scale_bytes);
+            }
+            if ((rc = make_qmat({&t[ti + 3]}, st, &L.wo))) break;
+            if ((rc = upload_f32(m, t[ti + 4], D, &L.g1, st)) || (rc = upload_f32(m, t[ti + 5], D, &L.be1, st)))
+                break;
+            if ((rc = make_qmat({&t[ti + 6]}, st, &L.w1))) break;
+            if ((rc = upload_f32(m, t[ti + 7], F, &L.b1, st))) break;
+            if ((rc = make_qmat({&t[ti + 8]}, st, &L.w2))) break;
+            if ((rc = upload_f32(m, t[ti + 9], D, &L.b2, st)) || (rc = upload_f32(m, t[ti + 10], D, &L.g2, st)) ||
+                (rc = upload_f32(m, t[ti + 11], D, &L.be2, st)))
+                break;
+            step += L.wo.code_bytes + L.wo.scale_bytes + L.w1.code_bytes + L.w1.scale_bytes + L.w2.code_bytes +
+                    L.w2.scale_bytes + (6 * D + F) * 4;
+        }
+        if (rc) break;
+        // sinusoid table for positions [0, max_seq_len + 4096), computed on the
+        // host exactly as compute_positional_encoding does
+        m->pe_rows = (long long)desc->max_seq_len + 4096;
+        std::vector<float> pe((size_t)m->pe_rows * D);
+        dz_positional_encoding(pe.data(), (size_t)m->pe_rows, D);
+        float* dpe = nullptr;
+        if (cudaMalloc(&dpe, pe.size() * 4) != cudaSuccess) { rc = fail(DZ_E_NOMEM, "pe table"); break; }
+        m->f32_allocs.push_back(dpe);
+        m->pe = dpe;
+        if (cudaMemcpyAsync(dpe, pe.data(), pe.size() * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess) {
+            rc = fail(DZ_E_DEVICE, "pe upload");
+            break;
+        }
+    } while (0);
+    cudaStreamSynchronize(st);
+    cudaStreamDestroy(st);
+    if (rc) {
+        model_release(m);
+        return rc;
+    }
+    m->step_bytes = step;
+    *out = m;
+    return DZ_OK;
+}
+
+extern "C" void dz_cuda_model_free(dz_cuda_model_t* m) { model_release(m); }
+
+extern "C" size_t dz_cuda_model_step_bytes(const dz_cuda_model_t* m) { return m ? m->step_bytes : 0; }
+
+// ------------------------------------------------------------------ cache
+
+struct GenKey {
+    size_t plen, n_new;
+    int strategy;
+    float temperature, top_p;
+    uint32_t top_k;
+    std::vector<uint32_t> masked;
+    const void* prompts;
+    const void* seeds;
+    const void* out;
+    bool operator<(const GenKey& o) const {
+        return std::tie(plen, n_new, strategy, temperature, top_p, top_k, masked, prompts, seeds, out) <
+               std::tie(o.plen, o.n_new, o.strategy, o.temperature, o.top_p, o.top_k, o.masked, o.prompts, o.seeds,
+                        o.out);
+    }
+};
+
+struct dz_cuda_cache {
+    dz_cuda_model_t* model = nullptr;
+    int B = 0, cap = 0;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    float *keys = nullptr, *values = nullptr;  // [L][B][cap][D]
+    int *start = nullptr, *length = nullptr, *slot = nullptr, *ctx = nullptr, *row_off = nullptr;
+    long long* total = nullptr;
+    float *hidden = nullptr, *q = nullptr, *concat = nullptr, *attn_raw = nullptr, *attn_norm = nullptr;
+    float *ff = nullptr, *ff_raw = nullptr, *logits = nullptr;
+    uint32_t* tok = nullptr;
+    uint64_t* rng = nullptr;
+    uint32_t* masked = nullptr;   // device copy of the masked ids (grown)
+    size_t masked_cap = 0;
+    // device buffers of the host-facing generate()
+    uint32_t* gen_prompts = nullptr;
+    size_t gen_prompts_cap = 0;
+    uint32_t* gen_out = nullptr;
+    size_t gen_out_cap = 0;
+    uint64_t* gen_seeds = nullptr;
+    uint64_t* host_rng = nullptr;  // pinned staging
+    uint32_t* host_ids = nullptr;
+    cudaGraphExec_t step_graph = nullptr;
+    std::map<GenKey, cudaGraphExec_t> gen_graphs;
+    double prof_ctx_bytes_per_layer = 0, prof_ctx_flops_per_layer = 0;  // set per profiled step
+    std::vector<void*> allocs;
+};
+
+static int cache_alloc(dz_cuda_cache_t* c, void** p, size_t bytes) {
+    DZ_CUDA(cudaMalloc(p, bytes));
+    c->allocs.push_back(*p);
+    return DZ_OK;
+}
+
+static void clear_graphs(dz_cuda_cache_t* c) {
+    if (c->step_graph) cudaGraphExecDestroy(c->step_graph);
+    c->step_graph = nullptr;
+    for (auto& kv : c->gen_graphs) cudaGraphExecDestroy(kv.second);
+    c->gen_graphs.clear();
+}
+
+extern "C" void dz_cuda_cache_free(dz_cuda_cache_t* c) {
+    if (!c) return;
+    {
+        DeviceGuard g(c->model->device);
+        if (c->stream) cudaStreamSynchronize(c->stream);
+        clear_graphs(c);
+        for (void* p : c->allocs) cudaFree(p);
+        cudaFree(c->gen_prompts);
+        cudaFree(c->gen_out);
+        cudaFree(c->masked);
+        cudaFreeHost(c->host_rng);
+        cudaFreeHost(c->host_ids);
+        if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
+    }
+    model_release(c->model);
+    delete c;
+}
+
+extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t capacity, dz_cuda_cache_t** out) {
+    if (!out) return fail(DZ_E_INVALID, "null output handle");
+    *out = nullptr;
+    if (!m || batch == 0 || batch > 65535 || capacity == 0 || capacity > m->desc.max_seq_len)
+        return fail(DZ_E_INVALID, "cache: batch must be 1..65535 and capacity 1..max_seq_len");
+    DeviceGuard g(m->device);
+    auto* c = new (std::nothrow) dz_cuda_cache;
+    if (!c) return fail(DZ_E_NOMEM, "host allocation");
+    m->refs++;
+    c->model = m;
+    c->B = (int)batch;
+    c->cap = (int)capacity;
+    const size_t D = m->desc.embedding_dim, F = 4 * D, V = m->desc.vocab_size, Lr = m->desc.num_layers;
+    const size_t B = batch;
+    int rc = DZ_OK;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        rc = fail(DZ_E_DEVICE, "stream creation failed");
+    } else {
+        c->own_stream = true;
+    }
+    if (!rc) rc = cache_alloc(c, (void**)&c->keys, Lr * B * capacity * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->values, Lr * B * capacity * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->start, B * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->length, B * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->slot, B * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->ctx, B * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->row_off, B * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->total, B * 8);
+    if (!rc) rc = cache_alloc(c, (void**)&c->hidden, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->q, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->concat, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->attn_raw, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->attn_norm, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->ff, B * F * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->ff_raw, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->logits, B * V * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->tok, B * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->rng, B * 8);
+    if (!rc) rc = cache_alloc(c, (void**)&c->gen_seeds, B * 8);
+    if (!rc && cudaMallocHost(&c->host_rng, B * 8) != cudaSuccess) rc = fail(DZ_E_NOMEM, "pinned host");
+    if (!rc && cudaMallocHost(&c->host_ids, B * 4) != cudaSuccess) rc = fail(DZ_E_NOMEM, "pinned host");
+    if (!rc) {
+        // the largest selection footprint (sorted vocabulary or top-k buffer)
+        const size_t smem = dz_select_smem_bytes((int)V, 2, SEL_TOPK_CAP);
+        if (smem > 48 * 1024 &&
+            cudaFuncSetAttribute(dz_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+                cudaSuccess)
+            rc = fail(DZ_E_DEVICE, "select kernel shared memory");
+    }
+    if (!rc) {
+        cudaMemsetAsync(c->start, 0, B * 4, c->stream);
+        cudaMemsetAsync(c->length, 0, B * 4, c->stream);
+        cudaMemsetAsync(c->total, 0, B * 8, c->stream);
+        if (cudaStreamSynchronize(c->stream) != cudaSuccess) rc = fail(DZ_E_DEVICE, "cache init");
+    }
+    if (rc) {
+        dz_cuda_cache_free(c);
+        return rc;
+    }
+    *out = c;
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_cache_set_stream(dz_cuda_cache_t* c, void* stream) {
+    if (!c) return fail(DZ_E_INVALID, "null cache");
+    DeviceGuard g(c->model->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->own_stream) cudaStreamDestroy(c->stream);
+    c->stream = (cudaStream_t)stream;
+    c->own_stream = false;
+    return DZ_OK;
+}
+
+extern "C" void* dz_cuda_cache_stream(const dz_cuda_cache_t* c) { return c ? (void*)c->stream : nullptr; }
+
+__global__ void dz_reset_kernel(int* start, int* length, long long* total, const uint8_t* mask, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B && (!mask || mask[b])) {
+        start[b] = 0;
+        length[b] = 0;
+        total[b] = 0;
+    }
+}
+
+extern "C" int dz_cuda_cache_reset(dz_cuda_cache_t* c, const uint8_t* seq_mask) {
+    if (!c) return fail(DZ_E_INVALID, "null cache");
+    DeviceGuard g(c->model->device);
+    uint8_t* dmask = nullptr;
+    if (seq_mask) {
+        DZ_CUDA(cudaMalloc(&dmask, c->B));
+        DZ_CUDA(cudaMemcpyAsync(dmask, seq_mask, c->B, cudaMemcpyHostToDevice, c->stream));
+    }
+    dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, dmask, c->B);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(dmask);
+    if (e != cudaSuccess) return fail(DZ_E_DEVICE, "reset: %s", cudaGetErrorString(e));
+    return DZ_OK;
+}
+
+// One decode step for all sequences; returns the number of kernel launches.
+static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long tok_stride) {
+    dz_cuda_model_t* m = c->model;
+    const int D = (int)m->desc.embedding_dim, F = 4 * D, V = (int)m->desc.vocab_size, H = (int)m->desc.num_heads;
+    const int hd = D / H, B = c->B, cap = c->cap;
+    cudaStream_t st = c->stream;
+    int launches = 0;
+    RingState rs{c->start, c->length, c->total, c->slot, c->ctx, c->row_off};
+    {
+        ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)B * D * 12, 0, st);
+        dz_step_begin_kernel<<<B, 128, 0, st>>>(rs, tokens, tok_stride, m->emb, m->pe, m->pe_rows, c->hidden, D,
+                                                V, cap);
+    }
+    launches++;
+    const size_t att_smem = (size_t)(cap + hd + ATT_THREADS) * 4;
+    for (size_t l = 0; l < m->layers.size(); l++) {
+        DevLayer& L = m->layers[l];
+        float* Kl = c->keys + l * (size_t)B * cap * D;
+        float* Vl = c->values + l * (size_t)B * cap * D;
+        if (L.fused_qkv) {
+            QmvEpilogue ep = plain_epilogue(L.qkv, c->q, D);
+            ep.nseg = 3;
+            ep.seg_start[0] = 0; ep.seg_start[1] = D; ep.seg_start[2] = 2 * D; ep.seg_start[3] = 3 * D;
+            ep.seg_ptr[1] = Kl; ep.seg_ld[1] = (long long)cap * D; ep.seg_row_off[1] = c->row_off;
+            ep.seg_ptr[2] = Vl; ep.seg_ld[2] = (long long)cap * D; ep.seg_row_off[2] = c->row_off;
+            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st);
+        } else {
+            QmvEpilogue eq = plain_epilogue(L.q, c->q, D);
+            launches += launch_qmv(L.q, c->hidden, D, B, eq, st);
+            QmvEpilogue ek = plain_epilogue(L.k, Kl, (long long)cap * D);
+            ek.seg_row_off[0] = c->row_off;
+            launches += launch_qmv(L.k, c->hidden, D, B, ek, st);
+            QmvEpilogue ev = plain_epilogue(L.v, Vl, (long long)cap * D);
+            ev.seg_row_off[0] = c->row_off;
+            launches += launch_qmv(L.v, c->hidden, D, B, ev, st);
+        }
+        {
+            // bytes: the K and V rows of every sequence's context (ctx <= cap; the
+            // exact per-step context is device state, so the capacity bound is used
+            // only when the profiler cannot read it) + q + output
+            ProfScope prof(DZ_KERNEL_ATTENTION, c->prof_ctx_bytes_per_layer + 8.0 * B * D,
+                           c->prof_ctx_flops_per_layer, st);
+            dz_attention_decode_kernel<<<dim3(H, B), ATT_THREADS, att_smem, st>>>(c->q, Kl, Vl, c->start, c->ctx,
+                                                                                 c->concat, D, hd, cap);
+        }
+        launches++;
+        QmvEpilogue eo = plain_epilogue(L.wo, c->attn_raw, D);
+        launches += launch_qmv(L.wo, c->concat, D, B, eo, st);
+        {
+            ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D, 0, st);
+            dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, D,
+                                                          1e-6f);
+        }
+        launches++;
+        QmvEpilogue e1 = plain_epilogue(L.w1, c->ff, F);
+        e1.bias = L.b1;
+        e1.relu = 1;
+        launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st);
+        QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
+        e2.bias = L.b2;
+        e2.residual = c->attn_norm;
+        e2.ld_res = D;
+        launches += launch_qmv(L.w2, c->ff, F, B, e2, st);
+        {
+            ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D, 0, st);
+            dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->ff_raw, nullptr, L.g2, L.be2, c->hidden, D, 1e-6f);
+        }
+        launches++;
+    }
+    QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
+    eh.bias = m->out_bias;
+    launches += launch_qmv(m->head, c->hidden, D, B, eh, st);
+    return launches;
+}
+
+static int ensure_masked(dz_cuda_cache_t* c, const dz_sampling_t* s) {
+    if (!s || s->n_masked == 0) return DZ_OK;
+    if (!s->masked_ids) return fail(DZ_E_INVALID, "masked_ids is NULL with n_masked > 0");
+    if (s->n_masked > c->masked_cap) {
+        clear_graphs(c);
+        cudaFree(c->masked);
+        c->masked = nullptr;
+        c->masked_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->masked, s->n_masked * 4));
+        c->masked_cap = s->n_masked;
+    }
+    return DZ_OK;
+}
+
+static int check_sampling(const dz_cuda_cache_t* c, const dz_sampling_t* s) {
+    if (!s) return DZ_OK;
+    const int V = (int)c->model->desc.vocab_size;
+    if (s->strategy < 0 || s->strategy > 2) return fail(DZ_E_INVALID, "unknown sampling strategy %d", s->strategy);
+    if (s->strategy == 2 && s->temperature > 0.0f && V > SEL_SORT_CAP)
+        return fail(DZ_E_UNSUPPORTED, "top-p over a vocabulary above %d ids", SEL_SORT_CAP);
+    if (s->strategy == 1 && s->temperature > 0.0f && V > SEL_SORT_CAP && s->top_k > (uint32_t)SEL_TOPK_CAP)
+        return fail(DZ_E_UNSUPPORTED, "top-k above %d over a vocabulary above %d ids", SEL_TOPK_CAP, SEL_SORT_CAP);
+    return DZ_OK;
+}
+
+static int enqueue_select(dz_cuda_cache_t* c, const dz_sampling_t* s, uint64_t* rng, uint32_t* out,
+                          long long out_stride, uint32_t* out2) {
+    SelectArgs a;
+    a.logits = c->logits;
+    a.V = (int)c->model->desc.vocab_size;
+    a.ld = a.V;
+    a.strategy = s ? s->strategy : 0;
+    a.temperature = s ? s->temperature : 0.0f;
+    a.top_k = s ? (int)s->top_k : 0;
+    a.top_p = s ? s->top_p : 0.0f;
+    a.masked = (s && s->n_masked) ? c->masked : nullptr;
+    a.n_masked = s ? (int)s->n_masked : 0;
+    a.rng = rng;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.out2 = out2;
+    const size_t smem = dz_select_smem_bytes(a.V, (a.rng && a.strategy) ? a.strategy : 0, a.top_k);
+    ProfScope prof(DZ_KERNEL_SELECT, 4.0 * c->B * a.V, 0, c->stream);
+    dz_select_kernel<<<c->B, SEL_THREADS, smem, c->stream>>>(a);
+    return 1;
+}
+
+extern "C" int dz_cuda_forward_tokens(dz_cuda_cache_t* c, const uint32_t* token_ids, float* logits_out) {
+    if (!c || !token_ids) return fail(DZ_E_INVALID, "null argument");
+    DeviceGuard g(c->model->device);
+    const size_t B = c->B, V = c->model->desc.vocab_size;
+    memcpy(c->host_ids, token_ids, B * 4);
+    DZ_CUDA(cudaMemcpyAsync(c->tok, c->host_ids, B * 4, cudaMemcpyHostToDevice, c->stream));
+    if (!c->step_graph) {
+        cudaGraph_t graph;
+        DZ_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        enqueue_step(c, c->tok, 1);
+        cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+        if (e != cudaSuccess) return fail(DZ_E_DEVICE, "capture: %s", cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&c->step_graph, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) {
+            c->step_graph = nullptr;
+            return fail(DZ_E_DEVICE, "instantiate: %s", cudaGetErrorString(e));
+        }
+    }
+    DZ_CUDA(cudaGraphLaunch(c->step_graph, c->stream));
+    if (logits_out) DZ_CUDA(cudaMemcpyAsync(logits_out, c->logits, B * V * 4, cudaMemcpyDeviceToHost, c->stream));
+    DZ_CUDA(cudaStreamSynchronize(c->stream));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_select(dz_cuda_cache_t* c, const dz_sampling_t* s, uint64_t* rng_states, uint32_t* out_ids) {
+    if (!c || !out_ids) return fail(DZ_E_INVALID, "null argument");
+    int rc = check_sampling(c, s);
+    if (rc) return rc;
+    DeviceGuard g(c->model->device);
+    if ((rc = ensure_masked(c, s))) return rc;
+    const size_t B = c->B;
+    if (s && s->n_masked)
+        DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
+    if (rng_states) {
+        memcpy(c->host_rng, rng_states, B * 8);
+        DZ_CUDA(cudaMemcpyAsync(c->rng, c->host_rng, B * 8, cudaMemcpyHostToDevice, c->stream));
+    }
+    enqueue_select(c, s, rng_states ? c->rng : nullptr, c->tok, 1, nullptr);
+    DZ_CUDA(cudaGetLastError());
+    DZ_CUDA(cudaMemcpyAsync(c->host_ids, c->tok, B * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (rng_states) DZ_CUDA(cudaMemcpyAsync(c->host_rng, c->rng, B * 8, cudaMemcpyDeviceToHost, c->stream));
+    DZ_CUDA(cudaStreamSynchronize(c->stream));
+    memcpy(out_ids, c->host_ids, B * 4);
+    if (rng_states) memcpy(rng_states, c->host_rng, B * 8);
+    return DZ_OK;
+}
+
+// The whole generation loop, enqueued on the cache's stream. Returns launches.
+static int enqueue_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                            const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
+    int launches = 0;
+    const bool sampled = seeds != nullptr;
+    if (sampled) {
+        dz_seed_kernel<<<(c->B + 127) / 128, 128, 0, c->stream>>>(seeds, c->rng, c->B, DZ_RNG_STREAM_SAMPLING);
+        launches++;
+    }
+    dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
+    launches++;
+    for (size_t t = 0; t < plen; t++) launches += enqueue_step(c, prompts + t, (long long)plen);
+    for (size_t i = 0; i < n_new; i++) {
+        launches += enqueue_select(c, s, sampled ? c->rng : nullptr, out + i, (long long)n_new, c->tok);
+        if (i + 1 < n_new) launches += enqueue_step(c, c->tok, 1);
+    }
+    return launches;
+}
+
+extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t plen, size_t n_new,
+                                            const dz_sampling_t* s) {
+    if (!c) return 0;
+    const dz_cuda_model_t* m = c->model;
+    size_t per_layer = 0;
+    for (const auto& L : m->layers) per_layer += (L.fused_qkv ? 1 : 3) + 6;
+    const size_t step = 1 + per_layer + 1;
+    const size_t seeded = (s && s->strategy != 0 && s->temperature > 0.0f) ? 1 : 0;
+    return seeded + 1 + plen * step + n_new + (n_new ? n_new - 1 : 0) * step;
+}
+
+extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                                      const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
+    if (!c || !prompts || !out || plen == 0 || n_new == 0)
+        return fail(DZ_E_INVALID, "generate: null buffer or empty prompt/decode length");
+    int rc = check_sampling(c, s);
+    if (rc) return rc;
+    DeviceGuard g(c->model->device);
+    if ((rc = ensure_masked(c, s))) return rc;
+    if (s && s->n_masked)
+        DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
+    const bool sampled = seeds && s && s->strategy != 0 && s->temperature > 0.0f;
+    GenKey key;
+    key.plen = plen;
+    key.n_new = n_new;
+    key.strategy = s ? s->strategy : 0;
+    key.temperature = s ? s->temperature : 0.0f;
+    key.top_p = s ? s->top_p : 0.0f;
+    key.top_k = s ? s->top_k : 0;
+    key.masked = s && s->n_masked ? std::vector<uint32_t>(s->masked_ids, s->masked_ids + s->n_masked)
+                                  : std::vector<uint32_t>();
+    key.prompts = prompts;
+    key.seeds = sampled ? seeds : nullptr;
+    key.out = out;
+    auto it = c->gen_graphs.find(key);
+    if (it == c->gen_graphs.end()) {
+        cudaGraph_t graph;
+        DZ_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out);
+        cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+        if (e != cudaSuccess) return fail(DZ_E_DEVICE, "capture: %s", cudaGetErrorString(e));
+        cudaGraphExec_t exec;
+        e = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (e != cudaSuccess) return fail(DZ_E_DEVICE, "instantiate: %s", cudaGetErrorString(e));
+        it = c->gen_graphs.emplace(key, exec).first;
+    }
+    DZ_CUDA(cudaGraphLaunch(it->second, c->stream));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                                const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out_tokens) {
+    if (!c || !prompts || !out_tokens || plen == 0 || n_new == 0)
+        return fail(DZ_E_INVALID, "generate: null buffer or empty prompt/decode length");
+    if (plen > (size_t)c->cap) return fail(DZ_E_INVALID, "prompt longer than the cache capacity");
+    DeviceGuard g(c->model->device);
+    const size_t B = c->B;
+    if (B * plen > c->gen_prompts_cap) {
+        clear_graphs(c);
+        cudaFree(c->gen_prompts);
+        c->gen_prompts = nullptr;
+        c->gen_prompts_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->gen_prompts, B * plen * 4));
+        c->gen_prompts_cap = B * plen;
+    }
+    if (B * n_new > c->gen_out_cap) {
+        clear_graphs(c);
+        cudaFree(c->gen_out);
+        c->gen_out = nullptr;
+        c->gen_out_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->gen_out, B * n_new * 4));
+        c->gen_out_cap = B * n_new;
+    }
+    DZ_CUDA(cudaMemcpyAsync(c->gen_prompts, prompts, B * plen * 4, cudaMemcpyHostToDevice, c->stream));
+    if (seeds) DZ_CUDA(cudaMemcpyAsync(c->gen_seeds, seeds, B * 8, cudaMemcpyHostToDevice, c->stream));
+    int rc = dz_cuda_generate_async(c, c->gen_prompts, plen, n_new, s, seeds ? c->gen_seeds : nullptr, c->gen_out);
+    if (rc) return rc;
+    DZ_CUDA(cudaMemcpyAsync(out_tokens, c->gen_out, B * n_new * 4, cudaMemcpyDeviceToHost, c->stream));
+    DZ_CUDA(cudaStreamSynchronize(c->stream));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                                        const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out,
+                                        dz_kernel_stat_t* stats, size_t n_stats) {
+    if (!c || !prompts || !out || !stats || plen == 0 || n_new == 0)
+        return fail(DZ_E_INVALID, "profile_generate: null buffer or empty lengths");
+    int rc = check_sampling(c, s);
+    if (rc) return rc;
+    DeviceGuard g(c->model->device);
+    if ((rc = ensure_masked(c, s))) return rc;
+    if (s && s->n_masked)
+        DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
+    const bool sampled = seeds && s && s->strategy != 0 && s->temperature > 0.0f;
+    std::vector<ProfRec> recs;
+    g_prof = &recs;
+    // eager launches, each bracketed by events; the attention byte count uses
+    // the mean context of the run (prefill then decode, all sequences in step)
+    const dz_cuda_model_t* m = c->model;
+    const double D = (double)m->desc.embedding_dim;
+    const double total_steps = (double)plen + (double)(n_new - 1);
+    const double mean_ctx = (total_steps + 1.0) / 2.0 < c->cap ? (total_steps + 1.0) / 2.0 : c->cap;
+    c->prof_ctx_bytes_per_layer = 8.0 * D * mean_ctx * c->B;
+    c->prof_ctx_flops_per_layer = 4.0 * D * mean_ctx * c->B;
+    enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out);
+    g_prof = nullptr;
+    cudaError_t e = cudaStreamSynchronize(c->stream);
+    for (size_t k = 0; k < n_stats; k++) {
+        stats[k].kind = (uint32_t)k;
+        stats[k].launches = 0;
+        stats[k].total_ms = 0;
+        stats[k].bytes = 0;
+        stats[k].flops = 0;
+    }
+    for (auto& r : recs) {
+        float ms = 0;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, r.a, r.b);
+        if (r.kind >= 0 && (size_t)r.kind < n_stats) {
+            stats[r.kind].launches++;
+            stats[r.kind].total_ms += ms;
+            stats[r.kind].bytes += r.bytes;
+            stats[r.kind].flops += r.flops;
+        }
+        cudaEventDestroy(r.a);
+        cudaEventDestroy(r.b);
+    }
+    if (e != cudaSuccess) return fail(DZ_E_DEVICE, "profile: %s", cudaGetErrorString(e));
+    return DZ_OK;
+}

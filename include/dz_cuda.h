@@ -1,0 +1,160 @@
+/*
+ * dranzer-b200 CUDA shim: the C ABI the reference's host code binds to run its
+ * quantized-weight inference path on a B200. Plain C types only; every
+ * function returns DZ_OK (0) or a negative DZ_E_* (dz_types.h), never throws
+ * and never prints. dz_cuda_last_error() holds the message of the calling
+ * thread's last failure. Handles are not safe for concurrent calls (the
+ * reference's rule for its own handles, docs/public-api.md:13-15).
+ *
+ * Reference interfaces each entry point replaces are cited beside it
+ * (paths relative to the DRANZER source tree).
+ */
+#ifndef DZ_CUDA_H
+#define DZ_CUDA_H
+
+#include "dz_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct dz_cuda_qmatrix dz_cuda_qmatrix_t;
+typedef struct dz_cuda_model dz_cuda_model_t;
+typedef struct dz_cuda_cache dz_cuda_cache_t;
+
+/* Token selection, the arguments of sample_next_token
+ * (src/include/cli/sampling.h: sample_next_token) plus the ids the generation
+ * loop masks to -FLT_MAX before each draw (src/cli/generation.c:31-46 control
+ * tokens, :250-254 EOS under a minimum length). */
+typedef struct {
+    int strategy;            /* 0 greedy, 1 top-k, 2 top-p (sampling_strategy_t) */
+    float temperature;
+    uint32_t top_k;
+    float top_p;
+    const uint32_t *masked_ids;
+    size_t n_masked;
+} dz_sampling_t;
+
+/* 1 when a CUDA device of compute capability 10.x is usable, else 0.
+ * Replaces gpu_matmul_available (src/include/backends/gpu/gpu_matmul.h:36). */
+int dz_cuda_available(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to
+ * n) and returns its status. Replaces the structured error of gpu_cuda.h
+ * (src/include/backends/gpu/gpu_cuda.h:25-36). */
+int dz_cuda_last_error(char *buf, size_t n);
+
+/* ---- Standalone quantized weight matrix: quantized_weight_matrix_t
+ * (src/include/core/quantized_matmul.h:13-22) resident on a device. The blob is
+ * the reference storage form (codes + scales); bits 4 or 8, any granularity. */
+int dz_cuda_qmatrix_create(int device, const dz_tensor_blob_t *weights, dz_cuda_qmatrix_t **out);
+void dz_cuda_qmatrix_free(dz_cuda_qmatrix_t *matrix);
+/* Device bytes of codes + scales the matmul streams per call. */
+size_t dz_cuda_qmatrix_bytes(const dz_cuda_qmatrix_t *matrix);
+/* quantize_unpack (src/core/quantize.c:272-303) computed on the device:
+ * dst[k*n] = scale * (code - qmax). Host destination. */
+int dz_cuda_qmatrix_unpack(const dz_cuda_qmatrix_t *matrix, float *dst);
+/* The device-resident codes converted back to the reference's packed bytes
+ * (host destination of quantized_packed_size bytes) - the layout round trip. */
+int dz_cuda_qmatrix_codes(const dz_cuda_qmatrix_t *matrix, uint8_t *packed);
+
+/* C (m x n) = A (m x k) . deq(W), host buffers, synchronous: the contract of
+ * matmul_quantized_weight (src/include/core/quantized_matmul.h:36-42,
+ * src/core/quantized_matmul.c:253-295); fp32 products and accumulation. */
+int dz_cuda_matmul_quantized(const float *A, const dz_cuda_qmatrix_t *weights, float *C,
+                             size_t m, size_t k);
+/* Same on device buffers, enqueued on `stream` (a cudaStream_t, NULL = legacy
+ * default stream), no synchronisation. */
+int dz_cuda_matmul_quantized_async(const float *A_dev, const dz_cuda_qmatrix_t *weights,
+                                   float *C_dev, size_t m, size_t k, void *stream);
+
+/* ---- Model: the parameters of a v2/v3 bundle kept as codes on the device.
+ * `tensors` are the n blobs of model_param_tensors() order
+ * (src/core/model_params.c:39-103), as dz_bundle_tensors() returns them; they are
+ * copied, the caller keeps ownership. Replaces the fp32 unpack at load
+ * (src/core/bundle.c:748) and the per-call weight cache of gpu_matmul
+ * (src/backends/gpu/gpu_matmul.c:419-519). Projections must be 4- or 8-bit;
+ * other tensors float32 (the default policy). */
+int dz_cuda_model_create(const dz_model_desc_t *desc, const dz_tensor_blob_t *tensors, size_t n,
+                         int device, dz_cuda_model_t **out);
+void dz_cuda_model_free(dz_cuda_model_t *model);
+/* Bytes of weights (codes, scales, fp32 tensors) one decode step reads. */
+size_t dz_cuda_model_step_bytes(const dz_cuda_model_t *model);
+
+/* ---- KV cache for `batch` independent sequences with ring capacity
+ * `capacity` (<= max_seq_len): model_kv_cache_init_with_capacity
+ * (src/core/transformer.c:586-645) per sequence. The cache retains its model
+ * (dranzer_cache_create semantics, src/include/dranzer.h:103-119). */
+int dz_cuda_cache_create(dz_cuda_model_t *model, size_t batch, size_t capacity,
+                         dz_cuda_cache_t **out);
+void dz_cuda_cache_free(dz_cuda_cache_t *cache);
+/* Use `stream` (a cudaStream_t) for all later work on this cache. */
+int dz_cuda_cache_set_stream(dz_cuda_cache_t *cache, void *stream);
+void *dz_cuda_cache_stream(const dz_cuda_cache_t *cache);
+/* model_kv_cache_reset (src/core/transformer.c:651-657) for the sequences
+ * whose seq_mask byte is non-zero (NULL: all). */
+int dz_cuda_cache_reset(dz_cuda_cache_t *cache, const uint8_t *seq_mask);
+
+/* One model_forward_token (src/core/transformer.c:755-858) for every sequence:
+ * token_ids[batch] (host) in, logits_out[batch][vocab] (host) out when not
+ * NULL. Synchronous. The early branch a GPU-backed model_forward_token /
+ * dranzer_cache_forward (src/api/dranzer.c:260-270) forwards to. */
+int dz_cuda_forward_tokens(dz_cuda_cache_t *cache, const uint32_t *token_ids, float *logits_out);
+
+/* sample_next_token on the logits of the last forward (src/cli/sampling.c:179-207)
+ * for every sequence, after masking sampling->masked_ids. rng_states[batch]
+ * (host, in/out) are dranzer_rng streams; NULL selects greedily as the
+ * reference does for a NULL stream. out_ids[batch] host. Synchronous. */
+int dz_cuda_select(dz_cuda_cache_t *cache, const dz_sampling_t *sampling, uint64_t *rng_states,
+                   uint32_t *out_ids);
+
+/* The generation loop of generation_decode_with_options
+ * (src/cli/generation.c:231-295) for every sequence at once, on the device:
+ * reset, prefill prompts[batch][prompt_len] token by token, then n_new draws,
+ * each followed by a forward of the drawn token except the last. seeds[batch]
+ * give the per-sequence streams dranzer_rng_stream(seed, SAMPLING) (NULL:
+ * greedy). out_tokens[batch][n_new]. Host buffers, synchronous; the whole loop
+ * runs as one CUDA graph. */
+int dz_cuda_generate(dz_cuda_cache_t *cache, const uint32_t *prompts, size_t prompt_len,
+                     size_t n_new, const dz_sampling_t *sampling, const uint64_t *seeds,
+                     uint32_t *out_tokens);
+/* Same with device-resident prompts/seeds/out_tokens, enqueued on the cache's
+ * stream without synchronisation. */
+int dz_cuda_generate_async(dz_cuda_cache_t *cache, const uint32_t *prompts_dev, size_t prompt_len,
+                           size_t n_new, const dz_sampling_t *sampling, const uint64_t *seeds_dev,
+                           uint32_t *out_tokens_dev);
+/* Number of kernel launches one dz_cuda_generate(_async) call issues. */
+size_t dz_cuda_generate_launches(const dz_cuda_cache_t *cache, size_t prompt_len, size_t n_new,
+                                 const dz_sampling_t *sampling);
+
+/* ---- Measurement. Kernel classes of the decode path. */
+enum {
+    DZ_KERNEL_STEP_BEGIN = 0, /* ring bookkeeping + embedding + position */
+    DZ_KERNEL_QMV = 1,        /* quantized matvec / skinny GEMM with fused epilogue */
+    DZ_KERNEL_ATTENTION = 2,  /* ring-KV decode attention */
+    DZ_KERNEL_LAYERNORM = 3,
+    DZ_KERNEL_SELECT = 4,     /* greedy / top-k / top-p selection */
+    DZ_KERNEL_CLASSES = 5
+};
+
+typedef struct {
+    uint32_t kind;
+    uint32_t launches;
+    double total_ms;   /* sum of per-launch CUDA-event durations */
+    double bytes;      /* algorithmic bytes of those launches */
+    double flops;
+} dz_kernel_stat_t;
+
+/* Runs one dz_cuda_generate_async loop eagerly (no graph) with CUDA events
+ * around every launch on the cache's stream, synchronises, and fills
+ * stats[kind] for kind < n_stats. No counterpart in the reference (its
+ * profiling is tools/gpu_latency.c wall-clock attribution). */
+int dz_cuda_profile_generate(dz_cuda_cache_t *cache, const uint32_t *prompts_dev, size_t prompt_len,
+                             size_t n_new, const dz_sampling_t *sampling, const uint64_t *seeds_dev,
+                             uint32_t *out_tokens_dev, dz_kernel_stat_t *stats, size_t n_stats);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

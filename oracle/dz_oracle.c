@@ -1,0 +1,562 @@
+/*
+ * Oracle: CPU restatement of DRANZER's quantized-weight inference path.
+ * TEST INFRASTRUCTURE ONLY - see dz_oracle.h. Only tests/, smoke() and
+ * bench.py's cpu_baseline leg load this library, always as the checker.
+ */
+#include "dz_oracle.h"
+
+#include <float.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ RNG */
+
+/* src/core/rng.c:18-23 (SplitMix64 finaliser). */
+static uint64_t or_splitmix64(uint64_t x) {
+    x += UINT64_C(0x9e3779b97f4a7c15);
+    x = (x ^ (x >> 30)) * UINT64_C(0xbf58476d1ce4e5b9);
+    x = (x ^ (x >> 27)) * UINT64_C(0x94d049bb133111eb);
+    return x ^ (x >> 31);
+}
+
+/* src/core/rng.c:25-33 */
+uint64_t or_rng_stream(uint64_t seed, uint64_t stream) {
+    uint64_t state = or_splitmix64(seed ^ or_splitmix64(stream));
+    return state ? state : UINT64_C(0x9e3779b97f4a7c15);
+}
+
+/* src/core/rng.c:35-44: xorshift64* (12, 25, 27). */
+uint64_t or_rng_next(uint64_t *state) {
+    uint64_t x = *state ? *state : UINT64_C(0x9e3779b97f4a7c15);
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *state = x;
+    return x * UINT64_C(2685821657736338717);
+}
+
+/* src/core/rng.c:46-52: top 53 bits over 2^53. */
+double or_rng_unit(uint64_t *state) {
+    return (double)(or_rng_next(state) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+void or_fill_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+    const double two_pi = 6.283185307179586476925286766559;
+    for (size_t i = 0; i < count; i++) {
+        double u1 = or_rng_unit(state);
+        if (u1 < 1.0 / 9007199254740992.0) u1 = 1.0 / 9007199254740992.0;
+        double u2 = or_rng_unit(state);
+        out[i] = (float)(sd * sqrt(-2.0 * log(u1)) * cos(two_pi * u2));
+    }
+}
+
+void or_prompt_ids(uint64_t *state, uint32_t *out, size_t count, uint32_t vocab,
+                   const uint32_t *excluded, size_t n_excluded) {
+    for (size_t i = 0; i < count;) {
+        uint32_t id = (uint32_t)(or_rng_next(state) % vocab);
+        int skip = 0;
+        for (size_t e = 0; e < n_excluded; e++) skip |= (id == excluded[e]);
+        if (!skip) out[i++] = id;
+    }
+}
+
+/* -------------------------------------------------------- quantization */
+
+/* src/core/quantize.c:21-23 */
+static int or_qmax(int bits) { return (1 << (bits - 1)) - 1; }
+
+/* src/core/quantize.c:48-50 */
+static float or_round_half_away(float v) {
+    return (v >= 0.0f) ? floorf(v + 0.5f) : ceilf(v - 0.5f);
+}
+
+/* src/core/quantize.c:183-197 */
+size_t or_scale_count(size_t rows, size_t cols, int granularity) {
+    return granularity == 0 ? 1 : granularity == 1 ? rows : cols;
+}
+
+/* src/core/quantize.c:199-204 */
+size_t or_packed_size(size_t values, int bits) {
+    return (values * (size_t)bits + 7) / 8;
+}
+
+/* src/core/quantize.c:206-211 */
+static size_t or_scale_index(size_t i, size_t cols, int granularity) {
+    if (granularity == 1) return i / cols;
+    if (granularity == 2) return i % cols;
+    return 0;
+}
+
+static int or_finite(float v) {
+    uint32_t b;
+    memcpy(&b, &v, 4);
+    return (b & 0x7f800000u) != 0x7f800000u;
+}
+
+/* src/core/quantize.c:235-270: two passes (per-group peak |w|, then codes
+ * level+qmax packed LSB-first at bit offset i*bits), then scale = peak/qmax. */
+int or_quantize_pack(const float *src, size_t rows, size_t cols, int bits, int granularity,
+                     float *scales, uint8_t *packed) {
+    if (!src || !scales || !packed || rows == 0 || cols == 0 || bits < 2 || bits > 16 ||
+        granularity < 0 || granularity > 2) return -1;
+    const size_t total = rows * cols;
+    const int qmax = or_qmax(bits);
+    const size_t ns = or_scale_count(rows, cols, granularity);
+    memset(scales, 0, ns * sizeof(float));
+    memset(packed, 0, or_packed_size(total, bits));
+    for (size_t i = 0; i < total; i++) {
+        if (!or_finite(src[i])) return -1;
+        size_t g = or_scale_index(i, cols, granularity);
+        float mag = fabsf(src[i]);
+        if (mag > scales[g]) scales[g] = mag;
+    }
+    for (size_t i = 0; i < total; i++) {
+        const float peak = scales[or_scale_index(i, cols, granularity)];
+        float level = 0.0f;
+        if (peak > 0.0f) {
+            const float inverse = (float)qmax / peak;
+            const float scaled = src[i] * inverse;
+            /* A subnormal peak makes qmax/peak overflow to +inf and a zero
+             * weight then gives 0 * inf = NaN. The reference build
+             * (-ffinite-math-only) resolves that NaN to +qmax through its
+             * clamp; restated explicitly (pinned by tests/golden/quant.npz). */
+            level = (scaled != scaled) ? (float)qmax : or_round_half_away(scaled);
+        }
+        if (level > (float)qmax) level = (float)qmax;
+        if (level < -(float)qmax) level = -(float)qmax;
+        uint32_t code = (uint32_t)((int)level + qmax);
+        size_t bit0 = i * (size_t)bits;
+        for (int b = 0; b < bits; b++) {
+            if (code & (UINT32_C(1) << b)) {
+                size_t pos = bit0 + (size_t)b;
+                packed[pos / 8] |= (uint8_t)(1u << (pos % 8));
+            }
+        }
+    }
+    /* quantize.c:265-267 writes `scales[g] /= (float)qmax`. The reference is
+     * built with -O3 -ffast-math (src/Makefile:46), whose -freciprocal-math
+     * compiles that division by a constant to a multiply by the rounded
+     * reciprocal; the shipped quantizer therefore stores peak * fl(1/qmax),
+     * which differs from peak / qmax by one ulp in some groups. The golden
+     * vectors in tests/golden/ pin this against the reference's own build. */
+    const float reciprocal = 1.0f / (float)qmax;
+    for (size_t g = 0; g < ns; g++) {
+        if (scales[g] > 0.0f) scales[g] = scales[g] * reciprocal;
+    }
+    return 0;
+}
+
+/* src/core/quantize.c:272-303: canonical decode; rejects non-finite or
+ * negative scales, codes above 2*qmax and non-zero padding bits. */
+int or_quantize_unpack(const float *scales, const uint8_t *packed, size_t rows, size_t cols,
+                       int bits, int granularity, float *dst) {
+    if (!scales || !packed || !dst || rows == 0 || cols == 0 || bits < 2 || bits > 16 ||
+        granularity < 0 || granularity > 2) return -1;
+    const size_t ns = or_scale_count(rows, cols, granularity);
+    for (size_t g = 0; g < ns; g++)
+        if (!or_finite(scales[g]) || scales[g] < 0.0f) return -1;
+    const size_t total = rows * cols;
+    const int qmax = or_qmax(bits);
+    for (size_t i = 0; i < total; i++) {
+        uint32_t code = 0;
+        size_t bit0 = i * (size_t)bits;
+        for (int b = 0; b < bits; b++) {
+            size_t pos = bit0 + (size_t)b;
+            if (packed[pos / 8] & (1u << (pos % 8))) code |= UINT32_C(1) << b;
+        }
+        if (code > (uint32_t)(2 * qmax)) return -1;
+        dst[i] = scales[or_scale_index(i, cols, granularity)] * (float)((int)code - qmax);
+    }
+    size_t used = total * (size_t)bits;
+    if (used % 8 != 0) {
+        uint8_t mask = (uint8_t)(0xFFu << (used % 8));
+        if (packed[or_packed_size(total, bits) - 1] & mask) return -1;
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------- matmul */
+
+/* src/core/quantized_matmul.c:67-96: one decoded weight, level * scale. */
+static float or_weight(const float *scales, const uint8_t *packed, int bits, int granularity,
+                       size_t n, size_t row, size_t col) {
+    size_t index = row * n + col;
+    int qmax = bits == 8 ? 127 : 7;
+    uint32_t code;
+    if (bits == 8) {
+        code = packed[index];
+    } else {
+        uint8_t byte = packed[index / 2];
+        code = (index & 1u) ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 0x0f);
+    }
+    float scale = granularity == 1 ? scales[row] : granularity == 2 ? scales[col] : scales[0];
+    return (float)((int)code - qmax) * scale;
+}
+
+/* src/core/quantized_matmul.c:253-295 with its AVX rungs' arithmetic: the
+ * weight is decoded to fp32 (level * scale) and accumulated with a fused
+ * multiply-add in ascending k. */
+int or_matmul_quantized(const float *A, size_t m, size_t k, size_t n,
+                        const float *scales, const uint8_t *packed, int bits, int granularity,
+                        float *C) {
+    if (!A || !C || !scales || !packed || m == 0 || k == 0 || n == 0 ||
+        (bits != 4 && bits != 8)) return -1;
+    #pragma omp parallel for schedule(static)
+    for (size_t j = 0; j < n; j++) {
+        for (size_t i = 0; i < m; i++) {
+            float sum = 0.0f;
+            for (size_t l = 0; l < k; l++)
+                sum = fmaf(A[i * k + l], or_weight(scales, packed, bits, granularity, n, l, j), sum);
+            C[i * n + j] = sum;
+        }
+    }
+    return 0;
+}
+
+/* -------------------------------------------------------- tensor ops */
+
+/* src/core/tensor_ops.c:227-248 */
+void or_positional_encoding(float *out, size_t rows, size_t dim) {
+    for (size_t pos = 0; pos < rows; pos++) or_positional_encoding_at(out + pos * dim, pos, dim);
+}
+
+/* src/core/tensor_ops.c:250-260. The source computes the inverse frequency
+ * as 1.0f / powf(10000.0f, x); the reference's -ffast-math build folds
+ * 1/pow(C, x) into exp(-x * ln C), which is what its tables hold (pinned by
+ * tests/golden/pe.npz to 1 ulp), so that is the form restated here. */
+void or_positional_encoding_at(float *out, size_t position, size_t dim) {
+    const float ln_base = logf(10000.0f);
+    for (size_t i = 0; i < dim; i++) {
+        float scale = expf(-((2.0f * (float)i) / (float)dim) * ln_base);
+        float angle = (float)position * scale;
+        out[i] = (i % 2 == 0) ? sinf(angle) : cosf(angle);
+    }
+}
+
+/* src/core/tensor_ops.c:55-76 */
+static void or_softmax(float *v, size_t n) {
+    if (n == 0) return;
+    float mx = v[0];
+    for (size_t i = 1; i < n; i++) if (v[i] > mx) mx = v[i];
+    float sum = 0.0f;
+    for (size_t i = 0; i < n; i++) { v[i] = expf(v[i] - mx); sum += v[i]; }
+    if (sum > 0) {
+        float inv = 1.0f / sum;
+        for (size_t i = 0; i < n; i++) v[i] *= inv;
+    }
+}
+
+/* src/core/tensor_ops.c:88-111 (layer_normalize -> layer_norm_internal). */
+static void or_layer_norm(const float *in, float *out, size_t n, const float *gamma,
+                          const float *beta, float eps) {
+    float mean = 0.0f;
+    for (size_t i = 0; i < n; i++) mean += in[i];
+    mean /= (float)n;
+    float var = 0.0f;
+    for (size_t i = 0; i < n; i++) { float d = in[i] - mean; var += d * d; }
+    var /= (float)n;
+    float sd = sqrtf(var + eps);
+    for (size_t i = 0; i < n; i++) out[i] = gamma[i] * ((in[i] - mean) / sd) + beta[i];
+}
+
+/* C[n] = a[k] . B[k x n], fp32 fused accumulation in ascending k. */
+static void or_matvec(const float *a, const float *B, float *c, size_t k, size_t n) {
+    for (size_t j = 0; j < n; j++) c[j] = 0.0f;
+    for (size_t l = 0; l < k; l++) {
+        const float al = a[l];
+        const float *row = B + l * n;
+        for (size_t j = 0; j < n; j++) c[j] = fmaf(al, row[j], c[j]);
+    }
+}
+
+/* -------------------------------------------------------------- model */
+
+typedef struct {
+    const float *wq, *wk, *wv, *wo, *g1, *be1, *w1, *b1, *w2, *b2, *g2, *be2;
+} or_layer_t;
+
+struct or_model {
+    size_t vocab, dim, heads, layers, max_seq;
+    float *params;
+    const float *emb, *out_proj, *out_bias;
+    or_layer_t *layer;
+    float *pe;
+};
+
+struct or_cache {
+    const or_model_t *m;
+    size_t capacity, length, start, total;
+    float *keys, *values; /* [layers][capacity][dim] */
+    float *hidden, *attn_norm, *query, *concat, *attn_raw, *ff, *ff_raw, *scores, *pe_row;
+};
+
+/* src/core/model.c:107-116 parameter count (default architecture). */
+size_t or_model_param_count(size_t vocab, size_t dim, size_t layers) {
+    return 2 * vocab * dim + vocab + layers * (12 * dim * dim + 9 * dim);
+}
+
+or_model_t *or_model_create(size_t vocab, size_t dim, size_t heads, size_t layers,
+                            size_t max_seq, const float *params) {
+    if (!params || vocab == 0 || dim == 0 || heads == 0 || dim % heads || layers == 0 ||
+        max_seq == 0) return NULL;
+    or_model_t *m = calloc(1, sizeof(*m));
+    size_t count = or_model_param_count(vocab, dim, layers);
+    m->params = malloc(count * sizeof(float));
+    m->layer = calloc(layers, sizeof(or_layer_t));
+    m->pe = malloc(max_seq * dim * sizeof(float));
+    if (!m->params || !m->layer || !m->pe) { or_model_free(m); return NULL; }
+    memcpy(m->params, params, count * sizeof(float));
+    m->vocab = vocab; m->dim = dim; m->heads = heads; m->layers = layers; m->max_seq = max_seq;
+    /* src/core/model.c:38-67,213-228 */
+    const float *p = m->params;
+    const size_t F = 4 * dim;
+    m->emb = p; p += vocab * dim;
+    m->out_proj = p; p += dim * vocab;
+    m->out_bias = p; p += vocab;
+    for (size_t l = 0; l < layers; l++) {
+        or_layer_t *L = &m->layer[l];
+        L->wq = p; p += dim * dim;
+        L->wk = p; p += dim * dim;
+        L->wv = p; p += dim * dim;
+        L->wo = p; p += dim * dim;
+        L->g1 = p; p += dim;
+        L->be1 = p; p += dim;
+        L->w1 = p; p += dim * F;
+        L->b1 = p; p += F;
+        L->w2 = p; p += F * dim;
+        L->b2 = p; p += dim;
+        L->g2 = p; p += dim;
+        L->be2 = p; p += dim;
+    }
+    or_positional_encoding(m->pe, max_seq, dim);
+    return m;
+}
+
+void or_model_free(or_model_t *m) {
+    if (!m) return;
+    free(m->params); free(m->layer); free(m->pe); free(m);
+}
+
+or_cache_t *or_cache_create(const or_model_t *m, size_t capacity) {
+    if (!m || capacity == 0 || capacity > m->max_seq) return NULL;
+    or_cache_t *c = calloc(1, sizeof(*c));
+    size_t d = m->dim;
+    c->m = m;
+    c->capacity = capacity;
+    c->keys = malloc(m->layers * capacity * d * sizeof(float));
+    c->values = malloc(m->layers * capacity * d * sizeof(float));
+    c->hidden = malloc(d * sizeof(float));
+    c->attn_norm = malloc(d * sizeof(float));
+    c->query = malloc(d * sizeof(float));
+    c->concat = malloc(d * sizeof(float));
+    c->attn_raw = malloc(d * sizeof(float));
+    c->ff = malloc(4 * d * sizeof(float));
+    c->ff_raw = malloc(d * sizeof(float));
+    c->scores = malloc(m->heads * capacity * sizeof(float));
+    c->pe_row = malloc(d * sizeof(float));
+    return c;
+}
+
+void or_cache_reset(or_cache_t *c) { c->length = 0; c->start = 0; c->total = 0; }
+
+void or_cache_free(or_cache_t *c) {
+    if (!c) return;
+    free(c->keys); free(c->values); free(c->hidden); free(c->attn_norm); free(c->query);
+    free(c->concat); free(c->attn_raw); free(c->ff); free(c->ff_raw); free(c->scores);
+    free(c->pe_row); free(c);
+}
+
+/* src/core/transformer.c:755-858 (model_forward_token), with
+ * attention_forward_token / attention_head_forward_token (:686-753). */
+int or_forward_token(const or_model_t *m, or_cache_t *c, uint32_t token, float *logits) {
+    const size_t d = m->dim, H = m->heads, hd = d / H, F = 4 * d, cap = c->capacity;
+    const float eps = 1e-6f;
+    size_t pos = c->total, slot, ctx;
+    if (c->length < cap) {
+        slot = (c->start + c->length) % cap;
+        ctx = c->length + 1;
+    } else {
+        slot = c->start;
+        c->start = (c->start + 1) % cap;
+        ctx = cap;
+    }
+    const float *pe;
+    if (pos < m->max_seq) {
+        pe = m->pe + pos * d;
+    } else {
+        or_positional_encoding_at(c->pe_row, pos, d);
+        pe = c->pe_row;
+    }
+    if (token >= m->vocab) token = 0;
+    for (size_t i = 0; i < d; i++) c->hidden[i] = m->emb[token * d + i] + pe[i];
+
+    for (size_t l = 0; l < m->layers; l++) {
+        const or_layer_t *L = &m->layer[l];
+        float *K = c->keys + l * cap * d, *V = c->values + l * cap * d;
+        or_matvec(c->hidden, L->wq, c->query, d, d);
+        or_matvec(c->hidden, L->wk, K + slot * d, d, d);
+        or_matvec(c->hidden, L->wv, V + slot * d, d, d);
+        for (size_t h = 0; h < H; h++) {
+            float *sc = c->scores + h * cap;
+            for (size_t j = 0; j < ctx; j++) {
+                size_t phys = (c->start + j) % cap;
+                float s = 0.0f;
+                for (size_t e = 0; e < hd; e++)
+                    s += c->query[h * hd + e] * K[phys * d + h * hd + e];
+                sc[j] = s / sqrtf((float)hd);
+            }
+            or_softmax(sc, ctx);
+            for (size_t e = 0; e < hd; e++) {
+                float s = 0.0f;
+                for (size_t j = 0; j < ctx; j++) {
+                    size_t phys = (c->start + j) % cap;
+                    s += sc[j] * V[phys * d + h * hd + e];
+                }
+                c->concat[h * hd + e] = s;
+            }
+        }
+        or_matvec(c->concat, L->wo, c->attn_raw, d, d);
+        for (size_t i = 0; i < d; i++) c->attn_raw[i] += c->hidden[i];
+        or_layer_norm(c->attn_raw, c->attn_norm, d, L->g1, L->be1, eps);
+        or_matvec(c->attn_norm, L->w1, c->ff, d, F);
+        for (size_t i = 0; i < F; i++) {
+            float pre = c->ff[i] + L->b1[i];
+            c->ff[i] = pre > 0.0f ? pre : 0.0f;
+        }
+        or_matvec(c->ff, L->w2, c->ff_raw, F, d);
+        for (size_t i = 0; i < d; i++) c->ff_raw[i] += L->b2[i] + c->attn_norm[i];
+        or_layer_norm(c->ff_raw, c->hidden, d, L->g2, L->be2, eps);
+    }
+    or_matvec(c->hidden, m->out_proj, logits, d, m->vocab);
+    for (size_t i = 0; i < m->vocab; i++) logits[i] += m->out_bias[i];
+    if (c->length < cap) c->length++;
+    c->total++;
+    return 0;
+}
+
+/* ----------------------------------------------------------- sampling */
+
+typedef struct { float prob; uint32_t idx; } or_pair_t;
+
+/* Descending order with ties kept in index order. src/cli/sampling.c sorts with
+ * qsort(compare_prob_desc); glibc's qsort is a stable merge sort for buffers
+ * it can allocate, so equal logits keep ascending index order. */
+static void or_sort_desc(or_pair_t *a, size_t n) {
+    or_pair_t *tmp = malloc(n * sizeof(*tmp));
+    for (size_t width = 1; width < n; width *= 2) {
+        for (size_t lo = 0; lo < n; lo += 2 * width) {
+            size_t mid = lo + width < n ? lo + width : n;
+            size_t hi = lo + 2 * width < n ? lo + 2 * width : n;
+            size_t i = lo, j = mid, o = lo;
+            while (i < mid && j < hi) tmp[o++] = (a[j].prob > a[i].prob) ? a[j++] : a[i++];
+            while (i < mid) tmp[o++] = a[i++];
+            while (j < hi) tmp[o++] = a[j++];
+        }
+        memcpy(a, tmp, n * sizeof(*a));
+    }
+    free(tmp);
+}
+
+/* src/cli/sampling.c:38-53 */
+static uint32_t or_greedy(const float *logits, size_t n) {
+    uint32_t best = 0;
+    float bv = logits[0];
+    for (uint32_t i = 1; i < n; i++) if (logits[i] > bv) { bv = logits[i]; best = i; }
+    return best;
+}
+
+/* src/cli/sampling.c:56-102 */
+static uint32_t or_topk(const float *logits, size_t n, size_t k, uint64_t *rng) {
+    if (k > n) k = n;
+    or_pair_t *p = malloc(n * sizeof(*p));
+    for (size_t i = 0; i < n; i++) { p[i].prob = logits[i]; p[i].idx = (uint32_t)i; }
+    or_sort_desc(p, n);
+    float best = p[0].prob, sum = 0.0f;
+    for (size_t i = 0; i < k; i++) { float e = expf(p[i].prob - best); p[i].prob = e; sum += e; }
+    float r = (float)or_rng_unit(rng) * sum, acc = 0.0f;
+    uint32_t sel = p[0].idx;
+    for (size_t i = 0; i < k; i++) {
+        acc += p[i].prob;
+        if (acc >= r) { sel = p[i].idx; break; }
+    }
+    free(p);
+    return sel;
+}
+
+/* src/cli/sampling.c:105-177 */
+static uint32_t or_topp(const float *logits, size_t n, float top_p, uint64_t *rng) {
+    or_pair_t *p = malloc(n * sizeof(*p));
+    float *e = malloc(n * sizeof(float));
+    for (size_t i = 0; i < n; i++) { p[i].prob = logits[i]; p[i].idx = (uint32_t)i; }
+    or_sort_desc(p, n);
+    float mx = p[0].prob, sum_all = 0.0f;
+    for (size_t i = 0; i < n; i++) { e[i] = expf(p[i].prob - mx); sum_all += e[i]; }
+    float cum = 0.0f, inv = 1.0f / sum_all;
+    size_t cand = n;
+    for (size_t i = 0; i < n; i++) {
+        cum += e[i] * inv;
+        if (cum >= top_p) { cand = i + 1; break; }
+    }
+    float nsum = 0.0f;
+    for (size_t i = 0; i < cand; i++) nsum += e[i];
+    float r = (float)or_rng_unit(rng) * nsum, acc = 0.0f;
+    uint32_t sel = p[0].idx;
+    for (size_t i = 0; i < cand; i++) {
+        acc += e[i];
+        if (acc >= r) { sel = p[i].idx; break; }
+    }
+    free(p); free(e);
+    return sel;
+}
+
+/* src/cli/sampling.c:179-207 */
+uint32_t or_sample_next_token(float *logits, size_t vocab, int strategy, float temperature,
+                              size_t top_k, float top_p, uint64_t *rng_state) {
+    if (!logits || vocab == 0) return 0;
+    if (strategy == 0 || temperature <= 0.0f || !rng_state) return or_greedy(logits, vocab);
+    float inv_t = 1.0f / temperature;
+    for (size_t i = 0; i < vocab; i++) logits[i] *= inv_t;
+    if (strategy == 1) {
+        if (top_k == 0) return or_greedy(logits, vocab);
+        return or_topk(logits, vocab, top_k, rng_state);
+    }
+    if (strategy == 2) {
+        if (top_p <= 0.0f || top_p > 1.0f) return or_greedy(logits, vocab);
+        return or_topp(logits, vocab, top_p, rng_state);
+    }
+    return or_greedy(logits, vocab);
+}
+
+int or_generate(const or_model_t *m, or_cache_t *c, const uint32_t *prompts, size_t n_seq,
+                size_t prompt_len, size_t n_new, int strategy, float temperature,
+                size_t top_k, float top_p, const uint64_t *seeds,
+                const uint32_t *masked, size_t n_masked,
+                uint32_t *out_tokens, float *out_logits) {
+    const size_t V = m->vocab;
+    float *logits = malloc(V * sizeof(float));
+    for (size_t q = 0; q < n_seq; q++) {
+        or_cache_reset(c);
+        for (size_t i = 0; i < prompt_len; i++)
+            or_forward_token(m, c, prompts[q * prompt_len + i], logits);
+        uint64_t rng = seeds ? or_rng_stream(seeds[q], OR_STREAM_SAMPLING) : 0;
+        for (size_t i = 0; i < n_new; i++) {
+            for (size_t k = 0; k < n_masked; k++)
+                if (masked[k] < V) logits[masked[k]] = -FLT_MAX;
+            if (out_logits) memcpy(out_logits + (q * n_new + i) * V, logits, V * sizeof(float));
+            uint32_t next = or_sample_next_token(logits, V, strategy, temperature, top_k, top_p,
+                                                 seeds ? &rng : NULL);
+            out_tokens[q * n_new + i] = next;
+            if (i + 1 < n_new) or_forward_token(m, c, next, logits);
+        }
+    }
+    free(logits);
+    return 0;
+}
+
+/* src/core/fingerprint.c:14-20 */
+uint64_t or_fnv1a(uint64_t running, const void *data, size_t size) {
+    const uint8_t *b = data;
+    for (size_t i = 0; i < size; i++) { running ^= b[i]; running *= UINT64_C(1099511628211); }
+    return running;
+}

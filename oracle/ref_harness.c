@@ -1,0 +1,212 @@
+/*
+ * Harness around the reference's own C sources (test infrastructure only).
+ *
+ * Compiled by oracle/Makefile (`make -C oracle ref`) together with the
+ * reference's core objects into oracle/_ref/libdzref.so. Every function here
+ * drives the reference's public or core API unchanged; nothing of the
+ * reference is re-implemented. Used to generate tests/golden/ fixtures and as
+ * the CPU baseline ("kind": "reference") beside the GPU numbers.
+ *
+ * Synthetic inputs follow one generator shared with the product and the
+ * oracle: dranzer_rng_stream(seed, DRANZER_RNG_STREAM_TESTING), one value per
+ * two dranzer_rng_unit() draws through Box-Muller (u1 floored at 2^-53),
+ * w = (float)(sd * sqrt(-2 ln u1) * cos(2 pi u2)).
+ */
+
+#include "core/bundle.h"
+#include "core/model.h"
+#include "core/model_params.h"
+#include "core/model_quantize.h"
+#include "core/quantize.h"
+#include "core/quantized_matmul.h"
+#include "core/rng.h"
+#include "core/transformer.h"
+#include "cli/sampling.h"
+#include "byte_pair_encoding.h"
+#include <float.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#include <time.h>
+#include <omp.h>
+
+#define RH_TWO_PI 6.283185307179586476925286766559
+
+float rh_gaussian(uint64_t *state, double sd) {
+    double u1 = dranzer_rng_unit(state);
+    if (u1 < 1.0 / 9007199254740992.0) u1 = 1.0 / 9007199254740992.0;
+    double u2 = dranzer_rng_unit(state);
+    return (float)(sd * sqrt(-2.0 * log(u1)) * cos(RH_TWO_PI * u2));
+}
+
+void rh_fill_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+    for (size_t i = 0; i < count; i++) out[i] = rh_gaussian(state, sd);
+}
+
+/* Build a model with the reference's allocator, overwrite its parameters with
+ * N(0, 0.02) for embeddings/projections (model_param_tensors order), 1/0 for
+ * LayerNorm gamma/beta and 0 for biases, then write a quantized bundle with the
+ * reference's own writer (projections only, per the default policy). */
+int rh_build_bundle(const char *path, size_t vocab, size_t dim, size_t heads,
+                    size_t layers, size_t max_seq, uint64_t weight_seed,
+                    int bits, int granularity) {
+    neural_model_t model = {0};
+    if (model_new_seeded(&model, vocab, dim, heads, layers, max_seq, 0) != MODEL_SUCCESS)
+        return -1;
+    size_t count = model_param_tensor_count(&model);
+    param_tensor_t *tensors = calloc(count, sizeof(*tensors));
+    if (!tensors) { model_free(&model); return -2; }
+    model_param_tensors(&model, tensors, count);
+    uint64_t state = dranzer_rng_stream(weight_seed, DRANZER_RNG_STREAM_TESTING);
+    for (size_t t = 0; t < count; t++) {
+        size_t n = tensors[t].rows * tensors[t].cols;
+        switch (tensors[t].kind) {
+            case PARAM_KIND_PROJECTION:
+            case PARAM_KIND_EMBEDDING:
+                rh_fill_gaussian(&state, tensors[t].values, n, 0.02);
+                break;
+            case PARAM_KIND_NORM:
+                for (size_t i = 0; i < n; i++)
+                    tensors[t].values[i] = strstr(tensors[t].name, "ln_gamma") != NULL ? 1.0f : 0.0f;
+                break;
+            default:
+                memset(tensors[t].values, 0, n * sizeof(float));
+        }
+    }
+    free(tensors);
+
+    bpe_encoder_t encoder = {0};
+    if (bpe_encoder_new_with_special_tokens(&encoder, vocab) != BPE_SUCCESS ||
+        bpe_encoder_freeze(&encoder) != BPE_SUCCESS) {
+        model_free(&model);
+        return -3;
+    }
+    model_bundle_metadata_t meta = {0};
+    meta.train_window = max_seq;
+    meta.seed = weight_seed;
+    model_quant_config_t config;
+    model_quantize_default_config(&config);
+    config.bits = bits;
+    config.granularity = (quant_granularity_t)granularity;
+    bundle_errors_t rc = model_bundle_save_quantized(&model, &encoder, &meta, &config, NULL, path);
+    bpe_encoder_free(&encoder);
+    model_free(&model);
+    return rc == BUNDLE_SUCCESS ? 0 : -10 - (int)rc;
+}
+
+typedef struct {
+    neural_model_t model;
+    bpe_encoder_t *encoder;
+    model_kv_cache_t cache;
+} rh_session_t;
+
+void *rh_load(const char *path) {
+    rh_session_t *s = calloc(1, sizeof(*s));
+    if (!s) return NULL;
+    model_bundle_metadata_t meta;
+    if (model_bundle_load(&s->model, &s->encoder, &meta, path) != BUNDLE_SUCCESS ||
+        model_kv_cache_init(&s->cache, &s->model) != MODEL_SUCCESS) {
+        free(s);
+        return NULL;
+    }
+    return s;
+}
+
+void rh_free(void *handle) {
+    rh_session_t *s = handle;
+    if (!s) return;
+    model_kv_cache_free(&s->cache);
+    if (s->encoder) { bpe_encoder_free(s->encoder); free(s->encoder); }
+    model_free(&s->model);
+    free(s);
+}
+
+size_t rh_param_count(void *handle) { return ((rh_session_t *)handle)->model.total_param_count; }
+const float *rh_params(void *handle) { return ((rh_session_t *)handle)->model.params; }
+void rh_reset(void *handle) { model_kv_cache_reset(&((rh_session_t *)handle)->cache); }
+
+int rh_forward_token(void *handle, uint32_t token, float *logits) {
+    rh_session_t *s = handle;
+    return model_forward_token(&s->model, &s->cache, token, logits) == MODEL_SUCCESS ? 0 : -1;
+}
+
+/* The decode loop of generation_decode_with_options (src/cli/generation.c:
+ * 231-295) with the tokenizer treated as fully trained (vocab_size == V):
+ * control ids `masked` are set to -FLT_MAX before each draw, repetition
+ * penalty 1.0 (a no-op), no stop sequences. Sequences run one after another,
+ * as the reference does. `out_tokens` is [n_seq][n_new]; `out_logits`, when not
+ * NULL, receives the raw logits each draw was taken from, [n_seq][n_new][V]. */
+int rh_generate(void *handle, const uint32_t *prompts, size_t n_seq,
+                size_t prompt_len, size_t n_new, int strategy,
+                float temperature, size_t top_k, float top_p,
+                const uint64_t *seeds, const uint32_t *masked, size_t n_masked,
+                uint32_t *out_tokens, float *out_logits) {
+    rh_session_t *s = handle;
+    const size_t vocab = s->model.vocab_size;
+    float *logits = s->model.ws_logits;
+    for (size_t q = 0; q < n_seq; q++) {
+        model_kv_cache_reset(&s->cache);
+        for (size_t i = 0; i < prompt_len; i++) {
+            if (model_forward_token(&s->model, &s->cache, prompts[q * prompt_len + i],
+                                    logits) != MODEL_SUCCESS) return -1;
+        }
+        uint64_t rng = seeds ? dranzer_rng_stream(seeds[q], DRANZER_RNG_STREAM_SAMPLING) : 0;
+        for (size_t i = 0; i < n_new; i++) {
+            for (size_t m = 0; m < n_masked; m++)
+                if (masked[m] < vocab) logits[masked[m]] = -FLT_MAX;
+            if (out_logits) memcpy(out_logits + (q * n_new + i) * vocab, logits, vocab * sizeof(float));
+            uint32_t next = sample_next_token(logits, vocab, (sampling_strategy_t)strategy,
+                                              temperature, top_k, top_p,
+                                              seeds ? &rng : NULL);
+            out_tokens[q * n_new + i] = next;
+            if (i + 1 < n_new &&
+                model_forward_token(&s->model, &s->cache, next, logits) != MODEL_SUCCESS)
+                return -2;
+        }
+    }
+    return 0;
+}
+
+/* Quantized weight matrix through the reference's encoder and INT8/INT4
+ * matmul (src/core/quantized_matmul.c). */
+void *rh_qmat_encode(const float *values, size_t k, size_t n, int bits, int granularity) {
+    quantized_weight_matrix_t *q = calloc(1, sizeof(*q));
+    if (!q) return NULL;
+    if (quantized_weight_matrix_encode(q, values, k, n, bits,
+                                       (quant_granularity_t)granularity) != 0) {
+        free(q);
+        return NULL;
+    }
+    return q;
+}
+
+const float *rh_qmat_scales(void *h, size_t *count) {
+    quantized_weight_matrix_t *q = h;
+    *count = q->scale_count;
+    return q->scales;
+}
+
+const uint8_t *rh_qmat_packed(void *h, size_t *size) {
+    quantized_weight_matrix_t *q = h;
+    *size = q->packed_size;
+    return q->packed;
+}
+
+int rh_qmat_matmul(void *h, const float *a, float *c, size_t m) {
+    quantized_weight_matrix_t *q = h;
+    return matmul_quantized_weight(a, q, c, m, q->rows, 0);
+}
+
+void rh_qmat_free(void *h) {
+    quantized_weight_matrix_free(h);
+    free(h);
+}
+
+double rh_now(void) {
+    struct timespec ts;
+    clock_gettime(CLOCK_MONOTONIC, &ts);
+    return (double)ts.tv_sec + 1e-9 * (double)ts.tv_nsec;
+}
+
+/* Threads the reference's OpenMP regions use from the calling thread on. */
+void rh_set_omp_threads(int n) { omp_set_num_threads(n); }

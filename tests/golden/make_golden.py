@@ -1,0 +1,226 @@
+"""Generate tests/golden/*.npz from the reference's own sources.
+
+Run here, where the DRANZER tree is present:  make -C oracle ref &&
+python tests/golden/make_golden.py. Every vector comes out of
+oracle/_ref/libdzref.so, i.e. the reference's C sources compiled with its own
+flags (-O3 -ffast-math) plus oracle/ref_harness.c. Inputs are the synthetic
+generators described in tests/_models.py and the fill patterns of the
+reference's tests (src/tests/core/test_quantize.c:81-90,
+src/tests/core/test_quantized_matmul.c:25-29), restated here.
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(HERE))
+
+from _native_oracle import (GREEDY, STREAM_DROPOUT, STREAM_INIT, STREAM_SAMPLING,  # noqa: E402
+                            STREAM_TESTING, TOPP, TOPK, FLT_MAX, RefHarness)
+
+ref = RefHarness()
+L = ref.L
+
+
+def rng_stream(seed, stream):
+    return L.dranzer_rng_stream(seed, stream)
+
+
+def gaussian(state, count, sd):
+    out = np.empty(count, np.float32)
+    L.rh_fill_gaussian(state.ctypes.data, out.ctypes.data, count, sd)
+    return out
+
+
+def prompt_ids(state, count, vocab, excluded=(256, 257, 258, 259)):
+    out = []
+    while len(out) < count:
+        t = L.dranzer_rng_next(state.ctypes.data) % vocab
+        if t not in excluded:
+            out.append(t)
+    return np.array(out, np.uint32)
+
+
+def fill_quantize_test(count, salt):
+    i = np.arange(count, dtype=np.int64)
+    base = ((i * 37 + salt * 11) % 71 - 35).astype(np.float32) / np.float32(17.0)
+    base = np.where(i % 23 == 0, base * np.float32(12.0), base)
+    return base.astype(np.float32)
+
+
+def fill_qmm_test(count, salt):
+    i = np.arange(count, dtype=np.int64)
+    return (((i * 29 + salt * 17) % 97 - 48).astype(np.float32) / np.float32(31.0)).astype(np.float32)
+
+
+def fnv(data):
+    data = np.ascontiguousarray(data).view(np.uint8)
+    h = 0xCBF29CE484222325
+    # vectorised FNV-1a is sequential; chunk through numpy scalars is slow, so use the oracle
+    from _native_oracle import Oracle
+    return Oracle().fnv1a(data, h)
+
+
+def gen_rng():
+    seeds = np.array([0, 1, 2, 3, 7, 42, 2000, 2063, 12345678901234], np.uint64)
+    streams = np.array([STREAM_INIT, STREAM_DROPOUT, STREAM_SAMPLING, STREAM_TESTING], np.uint64)
+    init = np.zeros((len(seeds), len(streams)), np.uint64)
+    draws = np.zeros((len(seeds), len(streams), 8), np.uint64)
+    units = np.zeros((len(seeds), len(streams), 4), np.float64)
+    for a, s in enumerate(seeds):
+        for b, st in enumerate(streams):
+            state = np.array([rng_stream(int(s), int(st))], np.uint64)
+            init[a, b] = state[0]
+            for k in range(8):
+                draws[a, b, k] = L.dranzer_rng_next(state.ctypes.data)
+            for k in range(4):
+                units[a, b, k] = L.dranzer_rng_unit(state.ctypes.data)
+    st = np.array([rng_stream(0, STREAM_TESTING)], np.uint64)
+    g = gaussian(st, 4096, 0.02)
+    np.savez_compressed(os.path.join(HERE, "rng.npz"), seeds=seeds, streams=streams, init=init,
+                        draws=draws, units=units, gaussian_seed0=g)
+
+
+def gen_quant():
+    cases = {}
+    shapes = [(1, 1), (1, 64), (64, 1), (3, 5), (16, 16), (7, 129)]
+    n = 0
+    for si, (r, c) in enumerate(shapes):
+        for bits in (2, 3, 4, 5, 8, 12, 16):
+            for g in (0, 1, 2):
+                w = fill_quantize_test(r * c, si * 7 + bits).reshape(r, c)
+                s, p = ref.quantize_pack(w, bits, g)
+                cases[f"c{n}_w"] = w
+                cases[f"c{n}_meta"] = np.array([r, c, bits, g], np.int64)
+                cases[f"c{n}_s"] = s
+                cases[f"c{n}_p"] = p
+                n += 1
+    # N(0, 0.02) matrix, the bundle generator's distribution
+    st = np.array([rng_stream(11, STREAM_TESTING)], np.uint64)
+    w = gaussian(st, 192 * 320, 0.02).reshape(192, 320)
+    # adversarial columns: exact half-steps (round-half-away ties), signed zeros,
+    # an all-zero column, subnormals, a lone outlier
+    qmax8 = 127
+    w[:, 0] = 0.0
+    w[:, 1] = -0.0
+    w[0, 2] = np.float32(127 * 0.001)
+    w[1:, 2] = (np.arange(191, dtype=np.float32) % 127 - 63 + 0.5).astype(np.float32) * np.float32(0.001)
+    w[:, 3] = np.float32(1e-40) * np.arange(192, dtype=np.float32)
+    w[5, 4] = np.float32(3.0)
+    cases["adv_w"] = w
+    for bits in (4, 8):
+        for g in (0, 1, 2):
+            s, p = ref.quantize_pack(w, bits, g)
+            cases[f"c{n}_meta"] = np.array([192, 320, bits, g], np.int64)
+            cases[f"c{n}_s"] = s
+            cases[f"c{n}_p"] = p
+            n += 1
+    cases["count"] = np.array(n)
+    # full C3 weight matrices (K=4096 x N), codes and scales pinned by FNV-1a
+    hashes = []
+    for N in (4096, 11008, 32000):
+        st = np.array([rng_stream(3, STREAM_TESTING)], np.uint64)
+        # X[M=1..512,K] comes first in the seed-3 stream; the largest M is drawn
+        # and W follows it, as bench and tests do
+        gaussian(st, 512 * 4096, 1.0)
+        wN = gaussian(st, 4096 * N, 0.02).reshape(4096, N)
+        for bits in (8, 4):
+            s, p = ref.quantize_pack(wN, bits, 2)
+            hashes.append([N, bits, fnv(s), fnv(p)])
+    cases["c3_hashes"] = np.array(hashes, np.uint64)
+    np.savez_compressed(os.path.join(HERE, "quant.npz"), **cases)
+
+
+def gen_qmm():
+    out = {}
+    shapes = [(1, 64, 257), (17, 33, 47), (5, 7, 3), (16, 16, 16)]
+    n = 0
+    for (m, k, nn) in shapes:
+        for bits in (4, 8):
+            for g in (0, 1, 2):
+                a = fill_qmm_test(m * k, 1).reshape(m, k)
+                b = fill_qmm_test(k * nn, 2).reshape(k, nn)
+                h = ref.qmat(b, bits, g)
+                c = ref.qmat_matmul(h, a, nn)
+                L.rh_qmat_free(h)
+                out[f"t{n}_a"], out[f"t{n}_b"], out[f"t{n}_c"] = a, b, c
+                out[f"t{n}_meta"] = np.array([m, k, nn, bits, g], np.int64)
+                n += 1
+    out["count"] = np.array(n)
+    # C3 shapes at K=4096, N=4096, M in {1, 8}: reference INT8/INT4 outputs
+    st = np.array([rng_stream(3, STREAM_TESTING)], np.uint64)
+    x = gaussian(st, 512 * 4096, 1.0).reshape(512, 4096)
+    w = gaussian(st, 4096 * 4096, 0.02).reshape(4096, 4096)
+    for bits in (8, 4):
+        h = ref.qmat(w, bits, 2)
+        out[f"c3_m8_int{bits}"] = ref.qmat_matmul(h, x[:8], 4096)
+        L.rh_qmat_free(h)
+    np.savez_compressed(os.path.join(HERE, "qmm.npz"), **out)
+
+
+def gen_model(name, vocab, dim, heads, layers, max_seq, wseed, bits, prompt_seed, n_seq, plen,
+              n_new, strategy, temperature, top_k, top_p, seeds, logits_seqs):
+    path = f"/tmp/dz_golden_{name}.bin"
+    rc = L.rh_build_bundle(path.encode(), vocab, dim, heads, layers, max_seq, wseed, bits, 2)
+    assert rc == 0, rc
+    h = L.rh_load(path.encode())
+    st = np.array([rng_stream(prompt_seed, STREAM_TESTING)], np.uint64)
+    prompts = prompt_ids(st, n_seq * plen, vocab).reshape(n_seq, plen)
+    toks = np.empty((n_seq, n_new), np.uint32)
+    lg = np.empty((n_seq, n_new, vocab), np.float32)
+    sd = np.array(seeds, np.uint64) if seeds is not None else None
+    mk = np.array([256, 257, 258, 259], np.uint32)
+    rc = L.rh_generate(h, prompts.ctypes.data, n_seq, plen, n_new, strategy, temperature, top_k,
+                       top_p, sd.ctypes.data if sd is not None else None, mk.ctypes.data, 4,
+                       toks.ctypes.data, lg.ctypes.data)
+    assert rc == 0
+    # prompt-position logits of sequence 0 (prefill parity)
+    L.rh_reset(h)
+    pl = np.empty((plen, vocab), np.float32)
+    for i in range(plen):
+        L.rh_forward_token(h, int(prompts[0, i]), pl[i].ctypes.data)
+    L.rh_free(h)
+    with open(path, "rb") as f:
+        blob = np.frombuffer(f.read(), np.uint8)
+    os.remove(path)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"),
+                        spec=np.array([vocab, dim, heads, layers, max_seq, wseed, bits], np.int64),
+                        prompts=prompts, tokens=toks, logits=lg[:logits_seqs],
+                        prompt_logits=pl, bundle_fnv=np.array([fnv(blob)], np.uint64),
+                        bundle_size=np.array([blob.size], np.int64),
+                        sampling=np.array([strategy, top_k], np.int64),
+                        sampling_f=np.array([temperature, top_p], np.float32),
+                        seeds=np.array(seeds if seeds is not None else [], np.uint64))
+
+
+def gen_bundle_small():
+    path = "/tmp/dz_golden_small_bundle.bin"
+    for bits in (4, 8):
+        assert L.rh_build_bundle(path.encode(), 300, 16, 2, 2, 8, 9, bits, 2) == 0
+        with open(path, "rb") as f:
+            blob = np.frombuffer(f.read(), np.uint8)
+        os.remove(path)
+        blob.tofile(os.path.join(HERE, f"bundle_small_int{bits}.bin"))
+
+
+def gen_pe():
+    t = np.empty((64, 128), np.float32)
+    assert L.compute_positional_encoding(t.ctypes.data, 64, 128) == 0
+    np.savez_compressed(os.path.join(HERE, "pe.npz"), pe_64x128=t)
+
+
+if __name__ == "__main__":
+    gen_rng()
+    gen_quant()
+    gen_qmm()
+    gen_pe()
+    gen_bundle_small()
+    # config 1: INT8 greedy, batch 1, 16 prompt + 48 decode
+    gen_model("c1", 512, 128, 4, 4, 64, 0, 8, 1, 1, 16, 48, GREEDY, 0.0, 0, 0.0, None, 1)
+    # config 2: INT4 top-p 0.9 at temperature 0.8, 64 x (32 + 32), seed 2*1000+i
+    gen_model("c2", 512, 128, 4, 4, 64, 0, 4, 2, 64, 32, 32, TOPP, 0.8, 0, 0.9,
+              [2000 + i for i in range(64)], 4)
+    # a ring-eviction case: capacity 32 (max_seq 32), 24 prompt + 40 decode, top-k 5
+    gen_model("ring", 400, 64, 2, 2, 32, 7, 8, 3, 2, 24, 40, TOPK, 0.8, 5, 0.0, [70, 71], 2)
+    print("golden fixtures written to", HERE)

@@ -1,0 +1,96 @@
+"""Quantized weight matrices on the device: layout round trip (bit-exact codes
+and unpack), and C = A . deq(W) against the reference's outputs and the oracle
+(tolerance of src/tests/core/test_quantized_matmul.c:79: 1e-4 * (1 + max|ref|))."""
+import numpy as np
+import pytest
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+
+def _tol_ok(c, ref):
+    err = np.abs(c - ref).max()
+    return err <= 1e-4 * (1 + np.abs(ref).max()), err
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (7, 3), (33, 47), (64, 257), (128, 384), (4096, 32000 // 16),
+                                   (600, 50257 // 8), (1000, 130)])
+@pytest.mark.parametrize("bits", [4, 8])
+@pytest.mark.parametrize("gran", [0, 1, 2])
+def test_layout_round_trip_bit_exact(gpu, shape, bits, gran):
+    rng = np.random.RandomState(shape[0] * 7 + shape[1])
+    w = (rng.randn(*shape) * 0.02).astype(np.float32)
+    s, p = gpu.quantize_pack(w, bits, gran)
+    q = gpu.QuantizedWeightMatrix(s, p, shape[0], shape[1], bits, gran)
+    np.testing.assert_array_equal(q.codes(), p)
+    ref = gpu.quantize_unpack(s, p, shape[0], shape[1], bits, gran)
+    np.testing.assert_array_equal(q.unpack().view(np.uint32), ref.view(np.uint32))
+    q.close()
+
+
+def test_matmul_reference_test_shapes(gpu):
+    g = golden("qmm.npz")
+    for n in range(int(g["count"])):
+        m, k, nn, bits, gran = (int(x) for x in g[f"t{n}_meta"])
+        q = gpu.QuantizedWeightMatrix.encode(g[f"t{n}_b"], bits, gran)
+        ok, err = _tol_ok(q.matmul(g[f"t{n}_a"]), g[f"t{n}_c"])
+        assert ok, (m, k, nn, bits, gran, err)
+        q.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_matmul_c3_reference_outputs(gpu, bits):
+    """C3 K=N=4096, M=8 and M=1 against the reference's matmul_quantized_weight."""
+    st = np.array([gpu.rng_stream(3, gpu.STREAM_TESTING)], np.uint64)
+    x = gpu.synth_gaussian(st, 512 * 4096, 1.0).reshape(512, 4096)
+    w = gpu.synth_gaussian(st, 4096 * 4096, 0.02).reshape(4096, 4096)
+    ref = golden("qmm.npz")[f"c3_m8_int{bits}"]
+    q = gpu.QuantizedWeightMatrix.encode(w, bits)
+    ok, err = _tol_ok(q.matmul(x[:8]), ref)
+    assert ok, err
+    ok1, err1 = _tol_ok(q.matmul(x[:1]), ref[:1])
+    assert ok1, err1
+    q.close()
+
+
+@pytest.mark.parametrize("N", [4096, 11008, 32000])
+@pytest.mark.parametrize("bits", [8, 4])
+def test_matmul_c3_sweep_vs_oracle(gpu, oracle, N, bits):
+    """Every C3 (M, N) at K=4096; the oracle checks a seeded sample of columns
+    (column scales make a column slice quantize to the same codes)."""
+    st = np.array([gpu.rng_stream(3, gpu.STREAM_TESTING)], np.uint64)
+    x = gpu.synth_gaussian(st, 512 * 4096, 1.0).reshape(512, 4096)
+    w = gpu.synth_gaussian(st, 4096 * N, 0.02).reshape(4096, N)
+    q = gpu.QuantizedWeightMatrix.encode(w, bits)
+    cols = np.sort(np.random.RandomState(N + bits).choice(N, 96, replace=False))
+    s_sub, p_sub = oracle.quantize_pack(np.ascontiguousarray(w[:, cols]), bits, 2)
+    for M in (1, 8, 64, 512):
+        c = q.matmul(x[:M])
+        assert c.shape == (M, N) and np.isfinite(c).all()
+        ref = oracle.matmul_quantized(x[:M], 4096, len(cols), s_sub, p_sub, bits, 2)
+        ok, err = _tol_ok(c[:, cols], ref)
+        assert ok, (M, err)
+    q.close()
+
+
+def test_matmul_ragged_and_unaligned(gpu, oracle):
+    rng = np.random.RandomState(1)
+    for (m, k, n) in [(13, 100, 77), (3, 9, 5), (1, 4095, 33), (9, 4104, 1)]:
+        for bits in (4, 8):
+            w = (rng.randn(k, n) * 0.05).astype(np.float32)
+            buf = rng.randn(m * k + 1).astype(np.float32)
+            a = buf[1:].reshape(m, k)                      # not 16-byte aligned
+            q = gpu.QuantizedWeightMatrix.encode(w, bits)
+            s, p = oracle.quantize_pack(w, bits, 2)
+            ref = oracle.matmul_quantized(np.ascontiguousarray(a), k, n, s, p, bits, 2)
+            ok, err = _tol_ok(q.matmul(a), ref)
+            assert ok, (m, k, n, bits, err)
+            q.close()
+
+
+def test_matmul_rejects_bad_k(gpu):
+    q = gpu.QuantizedWeightMatrix.encode(np.ones((8, 4), np.float32), 8)
+    with pytest.raises(gpu.DzError):
+        q.matmul(np.ones((2, 7), np.float32))
+    q.close()
