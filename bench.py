@@ -410,8 +410,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="c2")
     ap.add_argument("--impl", default="dz", choices=["dz", "reference"])
+    ap.add_argument("--probe", choices=["qmv"], help="run only the C3 quantized-matvec probe (profiling target)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.probe == "qmv":
+        import torch
+        import dranzer_b200 as dz
+        stream = torch.cuda.Stream()
+        print(json.dumps({"quant_matvec": quant_matvec_probe(dz, torch, stream, peaks()[0])}))
+        return
     from dranzer_b200 import workloads as W
     wl = W.WORKLOADS[args.workload]
     out = run_reference(args, wl) if args.impl == "reference" else run_dz(args, wl)
