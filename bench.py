@@ -314,9 +314,10 @@ def run_dz(args, wl):
         dev_ms, e2e_ms = float(t[0]), float(t[1])
 
     # per-kernel-class CUDA-event timing of one eager job
-    stats = (_native.DzKernelStat * 5)()
+    nk = len(_native.KERNEL_CLASSES) + len(_native.FUSED_PHASES)
+    stats = (_native.DzKernelStat * nk)()
     _native.check(L.dz_cuda_profile_generate(cache.handle, pd.data_ptr(), wl.prompt_len, wl.n_new,
-                                             ctypes.byref(samp.c), seeds_ptr, od.data_ptr(), stats, 5),
+                                             ctypes.byref(samp.c), seeds_ptr, od.data_ptr(), stats, nk),
                   "profile_generate")
     classes = {}
     for k, name in enumerate(_native.KERNEL_CLASSES):
@@ -325,6 +326,8 @@ def run_dz(args, wl):
             classes[name] = {"launches": int(s.launches), "total_ms": round(s.total_ms, 4),
                              "avg_us": round(1e3 * s.total_ms / s.launches, 3),
                              "bytes_per_launch": int(s.bytes / s.launches)}
+    phases = {name: round(stats[len(_native.KERNEL_CLASSES) + k].total_ms, 4)
+              for k, name in enumerate(_native.FUSED_PHASES) if stats[len(_native.KERNEL_CLASSES) + k].total_ms}
     dom = max(classes, key=lambda n: classes[n]["total_ms"])
     d = classes[dom]
     achieved = d["bytes_per_launch"] / (d["avg_us"] * 1e-6) / 1e9
@@ -358,8 +361,12 @@ def run_dz(args, wl):
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                          "traffic": None,
-                         "note": "all weights and KV of this workload fit in L2; the kernel is latency-bound"},
+                         "note": "bytes = weight codes+scales+fp32 tensors each sequence streams per step "
+                                 "x steps x sequences; all of it is L2-resident for this workload, so the "
+                                 "kernel is latency/L2 bound, not HBM bound"},
+            "path": "fused" if cache.uses_fused(samp) else "layered",
             "kernels": classes,
+            "fused_phases_ms": phases,
             "clocks": clk,
         }
     if rank == 0 and world == 1:

@@ -335,6 +335,14 @@ class KVCache:
         check(lib().dz_cuda_cache_create(model.handle, batch, self.capacity, ctypes.byref(h)), "cache_create")
         self.handle = h.value
 
+    PATH_AUTO, PATH_LAYERED, PATH_FUSED = 0, 1, 2
+
+    def set_path(self, path):
+        check(lib().dz_cuda_cache_set_path(self.handle, path), "cache_set_path")
+
+    def uses_fused(self, sampling=None):
+        return bool(lib().dz_cuda_cache_uses_fused(self.handle, ctypes.byref(sampling.c) if sampling else None))
+
     def set_stream(self, stream_ptr):
         check(lib().dz_cuda_cache_set_stream(self.handle, stream_ptr), "cache_set_stream")
 

@@ -52,7 +52,8 @@ class DzKernelStat(ctypes.Structure):
     _fields_ = [("kind", U32), ("launches", U32), ("total_ms", F64), ("bytes", F64), ("flops", F64)]
 
 
-KERNEL_CLASSES = ["step_begin", "qmv", "attention", "layernorm", "select"]
+KERNEL_CLASSES = ["step_begin", "qmv", "attention", "layernorm", "select", "seqgen"]
+FUSED_PHASES = ["embed", "weight_wait", "qmv", "attention", "layernorm", "select"]
 
 
 class DzSampling(ctypes.Structure):
@@ -110,6 +111,8 @@ SIGNATURES = {
     "dz_cuda_generate_async": (I32, [P, P, SZ, SZ, P, P, P]),
     "dz_cuda_generate_launches": (SZ, [P, SZ, SZ, P]),
     "dz_cuda_profile_generate": (I32, [P, P, SZ, SZ, P, P, P, P, SZ]),
+    "dz_cuda_cache_set_path": (I32, [P, I32]),
+    "dz_cuda_cache_uses_fused": (I32, [P, P]),
 }
 
 _lib = None

@@ -18,6 +18,7 @@
 #include "decode.cuh"
 #include "qmv.cuh"
 #include "select.cuh"
+#include "seqgen.cuh"
 
 using namespace dz;
 
@@ -426,6 +427,12 @@ struct dz_cuda_model {
     DevQMat head;
     size_t step_bytes = 0;
     std::vector<void*> f32_allocs;
+    // fused one-CTA-per-sequence generation (seqgen.cuh), when the model fits it
+    bool seq_ok = false;
+    int seq_bits = 0, seq_buf_bytes = 0;
+    SeqLayer* seq_layers = nullptr;   // device array [L]
+    SeqMat seq_head{};
+    std::vector<void*> seq_blobs;
 };
 
 static void model_release(dz_cuda_model_t* m) {
@@ -437,6 +444,8 @@ static void model_release(dz_cuda_model_t* m) {
     }
     free_qmat(m->head);
     for (void* p : m->f32_allocs) cudaFree(p);
+    cudaFree(m->seq_layers);
+    for (void* b : m->seq_blobs) cudaFree(b);
     delete m;
 }
 
@@ -450,6 +459,114 @@ static int upload_f32(dz_cuda_model_t* m, const dz_tensor_blob_t& t, size_t expe
     DZ_CUDA(cudaMemcpyAsync(d, t.f32, expect * 4, cudaMemcpyHostToDevice, st));
     *out = d;
     return DZ_OK;
+}
+
+constexpr int SEQ_SMEM_LIMIT = 232448;   // 227 KB of shared memory per block on sm_100
+constexpr int SEQ_BUF_LIMIT = 96 * 1024;
+
+// One fused-kernel blob: [codes | column scales (Np) | bias | gamma, beta], each
+// section 16-byte aligned, assembled on the device from the model's arrays.
+static bool seq_blob(dz_cuda_model_t* m, const DevQMat& q, const float* bias, int nbias, const float* gamma,
+                     const float* beta, int D, SeqMat* out) {
+    auto r16 = [](size_t n) { return (n + 15) & ~(size_t)15; };
+    size_t off = r16(q.code_bytes);
+    const size_t scale_off = off;
+    off += r16((size_t)q.Np * 4);
+    const size_t bias_off = bias ? off : 0;
+    if (bias) off += r16((size_t)nbias * 4);
+    const size_t gamma_off = gamma ? off : 0;
+    if (gamma) off += r16((size_t)D * 4) * 2;
+    uint8_t* blob = nullptr;
+    if (cudaMalloc(&blob, off) != cudaSuccess) return false;
+    m->seq_blobs.push_back(blob);
+    bool ok = cudaMemcpy(blob, q.codes, q.code_bytes, cudaMemcpyDeviceToDevice) == cudaSuccess &&
+              cudaMemcpy(blob + scale_off, q.col_scale, (size_t)q.Np * 4, cudaMemcpyDeviceToDevice) == cudaSuccess;
+    if (ok && bias) ok = cudaMemcpy(blob + bias_off, bias, (size_t)nbias * 4, cudaMemcpyDeviceToDevice) == cudaSuccess;
+    if (ok && gamma) {
+        ok = cudaMemcpy(blob + gamma_off, gamma, (size_t)D * 4, cudaMemcpyDeviceToDevice) == cudaSuccess &&
+             cudaMemcpy(blob + gamma_off + (size_t)D * 4, beta, (size_t)D * 4, cudaMemcpyDeviceToDevice) ==
+                 cudaSuccess;
+    }
+    if (!ok) return false;
+    out->blob = blob;
+    out->K = q.K;
+    out->N = q.N;
+    out->nchunks = q.nchunks;
+    out->nstrips = q.Np / 4;
+    out->bytes = (unsigned)off;
+    out->scale_off = (unsigned)scale_off;
+    out->bias_off = (unsigned)bias_off;
+    out->gamma_off = (unsigned)gamma_off;
+    return true;
+}
+
+
+// Shared-memory bytes of dz_seqgen_kernel (its carve-up in seqgen.cuh), with
+// or without the per-layer K/V staging area.
+static size_t seq_smem_bytes(const dz_cuda_model_t* m, int cap, bool kv_smem) {
+    const size_t D = m->desc.embedding_dim, F = 4 * D, V = m->desc.vocab_size, H = m->desc.num_heads;
+    size_t P = 1;
+    while (P < V) P <<= 1;
+    const size_t pv = V > (size_t)SEQ_THREADS ? V : (size_t)SEQ_THREADS;
+    auto r4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
+    const size_t table = (sizeof(SeqLayer) * m->layers.size() + 15) & ~(size_t)15;
+    return 2 * (size_t)m->seq_buf_bytes + 48 + table + 8 * (P > (size_t)SEQ_WARPS ? P : (size_t)SEQ_WARPS) +
+           4 * (5 * r4(D) + r4(F) + 2 * r4(V) + r4(H * (size_t)cap) + 64 + 2 * r4(pv)) +
+           (kv_smem ? 8 * r4((size_t)cap * D) : 0);
+}
+
+static bool seq_kv_smem(const dz_cuda_model_t* m, int cap) {
+    return seq_smem_bytes(m, cap, true) <= (size_t)SEQ_SMEM_LIMIT;
+}
+
+static size_t seq_smem_for(const dz_cuda_model_t* m, int cap) {
+    return seq_smem_bytes(m, cap, seq_kv_smem(m, cap));
+}
+
+// Decides whether the fused path can run this model and builds its blobs and
+// layer table.
+static void prepare_seqgen(dz_cuda_model_t* m) {
+    m->seq_ok = false;
+    if (m->layers.empty() || m->desc.embedding_dim % 4 != 0) return;  // 16-byte aligned activations
+    const int bits = m->head.bits;
+    if (bits != 4 && bits != 8 || m->head.k_scale) return;
+    for (auto& L : m->layers) {
+        if (!L.fused_qkv || L.qkv.k_scale || L.wo.k_scale || L.w1.k_scale || L.w2.k_scale) return;
+        for (const DevQMat* q : {&L.qkv, &L.wo, &L.w1, &L.w2})
+            if (q->bits != bits) return;
+    }
+    const int D = (int)m->desc.embedding_dim, F = 4 * D, V = (int)m->desc.vocab_size;
+    std::vector<SeqLayer> host(m->layers.size());
+    size_t buf = 0;
+    bool ok = true;
+    for (size_t l = 0; l < m->layers.size() && ok; l++) {
+        const DevLayer& L = m->layers[l];
+        ok = seq_blob(m, L.qkv, nullptr, 0, nullptr, nullptr, D, &host[l].qkv) &&
+             seq_blob(m, L.wo, nullptr, 0, L.g1, L.be1, D, &host[l].wo) &&
+             seq_blob(m, L.w1, L.b1, F, nullptr, nullptr, D, &host[l].w1) &&
+             seq_blob(m, L.w2, L.b2, D, L.g2, L.be2, D, &host[l].w2);
+        for (const SeqMat* q : {&host[l].qkv, &host[l].wo, &host[l].w1, &host[l].w2})
+            buf = q->bytes > buf ? q->bytes : buf;
+    }
+    ok = ok && seq_blob(m, m->head, m->out_bias, V, nullptr, nullptr, D, &m->seq_head);
+    if (ok) buf = m->seq_head.bytes > buf ? m->seq_head.bytes : buf;
+    if (ok && buf <= (size_t)SEQ_BUF_LIMIT && cudaMalloc(&m->seq_layers, host.size() * sizeof(SeqLayer)) == cudaSuccess) {
+        ok = cudaMemcpy(m->seq_layers, host.data(), host.size() * sizeof(SeqLayer), cudaMemcpyHostToDevice) ==
+             cudaSuccess;
+    } else {
+        ok = false;
+    }
+    if (!ok) {
+        cudaGetLastError();
+        for (void* b : m->seq_blobs) cudaFree(b);
+        m->seq_blobs.clear();
+        cudaFree(m->seq_layers);
+        m->seq_layers = nullptr;
+        return;
+    }
+    m->seq_bits = bits;
+    m->seq_buf_bytes = (int)buf;
+    m->seq_ok = true;
 }
 
 extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor_blob_t* tensors, size_t n,
@@ -543,6 +660,7 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
         return rc;
     }
     m->step_bytes = step;
+    prepare_seqgen(m);
     *out = m;
     return DZ_OK;
 }
@@ -594,6 +712,10 @@ struct dz_cuda_cache {
     cudaGraphExec_t step_graph = nullptr;
     std::map<GenKey, cudaGraphExec_t> gen_graphs;
     double prof_ctx_bytes_per_layer = 0, prof_ctx_flops_per_layer = 0;  // set per profiled step
+    int path = DZ_PATH_AUTO;
+    int* status = nullptr;        // device word the fused kernel reports a timeout in
+    unsigned long long* phase_ns = nullptr;  // [SEQ_PHASES] fused-kernel phase clock (profiling)
+    int* host_status = nullptr;   // pinned
     std::vector<void*> allocs;
 };
 
@@ -622,6 +744,7 @@ extern "C" void dz_cuda_cache_free(dz_cuda_cache_t* c) {
         cudaFree(c->masked);
         cudaFreeHost(c->host_rng);
         cudaFreeHost(c->host_ids);
+        cudaFreeHost(c->host_status);
         if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
     }
     model_release(c->model);
@@ -667,6 +790,9 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     if (!rc) rc = cache_alloc(c, (void**)&c->tok, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->rng, B * 8);
     if (!rc) rc = cache_alloc(c, (void**)&c->gen_seeds, B * 8);
+    if (!rc) rc = cache_alloc(c, (void**)&c->status, 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->phase_ns, SEQ_PHASES * 8);
+    if (!rc && cudaMallocHost(&c->host_status, 4) != cudaSuccess) rc = fail(DZ_E_NOMEM, "pinned host");
     if (!rc && cudaMallocHost(&c->host_rng, B * 8) != cudaSuccess) rc = fail(DZ_E_NOMEM, "pinned host");
     if (!rc && cudaMallocHost(&c->host_ids, B * 4) != cudaSuccess) rc = fail(DZ_E_NOMEM, "pinned host");
     if (!rc) {
@@ -677,7 +803,20 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
                 cudaSuccess)
             rc = fail(DZ_E_DEVICE, "select kernel shared memory");
     }
+    if (!rc && m->seq_ok) {
+        const size_t ss = seq_smem_for(m, c->cap);
+        if (ss <= (size_t)SEQ_SMEM_LIMIT) {
+            // the attribute is an upper bound shared by every cache: raise it to the limit
+            cudaError_t e = m->seq_bits == 8
+                ? cudaFuncSetAttribute(dz_seqgen_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SEQ_SMEM_LIMIT)
+                : cudaFuncSetAttribute(dz_seqgen_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SEQ_SMEM_LIMIT);
+            if (e != cudaSuccess) rc = fail(DZ_E_DEVICE, "fused kernel shared memory: %s", cudaGetErrorString(e));
+        }
+    }
     if (!rc) {
+        cudaMemsetAsync(c->status, 0, 4, c->stream);
         cudaMemsetAsync(c->start, 0, B * 4, c->stream);
         cudaMemsetAsync(c->length, 0, B * 4, c->stream);
         cudaMemsetAsync(c->total, 0, B * 8, c->stream);
@@ -898,10 +1037,71 @@ extern "C" int dz_cuda_select(dz_cuda_cache_t* c, const dz_sampling_t* s, uint64
     return DZ_OK;
 }
 
+// Whether the fused one-CTA-per-sequence kernel runs this generation.
+static bool use_seqgen(const dz_cuda_cache_t* c, const dz_sampling_t* s) {
+    const dz_cuda_model_t* m = c->model;
+    if (c->path == DZ_PATH_LAYERED || !m->seq_ok) return false;
+    if (seq_smem_for(m, c->cap) > (size_t)SEQ_SMEM_LIMIT) return false;
+    const bool sampled = s && s->strategy != 0 && s->temperature > 0.0f;
+    if (sampled && m->desc.vocab_size > (size_t)SEL_SORT_CAP) return false;
+    return true;
+}
+
+static int launch_seqgen(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                         const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
+    const dz_cuda_model_t* m = c->model;
+    SeqParams p;
+    memset(&p, 0, sizeof(p));
+    p.layers = m->seq_layers;
+    p.L = (int)m->layers.size();
+    p.D = (int)m->desc.embedding_dim;
+    p.H = (int)m->desc.num_heads;
+    p.V = (int)m->desc.vocab_size;
+    p.cap = c->cap;
+    p.bits = m->seq_bits;
+    p.head = m->seq_head;
+    p.emb = m->emb;
+    p.pe = m->pe;
+    p.pe_rows = m->pe_rows;
+    p.out_bias = m->out_bias;
+    p.keys = c->keys;
+    p.values = c->values;
+    p.start = c->start;
+    p.length = c->length;
+    p.total = c->total;
+    p.prompts = prompts;
+    p.plen = (int)plen;
+    p.out = out;
+    p.n_new = (int)n_new;
+    p.seeds = seeds;
+    p.strategy = s ? s->strategy : 0;
+    p.temperature = s ? s->temperature : 0.0f;
+    p.top_k = s ? (int)s->top_k : 0;
+    p.top_p = s ? s->top_p : 0.0f;
+    p.masked = (s && s->n_masked) ? c->masked : nullptr;
+    p.n_masked = s ? (int)s->n_masked : 0;
+    p.status = c->status;
+    p.buf_bytes = m->seq_buf_bytes;
+    p.B = c->B;
+    p.phase_ns = g_prof ? c->phase_ns : nullptr;
+    p.kv_smem = seq_kv_smem(m, c->cap) ? 1 : 0;
+    const size_t smem = seq_smem_for(m, c->cap);
+    ProfScope prof(DZ_KERNEL_SEQGEN, (double)m->step_bytes * c->B * ((double)plen + (double)n_new - 1.0), 0,
+                   c->stream);
+    // the dynamic shared-memory attribute was raised at cache creation (outside any capture)
+    if (m->seq_bits == 8) dz_seqgen_kernel<8><<<c->B, SEQ_THREADS, smem, c->stream>>>(p);
+    else dz_seqgen_kernel<4><<<c->B, SEQ_THREADS, smem, c->stream>>>(p);
+    return 1;
+}
+
 // The whole generation loop, enqueued on the cache's stream. Returns launches.
 static int enqueue_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
                             const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
     int launches = 0;
+    if (use_seqgen(c, s)) {
+        dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
+        return 1 + launch_seqgen(c, prompts, plen, n_new, s, seeds, out);
+    }
     const bool sampled = seeds != nullptr;
     if (sampled) {
         dz_seed_kernel<<<(c->B + 127) / 128, 128, 0, c->stream>>>(seeds, c->rng, c->B, DZ_RNG_STREAM_SAMPLING);
@@ -921,6 +1121,7 @@ extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t ple
                                             const dz_sampling_t* s) {
     if (!c) return 0;
     const dz_cuda_model_t* m = c->model;
+    if (use_seqgen(c, s)) return 2;
     size_t per_layer = 0;
     for (const auto& L : m->layers) per_layer += (L.fused_qkv ? 1 : 3) + 6;
     const size_t step = 1 + per_layer + 1;
@@ -996,8 +1197,28 @@ extern "C" int dz_cuda_generate(dz_cuda_cache_t* c, const uint32_t* prompts, siz
     int rc = dz_cuda_generate_async(c, c->gen_prompts, plen, n_new, s, seeds ? c->gen_seeds : nullptr, c->gen_out);
     if (rc) return rc;
     DZ_CUDA(cudaMemcpyAsync(out_tokens, c->gen_out, B * n_new * 4, cudaMemcpyDeviceToHost, c->stream));
+    DZ_CUDA(cudaMemcpyAsync(c->host_status, c->status, 4, cudaMemcpyDeviceToHost, c->stream));
     DZ_CUDA(cudaStreamSynchronize(c->stream));
+    if (*c->host_status != 0) {
+        cudaMemsetAsync(c->status, 0, 4, c->stream);
+        cudaStreamSynchronize(c->stream);
+        return fail(DZ_E_TIMEOUT, "generate: a weight-copy wait gave up on the device");
+    }
     return DZ_OK;
+}
+
+extern "C" int dz_cuda_cache_set_path(dz_cuda_cache_t* c, int path) {
+    if (!c || path < DZ_PATH_AUTO || path > DZ_PATH_FUSED) return fail(DZ_E_INVALID, "bad path");
+    if (path == DZ_PATH_FUSED && !c->model->seq_ok)
+        return fail(DZ_E_UNSUPPORTED, "the fused path cannot run this model");
+    DeviceGuard g(c->model->device);
+    clear_graphs(c);
+    c->path = path;
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_cache_uses_fused(const dz_cuda_cache_t* c, const dz_sampling_t* s) {
+    return c ? (int)use_seqgen(c, s) : 0;
 }
 
 extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
@@ -1013,6 +1234,7 @@ extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prom
         DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
     const bool sampled = seeds && s && s->strategy != 0 && s->temperature > 0.0f;
     std::vector<ProfRec> recs;
+    DZ_CUDA(cudaMemsetAsync(c->phase_ns, 0, SEQ_PHASES * 8, c->stream));
     g_prof = &recs;
     // eager launches, each bracketed by events; the attention byte count uses
     // the mean context of the run (prefill then decode, all sequences in step)
@@ -1045,5 +1267,13 @@ extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prom
         cudaEventDestroy(r.b);
     }
     if (e != cudaSuccess) return fail(DZ_E_DEVICE, "profile: %s", cudaGetErrorString(e));
+    if (use_seqgen(c, s) && n_stats > (size_t)DZ_PHASE_EMBED) {
+        unsigned long long ph[SEQ_PHASES];
+        DZ_CUDA(cudaMemcpy(ph, c->phase_ns, sizeof(ph), cudaMemcpyDeviceToHost));
+        for (int k = 0; k < SEQ_PHASES && (size_t)(DZ_PHASE_EMBED + k) < n_stats; k++) {
+            stats[DZ_PHASE_EMBED + k].launches = 0;
+            stats[DZ_PHASE_EMBED + k].total_ms = (double)ph[k] * 1e-6;
+        }
+    }
     return DZ_OK;
 }

@@ -1,0 +1,749 @@
+// Fused generation kernel for small models: one CTA runs a whole sequence -
+// prompt prefill, every decode step, every layer, the vocabulary head and the
+// draw - without leaving the kernel. It is the same arithmetic as the layered
+// path (qmv.cuh, decode.cuh, select.cuh: src/core/transformer.c:686-858,
+// src/cli/sampling.c:38-207, src/cli/generation.c:231-295), scheduled for
+// models whose every projection fits a shared-memory buffer (d = 128 at INT4
+// or INT8: 32 / 64 KB per matrix).
+//
+// Weights stream from L2/HBM into two shared-memory buffers with TMA bulk
+// copies (cp.async.bulk ... mbarrier::complete_tx): while the CTA computes
+// matrix i from one buffer, matrix i+1 lands in the other. One thread issues
+// the copies; waits on the mbarriers are bounded and, if one gives up, the CTA
+// records DZ_SEQ_TIMEOUT in the status word, lets its copies in flight land and
+// returns.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "qmv.cuh"
+#include "select.cuh"
+
+namespace dz {
+
+constexpr int SEQ_THREADS = 512;
+constexpr int SEQ_WARPS = SEQ_THREADS / 32;
+constexpr unsigned SEQ_WAIT_LIMIT = 1u << 30;  // poll bound behind the time bound
+constexpr uint64_t SEQ_WAIT_NS = 1000000000ull;  // a wait gives up after ~1 s
+constexpr int DZ_SEQ_TIMEOUT = 1;
+
+// One matrix as the fused kernel streams it: a contiguous blob of
+// [codes (strip layout) | column scales (Np floats) | extras], each section
+// 16-byte aligned. Extras: the bias of W1 / W2 / head, and for W_o and W2 the
+// gamma and beta of the LayerNorm that follows them. The TMA copy brings the
+// whole blob into shared memory, so epilogues read nothing from global memory.
+struct SeqMat {
+    const uint8_t* blob;
+    int K, N, nchunks, nstrips;
+    unsigned bytes;            // whole blob
+    unsigned scale_off;        // byte offset of the column scales
+    unsigned bias_off;         // byte offset of the bias (0: none)
+    unsigned gamma_off;        // byte offset of gamma, beta follows at +4*D bytes (0: none)
+};
+
+struct SeqLayer {
+    SeqMat qkv, wo, w1, w2;
+};
+
+struct SeqParams {
+    const SeqLayer* layers;
+    int L, D, H, V, cap, bits;
+    SeqMat head;
+    const float* emb;
+    const float* pe;
+    long long pe_rows;
+    const float* out_bias;
+    float* keys;               // [L][B][cap][D]
+    float* values;
+    int* start;                // ring state per sequence, read at entry, written at exit
+    int* length;
+    long long* total;
+    const uint32_t* prompts;   // [B][plen]
+    int plen;
+    uint32_t* out;             // [B][n_new]
+    int n_new;
+    const uint64_t* seeds;     // [B] or nullptr (greedy)
+    int strategy;
+    float temperature;
+    int top_k;
+    float top_p;
+    const uint32_t* masked;
+    int n_masked;
+    int* status;
+    int buf_bytes;             // bytes of each weight buffer
+    int B;
+    unsigned long long* phase_ns;  // optional [SEQ_PHASES]: CTA 0 accumulates time per phase
+    int kv_smem;               // stage each layer's K/V rows in shared memory
+};
+
+enum { SEQ_PH_EMBED = 0, SEQ_PH_WAIT, SEQ_PH_QMV, SEQ_PH_ATTENTION, SEQ_PH_NORM, SEQ_PH_SELECT, SEQ_PHASES };
+
+// ----------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Phase clock of CTA 0, thread 0 (profiling only).
+struct SeqClock {
+    unsigned long long* acc;
+    uint64_t t;
+    __device__ explicit SeqClock(unsigned long long* a) : acc(blockIdx.x == 0 && threadIdx.x == 0 ? a : nullptr) {
+        t = acc ? global_ns() : 0;
+    }
+    __device__ void mark(int phase) {
+        if (!acc) return;
+        const uint64_t n = global_ns();
+        acc[phase] += n - t;
+        t = n;
+    }
+};
+
+// Bounded wait (about one second); returns false when the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint64_t t0 = global_ns();
+    for (unsigned i = 0; i < SEQ_WAIT_LIMIT; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 255u && global_ns() - t0 > SEQ_WAIT_NS) return false;
+    }
+    return false;
+}
+
+// Global -> shared bulk copy completing on `bar` (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// --------------------------------------------------------- the kernel
+
+struct SeqSmem {
+    uint8_t* wbuf[2];
+    uint64_t* bar;     // [3]: weight buffers 0 and 1, K/V staging
+    float *x, *q, *att, *an, *ff, *fr, *logits, *scores, *red, *ev, *part, *part2;
+    float *ks, *vs;   // this layer's K / V rows staged in shared memory (or nullptr)
+    uint64_t* keys;
+    int* flag;         // [0] abort, [1] token broadcast, [2] top-p count, [3] drawn position
+    SeqLayer* layers;  // the layer table, copied from global memory at entry
+};
+
+// Matrices in consumption order within a step: per layer qkv, wo, w1, w2; then head.
+__device__ __forceinline__ const SeqMat& seq_mat(const SeqParams& p, const SeqLayer* layers, int idx) {
+    const int layer = idx >> 2;
+    if (layer >= p.L) return p.head;
+    const SeqLayer& L = layers[layer];
+    switch (idx & 3) {
+        case 0: return L.qkv;
+        case 1: return L.wo;
+        case 2: return L.w1;
+        default: return L.w2;
+    }
+}
+
+// Weight pipeline: matrix number `seq` (monotone over the whole job) lives in
+// buffer seq & 1; its barrier phase is (seq >> 1) & 1.
+struct SeqPipe {
+    int per_step;      // matrices per step: 4L + 1
+    long long issued;  // next matrix to issue
+    long long total;   // matrices the job consumes
+};
+
+__device__ __forceinline__ void seq_issue(const SeqParams& p, SeqSmem& s, SeqPipe& pipe) {
+    // thread 0 only; buffer (issued & 1) must be free
+    if (pipe.issued >= pipe.total) return;
+    const SeqMat& m = seq_mat(p, s.layers, (int)(pipe.issued % pipe.per_step));
+    const int b = (int)(pipe.issued & 1);
+    mbar_expect_tx(&s.bar[b], m.bytes);
+    const uint8_t* src = m.blob;
+    uint8_t* dst = s.wbuf[b];
+    for (unsigned off = 0; off < m.bytes; off += 32768u) {
+        const unsigned n = (m.bytes - off) < 32768u ? (m.bytes - off) : 32768u;
+        bulk_g2s(dst + off, src + off, n, &s.bar[b]);
+    }
+    pipe.issued++;
+}
+
+// Block-level quantized matvec from the shared-memory copy of matrix `m`:
+// y[n] = epi(n, sum_k x[k] * level(k, n) * col_scale[n]). Lanes split the
+// chunks of a strip in groups of G; groups reduce with shuffles.
+template <int BITS, typename Epi>
+__device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, const float* x, Epi epi) {
+    constexpr int KC = BITS == 8 ? 4 : 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int G = 1;
+    while (G < m.nchunks && G < 32) G <<= 1;
+    const int spw = 32 / G;                      // strips per warp per pass
+    const int gl = lane & (G - 1);
+    const uint4* w4 = reinterpret_cast<const uint4*>(wsm);
+    const float* scale = reinterpret_cast<const float*>(wsm + m.scale_off);
+    for (int s0 = warp * spw; s0 < m.nstrips; s0 += SEQ_WARPS * spw) {
+        const int s = s0 + lane / G;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        if (s < m.nstrips) {
+            for (int c = gl; c < m.nchunks; c += G) {
+                const uint4 w = w4[s * m.nchunks + c];
+                const int k0 = c * KC;
+                float xv[KC];
+                if (k0 + KC <= m.K) {
+#pragma unroll
+                    for (int q4 = 0; q4 < KC / 4; q4++) {
+                        const float4 v = reinterpret_cast<const float4*>(x + k0)[q4];
+                        xv[4 * q4] = v.x; xv[4 * q4 + 1] = v.y; xv[4 * q4 + 2] = v.z; xv[4 * q4 + 3] = v.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < KC; i++) xv[i] = (k0 + i < m.K) ? x[k0 + i] : 0.0f;
+                }
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float t = acc[j];
+#pragma unroll
+                    for (int i = 0; i < KC; i++)
+                        t = fmaf(xv[i], BITS == 8 ? dz_level8(ww[j], i) : dz_level4(ww[j], i), t);
+                    acc[j] = t;
+                }
+            }
+        }
+        // reduce the 4 column sums over the G lanes of the group
+        for (int off = G >> 1; off >= 1; off >>= 1) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+        }
+        if (s < m.nstrips) {
+            // every lane of the group holds the 4 sums; lanes 0..3 (or fewer,
+            // looping, when the group is narrower) write one column each
+            for (int j = gl; j < 4; j += G) {
+                const int n = s * 4 + j;
+                const float v = j == 0 ? acc[0] : j == 1 ? acc[1] : j == 2 ? acc[2] : acc[3];
+                if (n < m.N) epi(n, v * scale[n]);
+            }
+        }
+    }
+}
+
+// LayerNorm (src/core/tensor_ops.c:88-111) of D values in shared memory, by
+// warp 0 (shuffle reductions, no block barrier until the output is written).
+__device__ __forceinline__ void seq_layernorm(const float* in, float* out, const float* gamma, const float* beta,
+                                              int D, float* red) {
+    (void)red;
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float s = 0.0f;
+        for (int i = lane; i < D; i += 32) s += in[i];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        const float mean = s / (float)D;
+        float v = 0.0f;
+        for (int i = lane; i < D; i += 32) {
+            const float d = in[i] - mean;
+            v = fmaf(d, d, v);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        const float sd = sqrtf(v / (float)D + 1e-6f);
+        for (int i = lane; i < D; i += 32) out[i] = gamma[i] * ((in[i] - mean) / sd) + beta[i];
+    }
+    __syncthreads();
+}
+
+// Selection over the logits in shared memory; returns the token on every thread.
+__device__ uint32_t seq_select(const SeqParams& p, SeqSmem& s, uint64_t* rng) {
+    const int V = p.V;
+    float* lg = s.logits;
+    for (int m = threadIdx.x; m < p.n_masked; m += SEQ_THREADS) {
+        const uint32_t id = p.masked[m];
+        if (id < (uint32_t)V) lg[id] = -3.402823466e38f;
+    }
+    __syncthreads();
+    const bool greedy = p.strategy == 0 || !(p.temperature > 0.0f) || rng == nullptr ||
+                        (p.strategy == 1 && p.top_k == 0) ||
+                        (p.strategy == 2 && (p.top_p <= 0.0f || p.top_p > 1.0f)) ||
+                        (p.strategy != 1 && p.strategy != 2);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (greedy) {
+        uint64_t best = ~0ull;
+        for (int i = threadIdx.x; i < V; i += SEQ_THREADS) {
+            const uint64_t k = dz_desc_key(lg[i], (uint32_t)i);
+            best = k < best ? k : best;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, best, off);
+            best = o < best ? o : best;
+        }
+        if (lane == 0) s.keys[warp] = best;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint64_t mn = s.keys[0];
+            for (int w = 1; w < SEQ_WARPS; w++) mn = s.keys[w] < mn ? s.keys[w] : mn;
+            s.flag[1] = (int)(mn & 0xffffffffu);
+        }
+        __syncthreads();
+        const uint32_t tok = (uint32_t)s.flag[1];
+        __syncthreads();
+        return tok;
+    }
+    const float inv_t = 1.0f / p.temperature;
+    int P = 1;
+    while (P < V) P <<= 1;
+    for (int i = threadIdx.x; i < P; i += SEQ_THREADS)
+        s.keys[i] = i < V ? dz_desc_key(lg[i] * inv_t, (uint32_t)i) : ~0ull;
+    __syncthreads();
+    dz_bitonic_sort(s.keys, P);
+    const int nexp = p.strategy == 1 ? (p.top_k < V ? p.top_k : V) : V;
+    const float top = dz_key_value(s.keys[0]);
+    for (int i = threadIdx.x; i < nexp; i += SEQ_THREADS) s.ev[i] = dz_expf(dz_key_value(s.keys[i]) - top);
+    __syncthreads();
+    // The reference's running sums (sampling.c:80-94, :137-170) are sequential
+    // fp32 chains. One thread builds them as prefix arrays - every "acc +=
+    // e[i]" loop of the reference reads a prefix of the same chain P - with
+    // explicit round-to-nearest adds and multiplies (no FMA contraction, as
+    // the reference's x86 build has none); the searches then run in parallel.
+    float* Pre = s.part;                   // prefix sums of e
+    float* C = s.part2;                    // running sum of e[i] * (1/sum_all)
+    if (threadIdx.x == 0) {
+        // blocks of 8: loads first (they do not depend on the chain), then the
+        // dependent adds, then the stores
+        const float* ev = s.ev;
+        float acc = 0.0f;
+        int i = 0;
+        for (; i + 8 <= nexp; i += 8) {
+            float e8[8], o8[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) e8[u] = ev[i + u];
+#pragma unroll
+            for (int u = 0; u < 8; u++) { acc = __fadd_rn(acc, e8[u]); o8[u] = acc; }
+#pragma unroll
+            for (int u = 0; u < 8; u++) Pre[i + u] = o8[u];
+        }
+        for (; i < nexp; i++) {
+            acc = __fadd_rn(acc, ev[i]);
+            Pre[i] = acc;
+        }
+        if (p.strategy == 2) {
+            const float inv = __fdiv_rn(1.0f, acc);
+            float cum = 0.0f;
+            i = 0;
+            for (; i + 8 <= nexp; i += 8) {
+                float e8[8], o8[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) e8[u] = __fmul_rn(ev[i + u], inv);
+#pragma unroll
+                for (int u = 0; u < 8; u++) { cum = __fadd_rn(cum, e8[u]); o8[u] = cum; }
+#pragma unroll
+                for (int u = 0; u < 8; u++) C[i + u] = o8[u];
+            }
+            for (; i < nexp; i++) {
+                cum = __fadd_rn(cum, __fmul_rn(ev[i], inv));
+                C[i] = cum;
+            }
+        }
+        s.flag[2] = nexp;   // top-p candidate count, refined below
+        s.flag[3] = -1;     // selected position
+    }
+    __syncthreads();
+    if (p.strategy == 2) {
+        // cand = first i with C[i] >= top_p, plus one (nexp when none)
+        for (int i = threadIdx.x; i < nexp; i += SEQ_THREADS)
+            if (C[i] >= p.top_p) atomicMin(&s.flag[2], i + 1);
+        __syncthreads();
+    }
+    const int cand = s.flag[2];
+    if (threadIdx.x == 0) {
+        const float total = Pre[cand - 1];
+        s.red[0] = __fmul_rn((float)dz_rng_unit(rng), total);
+    }
+    __syncthreads();
+    const float r = s.red[0];
+    int* pos = &s.flag[3];
+    for (int i = threadIdx.x; i < cand; i += SEQ_THREADS)
+        if (Pre[i] >= r) atomicMin(reinterpret_cast<unsigned int*>(pos), (unsigned int)i);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const int at = s.flag[3] < 0 ? 0 : s.flag[3];   // no crossing: the reference keeps pairs[0]
+        s.flag[1] = (int)(s.keys[at] & 0xffffffffu);
+    }
+    __syncthreads();
+    const uint32_t tok = (uint32_t)s.flag[1];
+    __syncthreads();
+    return tok;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) {
+    extern __shared__ __align__(128) unsigned char seq_smem[];
+    const int b = blockIdx.x;
+    const int D = p.D, H = p.H, hd = D / H, F = 4 * D, V = p.V, cap = p.cap;
+
+    SeqSmem s;
+    unsigned char* cur = seq_smem;
+    s.wbuf[0] = cur; cur += p.buf_bytes;
+    s.wbuf[1] = cur; cur += p.buf_bytes;
+    s.bar = reinterpret_cast<uint64_t*>(cur); cur += 32;
+    s.flag = reinterpret_cast<int*>(cur); cur += 16;
+    s.layers = reinterpret_cast<SeqLayer*>(cur); cur += (sizeof(SeqLayer) * p.L + 15) & ~(size_t)15;
+    int P = 1;
+    while (P < V) P <<= 1;
+    s.keys = reinterpret_cast<uint64_t*>(cur); cur += 8 * (P > SEQ_WARPS ? P : SEQ_WARPS);
+    // float arrays, each rounded up to 16 bytes (bulk-copy destinations and
+    // float4 activation reads need the alignment); seq_smem_bytes mirrors this
+    float* f = reinterpret_cast<float*>(cur);
+    auto take = [&](int n) { float* r = f; f += (n + 3) & ~3; return r; };
+    s.x = take(D);
+    s.q = take(D);
+    s.att = take(D);
+    s.an = take(D);
+    s.fr = take(D);
+    s.ff = take(F);
+    s.logits = take(V);
+    s.ev = take(V);
+    s.scores = take(H * cap);
+    s.red = take(64);
+    const int pv = V > SEQ_THREADS ? V : SEQ_THREADS;
+    s.part = take(pv);
+    s.part2 = take(pv);
+    if (p.kv_smem) {
+        s.ks = take(cap * D);
+        s.vs = take(cap * D);
+    } else {
+        s.ks = s.vs = nullptr;
+    }
+
+    for (int i = threadIdx.x; i < (int)(sizeof(SeqLayer) * p.L / 4); i += SEQ_THREADS)
+        reinterpret_cast<uint32_t*>(s.layers)[i] = reinterpret_cast<const uint32_t*>(p.layers)[i];
+    if (threadIdx.x == 0) {
+        mbar_init(&s.bar[0], 1);
+        mbar_init(&s.bar[1], 1);
+        mbar_init(&s.bar[2], 1);
+        s.flag[0] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+
+    SeqPipe pipe;
+    pipe.per_step = 4 * p.L + 1;
+    const long long steps = (long long)p.plen + (p.n_new > 0 ? p.n_new - 1 : 0);
+    pipe.total = steps * pipe.per_step;
+    pipe.issued = 0;
+    if (threadIdx.x == 0) {
+        seq_issue(p, s, pipe);
+        seq_issue(p, s, pipe);
+    }
+    long long consumed = 0;
+
+    int start = p.start[b], length = p.length[b];
+    long long total = p.total[b];
+    uint64_t rng_state = 0;
+    uint64_t* rng = nullptr;
+    if (p.seeds) {
+        uint64_t st = dz_splitmix64(p.seeds[b] ^ dz_splitmix64(0x94d049bb133111ebull));
+        rng_state = st ? st : 0x9e3779b97f4a7c15ull;
+        rng = &rng_state;
+    }
+    const float denom = sqrtf((float)hd);
+    bool aborted = false;
+    unsigned kv_uses = 0;   // completed phases of the K/V staging barrier
+    bool kv_pending = false; // a K/V staging copy is in flight
+
+    // wait for matrix `consumed`, returns false on timeout (CTA-uniform)
+    SeqClock clk(p.phase_ns);
+    auto acquire = [&]() -> bool {
+        const int bi = (int)(consumed & 1);
+        const uint32_t parity = (uint32_t)((consumed >> 1) & 1);
+        if (threadIdx.x == 0 && !mbar_wait(&s.bar[bi], parity)) s.flag[0] = 1;
+        __syncthreads();
+        clk.mark(SEQ_PH_WAIT);
+        return s.flag[0] == 0;
+    };
+    // matrix `consumed` no longer read: refill its buffer with the one after next
+    auto release = [&]() {
+        // every thread is past its reads of this buffer; the next TMA write
+        // into it is issued after the barrier
+        __syncthreads();
+        if (threadIdx.x == 0) seq_issue(p, s, pipe);
+        consumed++;
+        clk.mark(SEQ_PH_QMV);
+    };
+
+    auto forward = [&](uint32_t tok) -> bool {
+        const long long pos = total;
+        int slot, ctx;
+        if (length < cap) {
+            slot = (start + length) % cap;
+            ctx = length + 1;
+        } else {
+            slot = start;
+            start = (start + 1) % cap;
+            ctx = cap;
+        }
+        if (tok >= (uint32_t)V) tok = 0;
+        const float* e = p.emb + (long long)tok * D;
+        if (pos < p.pe_rows) {
+            const float* pr = p.pe + pos * D;
+            for (int i = threadIdx.x; i < D; i += SEQ_THREADS) s.x[i] = e[i] + pr[i];
+        } else {
+            const float ln_base = logf(10000.0f);
+            for (int i = threadIdx.x; i < D; i += SEQ_THREADS) {
+                const float sc = expf(-((2.0f * (float)i) / (float)D) * ln_base);
+                const float ang = (float)pos * sc;
+                s.x[i] = e[i] + ((i % 2 == 0) ? sinf(ang) : cosf(ang));
+            }
+        }
+        __syncthreads();
+        clk.mark(SEQ_PH_EMBED);
+        for (int l = 0; l < p.L; l++) {
+            const SeqLayer& Ly = s.layers[l];
+            float* Kl = p.keys + (((long long)l * p.B + b) * cap) * D;
+            float* Vl = p.values + (((long long)l * p.B + b) * cap) * D;
+            // Stage the K/V rows this step attends to, except the new slot, into
+            // shared memory; the copy overlaps the QKV product below.
+            const int old_rows = ctx - 1 < cap ? (length < cap ? length : cap) : cap;
+            const bool staged = s.ks != nullptr && old_rows > 0;
+            kv_pending = staged;
+            if (staged && threadIdx.x == 0) {
+                // rows [0, old_rows) hold the retained tokens; the slot row is excluded
+                const int lo_rows = slot < old_rows ? slot : old_rows;
+                const int hi_first = slot + 1, hi_rows = old_rows - hi_first;
+                const unsigned bytes = (unsigned)((lo_rows + (hi_rows > 0 ? hi_rows : 0)) * D * 4) * 2u;
+                // order earlier generic writes (ring rows in global, last layer's
+                // reads of the staging area) before the async-proxy copy
+                asm volatile("fence.proxy.async;" ::: "memory");
+                mbar_expect_tx(&s.bar[2], bytes);
+                if (lo_rows > 0) {
+                    bulk_g2s(s.ks, Kl, (unsigned)(lo_rows * D * 4), &s.bar[2]);
+                    bulk_g2s(s.vs, Vl, (unsigned)(lo_rows * D * 4), &s.bar[2]);
+                }
+                if (hi_rows > 0) {
+                    bulk_g2s(s.ks + (long long)hi_first * D, Kl + (long long)hi_first * D, (unsigned)(hi_rows * D * 4),
+                             &s.bar[2]);
+                    bulk_g2s(s.vs + (long long)hi_first * D, Vl + (long long)hi_first * D, (unsigned)(hi_rows * D * 4),
+                             &s.bar[2]);
+                }
+            }
+            // QKV: q to shared memory, k and v into the ring slot (global, and
+            // the staged copy)
+            if (!acquire()) return false;
+            float* ksm = s.ks;
+            float* vsm = s.vs;
+            seq_qmv<BITS>(Ly.qkv, s.wbuf[consumed & 1], s.x, [&](int n, float y) {
+                if (n < D) {
+                    s.q[n] = y;
+                } else if (n < 2 * D) {
+                    Kl[(long long)slot * D + (n - D)] = y;
+                    if (ksm) ksm[slot * D + (n - D)] = y;
+                } else {
+                    Vl[(long long)slot * D + (n - 2 * D)] = y;
+                    if (vsm) vsm[slot * D + (n - 2 * D)] = y;
+                }
+            });
+            release();
+            if (staged) {
+                if (threadIdx.x == 0 && !mbar_wait(&s.bar[2], kv_uses & 1u)) s.flag[0] = 1;
+                kv_uses++;
+                __syncthreads();
+                if (s.flag[0]) return false;
+            }
+            kv_pending = false;
+            const float* Ksrc = ksm ? ksm : Kl;
+            const float* Vsrc = vsm ? vsm : Vl;
+            // attention over the ring (transformer.c:686-713). Scores: one warp
+            // per (head, key row), lanes across the head dimension (coalesced
+            // row reads), four rows in flight per warp.
+            {
+                const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+                const int rows = H * ctx;
+                for (int r0 = warp; r0 < rows; r0 += SEQ_WARPS * 4) {
+                    float part[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int r = r0 + u * SEQ_WARPS;
+                        part[u] = 0.0f;
+                        if (r < rows) {
+                            const int h = r / ctx, j = r - (r / ctx) * ctx;
+                            int phys = start + j;
+                            if (phys >= cap) phys -= cap;
+                            const float* kr = Ksrc + (long long)phys * D + h * hd;
+                            const float* qh = s.q + h * hd;
+                            for (int e2 = lane; e2 < hd; e2 += 32) part[u] = fmaf(qh[e2], kr[e2], part[u]);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+#pragma unroll
+                        for (int off = 16; off >= 1; off >>= 1)
+                            part[u] += __shfl_xor_sync(0xffffffffu, part[u], off);
+                    }
+                    if (lane == 0) {
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int r = r0 + u * SEQ_WARPS;
+                            if (r < rows) {
+                                const int h = r / ctx, j = r - (r / ctx) * ctx;
+                                s.scores[h * cap + j] = part[u] / denom;
+                            }
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            {
+                const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+                for (int h = warp; h < H; h += SEQ_WARPS) {
+                    float* sc = s.scores + h * cap;
+                    float mx = -3.402823466e38f;
+                    for (int j = lane; j < ctx; j += 32) mx = fmaxf(mx, sc[j]);
+#pragma unroll
+                    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                    float sum = 0.0f;
+                    for (int j = lane; j < ctx; j += 32) {
+                        const float ev = expf(sc[j] - mx);
+                        sc[j] = ev;
+                        sum += ev;
+                    }
+#pragma unroll
+                    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+                    const float inv = 1.0f / sum;
+                    for (int j = lane; j < ctx; j += 32) sc[j] = sc[j] * inv;
+                }
+            }
+            __syncthreads();
+            // o = sum_j p_j v_j: thread (g, t) sums rows j = g, g + G, ...
+            // (coalesced across t), groups combine through shared memory.
+            {
+                const int groups = D <= SEQ_THREADS ? SEQ_THREADS / D : 1;
+                for (int t0 = 0; t0 < D; t0 += SEQ_THREADS) {
+                    const int t = t0 + (threadIdx.x % (D < SEQ_THREADS ? D : SEQ_THREADS));
+                    const int g = D < SEQ_THREADS ? threadIdx.x / D : 0;
+                    float acc = 0.0f;
+                    if (g < groups && t < D) {
+                        const float* sc = s.scores + (t / hd) * cap;
+#pragma unroll 4
+                        for (int j = g; j < ctx; j += groups) {
+                            int phys = start + j;
+                            if (phys >= cap) phys -= cap;
+                            acc = fmaf(sc[j], Vsrc[(long long)phys * D + t], acc);
+                        }
+                    }
+                    s.part[threadIdx.x] = acc;
+                    __syncthreads();
+                    if (threadIdx.x < (D < SEQ_THREADS ? D : SEQ_THREADS) && t0 + threadIdx.x < D) {
+                        const int w = D < SEQ_THREADS ? D : SEQ_THREADS;
+                        float o = 0.0f;
+                        for (int gg = 0; gg < groups; gg++) o += s.part[gg * w + threadIdx.x];
+                        s.att[t0 + threadIdx.x] = o;
+                    }
+                    __syncthreads();
+                }
+            }
+            clk.mark(SEQ_PH_ATTENTION);
+            // W_o, + residual, then LayerNorm with the gamma/beta carried in W_o's blob
+            if (!acquire()) return false;
+            {
+                const uint8_t* wb = s.wbuf[consumed & 1];
+                seq_qmv<BITS>(Ly.wo, wb, s.att, [&](int n, float y) { s.fr[n] = y + s.x[n]; });
+                __syncthreads();
+                const float* g = reinterpret_cast<const float*>(wb + Ly.wo.gamma_off);
+                seq_layernorm(s.fr, s.an, g, g + D, D, s.red);
+            }
+            release();
+            clk.mark(SEQ_PH_NORM);
+            // FFN up + bias + ReLU
+            if (!acquire()) return false;
+            {
+                const uint8_t* wb = s.wbuf[consumed & 1];
+                const float* bias = reinterpret_cast<const float*>(wb + Ly.w1.bias_off);
+                seq_qmv<BITS>(Ly.w1, wb, s.an, [&](int n, float y) {
+                    const float pre = y + bias[n];
+                    s.ff[n] = pre > 0.0f ? pre : 0.0f;
+                });
+            }
+            release();
+            // FFN down + bias + residual, LayerNorm
+            if (!acquire()) return false;
+            {
+                const uint8_t* wb = s.wbuf[consumed & 1];
+                const float* bias = reinterpret_cast<const float*>(wb + Ly.w2.bias_off);
+                seq_qmv<BITS>(Ly.w2, wb, s.ff, [&](int n, float y) { s.fr[n] = y + bias[n] + s.an[n]; });
+                __syncthreads();
+                const float* g = reinterpret_cast<const float*>(wb + Ly.w2.gamma_off);
+                seq_layernorm(s.fr, s.x, g, g + D, D, s.red);
+            }
+            release();
+            clk.mark(SEQ_PH_NORM);
+        }
+        if (!acquire()) return false;
+        {
+            const uint8_t* wb = s.wbuf[consumed & 1];
+            const float* bias = reinterpret_cast<const float*>(wb + p.head.bias_off);
+            seq_qmv<BITS>(p.head, wb, s.x, [&](int n, float y) { s.logits[n] = y + bias[n]; });
+        }
+        release();
+        __syncthreads();
+        if (length < cap) length++;
+        total++;
+        return true;
+    };
+
+    for (int t = 0; t < p.plen && !aborted; t++)
+        if (!forward(p.prompts[(long long)b * p.plen + t])) aborted = true;
+    for (int i = 0; i < p.n_new && !aborted; i++) {
+        const uint32_t tok = seq_select(p, s, rng);
+        clk.mark(SEQ_PH_SELECT);
+        if (threadIdx.x == 0) p.out[(long long)b * p.n_new + i] = tok;
+        if (i + 1 < p.n_new && !forward(tok)) aborted = true;
+    }
+
+    if (aborted) {
+        // let copies in flight land before the CTA's shared memory goes away
+        if (threadIdx.x == 0) {
+            p.status[0] = DZ_SEQ_TIMEOUT;
+            for (long long m = consumed; m < pipe.issued; m++)
+                mbar_wait(&s.bar[m & 1], (uint32_t)((m >> 1) & 1));
+            if (kv_pending) mbar_wait(&s.bar[2], kv_uses & 1u);
+        }
+        __syncthreads();
+        return;
+    }
+    if (threadIdx.x == 0) {
+        p.start[b] = start;
+        p.length[b] = length;
+        p.total[b] = total;
+    }
+}
+
+}  // namespace dz

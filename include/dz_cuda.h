@@ -123,6 +123,17 @@ int dz_cuda_generate(dz_cuda_cache_t *cache, const uint32_t *prompts, size_t pro
 int dz_cuda_generate_async(dz_cuda_cache_t *cache, const uint32_t *prompts_dev, size_t prompt_len,
                            size_t n_new, const dz_sampling_t *sampling, const uint64_t *seeds_dev,
                            uint32_t *out_tokens_dev);
+/* Execution path of dz_cuda_generate(_async). AUTO runs the fused kernel (one
+ * thread block per sequence runs the whole generation, weights streamed into
+ * shared memory by TMA bulk copies) whenever the model fits it (every
+ * projection <= 96 KB in the device layout, column or tensor scales), else the
+ * layered path (one kernel per projection / attention / norm per step, one
+ * CUDA graph per job). No counterpart in the reference. */
+enum { DZ_PATH_AUTO = 0, DZ_PATH_LAYERED = 1, DZ_PATH_FUSED = 2 };
+int dz_cuda_cache_set_path(dz_cuda_cache_t *cache, int path);
+/* 1 when dz_cuda_generate with this sampling would take the fused path. */
+int dz_cuda_cache_uses_fused(const dz_cuda_cache_t *cache, const dz_sampling_t *sampling);
+
 /* Number of kernel launches one dz_cuda_generate(_async) call issues. */
 size_t dz_cuda_generate_launches(const dz_cuda_cache_t *cache, size_t prompt_len, size_t n_new,
                                  const dz_sampling_t *sampling);
@@ -134,7 +145,12 @@ enum {
     DZ_KERNEL_ATTENTION = 2,  /* ring-KV decode attention */
     DZ_KERNEL_LAYERNORM = 3,
     DZ_KERNEL_SELECT = 4,     /* greedy / top-k / top-p selection */
-    DZ_KERNEL_CLASSES = 5
+    DZ_KERNEL_SEQGEN = 5,     /* fused whole-generation kernel */
+    DZ_KERNEL_CLASSES = 6,
+    /* Phases inside the fused kernel, timed on its first thread block with the
+     * device's global timer (launches = 0, total_ms = time in the phase). */
+    DZ_PHASE_EMBED = 6, DZ_PHASE_WAIT = 7, DZ_PHASE_QMV = 8, DZ_PHASE_ATTENTION = 9,
+    DZ_PHASE_NORM = 10, DZ_PHASE_SELECT = 11, DZ_PROFILE_SLOTS = 12
 };
 
 typedef struct {

@@ -66,19 +66,32 @@ def _check_streams(got, ref, ref_logits=None):
     return bad
 
 
-def test_c1_greedy_stream(gpu, oracle, tmp_path):
+PATHS = {"layered": 1, "fused": 2}
+
+
+def _cache(gpu, model, batch, path, sampling, capacity=None):
+    cache = gpu.KVCache(model, batch, capacity)
+    cache.set_path(PATHS[path])
+    assert cache.uses_fused(sampling) == (path == "fused")
+    return cache
+
+
+@pytest.mark.parametrize("path", ["layered", "fused"])
+def test_c1_greedy_stream(gpu, oracle, tmp_path, path):
     g, spec, model = _model_from_golden(gpu, oracle, "c1", tmp_path)
-    cache = gpu.KVCache(model, 1)
-    toks = cache.generate(g["prompts"], 48, gpu.Sampling(gpu.GREEDY))
+    samp = gpu.Sampling(gpu.GREEDY)
+    cache = _cache(gpu, model, 1, path, samp)
+    toks = cache.generate(g["prompts"], 48, samp)
     assert _check_streams(toks, g["tokens"]) == []
     cache.close(); model.close()
 
 
-def test_c2_top_p_streams(gpu, oracle, tmp_path):
+@pytest.mark.parametrize("path", ["layered", "fused"])
+def test_c2_top_p_streams(gpu, oracle, tmp_path, path):
     """64 sequences x (32 prompt + 32 top-p 0.9 draws at T=0.8), per-sequence seeds."""
     g, spec, model = _model_from_golden(gpu, oracle, "c2", tmp_path)
-    cache = gpu.KVCache(model, 64)
     samp = gpu.Sampling(gpu.TOPP, 0.8, 0, 0.9)
+    cache = _cache(gpu, model, 64, path, samp)
     toks = cache.generate(g["prompts"], 32, samp, seeds=g["seeds"])
     bad = _check_streams(toks, g["tokens"])
     assert len(bad) <= 1, bad
@@ -87,11 +100,12 @@ def test_c2_top_p_streams(gpu, oracle, tmp_path):
     cache.close(); model.close()
 
 
-def test_ring_eviction_top_k(gpu, oracle, tmp_path):
+@pytest.mark.parametrize("path", ["layered", "fused"])
+def test_ring_eviction_top_k(gpu, oracle, tmp_path, path):
     """Capacity 32 with 24 + 40 tokens: ring eviction and positions past max_seq_len."""
     g, spec, model = _model_from_golden(gpu, oracle, "ring", tmp_path)
-    cache = gpu.KVCache(model, 2)
     samp = gpu.Sampling(gpu.TOPK, 0.8, 5, 0.0)
+    cache = _cache(gpu, model, 2, path, samp)
     toks = cache.generate(g["prompts"], 40, samp, seeds=g["seeds"])
     assert _check_streams(toks, g["tokens"]) == []
     cache.close(); model.close()
@@ -138,4 +152,45 @@ def test_batched_against_oracle_with_reset_mask(gpu, oracle):
     for t in range(5):
         r = om.forward_token(seqs[2, t])
     assert _rel(got[2], r) <= 1e-4
+    cache.close(); model.close()
+
+
+@pytest.mark.parametrize("bits", [4, 8])
+def test_fused_matches_layered_random_model(gpu, oracle, bits):
+    """Both paths on a model off the golden shapes (d=64, 5 heads... d=80 h=5, F=320, V=1000, L=3),
+    batch 7, greedy and top-k: identical token streams."""
+    spec = Spec(1000, 80, 5, 3, 48)
+    recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 33), bits)
+    model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, bits, 2) for (_, k, r, c, f, s, p) in recs])
+    rng = np.random.RandomState(bits)
+    prompts = rng.randint(0, 256, size=(7, 9)).astype(np.uint32)
+    seeds = np.arange(7, dtype=np.uint64) + 100
+    om = oracle.model(spec, flat)
+    for samp, sd, strat in ((gpu.Sampling(gpu.GREEDY), None, 0), (gpu.Sampling(gpu.TOPK, 0.7, 12, 0.0), seeds, 1)):
+        outs = []
+        for path in ("layered", "fused"):
+            cache = _cache(gpu, model, 7, path, samp)
+            outs.append(cache.generate(prompts, 20, samp, seeds=sd))
+            cache.close()
+        np.testing.assert_array_equal(outs[0], outs[1])
+        ref, _ = om.generate(prompts, 20, strat, samp.c.temperature, samp.c.top_k, 0.0, sd)
+        np.testing.assert_array_equal(outs[1], ref)
+    model.close()
+
+
+def test_fused_not_eligible_falls_back(gpu, oracle):
+    """A d=256 INT8 model (W1 is 256 KB in the device layout) runs layered under AUTO."""
+    spec = Spec(300, 256, 4, 1, 16)
+    recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 4), 8)
+    model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, 8, 2) for (_, k, r, c, f, s, p) in recs])
+    cache = gpu.KVCache(model, 2)
+    samp = gpu.Sampling(gpu.GREEDY)
+    assert not cache.uses_fused(samp)
+    with pytest.raises(gpu.DzError):
+        cache.set_path(2)
+    prompts = np.array([[1, 2, 3], [4, 5, 6]], np.uint32)
+    toks = cache.generate(prompts, 5, samp)
+    om = oracle.model(spec, flat)
+    ref, _ = om.generate(prompts, 5, 0, 0.0, 0, 0.0, None)
+    np.testing.assert_array_equal(toks, ref)
     cache.close(); model.close()
