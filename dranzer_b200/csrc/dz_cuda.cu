@@ -9,6 +9,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <map>
 #include <new>
 #include <string>
@@ -17,6 +18,7 @@
 
 #include "decode.cuh"
 #include "qmv.cuh"
+#include "qmma.cuh"
 #include "select.cuh"
 #include "seqgen.cuh"
 
@@ -81,8 +83,10 @@ extern "C" int dz_cuda_available(void) {
 
 // -------------------------------------------------------- device matrices
 
+// A quantized matrix on the device, codes in the MMA-fragment layout of qmma.cuh.
 struct DevQMat {
-    int K = 0, N = 0, Np = 0, bits = 0, gran = 0, nchunks = 0;
+    int K = 0, N = 0, Np = 0, bits = 0, gran = 0;
+    int ntiles = 0, nkg = 0;     // n-tiles of 16 columns, k-groups of 64 (INT4) / 32 (INT8) rows
     uint8_t* codes = nullptr;
     float* col_scale = nullptr;  // [Np] (COLUMN / TENSOR expanded), zero in padding
     float* k_scale = nullptr;    // [K] ROW granularity
@@ -109,13 +113,13 @@ static int check_blob(const dz_tensor_blob_t* w) {
     return DZ_OK;
 }
 
-// Builds the strip layout of the column concatenation of `srcs` (all with the
-// same K, bits and granularity; every source but the last with N % 4 == 0).
-// Device allocations are recorded in *out as they are made, so the caller's
-// free_qmat(*out) releases them on any failure.
+// Builds the fragment layout of the column concatenation of `srcs` (same K,
+// bits and granularity). Device allocations are recorded in *out as they are
+// made, so the caller's free_qmat(*out) releases them on any failure.
 static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cudaStream_t st, DevQMat& m,
-                          uint8_t*& staging) {
+                          std::vector<uint8_t*>& staging) {
     const dz_tensor_blob_t* s0 = srcs[0];
+    if (srcs.size() > 3) return fail(DZ_E_INVALID, "at most three concatenated matrices");
     for (auto* s : srcs) {
         int rc = check_blob(s);
         if (rc) return rc;
@@ -127,17 +131,21 @@ static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cuda
     m.K = (int)s0->rows;
     m.bits = s0->bits;
     m.gran = s0->granularity;
+    FragSources fs;
+    memset(&fs, 0, sizeof(fs));
+    fs.nsrc = (int)srcs.size();
     int N = 0;
     for (size_t i = 0; i < srcs.size(); i++) {
-        if (i + 1 < srcs.size() && srcs[i]->cols % 4 != 0)
-            return fail(DZ_E_INVALID, "concatenated matrix width not a multiple of 4");
+        fs.off[i] = N;
         N += (int)srcs[i]->cols;
     }
+    fs.off[srcs.size()] = N;
     m.N = N;
     m.Np = round_up(N, 16);
-    const int KC = m.bits == 8 ? 4 : 8;
-    m.nchunks = round_up(m.K, KC) / KC;
-    m.code_bytes = (size_t)(m.Np / 4) * m.nchunks * 16;
+    m.ntiles = m.Np / 16;
+    const int KG = m.bits == 8 ? 32 : 64;
+    m.nkg = round_up(m.K, KG) / KG;
+    m.code_bytes = (size_t)m.ntiles * m.nkg * 512;
     DZ_CUDA(cudaMalloc(&m.codes, m.code_bytes));
     DZ_CUDA(cudaMalloc(&m.col_scale, (size_t)m.Np * sizeof(float)));
     DZ_CUDA(cudaMemsetAsync(m.col_scale, 0, (size_t)m.Np * sizeof(float), st));
@@ -151,45 +159,34 @@ static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cuda
         DZ_CUDA(cudaStreamSynchronize(st));
         m.scale_bytes = (size_t)m.K * 4;
     }
-    size_t max_packed = 0;
-    for (auto* s : srcs) max_packed = s->packed_size > max_packed ? s->packed_size : max_packed;
-    DZ_CUDA(cudaMalloc(&staging, max_packed));
-    int col0 = 0;
-    for (auto* s : srcs) {
-        DZ_CUDA(cudaMemcpyAsync(staging, s->packed, s->packed_size, cudaMemcpyHostToDevice, st));
-        const int strips = (int)((s->cols + 3) / 4);
-        const long long nwords = (long long)strips * m.nchunks * 4;
-        uint32_t* dst = reinterpret_cast<uint32_t*>(m.codes) + (long long)(col0 / 4) * m.nchunks * 4;
-        dz_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(staging, dst, m.K, (int)s->cols,
-                                                                          m.bits, m.nchunks, nwords);
-        DZ_CUDA(cudaGetLastError());
+    for (size_t i = 0; i < srcs.size(); i++) {
+        uint8_t* d = nullptr;
+        DZ_CUDA(cudaMalloc(&d, srcs[i]->packed_size));
+        staging.push_back(d);
+        DZ_CUDA(cudaMemcpyAsync(d, srcs[i]->packed, srcs[i]->packed_size, cudaMemcpyHostToDevice, st));
+        fs.ref[i] = d;
         if (m.gran == DZ_GRAN_COLUMN) {
-            DZ_CUDA(cudaMemcpyAsync(m.col_scale + col0, s->scales, s->cols * 4, cudaMemcpyHostToDevice, st));
+            DZ_CUDA(cudaMemcpyAsync(m.col_scale + fs.off[i], srcs[i]->scales, srcs[i]->cols * 4,
+                                    cudaMemcpyHostToDevice, st));
         } else if (m.gran == DZ_GRAN_TENSOR) {
-            std::vector<float> rep(s->cols, s->scales[0]);
-            DZ_CUDA(cudaMemcpyAsync(m.col_scale + col0, rep.data(), s->cols * 4, cudaMemcpyHostToDevice, st));
+            std::vector<float> rep(srcs[i]->cols, srcs[i]->scales[0]);
+            DZ_CUDA(cudaMemcpyAsync(m.col_scale + fs.off[i], rep.data(), srcs[i]->cols * 4, cudaMemcpyHostToDevice,
+                                    st));
             DZ_CUDA(cudaStreamSynchronize(st));
         }
-        DZ_CUDA(cudaStreamSynchronize(st));  // staging is reused by the next source
-        col0 += (int)s->cols;
     }
-    // padding strips past the last source: all codes qmax (level 0)
-    const int used_strips = (col0 + 3) / 4;
-    if (used_strips < m.Np / 4) {
-        const long long nwords = (long long)(m.Np / 4 - used_strips) * m.nchunks * 4;
-        uint32_t* dst = reinterpret_cast<uint32_t*>(m.codes) + (long long)used_strips * m.nchunks * 4;
-        dz_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(nullptr, dst, m.K, 0, m.bits,
-                                                                          m.nchunks, nwords);
-        DZ_CUDA(cudaGetLastError());
-    }
+    const long long nwords = (long long)m.ntiles * m.nkg * 128;
+    dz_frag_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(fs, reinterpret_cast<uint32_t*>(m.codes),
+                                                                           m.K, m.bits, m.nkg, nwords);
+    DZ_CUDA(cudaGetLastError());
     DZ_CUDA(cudaStreamSynchronize(st));
     return DZ_OK;
 }
 
 static int make_qmat(const std::vector<const dz_tensor_blob_t*>& srcs, cudaStream_t st, DevQMat* out) {
-    uint8_t* staging = nullptr;
+    std::vector<uint8_t*> staging;
     int rc = make_qmat_into(srcs, st, *out, staging);
-    cudaFree(staging);
+    for (uint8_t* p : staging) cudaFree(p);
     return rc;
 }
 
@@ -227,57 +224,68 @@ struct ProfScope {
 
 // ------------------------------------------------------------- qmv plans
 
-template <int BITS, int MT, int ST>
-static void launch_qmv_t(const QmvArgs& a, bool vec, unsigned grid, cudaStream_t st) {
-    if (vec) dz_qmv_kernel<BITS, MT, ST, true><<<grid, QMV_THREADS, 0, st>>>(a);
-    else dz_qmv_kernel<BITS, MT, ST, false><<<grid, QMV_THREADS, 0, st>>>(a);
+template <int BITS, int NB, int NT>
+static void launch_qmm_t(const QmmArgs& a, unsigned grid, cudaStream_t st) {
+    dz_qmm_kernel<BITS, NB, NT><<<grid, QMV_THREADS, 0, st>>>(a);
 }
 
 template <int BITS>
-static void launch_qmv_bits(const QmvArgs& a, int MT, bool vec, unsigned grid, cudaStream_t st) {
-    switch (MT) {
-        case 1: launch_qmv_t<BITS, 1, 4>(a, vec, grid, st); break;
-        case 2: launch_qmv_t<BITS, 2, 2>(a, vec, grid, st); break;
-        case 4: launch_qmv_t<BITS, 4, 1>(a, vec, grid, st); break;
-        default: launch_qmv_t<BITS, 8, 1>(a, vec, grid, st); break;
+static void launch_qmm_bits(const QmmArgs& a, int NB, unsigned grid, cudaStream_t st) {
+    switch (NB) {
+        case 1: launch_qmm_t<BITS, 1, 4>(a, grid, st); break;
+        case 2: launch_qmm_t<BITS, 2, 2>(a, grid, st); break;
+        case 4: launch_qmm_t<BITS, 4, 2>(a, grid, st); break;
+        default: launch_qmm_t<BITS, 8, 1>(a, grid, st); break;
     }
 }
 
 static int g_num_sms = 148;
 
-// Y = epilogue(X . deq(W)) for M rows; returns the number of launches (1).
+// Bytes of split-activation scratch one matvec of this matrix needs for M rows.
+static size_t qmv_scratch_bytes(const DevQMat& W, int M) {
+    const int KG = W.bits == 8 ? 32 : 64;
+    return (size_t)M * 3 * (size_t)W.nkg * KG * 2;
+}
+
+// Y = epilogue(X . deq(W)) for M rows on the tensor cores: the activation split
+// into `scratch` (qmv_scratch_bytes), then the MMA kernel. Returns launches (2).
 static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep,
-                      cudaStream_t st) {
-    QmvArgs a;
+                      cudaStream_t st, __nv_bfloat16* scratch) {
+    const int KG = W.bits == 8 ? 32 : 64;
+    const int Kp = W.nkg * KG;
+    {
+        const long long n = (long long)M * Kp;
+        ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 6.0 * n, 0, st);
+        dz_split_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, scratch);
+    }
+    QmmArgs a;
     a.codes = W.codes;
     a.K = W.K;
     a.N = W.N;
-    a.nchunks = W.nchunks;
-    a.k_scale = W.k_scale;
-    a.X = X;
-    a.ldx = ldx;
+    a.nkg = W.nkg;
+    a.ntiles = W.ntiles;
+    a.Xs = scratch;
+    a.Kp = Kp;
     a.M = M;
     a.ep = ep;
-    int MT = M >= 8 ? 8 : M >= 4 ? 4 : M >= 2 ? 2 : 1;
-    const int ST = MT == 1 ? 4 : MT == 2 ? 2 : 1;
-    a.m_tiles = (M + MT - 1) / MT;
-    a.n_groups = W.Np / (4 * ST);
-    const long long units = (long long)a.n_groups * a.m_tiles;
-    const long long target = (long long)g_num_sms * 40;
+    const int NB = M <= 2 ? 1 : M <= 4 ? 2 : M <= 8 ? 4 : 8;
+    const int NT = NB == 1 ? 4 : NB == 8 ? 1 : 2;
+    a.m_passes = (M + 2 * NB - 1) / (2 * NB);
+    a.n_groups = (W.ntiles + NT - 1) / NT;
+    const long long units = (long long)a.n_groups * a.m_passes;
+    const long long target = (long long)g_num_sms * 32;
     int kp = 1;
-    while (kp < QMV_WARPS && units * kp * 2 <= target && W.nchunks / (kp * 2) >= 64) kp *= 2;
+    while (kp < QMV_WARPS && units * kp * 2 <= target && W.nkg / (kp * 2) >= 2) kp *= 2;
     a.kparts = kp;
-    a.chunks_per_part = (W.nchunks + kp - 1) / kp;
+    a.kg_per_part = (W.nkg + kp - 1) / kp;
     const int units_per_cta = QMV_WARPS / kp;
     const unsigned grid = (unsigned)((units + units_per_cta - 1) / units_per_cta);
-    const int KC = W.bits == 8 ? 4 : 8;
-    const bool vec = (ldx % 4 == 0) && ((reinterpret_cast<uintptr_t>(X) & 15) == 0) && (W.K % KC == 0);
     ProfScope prof(DZ_KERNEL_QMV,
-                   (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N,
+                   (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 6.0 * M * Kp + 4.0 * M * W.N,
                    2.0 * M * W.K * W.N, st);
-    if (W.bits == 8) launch_qmv_bits<8>(a, MT, vec, grid, st);
-    else launch_qmv_bits<4>(a, MT, vec, grid, st);
-    return 1;
+    if (W.bits == 8) launch_qmm_bits<8>(a, NB, grid, st);
+    else launch_qmm_bits<4>(a, NB, grid, st);
+    return 2;
 }
 
 static QmvEpilogue plain_epilogue(const DevQMat& W, float* Y, long long ldy) {
@@ -298,7 +306,20 @@ struct dz_cuda_qmatrix {
     int device;
     DevQMat m;
     cudaStream_t stream;
+    __nv_bfloat16* scratch = nullptr;   // split activations, grown to the largest M used
+    size_t scratch_bytes = 0;
 };
+
+static int qmatrix_scratch(dz_cuda_qmatrix_t* q, int M) {
+    const size_t need = qmv_scratch_bytes(q->m, M);
+    if (need <= q->scratch_bytes) return DZ_OK;
+    cudaFree(q->scratch);
+    q->scratch = nullptr;
+    q->scratch_bytes = 0;
+    DZ_CUDA(cudaMalloc(&q->scratch, need));
+    q->scratch_bytes = need;
+    return DZ_OK;
+}
 
 extern "C" int dz_cuda_qmatrix_create(int device, const dz_tensor_blob_t* w, dz_cuda_qmatrix_t** out) {
     if (!out) return fail(DZ_E_INVALID, "null output handle");
@@ -328,6 +349,7 @@ extern "C" void dz_cuda_qmatrix_free(dz_cuda_qmatrix_t* q) {
     if (!q) return;
     DeviceGuard g(q->device);
     free_qmat(q->m);
+    cudaFree(q->scratch);
     cudaStreamDestroy(q->stream);
     delete q;
 }
@@ -345,8 +367,8 @@ extern "C" int dz_cuda_qmatrix_unpack(const dz_cuda_qmatrix_t* q, float* dst) {
     DZ_CUDA(cudaMalloc(&d, total * 4));
     const float* scales = q->m.gran == DZ_GRAN_ROW ? q->m.k_scale : q->m.col_scale;
     int gran = q->m.gran == DZ_GRAN_TENSOR ? DZ_GRAN_COLUMN : q->m.gran;  // expanded per column
-    dz_dequant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, q->stream>>>(q->m.codes, scales, gran, d, q->m.K,
-                                                                           q->m.N, q->m.bits, q->m.nchunks);
+    dz_frag_dequant_kernel<<<(unsigned)((total + 255) / 256), 256, 0, q->stream>>>(q->m.codes, scales, gran, d,
+                                                                                q->m.K, q->m.N, q->m.bits, q->m.nkg);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaMemcpyAsync(dst, d, total * 4, cudaMemcpyDeviceToHost, q->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(q->stream);
@@ -362,8 +384,8 @@ extern "C" int dz_cuda_qmatrix_codes(const dz_cuda_qmatrix_t* q, uint8_t* packed
     dz_quantized_packed_size((size_t)q->m.K * q->m.N, q->m.bits, &nb);
     uint8_t* d = nullptr;
     DZ_CUDA(cudaMalloc(&d, nb));
-    dz_unrepack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, q->stream>>>(q->m.codes, d, q->m.K, q->m.N,
-                                                                        q->m.bits, q->m.nchunks, (long long)nb);
+    dz_frag_unrepack_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, q->stream>>>(q->m.codes, d, q->m.K, q->m.N,
+                                                                             q->m.bits, q->m.nkg, (long long)nb);
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaMemcpyAsync(packed, d, nb, cudaMemcpyDeviceToHost, q->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(q->stream);
@@ -377,8 +399,12 @@ extern "C" int dz_cuda_matmul_quantized_async(const float* A, const dz_cuda_qmat
     if (!q || !A || !C || m == 0 || k != (size_t)q->m.K || m > (1u << 24))
         return fail(DZ_E_INVALID, "matmul_quantized: bad arguments (k must equal the matrix rows)");
     DeviceGuard g(q->device);
+    // the scratch grows outside any stream work; a caller capturing this into a
+    // graph makes one uncaptured call with its largest m first
+    int rc = qmatrix_scratch(const_cast<dz_cuda_qmatrix_t*>(q), (int)m);
+    if (rc) return rc;
     QmvEpilogue ep = plain_epilogue(q->m, C, q->m.N);
-    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream);
+    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, q->scratch);
     DZ_CUDA(cudaGetLastError());
     return DZ_OK;
 }
@@ -491,8 +517,8 @@ static bool seq_blob(dz_cuda_model_t* m, const DevQMat& q, const float* bias, in
     out->blob = blob;
     out->K = q.K;
     out->N = q.N;
-    out->nchunks = q.nchunks;
-    out->nstrips = q.Np / 4;
+    out->nkg = q.nkg;
+    out->ntiles = q.ntiles;
     out->bytes = (unsigned)off;
     out->scale_off = (unsigned)scale_off;
     out->bias_off = (unsigned)bias_off;
@@ -510,9 +536,10 @@ static size_t seq_smem_bytes(const dz_cuda_model_t* m, int cap, bool kv_smem) {
     const size_t pv = V > (size_t)SEQ_THREADS ? V : (size_t)SEQ_THREADS;
     auto r4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t table = (sizeof(SeqLayer) * m->layers.size() + 15) & ~(size_t)15;
+    const size_t xs_stride = (F + 63) / 64 * 64;
     return 2 * (size_t)m->seq_buf_bytes + 48 + table + 8 * (P > (size_t)SEQ_WARPS ? P : (size_t)SEQ_WARPS) +
-           4 * (5 * r4(D) + r4(F) + 2 * r4(V) + r4(H * (size_t)cap) + 64 + 2 * r4(pv)) +
-           (kv_smem ? 8 * r4((size_t)cap * D) : 0);
+           4 * (5 * r4(D) + 2 * r4(V) + r4(H * (size_t)cap) + 64 + 2 * r4(pv)) +
+           (kv_smem ? 8 * r4((size_t)cap * D) : 0) + 2 * 4 * r4(3 * xs_stride / 2);
 }
 
 static bool seq_kv_smem(const dz_cuda_model_t* m, int cap) {
@@ -615,7 +642,7 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
         for (size_t l = 0; l < desc->num_layers && !rc; l++, ti += 12) {
             DevLayer& L = m->layers[l];
             const dz_tensor_blob_t *tq = &t[ti], *tk = &t[ti + 1], *tv = &t[ti + 2];
-            L.fused_qkv = tq->granularity != DZ_GRAN_ROW && D % 4 == 0;
+            L.fused_qkv = tq->granularity != DZ_GRAN_ROW;
             if (L.fused_qkv) {
                 if ((rc = make_qmat({tq, tk, tv}, st, &L.qkv))) break;
                 step += L.qkv.code_bytes + L.qkv.scale_bytes;
@@ -713,6 +740,7 @@ struct dz_cuda_cache {
     std::map<GenKey, cudaGraphExec_t> gen_graphs;
     double prof_ctx_bytes_per_layer = 0, prof_ctx_flops_per_layer = 0;  // set per profiled step
     int path = DZ_PATH_AUTO;
+    __nv_bfloat16* xs_scratch = nullptr;  // split activations of the layered path's matvecs
     int* status = nullptr;        // device word the fused kernel reports a timeout in
     unsigned long long* phase_ns = nullptr;  // [SEQ_PHASES] fused-kernel phase clock (profiling)
     int* host_status = nullptr;   // pinned
@@ -790,6 +818,14 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     if (!rc) rc = cache_alloc(c, (void**)&c->tok, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->rng, B * 8);
     if (!rc) rc = cache_alloc(c, (void**)&c->gen_seeds, B * 8);
+    if (!rc) {
+        size_t xs = 0;
+        for (const auto& L : m->layers)
+            for (const DevQMat* q : {&L.qkv, &L.q, &L.k, &L.v, &L.wo, &L.w1, &L.w2})
+                if (q->codes) xs = std::max(xs, qmv_scratch_bytes(*q, (int)B));
+        xs = std::max(xs, qmv_scratch_bytes(m->head, (int)B));
+        rc = cache_alloc(c, (void**)&c->xs_scratch, xs);
+    }
     if (!rc) rc = cache_alloc(c, (void**)&c->status, 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->phase_ns, SEQ_PHASES * 8);
     if (!rc && cudaMallocHost(&c->host_status, 4) != cudaSuccess) rc = fail(DZ_E_NOMEM, "pinned host");
@@ -892,16 +928,16 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             ep.seg_start[0] = 0; ep.seg_start[1] = D; ep.seg_start[2] = 2 * D; ep.seg_start[3] = 3 * D;
             ep.seg_ptr[1] = Kl; ep.seg_ld[1] = (long long)cap * D; ep.seg_row_off[1] = c->row_off;
             ep.seg_ptr[2] = Vl; ep.seg_ld[2] = (long long)cap * D; ep.seg_row_off[2] = c->row_off;
-            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st);
+            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st, c->xs_scratch);
         } else {
             QmvEpilogue eq = plain_epilogue(L.q, c->q, D);
-            launches += launch_qmv(L.q, c->hidden, D, B, eq, st);
+            launches += launch_qmv(L.q, c->hidden, D, B, eq, st, c->xs_scratch);
             QmvEpilogue ek = plain_epilogue(L.k, Kl, (long long)cap * D);
             ek.seg_row_off[0] = c->row_off;
-            launches += launch_qmv(L.k, c->hidden, D, B, ek, st);
+            launches += launch_qmv(L.k, c->hidden, D, B, ek, st, c->xs_scratch);
             QmvEpilogue ev = plain_epilogue(L.v, Vl, (long long)cap * D);
             ev.seg_row_off[0] = c->row_off;
-            launches += launch_qmv(L.v, c->hidden, D, B, ev, st);
+            launches += launch_qmv(L.v, c->hidden, D, B, ev, st, c->xs_scratch);
         }
         {
             // bytes: the K and V rows of every sequence's context (ctx <= cap; the
@@ -914,7 +950,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         }
         launches++;
         QmvEpilogue eo = plain_epilogue(L.wo, c->attn_raw, D);
-        launches += launch_qmv(L.wo, c->concat, D, B, eo, st);
+        launches += launch_qmv(L.wo, c->concat, D, B, eo, st, c->xs_scratch);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D, 0, st);
             dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, D,
@@ -924,12 +960,12 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         QmvEpilogue e1 = plain_epilogue(L.w1, c->ff, F);
         e1.bias = L.b1;
         e1.relu = 1;
-        launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st);
+        launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st, c->xs_scratch);
         QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
         e2.bias = L.b2;
         e2.residual = c->attn_norm;
         e2.ld_res = D;
-        launches += launch_qmv(L.w2, c->ff, F, B, e2, st);
+        launches += launch_qmv(L.w2, c->ff, F, B, e2, st, c->xs_scratch);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D, 0, st);
             dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->ff_raw, nullptr, L.g2, L.be2, c->hidden, D, 1e-6f);
@@ -938,7 +974,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
     }
     QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
     eh.bias = m->out_bias;
-    launches += launch_qmv(m->head, c->hidden, D, B, eh, st);
+    launches += launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch);
     return launches;
 }
 
@@ -1123,8 +1159,8 @@ extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t ple
     const dz_cuda_model_t* m = c->model;
     if (use_seqgen(c, s)) return 2;
     size_t per_layer = 0;
-    for (const auto& L : m->layers) per_layer += (L.fused_qkv ? 1 : 3) + 6;
-    const size_t step = 1 + per_layer + 1;
+    for (const auto& L : m->layers) per_layer += 2 * ((L.fused_qkv ? 1 : 3) + 3) + 3;  // matvec = split + MMA
+    const size_t step = 1 + per_layer + 2;
     const size_t seeded = (s && s->strategy != 0 && s->temperature > 0.0f) ? 1 : 0;
     return seeded + 1 + plen * step + n_new + (n_new ? n_new - 1 : 0) * step;
 }

@@ -16,6 +16,7 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "qmma.cuh"
 #include "qmv.cuh"
 #include "select.cuh"
 
@@ -33,8 +34,8 @@ constexpr int DZ_SEQ_TIMEOUT = 1;
 // gamma and beta of the LayerNorm that follows them. The TMA copy brings the
 // whole blob into shared memory, so epilogues read nothing from global memory.
 struct SeqMat {
-    const uint8_t* blob;
-    int K, N, nchunks, nstrips;
+    const uint8_t* blob;       // codes in the MMA-fragment layout (qmma.cuh) first
+    int K, N, nkg, ntiles;
     unsigned bytes;            // whole blob
     unsigned scale_off;        // byte offset of the column scales
     unsigned bias_off;         // byte offset of the bias (0: none)
@@ -154,8 +155,9 @@ __device__ __forceinline__ void fence_proxy_async() {
 struct SeqSmem {
     uint8_t* wbuf[2];
     uint64_t* bar;     // [3]: weight buffers 0 and 1, K/V staging
-    float *x, *q, *att, *an, *ff, *fr, *logits, *scores, *red, *ev, *part, *part2;
+    float *x, *q, *att, *an, *fr, *logits, *scores, *red, *ev, *part, *part2;
     float *ks, *vs;   // this layer's K / V rows staged in shared memory (or nullptr)
+    __nv_bfloat16* xs[2];  // bf16 hi/mid/lo splits of the matvec inputs, two alternating buffers
     uint64_t* keys;
     int* flag;         // [0] abort, [1] token broadcast, [2] top-p count, [3] drawn position
     SeqLayer* layers;  // the layer table, copied from global memory at entry
@@ -197,70 +199,93 @@ __device__ __forceinline__ void seq_issue(const SeqParams& p, SeqSmem& s, SeqPip
     pipe.issued++;
 }
 
-// Block-level quantized matvec from the shared-memory copy of matrix `m`:
-// y[n] = epi(n, sum_k x[k] * level(k, n) * col_scale[n]). Lanes split the
-// chunks of a strip in groups of G; groups reduce with shuffles.
+// Block-level quantized matvec on the tensor cores from the shared-memory copy
+// of matrix `m`: y[n] = epi(n, sum_k x[k] * level(k, n) * scale[n]). x enters
+// as its bf16 hi/mid/lo split (three arrays of `xs_stride` elements, zero past
+// K); B column g < 3 of each m16n8k16 MMA carries split g, the others are
+// zero. Work units are (n-tile, k-part); k-parts combine through `red`.
 template <int BITS, typename Epi>
-__device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, const float* x, Epi epi) {
-    constexpr int KC = BITS == 8 ? 4 : 8;
+__device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, const __nv_bfloat16* xs, int xs_stride,
+                                        float* red, Epi epi) {
+    constexpr int KT = FragGeom<BITS>::KT;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int G = 1;
-    while (G < m.nchunks && G < 32) G <<= 1;
-    const int spw = 32 / G;                      // strips per warp per pass
-    const int gl = lane & (G - 1);
-    const uint4* w4 = reinterpret_cast<const uint4*>(wsm);
+    const int g = lane >> 2, t = lane & 3;
+    int kp = 1;
+    while (kp < SEQ_WARPS && m.ntiles * kp * 2 <= SEQ_WARPS && m.nkg >= kp * 2) kp *= 2;
+    const int per = (m.nkg + kp - 1) / kp;
+    const int units = m.ntiles * kp;
     const float* scale = reinterpret_cast<const float*>(wsm + m.scale_off);
-    for (int s0 = warp * spw; s0 < m.nstrips; s0 += SEQ_WARPS * spw) {
-        const int s = s0 + lane / G;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        if (s < m.nstrips) {
-            for (int c = gl; c < m.nchunks; c += G) {
-                const uint4 w = w4[s * m.nchunks + c];
-                const int k0 = c * KC;
-                float xv[KC];
-                if (k0 + KC <= m.K) {
-#pragma unroll
-                    for (int q4 = 0; q4 < KC / 4; q4++) {
-                        const float4 v = reinterpret_cast<const float4*>(x + k0)[q4];
-                        xv[4 * q4] = v.x; xv[4 * q4 + 1] = v.y; xv[4 * q4 + 2] = v.z; xv[4 * q4 + 3] = v.w;
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < KC; i++) xv[i] = (k0 + i < m.K) ? x[k0 + i] : 0.0f;
-                }
+    const bool feeds = g < 3;
+    const uint32_t* xw = reinterpret_cast<const uint32_t*>(xs + (feeds ? g : 0) * xs_stride);
+    for (int u0 = 0; u0 < units; u0 += SEQ_WARPS) {
+        const int unit = u0 + warp;
+        const bool active = unit < units;
+        const int nt = active ? unit / kp : 0, kpart = active ? unit % kp : 0;
+        float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        if (active) {
+            const int kg1 = min((kpart + 1) * per, m.nkg);
+            for (int kg = kpart * per; kg < kg1; kg++) {
+                const uint4 w = reinterpret_cast<const uint4*>(wsm + ((size_t)nt * m.nkg + kg) * 512)[lane];
                 const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float t = acc[j];
-#pragma unroll
-                    for (int i = 0; i < KC; i++)
-                        t = fmaf(xv[i], BITS == 8 ? dz_level8(ww[j], i) : dz_level4(ww[j], i), t);
-                    acc[j] = t;
+                for (int kt = 0; kt < KT; kt++) {
+                    const int k0 = (kg * KT + kt) * 16;
+                    const uint32_t b0 = feeds ? xw[(k0 >> 1) + t] : 0u;
+                    const uint32_t b1 = feeds ? xw[(k0 >> 1) + t + 4] : 0u;
+                    uint32_t af[4];
+                    if (BITS == 4) {
+                        dz_frag_dequant(ww[kt], DZ_BF16X2_135, af);
+                        dz_mma_bf16(d[0], af, b0, b1);
+                    } else {
+                        dz_frag_dequant(ww[2 * kt], DZ_BF16X2_127, af);
+                        dz_mma_bf16(d[0], af, b0, b1);
+                        dz_frag_dequant(ww[2 * kt + 1], DZ_BF16X2_136, af);
+                        dz_mma_bf16(d[1], af, b0, b1);
+                    }
                 }
             }
         }
-        // reduce the 4 column sums over the G lanes of the group
-        for (int off = G >> 1; off >= 1; off >>= 1) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
-        }
-        if (s < m.nstrips) {
-            // every lane of the group holds the 4 sums; lanes 0..3 (or fewer,
-            // looping, when the group is narrower) write one column each
-            for (int j = gl; j < 4; j += G) {
-                const int n = s * 4 + j;
-                const float v = j == 0 ? acc[0] : j == 1 ? acc[1] : j == 2 ? acc[2] : acc[3];
-                if (n < m.N) epi(n, v * scale[n]);
+        // columns 0..2 (hi, mid, lo of the one row) sit in lanes t = 0 (cols 0, 1) and t = 1 (col 2)
+        float v0 = BITS == 8 ? 16.0f * (d[1][0] + d[1][1]) + (d[0][0] + d[0][1]) : d[0][0] + d[0][1];
+        float v1 = BITS == 8 ? 16.0f * (d[1][2] + d[1][3]) + (d[0][2] + d[0][3]) : d[0][2] + d[0][3];
+        v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+        v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+        if (active && t == 0) {
+            if (kp == 1) {
+                const int n0 = nt * 16 + g;
+                if (n0 < m.N) epi(n0, v0 * scale[n0]);
+                if (n0 + 8 < m.N) epi(n0 + 8, v1 * scale[n0 + 8]);
+            } else {
+                red[(nt * kp + kpart) * 16 + g] = v0;
+                red[(nt * kp + kpart) * 16 + g + 8] = v1;
             }
         }
     }
+    if (kp > 1) {
+        __syncthreads();
+        for (int n = threadIdx.x; n < m.ntiles * 16; n += SEQ_THREADS) {
+            const int nt = n >> 4, c = n & 15;
+            float sum = 0.0f;
+            for (int q = 0; q < kp; q++) sum += red[(nt * kp + q) * 16 + c];
+            if (n < m.N) epi(n, sum * scale[n]);
+        }
+    }
+}
+
+// hi / mid / lo bf16 split of v into element i of a split buffer.
+__device__ __forceinline__ void seq_split_store(__nv_bfloat16* xs, int stride, int i, float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(h);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    xs[i] = h;
+    xs[stride + i] = mid;
+    xs[2 * stride + i] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
 }
 
 // LayerNorm (src/core/tensor_ops.c:88-111) of D values in shared memory, by
 // warp 0 (shuffle reductions, no block barrier until the output is written).
 __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const float* gamma, const float* beta,
-                                              int D, float* red) {
-    (void)red;
+                                              int D, __nv_bfloat16* xs, int xs_stride) {
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float s = 0.0f;
@@ -276,7 +301,11 @@ __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
         const float sd = sqrtf(v / (float)D + 1e-6f);
-        for (int i = lane; i < D; i += 32) out[i] = gamma[i] * ((in[i] - mean) / sd) + beta[i];
+        for (int i = lane; i < D; i += 32) {
+            const float y = gamma[i] * ((in[i] - mean) / sd) + beta[i];
+            out[i] = y;
+            seq_split_store(xs, xs_stride, i, y);
+        }
     }
     __syncthreads();
 }
@@ -429,7 +458,6 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
     s.att = take(D);
     s.an = take(D);
     s.fr = take(D);
-    s.ff = take(F);
     s.logits = take(V);
     s.ev = take(V);
     s.scores = take(H * cap);
@@ -442,6 +470,13 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         s.vs = take(cap * D);
     } else {
         s.ks = s.vs = nullptr;
+    }
+    const int xs_stride = ((F + 63) / 64) * 64;   // longest matvec input, padded to a k-group
+    s.xs[0] = reinterpret_cast<__nv_bfloat16*>(take(3 * xs_stride / 2));
+    s.xs[1] = reinterpret_cast<__nv_bfloat16*>(take(3 * xs_stride / 2));
+    for (int i = threadIdx.x; i < 3 * xs_stride; i += SEQ_THREADS) {
+        s.xs[0][i] = __float2bfloat16_rn(0.0f);
+        s.xs[1][i] = __float2bfloat16_rn(0.0f);
     }
 
     for (int i = threadIdx.x; i < (int)(sizeof(SeqLayer) * p.L / 4); i += SEQ_THREADS)
@@ -515,13 +550,19 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         const float* e = p.emb + (long long)tok * D;
         if (pos < p.pe_rows) {
             const float* pr = p.pe + pos * D;
-            for (int i = threadIdx.x; i < D; i += SEQ_THREADS) s.x[i] = e[i] + pr[i];
+            for (int i = threadIdx.x; i < D; i += SEQ_THREADS) {
+                const float v = e[i] + pr[i];
+                s.x[i] = v;
+                seq_split_store(s.xs[0], xs_stride, i, v);
+            }
         } else {
             const float ln_base = logf(10000.0f);
             for (int i = threadIdx.x; i < D; i += SEQ_THREADS) {
                 const float sc = expf(-((2.0f * (float)i) / (float)D) * ln_base);
                 const float ang = (float)pos * sc;
-                s.x[i] = e[i] + ((i % 2 == 0) ? sinf(ang) : cosf(ang));
+                const float v = e[i] + ((i % 2 == 0) ? sinf(ang) : cosf(ang));
+                s.x[i] = v;
+                seq_split_store(s.xs[0], xs_stride, i, v);
             }
         }
         __syncthreads();
@@ -560,7 +601,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             if (!acquire()) return false;
             float* ksm = s.ks;
             float* vsm = s.vs;
-            seq_qmv<BITS>(Ly.qkv, s.wbuf[consumed & 1], s.x, [&](int n, float y) {
+            seq_qmv<BITS>(Ly.qkv, s.wbuf[consumed & 1], s.xs[0], xs_stride, s.part, [&](int n, float y) {
                 if (n < D) {
                     s.q[n] = y;
                 } else if (n < 2 * D) {
@@ -666,6 +707,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
                         float o = 0.0f;
                         for (int gg = 0; gg < groups; gg++) o += s.part[gg * w + threadIdx.x];
                         s.att[t0 + threadIdx.x] = o;
+                        seq_split_store(s.xs[1], xs_stride, t0 + threadIdx.x, o);
                     }
                     __syncthreads();
                 }
@@ -675,10 +717,10 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             if (!acquire()) return false;
             {
                 const uint8_t* wb = s.wbuf[consumed & 1];
-                seq_qmv<BITS>(Ly.wo, wb, s.att, [&](int n, float y) { s.fr[n] = y + s.x[n]; });
+                seq_qmv<BITS>(Ly.wo, wb, s.xs[1], xs_stride, s.part, [&](int n, float y) { s.fr[n] = y + s.x[n]; });
                 __syncthreads();
                 const float* g = reinterpret_cast<const float*>(wb + Ly.wo.gamma_off);
-                seq_layernorm(s.fr, s.an, g, g + D, D, s.red);
+                seq_layernorm(s.fr, s.an, g, g + D, D, s.xs[0], xs_stride);
             }
             release();
             clk.mark(SEQ_PH_NORM);
@@ -687,9 +729,9 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             {
                 const uint8_t* wb = s.wbuf[consumed & 1];
                 const float* bias = reinterpret_cast<const float*>(wb + Ly.w1.bias_off);
-                seq_qmv<BITS>(Ly.w1, wb, s.an, [&](int n, float y) {
+                seq_qmv<BITS>(Ly.w1, wb, s.xs[0], xs_stride, s.part, [&](int n, float y) {
                     const float pre = y + bias[n];
-                    s.ff[n] = pre > 0.0f ? pre : 0.0f;
+                    seq_split_store(s.xs[1], xs_stride, n, pre > 0.0f ? pre : 0.0f);
                 });
             }
             release();
@@ -698,10 +740,10 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             {
                 const uint8_t* wb = s.wbuf[consumed & 1];
                 const float* bias = reinterpret_cast<const float*>(wb + Ly.w2.bias_off);
-                seq_qmv<BITS>(Ly.w2, wb, s.ff, [&](int n, float y) { s.fr[n] = y + bias[n] + s.an[n]; });
+                seq_qmv<BITS>(Ly.w2, wb, s.xs[1], xs_stride, s.part, [&](int n, float y) { s.fr[n] = y + bias[n] + s.an[n]; });
                 __syncthreads();
                 const float* g = reinterpret_cast<const float*>(wb + Ly.w2.gamma_off);
-                seq_layernorm(s.fr, s.x, g, g + D, D, s.red);
+                seq_layernorm(s.fr, s.x, g, g + D, D, s.xs[0], xs_stride);
             }
             release();
             clk.mark(SEQ_PH_NORM);
@@ -710,7 +752,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         {
             const uint8_t* wb = s.wbuf[consumed & 1];
             const float* bias = reinterpret_cast<const float*>(wb + p.head.bias_off);
-            seq_qmv<BITS>(p.head, wb, s.x, [&](int n, float y) { s.logits[n] = y + bias[n]; });
+            seq_qmv<BITS>(p.head, wb, s.xs[0], xs_stride, s.part, [&](int n, float y) { s.logits[n] = y + bias[n]; });
         }
         release();
         __syncthreads();

@@ -157,13 +157,14 @@ def test_batched_against_oracle_with_reset_mask(gpu, oracle):
 
 @pytest.mark.parametrize("bits", [4, 8])
 def test_fused_matches_layered_random_model(gpu, oracle, bits):
-    """Both paths on a model off the golden shapes (d=64, 5 heads... d=80 h=5, F=320, V=1000, L=3),
+    """Both paths on a model off the golden shapes (d=80, 5 heads of 16, F=320, V=700, L=3),
     batch 7, greedy and top-k: identical token streams."""
-    spec = Spec(1000, 80, 5, 3, 48)
+    spec = Spec(700, 80, 5, 3, 48)
     recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 33), bits)
     model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, bits, 2) for (_, k, r, c, f, s, p) in recs])
     rng = np.random.RandomState(bits)
     prompts = rng.randint(0, 256, size=(7, 9)).astype(np.uint32)
+    assert gpu.KVCache(model, 7).uses_fused(gpu.Sampling(gpu.GREEDY))
     seeds = np.arange(7, dtype=np.uint64) + 100
     om = oracle.model(spec, flat)
     for samp, sd, strat in ((gpu.Sampling(gpu.GREEDY), None, 0), (gpu.Sampling(gpu.TOPK, 0.7, 12, 0.0), seeds, 1)):
