@@ -97,6 +97,7 @@ SIGNATURES = {
     "dz_cuda_qmatrix_codes": (I32, [P, P]),
     "dz_cuda_matmul_quantized": (I32, [P, P, P, SZ, SZ]),
     "dz_cuda_matmul_quantized_async": (I32, [P, P, P, SZ, SZ, P]),
+    "dz_cuda_matmul_quantized_noalloc": (I32, [P, P, P, SZ, SZ, P]),
     "dz_cuda_model_create": (I32, [P, P, SZ, I32, P]),
     "dz_cuda_model_free": (None, [P]),
     "dz_cuda_model_step_bytes": (SZ, [P]),

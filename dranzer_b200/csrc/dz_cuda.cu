@@ -11,6 +11,7 @@
 #include <cstring>
 #include <algorithm>
 #include <map>
+#include <mutex>
 #include <new>
 #include <string>
 #include <tuple>
@@ -1311,5 +1312,56 @@ extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prom
             stats[DZ_PHASE_EMBED + k].total_ms = (double)ph[k] * 1e-6;
         }
     }
+    return DZ_OK;
+}
+
+// ------------------------------------------------ allocation-free matmul
+
+// Scratch of dz_cuda_matmul_quantized_noalloc: the bf16 hi/mid/lo split of the
+// activation rows (m x 3 x padded k). Every GPU that loads this library holds
+// it until the process exits. It is shared by all calls on a device and keeps
+// the last call's contents; the split kernel overwrites every byte a call then
+// reads, so nothing needs clearing between calls.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[DZ_NOALLOC_SCRATCH_BYTES];
+
+static std::mutex g_noalloc_mutex;
+static void* g_noalloc_addr[256];   // device address of g_noalloc_scratch, per device ordinal
+
+// The array's device address for `device` (current at the call). In host code
+// the symbol names a host-side stand-in, not device memory, so the address is
+// looked up once per device and cached.
+static int noalloc_scratch(int device, void** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (device < 0 || device >= 256) return fail(DZ_E_INVALID, "device ordinal %d out of range", device);
+    if (!g_noalloc_addr[device]) {
+        void* addr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+        if (e != cudaSuccess || !addr)
+            return fail(DZ_E_DEVICE, "cudaGetSymbolAddress(static scratch) on device %d: %s", device,
+                        cudaGetErrorString(e));
+        g_noalloc_addr[device] = addr;
+    }
+    *out = g_noalloc_addr[device];
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_matmul_quantized_noalloc(const float* A, const dz_cuda_qmatrix_t* q, float* C, size_t m,
+                                                size_t k, void* stream) {
+    if (!q || !A || !C || m == 0 || k != (size_t)q->m.K || m > (1u << 24))
+        return fail(DZ_E_INVALID, "matmul_quantized_noalloc: bad arguments (k must equal the matrix rows)");
+    const size_t need = qmv_scratch_bytes(q->m, (int)m);
+    if (need > (size_t)DZ_NOALLOC_SCRATCH_BYTES)
+        return fail(DZ_E_INVALID,
+                    "matmul_quantized_noalloc: m=%zu rows x k=%zu need %zu bytes of scratch, above the static "
+                    "limit of %u bytes (m * 3 * k padded to 64 * 2 bytes)",
+                    m, k, need, (unsigned)DZ_NOALLOC_SCRATCH_BYTES);
+    DeviceGuard g(q->device);
+    if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", q->device);
+    void* scratch = nullptr;
+    int rc = noalloc_scratch(q->device, &scratch);
+    if (rc) return rc;
+    QmvEpilogue ep = plain_epilogue(q->m, C, q->m.N);
+    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, static_cast<__nv_bfloat16*>(scratch));
+    DZ_CUDA(cudaGetLastError());
     return DZ_OK;
 }

@@ -68,6 +68,22 @@ int dz_cuda_matmul_quantized(const float *A, const dz_cuda_qmatrix_t *weights, f
 int dz_cuda_matmul_quantized_async(const float *A_dev, const dz_cuda_qmatrix_t *weights,
                                    float *C_dev, size_t m, size_t k, void *stream);
 
+/* Same product as dz_cuda_matmul_quantized_async, for callers that cannot
+ * allocate device memory when they call: code recording a CUDA graph (a stream
+ * capture forbids cudaMalloc) and hosts that hand the library no allocation
+ * rights after start-up. The async entry point grows a per-matrix scratch
+ * buffer with cudaMalloc the first time it sees a larger m; this one allocates
+ * nothing and uses a fixed DZ_NOALLOC_SCRATCH_BYTES array that every GPU which
+ * loads the library holds until exit. m * 3 * (k rounded up to 64) * 2 bytes
+ * must fit in it (e.g. m <= 170 at k = 4096); larger calls return DZ_E_INVALID.
+ * The first call on a device looks up the array's device address (make that
+ * call before any stream capture). All calls on a device share the array, so
+ * calls whose work overlaps on the GPU (different streams, no ordering) race.
+ * No counterpart in the reference. */
+#define DZ_NOALLOC_SCRATCH_BYTES (4u << 20)
+int dz_cuda_matmul_quantized_noalloc(const float *A_dev, const dz_cuda_qmatrix_t *weights, float *C_dev,
+                                     size_t m, size_t k, void *stream);
+
 /* ---- Model: the parameters of a v2/v3 bundle kept as codes on the device.
  * `tensors` are the n blobs of model_param_tensors() order
  * (src/core/model_params.c:39-103), as dz_bundle_tensors() returns them; they are
