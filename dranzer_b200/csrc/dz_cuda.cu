@@ -242,22 +242,146 @@ static void launch_qmm_bits(const QmmArgs& a, int NB, unsigned grid, cudaStream_
 
 static int g_num_sms = 148;
 
-// Bytes of split-activation scratch one matvec of this matrix needs for M rows.
-static size_t qmv_scratch_bytes(const DevQMat& W, int M) {
+static size_t r256(size_t n) { return (n + 255) & ~(size_t)255; }
+
+// Bytes of split-activation scratch one matvec of this matrix needs for M
+// rows: the B-fragment-ordered splits (16 bytes per k row per row pair), then
+// the M row exponents.
+static size_t qmv_xf_bytes(const DevQMat& W, int M) {
     const int KG = W.bits == 8 ? 32 : 64;
-    return (size_t)M * 3 * (size_t)W.nkg * KG * 2;
+    return (size_t)W.nkg * KG * (size_t)((M + 1) / 2) * 16;
+}
+static size_t qmv_scratch_bytes(const DevQMat& W, int M) { return r256(qmv_xf_bytes(W, M)) + r256((size_t)M * 4); }
+
+template <int BITS, int NB, int NT, bool XSM>
+static void launch_qms_t(const QmsArgs& a, unsigned grid, size_t smem, cudaStream_t st) {
+    dz_qms_kernel<BITS, NB, NT, XSM><<<grid, QMV_THREADS, smem, st>>>(a);
 }
 
-// Y = epilogue(X . deq(W)) for M rows on the tensor cores: the activation split
-// into `scratch` (qmv_scratch_bytes), then the MMA kernel. Returns launches (2).
-static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep,
-                      cudaStream_t st, __nv_bfloat16* scratch) {
+// (NB, NT) per row count: NB row pairs per MMA group, NT n-tiles per warp.
+static void qms_shape(int M, int* NB, int* NT) {
+    *NB = M <= 2 ? 1 : M <= 4 ? 2 : M <= 8 ? 4 : 8;
+    *NT = *NB == 1 ? 1 : *NB == 2 ? 2 : *NB == 4 ? 4 : 2;
+}
+
+template <int BITS, bool XSM>
+static void launch_qms_bits(const QmsArgs& a, int NB, unsigned grid, size_t smem, cudaStream_t st) {
+    switch (NB) {
+        case 1: launch_qms_t<BITS, 1, 1, XSM>(a, grid, smem, st); break;
+        case 2: launch_qms_t<BITS, 2, 2, XSM>(a, grid, smem, st); break;
+        case 4: launch_qms_t<BITS, 4, 4, XSM>(a, grid, smem, st); break;
+        default: launch_qms_t<BITS, 8, 2, XSM>(a, grid, smem, st); break;
+    }
+}
+
+// The streaming kernels take more than the default 48 KB of shared memory;
+// the attribute is set once per device, outside any stream capture.
+static std::mutex g_qms_mutex;
+static bool g_qms_ready[256];
+static int g_smem_optin = 232448;
+
+static int qms_prepare(int device) {
+    if (device < 0 || device >= 256) return fail(DZ_E_DEVICE, "device %d out of range", device);
+    std::lock_guard<std::mutex> lock(g_qms_mutex);
+    if (g_qms_ready[device]) return DZ_OK;
+    int optin = 0;
+    DZ_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    g_smem_optin = optin;
+#define DZ_QMS_ATTR(B, NB, NT, X) \
+    DZ_CUDA(cudaFuncSetAttribute(dz_qms_kernel<B, NB, NT, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
+#define DZ_QMS_ATTR2(B, X) \
+    DZ_QMS_ATTR(B, 1, 1, X); DZ_QMS_ATTR(B, 2, 2, X); DZ_QMS_ATTR(B, 4, 4, X); DZ_QMS_ATTR(B, 8, 2, X)
+    DZ_QMS_ATTR2(4, false); DZ_QMS_ATTR2(4, true); DZ_QMS_ATTR2(8, false); DZ_QMS_ATTR2(8, true);
+#undef DZ_QMS_ATTR2
+#undef DZ_QMS_ATTR
+    g_qms_ready[device] = true;
+    return DZ_OK;
+}
+
+// Rows up to which the streaming kernel serves a product.
+constexpr int QMS_MAX_M = 16;
+// B fragments up to this size are copied into each CTA's shared memory.
+constexpr unsigned QMS_XF_SMEM_MAX = 96u << 10;
+
+// k-parts for the streaming kernel: the split of n-groups x k-groups over the
+// warps of g_num_sms persistent CTAs with the fewest k-groups on the busiest
+// warp (ties: fewer k-parts, fewer reductions).
+static int qms_kparts(int n_groups, int nkg, int* nrounds_out, unsigned* grid_out) {
+    long long best_cost = -1;
+    int best = 1;
+    for (int kp = 1; kp <= QMV_WARPS; kp *= 2) {
+        const long long per_round = QMV_WARPS / kp;
+        const long long rounds = (n_groups + per_round - 1) / per_round;
+        const long long grid = std::min<long long>(rounds, g_num_sms);
+        const long long waves = (rounds + grid - 1) / grid;
+        const long long per = (nkg + kp - 1) / kp;
+        const long long cost = waves * per + waves;   // + one reduction per round
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            best = kp;
+        }
+    }
+    const long long per_round = QMV_WARPS / best;
+    const long long rounds = (n_groups + per_round - 1) / per_round;
+    *nrounds_out = (int)rounds;
+    *grid_out = (unsigned)std::min<long long>(rounds, g_num_sms);
+    return best;
+}
+
+// Y = epilogue(X . deq(W)) for M rows on the tensor cores: the activation
+// split into `scratch` (qmv_scratch_bytes), then the MMA kernel (streaming for
+// M <= QMS_MAX_M). A bulk-copy wait that gives up sets *status (when given)
+// and leaves NaN in the tile. Returns launches (2).
+static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
+                      cudaStream_t st, void* scratch, int* status) {
     const int KG = W.bits == 8 ? 32 : 64;
+    const int KT = KG / 16;
     const int Kp = W.nkg * KG;
+    const int nbt = (M + 1) / 2;
+    uint32_t* XF = static_cast<uint32_t*>(scratch);
+    int* shift = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + r256(qmv_xf_bytes(W, M)));
     {
-        const long long n = (long long)M * Kp;
-        ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 6.0 * n, 0, st);
-        dz_split_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, scratch);
+        ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 16.0 * nbt * Kp, 0, st);
+        dz_split_rows_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, KT, W.nkg, nbt, XF, shift);
+    }
+    QmvEpilogue ep = ep_in;
+    ep.row_shift = shift;
+    const double qmv_bytes =
+        (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 16.0 * nbt * Kp + 4.0 * M * W.N;
+    if (M <= QMS_MAX_M) {
+        int NB, NT;
+        qms_shape(M, &NB, &NT);
+        QmsArgs a;
+        a.codes = W.codes;
+        a.N = W.N;
+        a.nkg = W.nkg;
+        a.ntiles = W.ntiles;
+        a.XF = XF;
+        a.nbt = nbt;
+        a.M = M;
+        a.status = status;
+        a.ep = ep;
+        a.n_groups = (W.ntiles + NT - 1) / NT;
+        unsigned grid = 1;
+        a.kparts = qms_kparts(a.n_groups, W.nkg, &a.nrounds, &grid);
+        a.per = (W.nkg + a.kparts - 1) / a.kparts;
+        const size_t xf = qmv_xf_bytes(W, M);
+        const bool xsm = xf <= QMS_XF_SMEM_MAX;
+        a.xf_bytes = xsm ? (unsigned)xf : 0u;
+        const size_t fixed = dz_qms_smem_bytes(0, NT, NB, a.xf_bytes);
+        const int pk_budget = (int)(((size_t)g_smem_optin - fixed) / ((size_t)QMV_WARPS * QMS_STAGES * NT * 512));
+        a.pk = std::max(1, std::min(16 / NT, pk_budget));
+        a.pk = std::min(a.pk, std::max(1, a.per));
+        const size_t smem = dz_qms_smem_bytes(a.pk, NT, NB, a.xf_bytes);
+        ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
+        if (W.bits == 8) {
+            if (xsm) launch_qms_bits<8, true>(a, NB, grid, smem, st);
+            else launch_qms_bits<8, false>(a, NB, grid, smem, st);
+        } else {
+            if (xsm) launch_qms_bits<4, true>(a, NB, grid, smem, st);
+            else launch_qms_bits<4, false>(a, NB, grid, smem, st);
+        }
+        return 2;
     }
     QmmArgs a;
     a.codes = W.codes;
@@ -265,8 +389,8 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     a.N = W.N;
     a.nkg = W.nkg;
     a.ntiles = W.ntiles;
-    a.Xs = scratch;
-    a.Kp = Kp;
+    a.XF = XF;
+    a.nbt = nbt;
     a.M = M;
     a.ep = ep;
     const int NB = M <= 2 ? 1 : M <= 4 ? 2 : M <= 8 ? 4 : 8;
@@ -281,9 +405,7 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     a.kg_per_part = (W.nkg + kp - 1) / kp;
     const int units_per_cta = QMV_WARPS / kp;
     const unsigned grid = (unsigned)((units + units_per_cta - 1) / units_per_cta);
-    ProfScope prof(DZ_KERNEL_QMV,
-                   (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 6.0 * M * Kp + 4.0 * M * W.N,
-                   2.0 * M * W.K * W.N, st);
+    ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
     if (W.bits == 8) launch_qmm_bits<8>(a, NB, grid, st);
     else launch_qmm_bits<4>(a, NB, grid, st);
     return 2;
@@ -307,8 +429,9 @@ struct dz_cuda_qmatrix {
     int device;
     DevQMat m;
     cudaStream_t stream;
-    __nv_bfloat16* scratch = nullptr;   // split activations, grown to the largest M used
+    void* scratch = nullptr;            // split activations, grown to the largest M used
     size_t scratch_bytes = 0;
+    int* status = nullptr;              // device word: a weight-copy wait gave up
 };
 
 static int qmatrix_scratch(dz_cuda_qmatrix_t* q, int M) {
@@ -335,9 +458,13 @@ extern "C" int dz_cuda_qmatrix_create(int device, const dz_tensor_blob_t* w, dz_
         delete q;
         return fail(DZ_E_DEVICE, "stream creation failed");
     }
-    int rc = make_qmat({w}, q->stream, &q->m);
+    int rc = qms_prepare(device);
+    if (!rc) rc = make_qmat({w}, q->stream, &q->m);
+    if (!rc && cudaMalloc(&q->status, 4) != cudaSuccess) rc = fail(DZ_E_NOMEM, "device allocation");
+    if (!rc && cudaMemsetAsync(q->status, 0, 4, q->stream) != cudaSuccess) rc = fail(DZ_E_DEVICE, "memset");
     if (rc) {
         free_qmat(q->m);
+        cudaFree(q->status);
         cudaStreamDestroy(q->stream);
         delete q;
         return rc;
@@ -351,6 +478,7 @@ extern "C" void dz_cuda_qmatrix_free(dz_cuda_qmatrix_t* q) {
     DeviceGuard g(q->device);
     free_qmat(q->m);
     cudaFree(q->scratch);
+    cudaFree(q->status);
     cudaStreamDestroy(q->stream);
     delete q;
 }
@@ -405,7 +533,7 @@ extern "C" int dz_cuda_matmul_quantized_async(const float* A, const dz_cuda_qmat
     int rc = qmatrix_scratch(const_cast<dz_cuda_qmatrix_t*>(q), (int)m);
     if (rc) return rc;
     QmvEpilogue ep = plain_epilogue(q->m, C, q->m.N);
-    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, q->scratch);
+    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, q->scratch, q->status);
     DZ_CUDA(cudaGetLastError());
     return DZ_OK;
 }
@@ -425,12 +553,19 @@ extern "C" int dz_cuda_matmul_quantized(const float* A, const dz_cuda_qmatrix_t*
     cudaError_t e = cudaMemcpyAsync(dA, A, m * k * 4, cudaMemcpyHostToDevice, q->stream);
     int rc = DZ_OK;
     if (e == cudaSuccess) rc = dz_cuda_matmul_quantized_async(dA, q, dC, m, k, q->stream);
+    int timed_out = 0;
     if (e == cudaSuccess && rc == DZ_OK) e = cudaMemcpyAsync(C, dC, m * n * 4, cudaMemcpyDeviceToHost, q->stream);
+    if (e == cudaSuccess && rc == DZ_OK)
+        e = cudaMemcpyAsync(&timed_out, q->status, 4, cudaMemcpyDeviceToHost, q->stream);
     if (e == cudaSuccess && rc == DZ_OK) e = cudaStreamSynchronize(q->stream);
     cudaFree(dA);
     cudaFree(dC);
     if (rc) return rc;
     if (e != cudaSuccess) return fail(DZ_E_DEVICE, "matmul_quantized: %s", cudaGetErrorString(e));
+    if (timed_out) {
+        cudaMemsetAsync(q->status, 0, 4, q->stream);
+        return fail(DZ_E_TIMEOUT, "matmul_quantized: a weight copy did not arrive within 1 s");
+    }
     return DZ_OK;
 }
 
@@ -538,8 +673,8 @@ static size_t seq_smem_bytes(const dz_cuda_model_t* m, int cap, bool kv_smem) {
     auto r4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t table = (sizeof(SeqLayer) * m->layers.size() + 15) & ~(size_t)15;
     const size_t xs_stride = (F + 63) / 64 * 64;
-    return 2 * (size_t)m->seq_buf_bytes + 48 + table + 8 * (P > (size_t)SEQ_WARPS ? P : (size_t)SEQ_WARPS) +
-           4 * (5 * r4(D) + 2 * r4(V) + r4(H * (size_t)cap) + 64 + 2 * r4(pv)) +
+    return 2 * (size_t)m->seq_buf_bytes + 64 + table + 8 * (P > (size_t)SEQ_WARPS ? P : (size_t)SEQ_WARPS) +
+           4 * (5 * r4(D) + r4(F) + 2 * r4(V) + r4(H * (size_t)cap) + 64 + 2 * r4(pv)) +
            (kv_smem ? 8 * r4((size_t)cap * D) : 0) + 2 * 4 * r4(3 * xs_stride / 2);
 }
 
@@ -621,6 +756,7 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
     DeviceGuard g(device);
     if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", device);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, device);
+    if (int rc0 = qms_prepare(device)) return rc0;
     auto* m = new (std::nothrow) dz_cuda_model;
     if (!m) return fail(DZ_E_NOMEM, "host allocation");
     m->device = device;
@@ -741,7 +877,7 @@ struct dz_cuda_cache {
     std::map<GenKey, cudaGraphExec_t> gen_graphs;
     double prof_ctx_bytes_per_layer = 0, prof_ctx_flops_per_layer = 0;  // set per profiled step
     int path = DZ_PATH_AUTO;
-    __nv_bfloat16* xs_scratch = nullptr;  // split activations of the layered path's matvecs
+    void* xs_scratch = nullptr;          // split activations of the layered path's matvecs
     int* status = nullptr;        // device word the fused kernel reports a timeout in
     unsigned long long* phase_ns = nullptr;  // [SEQ_PHASES] fused-kernel phase clock (profiling)
     int* host_status = nullptr;   // pinned
@@ -929,16 +1065,16 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             ep.seg_start[0] = 0; ep.seg_start[1] = D; ep.seg_start[2] = 2 * D; ep.seg_start[3] = 3 * D;
             ep.seg_ptr[1] = Kl; ep.seg_ld[1] = (long long)cap * D; ep.seg_row_off[1] = c->row_off;
             ep.seg_ptr[2] = Vl; ep.seg_ld[2] = (long long)cap * D; ep.seg_row_off[2] = c->row_off;
-            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st, c->xs_scratch);
+            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st, c->xs_scratch, c->status);
         } else {
             QmvEpilogue eq = plain_epilogue(L.q, c->q, D);
-            launches += launch_qmv(L.q, c->hidden, D, B, eq, st, c->xs_scratch);
+            launches += launch_qmv(L.q, c->hidden, D, B, eq, st, c->xs_scratch, c->status);
             QmvEpilogue ek = plain_epilogue(L.k, Kl, (long long)cap * D);
             ek.seg_row_off[0] = c->row_off;
-            launches += launch_qmv(L.k, c->hidden, D, B, ek, st, c->xs_scratch);
+            launches += launch_qmv(L.k, c->hidden, D, B, ek, st, c->xs_scratch, c->status);
             QmvEpilogue ev = plain_epilogue(L.v, Vl, (long long)cap * D);
             ev.seg_row_off[0] = c->row_off;
-            launches += launch_qmv(L.v, c->hidden, D, B, ev, st, c->xs_scratch);
+            launches += launch_qmv(L.v, c->hidden, D, B, ev, st, c->xs_scratch, c->status);
         }
         {
             // bytes: the K and V rows of every sequence's context (ctx <= cap; the
@@ -951,7 +1087,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         }
         launches++;
         QmvEpilogue eo = plain_epilogue(L.wo, c->attn_raw, D);
-        launches += launch_qmv(L.wo, c->concat, D, B, eo, st, c->xs_scratch);
+        launches += launch_qmv(L.wo, c->concat, D, B, eo, st, c->xs_scratch, c->status);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D, 0, st);
             dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, D,
@@ -961,12 +1097,12 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         QmvEpilogue e1 = plain_epilogue(L.w1, c->ff, F);
         e1.bias = L.b1;
         e1.relu = 1;
-        launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st, c->xs_scratch);
+        launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st, c->xs_scratch, c->status);
         QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
         e2.bias = L.b2;
         e2.residual = c->attn_norm;
         e2.ld_res = D;
-        launches += launch_qmv(L.w2, c->ff, F, B, e2, st, c->xs_scratch);
+        launches += launch_qmv(L.w2, c->ff, F, B, e2, st, c->xs_scratch, c->status);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D, 0, st);
             dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->ff_raw, nullptr, L.g2, L.be2, c->hidden, D, 1e-6f);
@@ -975,7 +1111,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
     }
     QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
     eh.bias = m->out_bias;
-    launches += launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch);
+    launches += launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status);
     return launches;
 }
 
@@ -1361,7 +1497,7 @@ extern "C" int dz_cuda_matmul_quantized_noalloc(const float* A, const dz_cuda_qm
     int rc = noalloc_scratch(q->device, &scratch);
     if (rc) return rc;
     QmvEpilogue ep = plain_epilogue(q->m, C, q->m.N);
-    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, static_cast<__nv_bfloat16*>(scratch));
+    launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, scratch, q->status);
     DZ_CUDA(cudaGetLastError());
     return DZ_OK;
 }

@@ -12,6 +12,7 @@ constexpr int QMV_THREADS = 256;
 constexpr int QMV_WARPS = QMV_THREADS / 32;
 
 struct QmvEpilogue {
+    const int* row_shift;     // [M] exponent to undo the activation scaling, or nullptr
     const float* col_scale;   // [Np] per-column scale, or nullptr (scale 1)
     const float* bias;        // [N] or nullptr
     const float* residual;    // [M][ld_res] or nullptr, added after bias
@@ -28,6 +29,7 @@ struct QmvEpilogue {
 
 __device__ __forceinline__ void dz_qmv_store_row(const QmvEpilogue& e, int M, int N, int m, int n, float acc) {
     if (m >= M || n >= N) return;
+    if (e.row_shift) acc = ldexpf(acc, e.row_shift[m]);
     float y = e.col_scale ? acc * e.col_scale[n] : acc;
     if (e.bias) y = y + e.bias[n];
     if (e.residual) y = y + e.residual[(long long)m * e.ld_res + n];

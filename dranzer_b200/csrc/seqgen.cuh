@@ -155,9 +155,10 @@ __device__ __forceinline__ void fence_proxy_async() {
 struct SeqSmem {
     uint8_t* wbuf[2];
     uint64_t* bar;     // [3]: weight buffers 0 and 1, K/V staging
-    float *x, *q, *att, *an, *fr, *logits, *scores, *red, *ev, *part, *part2;
+    float *x, *q, *att, *an, *fr, *hid, *logits, *scores, *red, *ev, *part, *part2;
     float *ks, *vs;   // this layer's K / V rows staged in shared memory (or nullptr)
-    __nv_bfloat16* xs[2];  // bf16 hi/mid/lo splits of the matvec inputs, two alternating buffers
+    __half* xs[2];     // fp16 hi/mid/lo splits of the matvec inputs, two alternating buffers
+    int* xsh;          // [2] exponent undoing each buffer's row scaling
     uint64_t* keys;
     int* flag;         // [0] abort, [1] token broadcast, [2] top-p count, [3] drawn position
     SeqLayer* layers;  // the layer table, copied from global memory at entry
@@ -201,12 +202,13 @@ __device__ __forceinline__ void seq_issue(const SeqParams& p, SeqSmem& s, SeqPip
 
 // Block-level quantized matvec on the tensor cores from the shared-memory copy
 // of matrix `m`: y[n] = epi(n, sum_k x[k] * level(k, n) * scale[n]). x enters
-// as its bf16 hi/mid/lo split (three arrays of `xs_stride` elements, zero past
-// K); B column g < 3 of each m16n8k16 MMA carries split g, the others are
-// zero. Work units are (n-tile, k-part); k-parts combine through `red`.
+// as its fp16 hi/mid/lo split of x * 2^-xshift (three arrays of `xs_stride`
+// elements, zero past K); B column g < 3 of each m16n8k16 MMA carries split
+// g, the others are zero. Work units are (n-tile, k-part); k-parts combine
+// through `red`.
 template <int BITS, typename Epi>
-__device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, const __nv_bfloat16* xs, int xs_stride,
-                                        float* red, Epi epi) {
+__device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, const __half* xs, int xs_stride,
+                                        int xshift, float* red, Epi epi) {
     constexpr int KT = FragGeom<BITS>::KT;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
@@ -217,6 +219,8 @@ __device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, con
     const float* scale = reinterpret_cast<const float*>(wsm + m.scale_off);
     const bool feeds = g < 3;
     const uint32_t* xw = reinterpret_cast<const uint32_t*>(xs + (feeds ? g : 0) * xs_stride);
+    // INT4 outputs n+8 carry 16x (dz_deq4)
+    const int sh_lo = xshift, sh_hi = BITS == 4 ? xshift - 4 : xshift;
     for (int u0 = 0; u0 < units; u0 += SEQ_WARPS) {
         const int unit = u0 + warp;
         const bool active = unit < units;
@@ -233,28 +237,22 @@ __device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, con
                     const uint32_t b0 = feeds ? xw[(k0 >> 1) + t] : 0u;
                     const uint32_t b1 = feeds ? xw[(k0 >> 1) + t + 4] : 0u;
                     uint32_t af[4];
-                    if (BITS == 4) {
-                        dz_frag_dequant(ww[kt], DZ_BF16X2_135, af);
-                        dz_mma_bf16(d[0], af, b0, b1);
-                    } else {
-                        dz_frag_dequant(ww[2 * kt], DZ_BF16X2_127, af);
-                        dz_mma_bf16(d[0], af, b0, b1);
-                        dz_frag_dequant(ww[2 * kt + 1], DZ_BF16X2_136, af);
-                        dz_mma_bf16(d[1], af, b0, b1);
-                    }
+                    if (BITS == 4) dz_deq4(ww[kt], af);
+                    else dz_deq8(ww[2 * kt], ww[2 * kt + 1], af);
+                    dz_mma_f16(d[kt & 1], af, b0, b1);
                 }
             }
         }
         // columns 0..2 (hi, mid, lo of the one row) sit in lanes t = 0 (cols 0, 1) and t = 1 (col 2)
-        float v0 = BITS == 8 ? 16.0f * (d[1][0] + d[1][1]) + (d[0][0] + d[0][1]) : d[0][0] + d[0][1];
-        float v1 = BITS == 8 ? 16.0f * (d[1][2] + d[1][3]) + (d[0][2] + d[0][3]) : d[0][2] + d[0][3];
+        float v0 = (d[0][0] + d[0][1]) + (d[1][0] + d[1][1]);
+        float v1 = (d[0][2] + d[0][3]) + (d[1][2] + d[1][3]);
         v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
         v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
         if (active && t == 0) {
             if (kp == 1) {
                 const int n0 = nt * 16 + g;
-                if (n0 < m.N) epi(n0, v0 * scale[n0]);
-                if (n0 + 8 < m.N) epi(n0 + 8, v1 * scale[n0 + 8]);
+                if (n0 < m.N) epi(n0, ldexpf(v0, sh_lo) * scale[n0]);
+                if (n0 + 8 < m.N) epi(n0 + 8, ldexpf(v1, sh_hi) * scale[n0 + 8]);
             } else {
                 red[(nt * kp + kpart) * 16 + g] = v0;
                 red[(nt * kp + kpart) * 16 + g + 8] = v1;
@@ -267,25 +265,43 @@ __device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, con
             const int nt = n >> 4, c = n & 15;
             float sum = 0.0f;
             for (int q = 0; q < kp; q++) sum += red[(nt * kp + q) * 16 + c];
-            if (n < m.N) epi(n, sum * scale[n]);
+            if (n < m.N) epi(n, ldexpf(sum, c < 8 ? sh_lo : sh_hi) * scale[n]);
         }
     }
 }
 
-// hi / mid / lo bf16 split of v into element i of a split buffer.
-__device__ __forceinline__ void seq_split_store(__nv_bfloat16* xs, int stride, int i, float v) {
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    const float r1 = v - __bfloat162float(h);
-    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
-    xs[i] = h;
-    xs[stride + i] = mid;
-    xs[2 * stride + i] = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+// fp16 hi / mid / lo split of v * 2^sh into element i of a split buffer.
+__device__ __forceinline__ void seq_split_store(__half* xs, int stride, int i, float v, int sh) {
+    const DzSplit3 p = dz_split3(ldexpf(v, sh));
+    xs[i] = p.h;
+    xs[stride + i] = p.m;
+    xs[2 * stride + i] = p.l;
+}
+
+// Split the n values of src (complete and visible to the block) into a split
+// buffer with the row's exponent shift; block-wide, ends with the buffer
+// written but not yet behind a barrier (the next acquire() is one).
+__device__ __forceinline__ void seq_split_block(const float* src, int n, __half* xs, int stride, int* shift_slot,
+                                                float* red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float mx = 0.0f;
+    for (int i = threadIdx.x; i < n; i += SEQ_THREADS) mx = fmaxf(mx, fabsf(src[i]));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    float amax = 0.0f;
+#pragma unroll
+    for (int w = 0; w < SEQ_WARPS; w++) amax = fmaxf(amax, red[w]);
+    const int sh = dz_row_shift(amax);
+    for (int i = threadIdx.x; i < n; i += SEQ_THREADS) seq_split_store(xs, stride, i, src[i], sh);
+    if (threadIdx.x == 0) *shift_slot = -sh;
 }
 
 // LayerNorm (src/core/tensor_ops.c:88-111) of D values in shared memory, by
 // warp 0 (shuffle reductions, no block barrier until the output is written).
 __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const float* gamma, const float* beta,
-                                              int D, __nv_bfloat16* xs, int xs_stride) {
+                                              int D, __half* xs, int xs_stride, int* shift_slot) {
     if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float s = 0.0f;
@@ -301,11 +317,17 @@ __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
         const float sd = sqrtf(v / (float)D + 1e-6f);
+        float mx = 0.0f;
         for (int i = lane; i < D; i += 32) {
             const float y = gamma[i] * ((in[i] - mean) / sd) + beta[i];
             out[i] = y;
-            seq_split_store(xs, xs_stride, i, y);
+            mx = fmaxf(mx, fabsf(y));
         }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const int sh = dz_row_shift(mx);
+        for (int i = lane; i < D; i += 32) seq_split_store(xs, xs_stride, i, out[i], sh);
+        if (lane == 0) *shift_slot = -sh;
     }
     __syncthreads();
 }
@@ -445,6 +467,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
     s.wbuf[1] = cur; cur += p.buf_bytes;
     s.bar = reinterpret_cast<uint64_t*>(cur); cur += 32;
     s.flag = reinterpret_cast<int*>(cur); cur += 16;
+    s.xsh = reinterpret_cast<int*>(cur); cur += 16;
     s.layers = reinterpret_cast<SeqLayer*>(cur); cur += (sizeof(SeqLayer) * p.L + 15) & ~(size_t)15;
     int P = 1;
     while (P < V) P <<= 1;
@@ -458,6 +481,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
     s.att = take(D);
     s.an = take(D);
     s.fr = take(D);
+    s.hid = take(F);
     s.logits = take(V);
     s.ev = take(V);
     s.scores = take(H * cap);
@@ -472,11 +496,11 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         s.ks = s.vs = nullptr;
     }
     const int xs_stride = ((F + 63) / 64) * 64;   // longest matvec input, padded to a k-group
-    s.xs[0] = reinterpret_cast<__nv_bfloat16*>(take(3 * xs_stride / 2));
-    s.xs[1] = reinterpret_cast<__nv_bfloat16*>(take(3 * xs_stride / 2));
+    s.xs[0] = reinterpret_cast<__half*>(take(3 * xs_stride / 2));
+    s.xs[1] = reinterpret_cast<__half*>(take(3 * xs_stride / 2));
     for (int i = threadIdx.x; i < 3 * xs_stride; i += SEQ_THREADS) {
-        s.xs[0][i] = __float2bfloat16_rn(0.0f);
-        s.xs[1][i] = __float2bfloat16_rn(0.0f);
+        s.xs[0][i] = __float2half_rn(0.0f);
+        s.xs[1][i] = __float2half_rn(0.0f);
     }
 
     for (int i = threadIdx.x; i < (int)(sizeof(SeqLayer) * p.L / 4); i += SEQ_THREADS)
@@ -551,21 +575,18 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         if (pos < p.pe_rows) {
             const float* pr = p.pe + pos * D;
             for (int i = threadIdx.x; i < D; i += SEQ_THREADS) {
-                const float v = e[i] + pr[i];
-                s.x[i] = v;
-                seq_split_store(s.xs[0], xs_stride, i, v);
+                s.x[i] = e[i] + pr[i];
             }
         } else {
             const float ln_base = logf(10000.0f);
             for (int i = threadIdx.x; i < D; i += SEQ_THREADS) {
                 const float sc = expf(-((2.0f * (float)i) / (float)D) * ln_base);
                 const float ang = (float)pos * sc;
-                const float v = e[i] + ((i % 2 == 0) ? sinf(ang) : cosf(ang));
-                s.x[i] = v;
-                seq_split_store(s.xs[0], xs_stride, i, v);
+                s.x[i] = e[i] + ((i % 2 == 0) ? sinf(ang) : cosf(ang));
             }
         }
         __syncthreads();
+        seq_split_block(s.x, D, s.xs[0], xs_stride, &s.xsh[0], s.red);
         clk.mark(SEQ_PH_EMBED);
         for (int l = 0; l < p.L; l++) {
             const SeqLayer& Ly = s.layers[l];
@@ -601,7 +622,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             if (!acquire()) return false;
             float* ksm = s.ks;
             float* vsm = s.vs;
-            seq_qmv<BITS>(Ly.qkv, s.wbuf[consumed & 1], s.xs[0], xs_stride, s.part, [&](int n, float y) {
+            seq_qmv<BITS>(Ly.qkv, s.wbuf[consumed & 1], s.xs[0], xs_stride, s.xsh[0], s.part, [&](int n, float y) {
                 if (n < D) {
                     s.q[n] = y;
                 } else if (n < 2 * D) {
@@ -707,20 +728,21 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
                         float o = 0.0f;
                         for (int gg = 0; gg < groups; gg++) o += s.part[gg * w + threadIdx.x];
                         s.att[t0 + threadIdx.x] = o;
-                        seq_split_store(s.xs[1], xs_stride, t0 + threadIdx.x, o);
                     }
                     __syncthreads();
                 }
             }
+            seq_split_block(s.att, D, s.xs[1], xs_stride, &s.xsh[1], s.red);
             clk.mark(SEQ_PH_ATTENTION);
             // W_o, + residual, then LayerNorm with the gamma/beta carried in W_o's blob
             if (!acquire()) return false;
             {
                 const uint8_t* wb = s.wbuf[consumed & 1];
-                seq_qmv<BITS>(Ly.wo, wb, s.xs[1], xs_stride, s.part, [&](int n, float y) { s.fr[n] = y + s.x[n]; });
+                seq_qmv<BITS>(Ly.wo, wb, s.xs[1], xs_stride, s.xsh[1], s.part,
+                              [&](int n, float y) { s.fr[n] = y + s.x[n]; });
                 __syncthreads();
                 const float* g = reinterpret_cast<const float*>(wb + Ly.wo.gamma_off);
-                seq_layernorm(s.fr, s.an, g, g + D, D, s.xs[0], xs_stride);
+                seq_layernorm(s.fr, s.an, g, g + D, D, s.xs[0], xs_stride, &s.xsh[0]);
             }
             release();
             clk.mark(SEQ_PH_NORM);
@@ -729,21 +751,23 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             {
                 const uint8_t* wb = s.wbuf[consumed & 1];
                 const float* bias = reinterpret_cast<const float*>(wb + Ly.w1.bias_off);
-                seq_qmv<BITS>(Ly.w1, wb, s.xs[0], xs_stride, s.part, [&](int n, float y) {
+                seq_qmv<BITS>(Ly.w1, wb, s.xs[0], xs_stride, s.xsh[0], s.part, [&](int n, float y) {
                     const float pre = y + bias[n];
-                    seq_split_store(s.xs[1], xs_stride, n, pre > 0.0f ? pre : 0.0f);
+                    s.hid[n] = pre > 0.0f ? pre : 0.0f;
                 });
             }
             release();
+            seq_split_block(s.hid, F, s.xs[1], xs_stride, &s.xsh[1], s.red);
             // FFN down + bias + residual, LayerNorm
             if (!acquire()) return false;
             {
                 const uint8_t* wb = s.wbuf[consumed & 1];
                 const float* bias = reinterpret_cast<const float*>(wb + Ly.w2.bias_off);
-                seq_qmv<BITS>(Ly.w2, wb, s.xs[1], xs_stride, s.part, [&](int n, float y) { s.fr[n] = y + bias[n] + s.an[n]; });
+                seq_qmv<BITS>(Ly.w2, wb, s.xs[1], xs_stride, s.xsh[1], s.part,
+                              [&](int n, float y) { s.fr[n] = y + bias[n] + s.an[n]; });
                 __syncthreads();
                 const float* g = reinterpret_cast<const float*>(wb + Ly.w2.gamma_off);
-                seq_layernorm(s.fr, s.x, g, g + D, D, s.xs[0], xs_stride);
+                seq_layernorm(s.fr, s.x, g, g + D, D, s.xs[0], xs_stride, &s.xsh[0]);
             }
             release();
             clk.mark(SEQ_PH_NORM);
@@ -752,7 +776,8 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         {
             const uint8_t* wb = s.wbuf[consumed & 1];
             const float* bias = reinterpret_cast<const float*>(wb + p.head.bias_off);
-            seq_qmv<BITS>(p.head, wb, s.xs[0], xs_stride, s.part, [&](int n, float y) { s.logits[n] = y + bias[n]; });
+            seq_qmv<BITS>(p.head, wb, s.xs[0], xs_stride, s.xsh[0], s.part,
+                          [&](int n, float y) { s.logits[n] = y + bias[n]; });
         }
         release();
         __syncthreads();
