@@ -253,26 +253,31 @@ static size_t qmv_xf_bytes(const DevQMat& W, int M) {
 }
 static size_t qmv_scratch_bytes(const DevQMat& W, int M) { return r256(qmv_xf_bytes(W, M)) + r256((size_t)M * 4); }
 
-template <int BITS, int NB, int NT, bool XSM>
+template <int BITS, int NB, int NT, int W, bool XIN>
 static void launch_qms_t(const QmsArgs& a, unsigned grid, size_t smem, cudaStream_t st) {
-    dz_qms_kernel<BITS, NB, NT, XSM><<<grid, QMV_THREADS, smem, st>>>(a);
+    dz_qms_kernel<BITS, NB, NT, W, XIN><<<grid, W * 32, smem, st>>>(a);
 }
 
-// (NB, NT) per row count: NB row pairs per MMA group, NT n-tiles per warp.
-static void qms_shape(int M, int* NB, int* NT) {
+// Streaming-kernel shape per row count: NB row pairs per MMA group, NT n-tiles
+// per warp, W warps per CTA.
+static void qms_shape(int M, int* NB, int* NT, int* W) {
     *NB = M <= 2 ? 1 : M <= 4 ? 2 : M <= 8 ? 4 : 8;
     *NT = *NB == 1 ? 1 : *NB == 2 ? 2 : *NB == 4 ? 4 : 2;
+    *W = *NB <= 2 ? 16 : 8;
 }
 
-template <int BITS, bool XSM>
+template <int BITS, bool XIN>
 static void launch_qms_bits(const QmsArgs& a, int NB, unsigned grid, size_t smem, cudaStream_t st) {
     switch (NB) {
-        case 1: launch_qms_t<BITS, 1, 1, XSM>(a, grid, smem, st); break;
-        case 2: launch_qms_t<BITS, 2, 2, XSM>(a, grid, smem, st); break;
-        case 4: launch_qms_t<BITS, 4, 4, XSM>(a, grid, smem, st); break;
-        default: launch_qms_t<BITS, 8, 2, XSM>(a, grid, smem, st); break;
+        case 1: launch_qms_t<BITS, 1, 1, 16, XIN>(a, grid, smem, st); break;
+        case 2: launch_qms_t<BITS, 2, 2, 16, XIN>(a, grid, smem, st); break;
+        case 4: launch_qms_t<BITS, 4, 4, 8, XIN>(a, grid, smem, st); break;
+        default: launch_qms_t<BITS, 8, 2, 8, XIN>(a, grid, smem, st); break;
     }
 }
+
+// Warps per CTA of the stream-K matvec (M <= 2).
+constexpr int QMV1_WARPS = 16;
 
 // The streaming kernels take more than the default 48 KB of shared memory;
 // the attribute is set once per device, outside any stream capture.
@@ -287,13 +292,17 @@ static int qms_prepare(int device) {
     int optin = 0;
     DZ_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
     g_smem_optin = optin;
-#define DZ_QMS_ATTR(B, NB, NT, X) \
-    DZ_CUDA(cudaFuncSetAttribute(dz_qms_kernel<B, NB, NT, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
+#define DZ_QMS_ATTR(B, NB, NT, W, X) \
+    DZ_CUDA(cudaFuncSetAttribute(dz_qms_kernel<B, NB, NT, W, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
 #define DZ_QMS_ATTR2(B, X) \
-    DZ_QMS_ATTR(B, 1, 1, X); DZ_QMS_ATTR(B, 2, 2, X); DZ_QMS_ATTR(B, 4, 4, X); DZ_QMS_ATTR(B, 8, 2, X)
+    DZ_QMS_ATTR(B, 1, 1, 16, X); DZ_QMS_ATTR(B, 2, 2, 16, X); DZ_QMS_ATTR(B, 4, 4, 8, X); DZ_QMS_ATTR(B, 8, 2, 8, X)
     DZ_QMS_ATTR2(4, false); DZ_QMS_ATTR2(4, true); DZ_QMS_ATTR2(8, false); DZ_QMS_ATTR2(8, true);
 #undef DZ_QMS_ATTR2
 #undef DZ_QMS_ATTR
+#define DZ_QMV1_ATTR(B, X) \
+    DZ_CUDA(cudaFuncSetAttribute(dz_qmv1_kernel<B, QMV1_WARPS, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
+    DZ_QMV1_ATTR(4, false); DZ_QMV1_ATTR(4, true); DZ_QMV1_ATTR(8, false); DZ_QMV1_ATTR(8, true);
+#undef DZ_QMV1_ATTR
     g_qms_ready[device] = true;
     return DZ_OK;
 }
@@ -306,11 +315,11 @@ constexpr unsigned QMS_XF_SMEM_MAX = 96u << 10;
 // k-parts for the streaming kernel: the split of n-groups x k-groups over the
 // warps of g_num_sms persistent CTAs with the fewest k-groups on the busiest
 // warp (ties: fewer k-parts, fewer reductions).
-static int qms_kparts(int n_groups, int nkg, int* nrounds_out, unsigned* grid_out) {
+static int qms_kparts(int n_groups, int nkg, int W, int* nrounds_out, unsigned* grid_out) {
     long long best_cost = -1;
     int best = 1;
-    for (int kp = 1; kp <= QMV_WARPS; kp *= 2) {
-        const long long per_round = QMV_WARPS / kp;
+    for (int kp = 1; kp <= W; kp *= 2) {
+        const long long per_round = W / kp;
         const long long rounds = (n_groups + per_round - 1) / per_round;
         const long long grid = std::min<long long>(rounds, g_num_sms);
         const long long waves = (rounds + grid - 1) / grid;
@@ -321,17 +330,63 @@ static int qms_kparts(int n_groups, int nkg, int* nrounds_out, unsigned* grid_ou
             best = kp;
         }
     }
-    const long long per_round = QMV_WARPS / best;
+    const long long per_round = W / best;
     const long long rounds = (n_groups + per_round - 1) / per_round;
     *nrounds_out = (int)rounds;
     *grid_out = (unsigned)std::min<long long>(rounds, g_num_sms);
     return best;
 }
 
-// Y = epilogue(X . deq(W)) for M rows on the tensor cores: the activation
-// split into `scratch` (qmv_scratch_bytes), then the MMA kernel (streaming for
-// M <= QMS_MAX_M). A bulk-copy wait that gives up sets *status (when given)
-// and leaves NaN in the tile. Returns launches (2).
+// The stream-K matvec for M <= 2 (dz_qmv1_kernel). False when its shared
+// memory does not fit (very wide matrices); the caller then uses the
+// round-based streaming kernel.
+static bool qmv1_launch(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep,
+                        cudaStream_t st, const uint32_t* XF, const int* shift, unsigned xf_bytes, int* status,
+                        double qmv_bytes) {
+    constexpr int WP = QMV1_WARPS;
+    Qmv1Args a;
+    memset(&a, 0, sizeof(a));
+    a.codes = W.codes;
+    a.N = W.N;
+    a.nkg = W.nkg;
+    a.ntiles = W.ntiles;
+    a.X = X;
+    a.ldx = ldx;
+    a.k_scale = W.k_scale;
+    a.K = W.K;
+    a.XF = XF;
+    a.row_shift = shift;
+    a.M = M;
+    a.xf_bytes = xf_bytes;
+    a.status = status;
+    a.ep = ep;
+    a.ep.row_shift = nullptr;
+    const int G = std::min(g_num_sms, W.ntiles);
+    a.max_tiles = (W.ntiles + G - 1) / G;
+    // a tile meets at most (nkg - 2) / shortest range + 2 non-empty warp ranges
+    const long long per_min = (long long)(W.ntiles / G) * W.nkg / WP;
+    a.max_parts = per_min >= 1 ? (int)std::min<long long>(WP, std::max<long long>(1, (W.nkg - 2) / per_min + 2)) : WP;
+    const size_t fixed = dz_qmv1_smem_bytes(0, WP, xf_bytes, a.max_tiles, a.max_parts);
+    if (fixed + (size_t)WP * QMS_STAGES * 512 > (size_t)g_smem_optin) return false;
+    a.pk = (int)std::min<size_t>(16, ((size_t)g_smem_optin - fixed) / ((size_t)WP * QMS_STAGES * 512));
+    const size_t smem = dz_qmv1_smem_bytes(a.pk, WP, xf_bytes, a.max_tiles, a.max_parts);
+    ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
+    if (W.bits == 8) {
+        if (xf_bytes) dz_qmv1_kernel<8, WP, true><<<G, WP * 32, smem, st>>>(a);
+        else dz_qmv1_kernel<8, WP, false><<<G, WP * 32, smem, st>>>(a);
+    } else {
+        if (xf_bytes) dz_qmv1_kernel<4, WP, true><<<G, WP * 32, smem, st>>>(a);
+        else dz_qmv1_kernel<4, WP, false><<<G, WP * 32, smem, st>>>(a);
+    }
+    return true;
+}
+
+// Y = epilogue(X . deq(W)) for M rows on the tensor cores. Up to
+// QMS_MAX_M rows whose B fragments fit QMS_XF_SMEM_MAX: one streaming kernel
+// that splits the activations itself. Otherwise the activation split into
+// `scratch` (qmv_scratch_bytes), then the streaming (M <= QMS_MAX_M) or the
+// register-blocked MMA kernel. A bulk-copy wait that gives up sets *status
+// (when given) and leaves NaN in the tile. Returns the launches (1 or 2).
 static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
                       cudaStream_t st, void* scratch, int* status) {
     const int KG = W.bits == 8 ? 32 : 64;
@@ -340,48 +395,65 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     const int nbt = (M + 1) / 2;
     uint32_t* XF = static_cast<uint32_t*>(scratch);
     int* shift = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + r256(qmv_xf_bytes(W, M)));
-    {
+    const size_t xf = qmv_xf_bytes(W, M);
+    bool xin = M <= QMS_MAX_M && xf <= QMS_XF_SMEM_MAX;
+    if (xin) {   // the in-kernel split holds QMS_XIN_PAIRS element pairs per thread
+        int NB, NT, WP;
+        qms_shape(M, &NB, &NT, &WP);
+        xin = (long long)Kp / 2 <= (long long)QMS_XIN_PAIRS * WP * 32;
+    }
+    int launches = 1;
+    if (!xin) {
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 16.0 * nbt * Kp, 0, st);
-        dz_split_rows_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, KT, W.nkg, nbt, XF, shift);
+        const dim3 grid((unsigned)((Kp / 2 + DZ_SPLIT_PAIRS - 1) / DZ_SPLIT_PAIRS), (unsigned)M);
+        if (KT == 2) dz_split_rows_kernel<2><<<grid, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, W.nkg, nbt, XF, shift);
+        else dz_split_rows_kernel<4><<<grid, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, W.nkg, nbt, XF, shift);
+        launches++;
     }
     QmvEpilogue ep = ep_in;
     ep.row_shift = shift;
-    const double qmv_bytes =
-        (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 16.0 * nbt * Kp + 4.0 * M * W.N;
+    const double qmv_bytes = (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N;
+    if (M <= 2 && qmv1_launch(W, X, ldx, M, ep_in, st, XF, shift, xin ? (unsigned)xf : 0u, status, qmv_bytes))
+        return launches;
     if (M <= QMS_MAX_M) {
-        int NB, NT;
-        qms_shape(M, &NB, &NT);
+        int NB, NT, WP;
+        qms_shape(M, &NB, &NT, &WP);
         QmsArgs a;
+        memset(&a, 0, sizeof(a));
         a.codes = W.codes;
         a.N = W.N;
         a.nkg = W.nkg;
         a.ntiles = W.ntiles;
+        a.X = X;
+        a.ldx = ldx;
+        a.k_scale = W.k_scale;
+        a.K = W.K;
         a.XF = XF;
+        a.row_shift = shift;
         a.nbt = nbt;
         a.M = M;
         a.status = status;
-        a.ep = ep;
+        a.ep = ep_in;
+        a.ep.row_shift = nullptr;
         a.n_groups = (W.ntiles + NT - 1) / NT;
         unsigned grid = 1;
-        a.kparts = qms_kparts(a.n_groups, W.nkg, &a.nrounds, &grid);
+        a.kparts = qms_kparts(a.n_groups, W.nkg, WP, &a.nrounds, &grid);
         a.per = (W.nkg + a.kparts - 1) / a.kparts;
-        const size_t xf = qmv_xf_bytes(W, M);
-        const bool xsm = xf <= QMS_XF_SMEM_MAX;
-        a.xf_bytes = xsm ? (unsigned)xf : 0u;
-        const size_t fixed = dz_qms_smem_bytes(0, NT, NB, a.xf_bytes);
-        const int pk_budget = (int)(((size_t)g_smem_optin - fixed) / ((size_t)QMV_WARPS * QMS_STAGES * NT * 512));
+        a.xf_bytes = xin ? (unsigned)xf : 0u;
+        const size_t fixed = dz_qms_smem_bytes(0, NT, NB, WP, a.xf_bytes);
+        const int pk_budget = (int)(((size_t)g_smem_optin - fixed) / ((size_t)WP * QMS_STAGES * NT * 512));
         a.pk = std::max(1, std::min(16 / NT, pk_budget));
         a.pk = std::min(a.pk, std::max(1, a.per));
-        const size_t smem = dz_qms_smem_bytes(a.pk, NT, NB, a.xf_bytes);
+        const size_t smem = dz_qms_smem_bytes(a.pk, NT, NB, WP, a.xf_bytes);
         ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
         if (W.bits == 8) {
-            if (xsm) launch_qms_bits<8, true>(a, NB, grid, smem, st);
+            if (xin) launch_qms_bits<8, true>(a, NB, grid, smem, st);
             else launch_qms_bits<8, false>(a, NB, grid, smem, st);
         } else {
-            if (xsm) launch_qms_bits<4, true>(a, NB, grid, smem, st);
+            if (xin) launch_qms_bits<4, true>(a, NB, grid, smem, st);
             else launch_qms_bits<4, false>(a, NB, grid, smem, st);
         }
-        return 2;
+        return launches;
     }
     QmmArgs a;
     a.codes = W.codes;
@@ -408,7 +480,7 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
     if (W.bits == 8) launch_qmm_bits<8>(a, NB, grid, st);
     else launch_qmm_bits<4>(a, NB, grid, st);
-    return 2;
+    return launches;
 }
 
 static QmvEpilogue plain_epilogue(const DevQMat& W, float* Y, long long ldy) {

@@ -180,6 +180,13 @@ __device__ __forceinline__ int dz_row_shift(float amax) {
     return 14 - ilogbf(amax);
 }
 
+// v * 2^e, exact unless the result is subnormal (e in [-300, 300]).
+__device__ __forceinline__ float dz_mul_pow2(float v, int e) {
+    if (e >= -126 && e <= 127) return v * __int_as_float((e + 127) << 23);
+    const int h = e / 2;
+    return (v * __int_as_float((h + 127) << 23)) * __int_as_float((e - h + 127) << 23);
+}
+
 // fp16 hi / mid / lo of v (already scaled); hi + mid + lo == v exactly for
 // |v| >= 2^-1 (and to 2^-25 absolute below).
 struct DzSplit3 {
@@ -206,18 +213,14 @@ __device__ __forceinline__ uint32_t dz_pack_h2(__half lo, __half hi) {
 // and per k-tile kt the words are (k0+2t, k0+2t+1) and (k0+8+2t, k0+9+2t):
 //   XF[((kg * nbt + u) * 32 + l) * 2KT + 2kt + j]
 // so one chunk's B fragments are one (INT8) or two (INT4) 16-byte loads.
-// One block per row: the row maximum sets the row's exponent shift (stored
-// negated in row_shift, to undo after the k-sum), then every pair of elements
-// is split. ROW-granularity scales (k_scale) are folded in first.
-__global__ void __launch_bounds__(256) dz_split_rows_kernel(const float* __restrict__ X, long long ldx,
-                                                            const float* __restrict__ k_scale, int M, int K, int KT,
-                                                            int nkg, int nbt, uint32_t* __restrict__ XF,
-                                                            int* __restrict__ row_shift) {
-    const int r = blockIdx.x;
-    const float* x = X + (long long)r * ldx;
-    __shared__ float wmax[8];
-    __shared__ int sh_s;
+// ROW-granularity scales (k_scale) are folded in first.
+
+// Largest |x k_scale| of a row, block-wide (every thread gets it); `wred`
+// holds one float per warp.
+__device__ __forceinline__ float dz_row_amax(const float* __restrict__ x, const float* __restrict__ k_scale, int K,
+                                             float* wred) {
     float m = 0.0f;
+#pragma unroll 8
     for (int k = threadIdx.x; k < K; k += blockDim.x) {
         float v = x[k];
         if (k_scale) v *= k_scale[k];
@@ -225,46 +228,105 @@ __global__ void __launch_bounds__(256) dz_split_rows_kernel(const float* __restr
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+    __syncthreads();   // wred may still be read by a previous call
+    if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        float a = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) a = fmaxf(a, wmax[w]);
-        sh_s = dz_row_shift(a);
-        row_shift[r] = -sh_s;
-    }
-    __syncthreads();
-    const int sh = sh_s;
-    const int u = r >> 1, rh = r & 1;
-    const bool pad_next = (r == M - 1) && (M & 1);   // this block also zeroes the phantom row
-    const long long pairs = (long long)nkg * KT * 8;
-    for (long long q = threadIdx.x; q < pairs; q += blockDim.x) {
-        const long long k = 2 * q;
-        const int kg = (int)(k / (16 * KT));
-        const int kt = (int)((k / 16) % KT);
-        const int kk = (int)(k & 15);
-        const int j = kk >> 3, t = (kk & 7) >> 1;
-        float v0 = 0.0f, v1 = 0.0f;
-        if (k < K) {
-            v0 = x[k];
-            if (k_scale) v0 *= k_scale[k];
-        }
-        if (k + 1 < K) {
-            v1 = x[k + 1];
-            if (k_scale) v1 *= k_scale[k + 1];
-        }
-        const DzSplit3 s0 = dz_split3(ldexpf(v0, sh)), s1 = dz_split3(ldexpf(v1, sh));
-        const long long base = (((long long)kg * nbt + u) * 32) * 2 * KT + 2 * kt + j;
-        const int g0 = rh * 4;
-        XF[base + (long long)((g0 + 0) * 4 + t) * 2 * KT] = dz_pack_h2(s0.h, s1.h);
-        XF[base + (long long)((g0 + 1) * 4 + t) * 2 * KT] = dz_pack_h2(s0.m, s1.m);
-        XF[base + (long long)((g0 + 2) * 4 + t) * 2 * KT] = dz_pack_h2(s0.l, s1.l);
-        XF[base + (long long)((g0 + 3) * 4 + t) * 2 * KT] = 0u;
-        if (pad_next) {
+    float a = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) a = fmaxf(a, wred[w]);
+    return a;
+}
+
+// Store the XF words of element pair q (k = 2q, 2q+1, values v0, v1 already
+// scaled by k_scale) of row r with exponent shift sh.
+template <int KT>
+__device__ __forceinline__ void dz_split_store_pair(uint32_t* __restrict__ XF, int nbt, int M, int r, int q, float v0,
+                                                    float v1, int sh) {
+    const int k = 2 * q;
+    const int kg = k / (16 * KT);   // KT is 2 or 4: shifts
+    const int kt = (k >> 4) & (KT - 1);
+    const int kk = k & 15;
+    const int j = kk >> 3, t = (kk & 7) >> 1;
+    const DzSplit3 s0 = dz_split3(dz_mul_pow2(v0, sh)), s1 = dz_split3(dz_mul_pow2(v1, sh));
+    uint32_t* base = XF + ((size_t)kg * nbt + (r >> 1)) * 32 * 2 * KT + 2 * kt + j;
+    const int g0 = (r & 1) * 4;
+    base[((g0 + 0) * 4 + t) * 2 * KT] = dz_pack_h2(s0.h, s1.h);
+    base[((g0 + 1) * 4 + t) * 2 * KT] = dz_pack_h2(s0.m, s1.m);
+    base[((g0 + 2) * 4 + t) * 2 * KT] = dz_pack_h2(s0.l, s1.l);
+    base[((g0 + 3) * 4 + t) * 2 * KT] = 0u;
+    if (r == M - 1 && (M & 1)) {   // the phantom row after an odd last row reads zero
 #pragma unroll
-            for (int sp = 0; sp < 4; sp++) XF[base + (long long)((4 + sp) * 4 + t) * 2 * KT] = 0u;
+        for (int sp = 0; sp < 4; sp++) base[((4 + sp) * 4 + t) * 2 * KT] = 0u;
+    }
+}
+
+// Element k of row x with its ROW-granularity scale, zero past K.
+__device__ __forceinline__ float dz_x_at(const float* __restrict__ x, const float* __restrict__ k_scale, int K,
+                                         int k) {
+    if (k >= K) return 0.0f;
+    float v = x[k];
+    if (k_scale) v *= k_scale[k];
+    return v;
+}
+
+// Block-wide split of the M rows into XF (shared or global memory) with every
+// element pair held in registers: thread j takes pairs j + i * blockDim.x,
+// i < PMAX, so the row is read once with all loads in flight. Needs
+// pairs <= PMAX * blockDim.x. Thread 0 stores the negated shifts.
+template <int PMAX, int KT>
+__device__ __forceinline__ void dz_split_rows_block(const float* __restrict__ X, long long ldx,
+                                                    const float* __restrict__ k_scale, int M, int K, int pairs,
+                                                    int nbt, uint32_t* __restrict__ XF, int* __restrict__ shifts,
+                                                    float* wred) {
+    for (int r = 0; r < M; r++) {
+        const float* x = X + (long long)r * ldx;
+        float v[PMAX][2];
+        float m = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PMAX; i++) {
+            const int q = threadIdx.x + i * blockDim.x;
+            v[i][0] = dz_x_at(x, k_scale, K, 2 * q);
+            v[i][1] = dz_x_at(x, k_scale, K, 2 * q + 1);
+            m = fmaxf(m, fmaxf(fabsf(v[i][0]), fabsf(v[i][1])));
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        __syncthreads();   // wred may still be read for the previous row
+        if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = m;
+        __syncthreads();
+        float amax = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) amax = fmaxf(amax, wred[w]);
+        const int sh = dz_row_shift(amax);
+        if (threadIdx.x == 0) shifts[r] = -sh;
+#pragma unroll
+        for (int i = 0; i < PMAX; i++) {
+            const int q = threadIdx.x + i * blockDim.x;
+            if (q < pairs) dz_split_store_pair<KT>(XF, nbt, M, r, q, v[i][0], v[i][1], sh);
         }
     }
+}
+
+constexpr int DZ_SPLIT_PAIRS = 512;   // element pairs per block of dz_split_rows_kernel
+
+// Grid (ceil(Kp / 2 / DZ_SPLIT_PAIRS), M): each block finds its row's maximum
+// (the row's exponent shift, stored negated in row_shift) and splits its
+// DZ_SPLIT_PAIRS pairs.
+template <int KT>
+__global__ void __launch_bounds__(256) dz_split_rows_kernel(const float* __restrict__ X, long long ldx,
+                                                            const float* __restrict__ k_scale, int M, int K, int nkg,
+                                                            int nbt, uint32_t* __restrict__ XF,
+                                                            int* __restrict__ row_shift) {
+    __shared__ float wred[8];
+    const int r = blockIdx.y;
+    const float* x = X + (long long)r * ldx;
+    const int sh = dz_row_shift(dz_row_amax(x, k_scale, K, wred));
+    if (blockIdx.x == 0 && threadIdx.x == 0) row_shift[r] = -sh;
+    const int pairs = nkg * KT * 8;
+    const int q0 = blockIdx.x * DZ_SPLIT_PAIRS;
+    const int q1 = q0 + DZ_SPLIT_PAIRS < pairs ? q0 + DZ_SPLIT_PAIRS : pairs;
+#pragma unroll 2
+    for (int q = q0 + threadIdx.x; q < q1; q += blockDim.x)
+        dz_split_store_pair<KT>(XF, nbt, M, r, q, dz_x_at(x, k_scale, K, 2 * q), dz_x_at(x, k_scale, K, 2 * q + 1),
+                                sh);
 }
 
 struct QmmArgs {
@@ -452,22 +514,30 @@ __device__ __forceinline__ void dz_bulk_g2s(void* dst, const void* src, uint32_t
         : "memory");
 }
 
-constexpr int QMS_STAGES = 3;   // ring stages per warp
+constexpr int QMS_STAGES = 3;      // ring stages per warp
+constexpr int QMS_XIN_PAIRS = 8;   // element pairs per thread of the in-kernel split
 
 struct QmsArgs {
     const uint8_t* codes;     // fragment layout
     int N, nkg, ntiles;
-    const uint32_t* XF;       // split activations in B-fragment order (dz_split_rows_kernel)
-    int nbt;                  // row pairs in XF
+    // activations: XIN kernels split X themselves into shared memory; the
+    // others read XF / row_shift (dz_split_rows_kernel)
+    const float* X;
+    long long ldx;
+    const float* k_scale;
+    int K;
+    const uint32_t* XF;
+    const int* row_shift;
+    int nbt;                  // row pairs
     int M;
-    int kparts;               // warps sharing one n-group's k-groups (1, 2, 4 or 8)
+    int kparts;               // warps sharing one n-group's k-groups
     int per;                  // k-groups per k-part
     int n_groups;             // groups of NT n-tiles
-    int nrounds;              // rounds of QMV_WARPS / kparts n-groups
+    int nrounds;              // rounds of W / kparts n-groups
     int pk;                   // k-groups per piece (a stage holds NT * pk chunks)
-    unsigned xf_bytes;        // XF bytes copied to shared memory (XSM kernels)
+    unsigned xf_bytes;        // XF bytes in shared memory (XIN kernels)
     int* status;              // set to 1 when a copy wait gave up (may be null)
-    QmvEpilogue ep;
+    QmvEpilogue ep;           // row_shift is applied by the kernel, ep.row_shift unused
 };
 
 // One piece of a warp's stream: n-group ng (n-tiles NT*ng ..), k-groups
@@ -477,14 +547,15 @@ struct QmsPiece {
     bool first, last;
 };
 
-// Piece idx of warp `warp`: round r = blockIdx.x + (idx / ppr) * gridDim.x owns
-// n-groups r * (QMV_WARPS / kparts) + [0, QMV_WARPS / kparts); the warp takes
-// n-group warp / kparts, k-part warp % kparts, in pieces of pk k-groups.
+// Piece idx of warp `warp` of W: round r = blockIdx.x + (idx / ppr) * gridDim.x
+// owns n-groups r * (W / kparts) + [0, W / kparts); the warp takes n-group
+// warp / kparts, k-part warp % kparts, in pieces of pk k-groups.
+template <int W>
 __device__ __forceinline__ QmsPiece dz_qms_piece(const QmsArgs& a, int warp, int ppr, int idx) {
     QmsPiece p;
     const int j = idx / ppr, q = idx - j * ppr;
     const long long r = blockIdx.x + (long long)j * gridDim.x;
-    p.ng = (int)(r * (QMV_WARPS / a.kparts) + warp / a.kparts);
+    p.ng = (int)(r * (W / a.kparts) + warp / a.kparts);
     const int kstart = (warp % a.kparts) * a.per;
     const int kend = min(kstart + a.per, a.nkg);
     p.kg0 = kstart + q * a.pk;
@@ -495,27 +566,32 @@ __device__ __forceinline__ QmsPiece dz_qms_piece(const QmsArgs& a, int warp, int
 }
 
 // Shared memory of dz_qms_kernel: the rings, the XF copy, the k-part
-// reduction area and the barriers.
-__host__ __device__ constexpr size_t dz_qms_ring_bytes(int pk, int NT) {
-    return (size_t)QMV_WARPS * QMS_STAGES * NT * pk * 512;
+// reduction area, the barriers, row shifts and a per-warp scratch float.
+__host__ __device__ constexpr size_t dz_qms_ring_bytes(int pk, int NT, int W) {
+    return (size_t)W * QMS_STAGES * NT * pk * 512;
 }
-__host__ __device__ constexpr size_t dz_qms_smem_bytes(int pk, int NT, int NB, unsigned xf_bytes) {
-    return dz_qms_ring_bytes(pk, NT) + xf_bytes + (size_t)QMV_WARPS * NT * NB * 2 * 32 * 4 +
-           ((size_t)QMV_WARPS * QMS_STAGES + 1) * 8;
+__host__ __device__ constexpr size_t dz_qms_smem_bytes(int pk, int NT, int NB, int W, unsigned xf_bytes) {
+    return dz_qms_ring_bytes(pk, NT, W) + xf_bytes + (size_t)W * NT * NB * 2 * 32 * 4 +
+           (size_t)W * QMS_STAGES * 8 + 16 * 4 + 32 * 4;
+}
+
+__device__ __forceinline__ void dz_named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 // Y = epilogue(X . deq(W)) for M <= 2 * NB rows, streaming the weights. One
-// persistent CTA per SM; each warp streams its pieces (NT n-tiles x pk
-// k-groups) through its own QMS_STAGES-deep shared-memory ring with bulk
-// copies, lane 0 keeping two pieces in flight. With XSM the activations'
-// B fragments are copied to shared memory once per CTA; otherwise they are
-// read through L1. Each chunk is dequantized from shared memory into fp16
-// A fragments (dz_deq4 / dz_deq8) feeding NB MMAs per n-tile; CH independent
-// accumulator chains per (n-tile, row pair) keep the tensor pipe busy when
-// NT * NB is small. The k-parts of an n-group are summed in shared memory in
-// k-part order, so results do not depend on the grid.
-template <int BITS, int NB, int NT, bool XSM>
-__global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
+// persistent CTA of W warps per SM; each warp streams its pieces (NT n-tiles
+// x pk k-groups) through its own QMS_STAGES-deep shared-memory ring with bulk
+// copies, lane 0 keeping two pieces in flight. XIN kernels split the
+// activations into B-fragment order in shared memory themselves (while the
+// first weight pieces are in flight); the others read XF through L1. Each
+// chunk is dequantized from shared memory into fp16 A fragments (dz_deq4 /
+// dz_deq8) feeding NB MMAs per n-tile; CH independent accumulator chains per
+// (n-tile, row pair) keep the tensor pipe fed when NT * NB is small. The
+// k-parts of an n-group are summed in shared memory in k-part order (named
+// barrier per group), so results do not depend on the grid.
+template <int BITS, int NB, int NT, int W, bool XIN>
+__global__ void __launch_bounds__(W * 32, 1) dz_qms_kernel(QmsArgs a) {
     constexpr int KT = FragGeom<BITS>::KT;
     constexpr int XV = KT / 2;
     constexpr int CH = NT * NB >= 4 ? 1 : (4 / (NT * NB) < KT ? 4 / (NT * NB) : KT);
@@ -525,11 +601,11 @@ __global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
     const int g = lane >> 2, t = lane & 3;
     const int stage_bytes = NT * a.pk * 512;
     uint8_t* ring = qms_smem + (size_t)warp * QMS_STAGES * stage_bytes;
-    uint8_t* xf_sm = qms_smem + dz_qms_ring_bytes(a.pk, NT);
+    uint8_t* xf_sm = qms_smem + dz_qms_ring_bytes(a.pk, NT, W);
     float* red = reinterpret_cast<float*>(xf_sm + a.xf_bytes);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(red + QMV_WARPS * NV * 32);
-    uint64_t* xbar = bars + QMV_WARPS * QMS_STAGES;
-    bars += warp * QMS_STAGES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(red + W * NV * 32) + warp * QMS_STAGES;
+    int* rsh = reinterpret_cast<int*>(reinterpret_cast<uint64_t*>(red + W * NV * 32) + W * QMS_STAGES);
+    float* wred = reinterpret_cast<float*>(rsh + 16);
 
     const int ppr = (a.per + a.pk - 1) / a.pk;
     const int rounds_here =
@@ -538,25 +614,13 @@ __global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
 
     if (lane == 0) {
         for (int st = 0; st < QMS_STAGES; st++) dz_mbar_init(&bars[st]);
-        if (XSM && warp == 0) dz_mbar_init(xbar);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (XSM) {
-        __syncthreads();   // xbar initialised before anyone waits on it
-        if (threadIdx.x == 0) {
-            dz_mbar_expect_tx(xbar, a.xf_bytes);
-            for (unsigned off = 0; off < a.xf_bytes; off += 32768u) {
-                const unsigned n = a.xf_bytes - off < 32768u ? a.xf_bytes - off : 32768u;
-                dz_bulk_g2s(xf_sm + off, reinterpret_cast<const uint8_t*>(a.XF) + off, n, xbar);
-            }
-        }
-    } else {
-        __syncwarp();
-    }
+    __syncwarp();
 
     // lane 0: put piece idx in flight into stage idx % QMS_STAGES
     auto issue = [&](int idx) {
-        const QmsPiece pc = dz_qms_piece(a, warp, ppr, idx);
+        const QmsPiece pc = dz_qms_piece<W>(a, warp, ppr, idx);
         uint64_t* bar = &bars[idx % QMS_STAGES];
         int tiles = 0;
         for (int i = 0; i < NT; i++) tiles += pc.ng * NT + i < a.ntiles ? 1 : 0;
@@ -575,23 +639,23 @@ __global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
     if (lane == 0)
         for (int i = 0; i < issued; i++) issue(i);
 
+    const int* shifts = a.row_shift;
+    if (XIN) {
+        // split the activations into shared memory while the weights stream in
+        // (pairs <= QMS_XIN_PAIRS * W * 32, checked by the host)
+        dz_split_rows_block<QMS_XIN_PAIRS, KT>(a.X, a.ldx, a.k_scale, a.M, a.K, a.nkg * KT * 8, a.nbt,
+                                               reinterpret_cast<uint32_t*>(xf_sm), rsh, wred);
+        __syncthreads();
+        shifts = rsh;
+    }
+    const uint4* xl = (XIN ? reinterpret_cast<const uint4*>(xf_sm) : reinterpret_cast<const uint4*>(a.XF)) + lane * XV;
+    const long long xkg = (long long)a.nbt * 32 * XV;   // uint4 per k-group
+
     bool failed = false;
     int failed_at = -1;   // first piece whose wait gave up
-    if (XSM) {
-        int ok = 1;
-        if (lane == 0) ok = dz_mbar_wait(xbar, 0) ? 1 : 0;
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        if (!ok) {
-            failed = true;
-            failed_at = 0;
-            if (lane == 0 && a.status) atomicExch(a.status, 1);
-        }
-    }
-    const uint4* xf4 = XSM ? reinterpret_cast<const uint4*>(xf_sm) : reinterpret_cast<const uint4*>(a.XF);
-
     float acc[CH][NT][NB][4];
     for (int idx = 0; idx < npieces; idx++) {
-        const QmsPiece pc = dz_qms_piece(a, warp, ppr, idx);
+        const QmsPiece pc = dz_qms_piece<W>(a, warp, ppr, idx);
         if (pc.first) {
 #pragma unroll
             for (int c = 0; c < CH; c++)
@@ -619,20 +683,20 @@ __global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
             }
         }
         if (!failed) {
-            const uint4* w4 = reinterpret_cast<const uint4*>(ring + stage * stage_bytes);
-            for (int c = 0; c < pc.nkg; c++) {
-                const int kg = pc.kg0 + c;
+            const uint4* w4 = reinterpret_cast<const uint4*>(ring + stage * stage_bytes) + lane;
+            const uint4* xk = xl + pc.kg0 * xkg;
+#pragma unroll 2
+            for (int c = 0; c < pc.nkg; c++, xk += xkg) {
                 uint4 xv[NB][XV];
 #pragma unroll
                 for (int u = 0; u < NB; u++)
 #pragma unroll
-                    for (int h = 0; h < XV; h++) {
-                        const long long at = (((long long)kg * a.nbt + u) * 32 + lane) * XV + h;
-                        xv[u][h] = u < a.nbt ? (XSM ? xf4[at] : __ldg(xf4 + at)) : make_uint4(0u, 0u, 0u, 0u);
-                    }
+                    for (int h = 0; h < XV; h++)
+                        xv[u][h] = u < a.nbt ? (XIN ? xk[u * 32 * XV + h] : __ldg(xk + u * 32 * XV + h))
+                                             : make_uint4(0u, 0u, 0u, 0u);
                 uint4 w[NT];
 #pragma unroll
-                for (int i = 0; i < NT; i++) w[i] = w4[(i * a.pk + c) * 32 + lane];
+                for (int i = 0; i < NT; i++) w[i] = w4[(i * a.pk + c) * 32];
 #pragma unroll
                 for (int kt = 0; kt < KT; kt++) {
 #pragma unroll
@@ -672,9 +736,10 @@ __global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
         }
         bool owner = true;
         if (a.kparts > 1) {
+            const int grp = warp / a.kparts;
 #pragma unroll
             for (int q = 0; q < NV; q++) red[(warp * NV + q) * 32 + lane] = v[q];
-            __syncthreads();
+            dz_named_sync(1 + grp, 32 * a.kparts);
             owner = warp % a.kparts == 0;
             if (owner) {
 #pragma unroll
@@ -684,25 +749,275 @@ __global__ void __launch_bounds__(QMV_THREADS, 1) dz_qms_kernel(QmsArgs a) {
                     v[q] = sum;
                 }
             }
-            __syncthreads();
+            dz_named_sync(1 + grp, 32 * a.kparts);
         }
         if (owner && pc.ng < a.n_groups && !(t & 1)) {
 #pragma unroll
-            for (int i = 0; i < NT; i++)
+            for (int u = 0; u < NB; u++) {
+                const int row = 2 * u + (t >> 1);
+                if (row >= a.M) continue;
+                const int e = shifts[row];
 #pragma unroll
-                for (int u = 0; u < NB; u++) {
-                    const int row = 2 * u + (t >> 1);
+                for (int i = 0; i < NT; i++) {
                     const int n = (pc.ng * NT + i) * 16 + g;
                     if (n < a.ntiles * 16) {
-                        dz_qmv_store_row(a.ep, a.M, a.N, row, n, v[(i * NB + u) * 2]);
-                        dz_qmv_store_row(a.ep, a.M, a.N, row, n + 8, v[(i * NB + u) * 2 + 1]);
+                        dz_qmv_store_row(a.ep, a.M, a.N, row, n, dz_mul_pow2(v[(i * NB + u) * 2], e));
+                        dz_qmv_store_row(a.ep, a.M, a.N, row, n + 8, dz_mul_pow2(v[(i * NB + u) * 2 + 1], e));
                     }
                 }
+            }
         }
     }
     if (failed_at >= 0 && lane == 0) {
         // copies still in flight land before the shared memory is released
-        if (XSM && warp == 0) dz_mbar_wait(xbar, 0);
+        for (int i = failed_at; i < issued; i++)
+            if (!dz_mbar_wait(&bars[i % QMS_STAGES], (uint32_t)((i / QMS_STAGES) & 1))) break;
+    }
+}
+
+// ------------------------------------------- stream-K matvec for M <= 2
+
+struct Qmv1Args {
+    const uint8_t* codes;     // fragment layout
+    int N, nkg, ntiles;
+    const float* X;           // XIN: rows split in the kernel
+    long long ldx;
+    const float* k_scale;
+    int K;
+    const uint32_t* XF;       // otherwise: dz_split_rows_kernel output
+    const int* row_shift;
+    int M;                    // 1 or 2
+    int pk;                   // chunks per piece
+    int max_tiles;            // n-tiles per CTA at most
+    int max_parts;            // warps sharing one n-tile at most
+    unsigned xf_bytes;        // XIN: XF bytes in shared memory
+    int* status;              // set to 1 when a copy wait gave up (may be null)
+    QmvEpilogue ep;           // row shifts are applied by the kernel
+};
+
+__host__ __device__ constexpr size_t dz_qmv1_smem_bytes(int pk, int W, unsigned xf_bytes, int max_tiles,
+                                                        int max_parts) {
+    return (size_t)W * QMS_STAGES * pk * 512 + xf_bytes + (size_t)max_tiles * max_parts * 32 * 4 +
+           (size_t)((max_tiles + 3) & ~3) * 4 + (size_t)W * QMS_STAGES * 8 + 16 * 4 + 32 * 4;
+}
+
+// Y = epilogue(X . deq(W)) for M <= 2 rows. The weights are one array of
+// 512-byte chunks, n-tile major. CTA c takes the whole n-tiles
+// [c * ntiles / G, (c+1) * ntiles / G); its W warps split that run's chunks
+// into W equal contiguous ranges (stream-K), so every warp streams the same
+// number of bytes whatever the tile count. A warp streams its range through
+// its own QMS_STAGES-deep shared-memory ring with bulk copies (pieces never
+// cross an n-tile end), accumulating on the tensor cores as dz_qms_kernel
+// does. An n-tile covered by one warp is stored directly; one shared by
+// several warps is combined in shared memory: each warp deposits its part and
+// the last to arrive (a shared-memory counter) adds the parts in warp order,
+// so results do not depend on timing.
+template <int BITS, int W, bool XIN>
+__global__ void __launch_bounds__(W * 32, 1) dz_qmv1_kernel(Qmv1Args a) {
+    constexpr int KT = FragGeom<BITS>::KT;
+    constexpr int XV = KT / 2;
+    constexpr int CH = KT;   // one accumulator chain per k-tile
+    extern __shared__ __align__(128) unsigned char qmv1_smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int stage_bytes = a.pk * 512;
+    uint8_t* ring = qmv1_smem + (size_t)warp * QMS_STAGES * stage_bytes;
+    uint8_t* xf_sm = qmv1_smem + (size_t)W * QMS_STAGES * stage_bytes;
+    float* slots = reinterpret_cast<float*>(xf_sm + a.xf_bytes);
+    int* cnt = reinterpret_cast<int*>(slots + (size_t)a.max_tiles * a.max_parts * 32);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(cnt + ((a.max_tiles + 3) & ~3)) + warp * QMS_STAGES;
+    int* rsh = reinterpret_cast<int*>(reinterpret_cast<uint64_t*>(cnt + ((a.max_tiles + 3) & ~3)) + W * QMS_STAGES);
+    float* wred = reinterpret_cast<float*>(rsh + 16);
+
+    // chunk indices fit 32 bits (2^31 chunks = 1 TB of codes)
+    const int G = gridDim.x;
+    const int t0 = (int)((long long)blockIdx.x * a.ntiles / G), t1 = (int)(((long long)blockIdx.x + 1) * a.ntiles / G);
+    const int C0 = t0 * a.nkg, L = (t1 - t0) * a.nkg;
+    auto wstart = [&](int w) { return C0 + (int)((long long)w * L / W); };
+    const int my0 = wstart(warp), my1 = wstart(warp + 1);
+    // a position in this warp's range: chunk pos = tile * nkg + kg
+    struct Cursor {
+        int pos, tile, kg;
+    };
+    auto cursor_at = [&](int p) {
+        Cursor c;
+        c.pos = p;
+        c.tile = p / a.nkg;
+        c.kg = p - c.tile * a.nkg;
+        return c;
+    };
+    // the piece at c: up to pk chunks, not past the n-tile or the range
+    auto piece_len = [&](const Cursor& c) { return min(a.pk, min(a.nkg - c.kg, my1 - c.pos)); };
+    auto advance = [&](Cursor& c, int n) {
+        c.pos += n;
+        c.kg += n;
+        if (c.kg == a.nkg) {
+            c.kg = 0;
+            c.tile++;
+        }
+    };
+
+    for (int i = threadIdx.x; i < a.max_tiles; i += blockDim.x) cnt[i] = 0;
+    if (lane == 0) {
+        for (int st = 0; st < QMS_STAGES; st++) dz_mbar_init(&bars[st]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+
+    // lane 0 keeps two pieces in flight: piece i -> stage i % QMS_STAGES
+    Cursor ic = cursor_at(my0);
+    int issued = 0, istage = 0;
+    auto issue = [&]() {
+        const int n = piece_len(ic);
+        uint64_t* bar = &bars[istage];
+        dz_mbar_expect_tx(bar, (uint32_t)n * 512u);
+        dz_bulk_g2s(ring + istage * stage_bytes, a.codes + (size_t)ic.pos * 512, (uint32_t)n * 512u, bar);
+        advance(ic, n);
+        issued++;
+        istage = istage == QMS_STAGES - 1 ? 0 : istage + 1;
+    };
+    if (lane == 0)
+        for (int i = 0; i < QMS_STAGES - 1 && ic.pos < my1; i++) issue();
+
+    const int* shifts = a.row_shift;
+    if (XIN) {
+        dz_split_rows_block<QMS_XIN_PAIRS, KT>(a.X, a.ldx, a.k_scale, a.M, a.K, a.nkg * KT * 8, 1,
+                                               reinterpret_cast<uint32_t*>(xf_sm), rsh, wred);
+        shifts = rsh;
+    }
+    __syncthreads();   // counters zeroed, XF written
+    const uint4* xl = (XIN ? reinterpret_cast<const uint4*>(xf_sm) : reinterpret_cast<const uint4*>(a.XF)) + lane * XV;
+
+    // warp owning chunk x of this CTA's run (ranges may be empty when L < W)
+    auto owner_of = [&](int x) {
+        int w = (int)(((long long)(x - C0) * W) / (L > 0 ? L : 1));
+        if (w > W - 1) w = W - 1;
+        while (w < W - 1 && wstart(w + 1) <= x) w++;
+        while (w > 0 && wstart(w) > x) w--;
+        return w;
+    };
+
+    bool failed = false;
+    int failed_at = -1;   // first piece whose wait gave up
+    Cursor cc = cursor_at(my0);
+    int consumed = 0, cstage = 0;
+    uint32_t cphase = 0;
+    float acc[CH][4];
+#pragma unroll
+    for (int c = 0; c < CH; c++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) acc[c][q] = 0.0f;
+    while (cc.pos < my1) {
+        const int n = piece_len(cc);
+        if (!failed && lane == 0 && ic.pos < my1) issue();
+        const int stage = cstage;
+        if (!failed) {
+            int ok = 1;
+            if (lane == 0) ok = dz_mbar_wait(&bars[stage], cphase) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) {
+                failed = true;
+                failed_at = consumed;
+                if (lane == 0 && a.status) atomicExch(a.status, 1);
+            }
+        }
+        const int tile = cc.tile;
+        const int kg0 = cc.kg;
+        if (!failed) {
+            const uint4* w4 = reinterpret_cast<const uint4*>(ring + stage * stage_bytes) + lane;
+            const uint4* xk = xl + (long long)kg0 * 32 * XV;
+#pragma unroll 2
+            for (int c = 0; c < n; c++, xk += 32 * XV) {
+                uint4 xv[XV];
+#pragma unroll
+                for (int h = 0; h < XV; h++) xv[h] = XIN ? xk[h] : __ldg(xk + h);
+                const uint4 w = w4[c * 32];
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                for (int kt = 0; kt < KT; kt++) {
+                    uint32_t af[4];
+                    if (BITS == 4) dz_deq4(ww[kt], af);
+                    else dz_deq8(ww[2 * kt], ww[2 * kt + 1], af);
+                    dz_mma_f16(acc[kt % CH], af, dz_xw(xv, 2 * kt), dz_xw(xv, 2 * kt + 1));
+                }
+            }
+        }
+        __syncwarp();   // the stage is free for lane 0 to refill
+        consumed++;
+        if (++cstage == QMS_STAGES) {
+            cstage = 0;
+            cphase ^= 1u;
+        }
+        advance(cc, n);
+        const int tile_start = tile * a.nkg, tile_end = tile_start + a.nkg;
+        if (cc.pos != tile_end && cc.pos != my1) continue;
+
+        // this warp's share of the n-tile is done
+        float d[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            d[q] = acc[0][q];
+#pragma unroll
+            for (int c = 1; c < CH; c++) d[q] += acc[c][q];
+        }
+        float v0, v1;
+        dz_combine<BITS>(d, v0, v1);
+        if (failed) v0 = v1 = __int_as_float(0x7fc00000);   // a failed tile reads NaN
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) acc[c][q] = 0.0f;
+        const int row = t >> 1;
+        const int n0 = tile * 16 + g;
+        const bool whole = my0 <= tile_start && my1 >= tile_end;
+        if (whole) {
+            if (!(t & 1) && row < a.M) {
+                const int e = shifts[row];
+                dz_qmv_store_row(a.ep, a.M, a.N, row, n0, dz_mul_pow2(v0, e));
+                dz_qmv_store_row(a.ep, a.M, a.N, row, n0 + 8, dz_mul_pow2(v1, e));
+            }
+            continue;
+        }
+        // shared n-tile: parts are the non-empty warp ranges meeting it, in warp order
+        const int wf = owner_of(tile_start > C0 ? tile_start : C0);
+        const int wl = owner_of((tile_end < C0 + L ? tile_end : C0 + L) - 1);
+        int part = 0, nparts = 0;
+        for (int w = wf; w <= wl; w++) {
+            if (wstart(w + 1) > wstart(w)) {
+                if (w < warp) part++;
+                nparts++;
+            }
+        }
+        const int lt = tile - t0;
+        float* mine = slots + ((size_t)lt * a.max_parts + part) * 32;
+        if (!(t & 1)) {
+            mine[row * 16 + g] = v0;
+            mine[row * 16 + g + 8] = v1;
+        }
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(&cnt[lt], 1) == nparts - 1 ? 1 : 0;
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+            __threadfence_block();
+            if (!(t & 1) && row < a.M) {
+                float s0 = 0.0f, s1 = 0.0f;
+                for (int pp = 0; pp < nparts; pp++) {
+                    const float* sl = slots + ((size_t)lt * a.max_parts + pp) * 32;
+                    s0 += sl[row * 16 + g];
+                    s1 += sl[row * 16 + g + 8];
+                }
+                const int e = shifts[row];
+                dz_qmv_store_row(a.ep, a.M, a.N, row, n0, dz_mul_pow2(s0, e));
+                dz_qmv_store_row(a.ep, a.M, a.N, row, n0 + 8, dz_mul_pow2(s1, e));
+            }
+        }
+    }
+    if (failed_at >= 0 && lane == 0) {
+        // copies still in flight land before the shared memory is released
         for (int i = failed_at; i < issued; i++)
             if (!dz_mbar_wait(&bars[i % QMS_STAGES], (uint32_t)((i / QMS_STAGES) & 1))) break;
     }

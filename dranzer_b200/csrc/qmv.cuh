@@ -29,7 +29,15 @@ struct QmvEpilogue {
 
 __device__ __forceinline__ void dz_qmv_store_row(const QmvEpilogue& e, int M, int N, int m, int n, float acc) {
     if (m >= M || n >= N) return;
-    if (e.row_shift) acc = ldexpf(acc, e.row_shift[m]);
+    if (e.row_shift) {   // acc * 2^row_shift[m], exact for normal results
+        const int x = e.row_shift[m];
+        if (x >= -126 && x <= 127) {
+            acc *= __int_as_float((x + 127) << 23);
+        } else {
+            const int h = x / 2;
+            acc = (acc * __int_as_float((h + 127) << 23)) * __int_as_float((x - h + 127) << 23);
+        }
+    }
     float y = e.col_scale ? acc * e.col_scale[n] : acc;
     if (e.bias) y = y + e.bias[n];
     if (e.residual) y = y + e.residual[(long long)m * e.ld_res + n];

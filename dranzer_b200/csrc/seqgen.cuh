@@ -251,8 +251,8 @@ __device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, con
         if (active && t == 0) {
             if (kp == 1) {
                 const int n0 = nt * 16 + g;
-                if (n0 < m.N) epi(n0, ldexpf(v0, sh_lo) * scale[n0]);
-                if (n0 + 8 < m.N) epi(n0 + 8, ldexpf(v1, sh_hi) * scale[n0 + 8]);
+                if (n0 < m.N) epi(n0, dz_mul_pow2(v0, sh_lo) * scale[n0]);
+                if (n0 + 8 < m.N) epi(n0 + 8, dz_mul_pow2(v1, sh_hi) * scale[n0 + 8]);
             } else {
                 red[(nt * kp + kpart) * 16 + g] = v0;
                 red[(nt * kp + kpart) * 16 + g + 8] = v1;
@@ -265,14 +265,14 @@ __device__ __forceinline__ void seq_qmv(const SeqMat& m, const uint8_t* wsm, con
             const int nt = n >> 4, c = n & 15;
             float sum = 0.0f;
             for (int q = 0; q < kp; q++) sum += red[(nt * kp + q) * 16 + c];
-            if (n < m.N) epi(n, ldexpf(sum, c < 8 ? sh_lo : sh_hi) * scale[n]);
+            if (n < m.N) epi(n, dz_mul_pow2(sum, c < 8 ? sh_lo : sh_hi) * scale[n]);
         }
     }
 }
 
 // fp16 hi / mid / lo split of v * 2^sh into element i of a split buffer.
 __device__ __forceinline__ void seq_split_store(__half* xs, int stride, int i, float v, int sh) {
-    const DzSplit3 p = dz_split3(ldexpf(v, sh));
+    const DzSplit3 p = dz_split3(dz_mul_pow2(v, sh));
     xs[i] = p.h;
     xs[stride + i] = p.m;
     xs[2 * stride + i] = p.l;
