@@ -268,40 +268,54 @@ __device__ __forceinline__ float dz_x_at(const float* __restrict__ x, const floa
     return v;
 }
 
-// Block-wide split of the M rows into XF (shared or global memory) with every
+// Block-wide split of a row into XF (shared or global memory) with every
 // element pair held in registers: thread j takes pairs j + i * blockDim.x,
 // i < PMAX, so the row is read once with all loads in flight. Needs
-// pairs <= PMAX * blockDim.x. Thread 0 stores the negated shifts.
+// pairs <= PMAX * blockDim.x. dz_split_row_load issues the loads;
+// dz_split_row_store finds the row maximum and writes the parts (thread 0
+// stores the negated shift).
+template <int PMAX>
+__device__ __forceinline__ void dz_split_row_load(const float* __restrict__ x, const float* __restrict__ k_scale,
+                                                  int K, float (&v)[PMAX][2]) {
+#pragma unroll
+    for (int i = 0; i < PMAX; i++) {
+        const int q = threadIdx.x + i * blockDim.x;
+        v[i][0] = dz_x_at(x, k_scale, K, 2 * q);
+        v[i][1] = dz_x_at(x, k_scale, K, 2 * q + 1);
+    }
+}
+
+template <int PMAX, int KT>
+__device__ __forceinline__ void dz_split_row_store(const float (&v)[PMAX][2], int r, int M, int pairs, int nbt,
+                                                   uint32_t* __restrict__ XF, int* __restrict__ shifts, float* wred) {
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PMAX; i++) m = fmaxf(m, fmaxf(fabsf(v[i][0]), fabsf(v[i][1])));
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    __syncthreads();   // wred may still be read for the previous row
+    if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = m;
+    __syncthreads();
+    float amax = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) amax = fmaxf(amax, wred[w]);
+    const int sh = dz_row_shift(amax);
+    if (threadIdx.x == 0) shifts[r] = -sh;
+#pragma unroll
+    for (int i = 0; i < PMAX; i++) {
+        const int q = threadIdx.x + i * blockDim.x;
+        if (q < pairs) dz_split_store_pair<KT>(XF, nbt, M, r, q, v[i][0], v[i][1], sh);
+    }
+}
+
 template <int PMAX, int KT>
 __device__ __forceinline__ void dz_split_rows_block(const float* __restrict__ X, long long ldx,
                                                     const float* __restrict__ k_scale, int M, int K, int pairs,
                                                     int nbt, uint32_t* __restrict__ XF, int* __restrict__ shifts,
                                                     float* wred) {
     for (int r = 0; r < M; r++) {
-        const float* x = X + (long long)r * ldx;
         float v[PMAX][2];
-        float m = 0.0f;
-#pragma unroll
-        for (int i = 0; i < PMAX; i++) {
-            const int q = threadIdx.x + i * blockDim.x;
-            v[i][0] = dz_x_at(x, k_scale, K, 2 * q);
-            v[i][1] = dz_x_at(x, k_scale, K, 2 * q + 1);
-            m = fmaxf(m, fmaxf(fabsf(v[i][0]), fabsf(v[i][1])));
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        __syncthreads();   // wred may still be read for the previous row
-        if ((threadIdx.x & 31) == 0) wred[threadIdx.x >> 5] = m;
-        __syncthreads();
-        float amax = 0.0f;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) amax = fmaxf(amax, wred[w]);
-        const int sh = dz_row_shift(amax);
-        if (threadIdx.x == 0) shifts[r] = -sh;
-#pragma unroll
-        for (int i = 0; i < PMAX; i++) {
-            const int q = threadIdx.x + i * blockDim.x;
-            if (q < pairs) dz_split_store_pair<KT>(XF, nbt, M, r, q, v[i][0], v[i][1], sh);
-        }
+        dz_split_row_load<PMAX>(X + (long long)r * ldx, k_scale, K, v);
+        dz_split_row_store<PMAX, KT>(v, r, M, pairs, nbt, XF, shifts, wred);
     }
 }
 
@@ -514,6 +528,22 @@ __device__ __forceinline__ void dz_bulk_g2s(void* dst, const void* src, uint32_t
         : "memory");
 }
 
+// L2 policy for streamed weights: read once per product, so they should not
+// evict activations and other reused data.
+__device__ __forceinline__ uint64_t dz_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void dz_bulk_g2s_stream(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                   uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dz_smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(dz_smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 constexpr int QMS_STAGES = 3;      // ring stages per warp
 constexpr int QMS_XIN_PAIRS = 8;   // element pairs per thread of the in-kernel split
 
@@ -618,6 +648,7 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qms_kernel(QmsArgs a) {
     }
     __syncwarp();
 
+    const uint64_t wpolicy = dz_policy_evict_first();
     // lane 0: put piece idx in flight into stage idx % QMS_STAGES
     auto issue = [&](int idx) {
         const QmsPiece pc = dz_qms_piece<W>(a, warp, ppr, idx);
@@ -632,8 +663,8 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qms_kernel(QmsArgs a) {
         dz_mbar_expect_tx(bar, bytes * tiles);
         uint8_t* dst = ring + (idx % QMS_STAGES) * stage_bytes;
         for (int i = 0; i < tiles; i++)
-            dz_bulk_g2s(dst + (size_t)i * a.pk * 512,
-                        a.codes + ((size_t)(pc.ng * NT + i) * a.nkg + pc.kg0) * 512, bytes, bar);
+            dz_bulk_g2s_stream(dst + (size_t)i * a.pk * 512,
+                               a.codes + ((size_t)(pc.ng * NT + i) * a.nkg + pc.kg0) * 512, bytes, bar, wpolicy);
     };
     int issued = min(npieces, QMS_STAGES - 1);
     if (lane == 0)
@@ -867,22 +898,32 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1_kernel(Qmv1Args a) {
     // lane 0 keeps two pieces in flight: piece i -> stage i % QMS_STAGES
     Cursor ic = cursor_at(my0);
     int issued = 0, istage = 0;
+    const uint64_t wpolicy = dz_policy_evict_first();
     auto issue = [&]() {
         const int n = piece_len(ic);
         uint64_t* bar = &bars[istage];
         dz_mbar_expect_tx(bar, (uint32_t)n * 512u);
-        dz_bulk_g2s(ring + istage * stage_bytes, a.codes + (size_t)ic.pos * 512, (uint32_t)n * 512u, bar);
+        dz_bulk_g2s_stream(ring + istage * stage_bytes, a.codes + (size_t)ic.pos * 512, (uint32_t)n * 512u, bar,
+                           wpolicy);
         advance(ic, n);
         issued++;
         istage = istage == QMS_STAGES - 1 ? 0 : istage + 1;
     };
+    // the activation rows are requested before the first weight pieces, so
+    // they do not queue behind them
+    float xr[2][QMS_XIN_PAIRS][2];
+    if (XIN) {
+        dz_split_row_load<QMS_XIN_PAIRS>(a.X, a.k_scale, a.K, xr[0]);
+        if (a.M > 1) dz_split_row_load<QMS_XIN_PAIRS>(a.X + a.ldx, a.k_scale, a.K, xr[1]);
+    }
     if (lane == 0)
         for (int i = 0; i < QMS_STAGES - 1 && ic.pos < my1; i++) issue();
 
     const int* shifts = a.row_shift;
     if (XIN) {
-        dz_split_rows_block<QMS_XIN_PAIRS, KT>(a.X, a.ldx, a.k_scale, a.M, a.K, a.nkg * KT * 8, 1,
-                                               reinterpret_cast<uint32_t*>(xf_sm), rsh, wred);
+        uint32_t* xf32 = reinterpret_cast<uint32_t*>(xf_sm);
+        dz_split_row_store<QMS_XIN_PAIRS, KT>(xr[0], 0, a.M, a.nkg * KT * 8, 1, xf32, rsh, wred);
+        if (a.M > 1) dz_split_row_store<QMS_XIN_PAIRS, KT>(xr[1], 1, a.M, a.nkg * KT * 8, 1, xf32, rsh, wred);
         shifts = rsh;
     }
     __syncthreads();   // counters zeroed, XF written
