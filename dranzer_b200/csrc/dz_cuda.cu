@@ -1561,7 +1561,7 @@ extern "C" int dz_cuda_matmul_quantized_noalloc(const float* A, const dz_cuda_qm
     if (need > (size_t)DZ_NOALLOC_SCRATCH_BYTES)
         return fail(DZ_E_INVALID,
                     "matmul_quantized_noalloc: m=%zu rows x k=%zu need %zu bytes of scratch, above the static "
-                    "limit of %u bytes (m * 3 * k padded to 64 * 2 bytes)",
+                    "limit of %u bytes (ceil(m/2) * 16 * k padded to 32/64, + 4m)",
                     m, k, need, (unsigned)DZ_NOALLOC_SCRATCH_BYTES);
     DeviceGuard g(q->device);
     if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", q->device);

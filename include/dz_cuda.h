@@ -74,8 +74,10 @@ int dz_cuda_matmul_quantized_async(const float *A_dev, const dz_cuda_qmatrix_t *
  * rights after start-up. The async entry point grows a per-matrix scratch
  * buffer with cudaMalloc the first time it sees a larger m; this one allocates
  * nothing and uses a fixed DZ_NOALLOC_SCRATCH_BYTES array that every GPU which
- * loads the library holds until exit. m * 3 * (k rounded up to 64) * 2 bytes
- * must fit in it (e.g. m <= 170 at k = 4096); larger calls return DZ_E_INVALID.
+ * loads the library holds until exit. ceil(m / 2) * 16 * kp bytes of split
+ * activations (kp = k rounded up to 32 for INT8, 64 for INT4) plus 4 * m bytes
+ * of row exponents, each rounded up to 256, must fit in it (e.g. m <= 126 at
+ * k = 4096); larger calls return DZ_E_INVALID.
  * The first call on a device looks up the array's device address (make that
  * call before any stream capture). All calls on a device share the array, so
  * calls whose work overlaps on the GPU (different streams, no ordering) race.

@@ -49,7 +49,7 @@ def test_noalloc_rejects_oversized_calls(gpu):
     q = gpu.QuantizedWeightMatrix.encode(np.ones((4096, 16), np.float32), 8)
     a = torch.zeros((171, 4096), dtype=torch.float32, device="cuda")
     c = torch.zeros((171, 16), dtype=torch.float32, device="cuda")
-    # 171 rows x 3 x 4096 x 2 bytes is above the 4 MiB array
+    # 86 row pairs x 16 x 4096 bytes of split activations are above the 4 MiB array
     st = L.dz_cuda_matmul_quantized_noalloc(a.data_ptr(), q.handle, c.data_ptr(), 171, 4096, None)
     assert st == -1
     assert "static" in _native.last_error()[1]
