@@ -188,24 +188,24 @@ def dist_init():
     return world, rank, local
 
 
-def quant_matvec_probe(dz, torch, stream, hbm):
-    """C3 rows: K=4096, N=32000, M in {1, 8}, INT8 and INT4; enough weight copies
-    rotated per launch that the weights exceed L2 (126 MB)."""
-    from dranzer_b200 import workloads as W  # noqa: F401
+def quant_matvec_probe(dz, torch, stream, hbm, bf16=None):
+    """C3 rows: K=4096, N=32000, M in {1, 8, 64, 512}, INT8 and INT4; enough
+    weight copies rotated per launch that the weights exceed L2 (126 MB)."""
     res = []
     st = np.array([dz.rng_stream(3, dz.STREAM_TESTING)], np.uint64)
-    x = dz.synth_gaussian(st, 8 * 4096, 1.0).reshape(8, 4096)
+    Ms = (1, 8, 64, 512)
+    x = dz.synth_gaussian(st, max(Ms) * 4096, 1.0).reshape(max(Ms), 4096)
     w = dz.synth_gaussian(st, 4096 * 32000, 0.02).reshape(4096, 32000)
     xd = torch.from_numpy(x).cuda()
-    yd = torch.empty((8, 32000), dtype=torch.float32, device="cuda")
+    yd = torch.empty((max(Ms), 32000), dtype=torch.float32, device="cuda")
     for bits in (8, 4):
         s, p = dz.quantize_pack(w, bits)
         copies = 2 if bits == 8 else 4
         mats = [dz.QuantizedWeightMatrix(s, p, 4096, 32000, bits) for _ in range(copies)]
-        for M in (1, 8):
+        for M in Ms:
             for i in range(6):
                 mats[i % copies].matmul_async(xd.data_ptr(), yd.data_ptr(), M, stream.cuda_stream)
-            reps = 24
+            reps = 24 if M <= 64 else 8
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
             torch.cuda.synchronize()
             for i in range(reps):
@@ -216,8 +216,13 @@ def quant_matvec_probe(dz, torch, stream, hbm):
             ms = statistics.median(a.elapsed_time(b) for a, b in evs)
             nbytes = 4096 * 32000 * bits / 8 + 32000 * 4 + M * 4096 * 4 + M * 32000 * 4
             gbs = nbytes / (ms * 1e-3) / 1e9
-            res.append({"bits": bits, "M": M, "K": 4096, "N": 32000, "us": round(ms * 1e3, 2),
-                        "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "bytes": int(nbytes)})
+            tflops = 2.0 * M * 4096 * 32000 / (ms * 1e-3) / 1e12
+            r = {"bits": bits, "M": M, "K": 4096, "N": 32000, "us": round(ms * 1e3, 2),
+                 "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "TFLOP/s": round(tflops, 1),
+                 "bytes": int(nbytes)}
+            if bf16:
+                r["tensor_frac_of_bf16"] = round(tflops / bf16, 4)
+            res.append(r)
         for m in mats:
             m.close()
     return res
@@ -375,7 +380,7 @@ def run_dz(args, wl):
             "clocks": clk,
         }
     if rank == 0 and world == 1:
-        out["quant_matvec"] = quant_matvec_probe(dz, torch, stream, hbm)
+        out["quant_matvec"] = quant_matvec_probe(dz, torch, stream, hbm, bf16)
         cpu, cpu_tokens = cpu_reference(wl)
         out["cpu_baseline"] = {k: v for k, v in cpu.items() if k != "seconds"}
         out["cpu_baseline"]["tokens_match_gpu"] = bool(np.array_equal(cpu_tokens, got))
@@ -429,7 +434,8 @@ def main():
         import torch
         import dranzer_b200 as dz
         stream = torch.cuda.Stream()
-        print(json.dumps({"quant_matvec": quant_matvec_probe(dz, torch, stream, peaks()[0])}))
+        hbm, bf16, _ = peaks()
+        print(json.dumps({"quant_matvec": quant_matvec_probe(dz, torch, stream, hbm, bf16)}))
         return
     from dranzer_b200 import workloads as W
     wl = W.WORKLOADS[args.workload]

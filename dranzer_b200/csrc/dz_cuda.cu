@@ -22,6 +22,7 @@
 #include "qmma.cuh"
 #include "select.cuh"
 #include "seqgen.cuh"
+#include "umma.cuh"
 
 using namespace dz;
 
@@ -92,13 +93,48 @@ struct DevQMat {
     float* col_scale = nullptr;  // [Np] (COLUMN / TENSOR expanded), zero in padding
     float* k_scale = nullptr;    // [K] ROW granularity
     size_t code_bytes = 0, scale_bytes = 0;
+    // INT8 only: the codes again in the reference's k x n byte order (rows
+    // kn_ld bytes apart) with their TMA map, for the tensor-core GEMM
+    uint8_t* kn = nullptr;
+    int kn_ld = 0;
+    CUtensorMap tm_kn;
 };
 
 static void free_qmat(DevQMat& m) {
     cudaFree(m.codes);
     cudaFree(m.col_scale);
     cudaFree(m.k_scale);
+    cudaFree(m.kn);
     m = DevQMat();
+}
+
+// cuTensorMapEncodeTiled from the driver (no link-time dependency on libcuda).
+using TensorMapEncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static TensorMapEncodeFn tensor_map_encoder() {
+    static TensorMapEncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<TensorMapEncodeFn>(p);
+    });
+    return fn;
+}
+
+// A 128 x 128-byte tiled uint8 TMA map with the 128-byte swizzle over a
+// tensor of `rank` dims (dims[0] innermost, strides in bytes for dims 1..).
+static bool encode_u8_map(CUtensorMap* tm, void* base, int rank, const cuuint64_t* dims, const cuuint64_t* strides,
+                          const cuuint32_t* box) {
+    TensorMapEncodeFn enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint32_t es[3] = {1, 1, 1};
+    return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank, base, dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 static int round_up(int x, int m) { return (x + m - 1) / m * m; }
@@ -180,6 +216,21 @@ static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cuda
     dz_frag_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(fs, reinterpret_cast<uint32_t*>(m.codes),
                                                                            m.K, m.bits, m.nkg, nwords);
     DZ_CUDA(cudaGetLastError());
+    if (m.bits == 8 && tensor_map_encoder()) {
+        // k x n codes for the tensor-core GEMM: the sources side by side
+        m.kn_ld = round_up(N, 16);
+        DZ_CUDA(cudaMalloc(&m.kn, (size_t)m.K * m.kn_ld));
+        for (size_t i = 0; i < srcs.size(); i++)
+            DZ_CUDA(cudaMemcpy2DAsync(m.kn + fs.off[i], (size_t)m.kn_ld, fs.ref[i], srcs[i]->cols, srcs[i]->cols,
+                                      (size_t)m.K, cudaMemcpyDeviceToDevice, st));
+        const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)m.K};
+        const cuuint64_t strides[1] = {(cuuint64_t)m.kn_ld};
+        const cuuint32_t box[2] = {UG_BN, UG_BK};
+        if (!encode_u8_map(&m.tm_kn, m.kn, 2, dims, strides, box)) {
+            cudaFree(m.kn);
+            m.kn = nullptr;
+        }
+    }
     DZ_CUDA(cudaStreamSynchronize(st));
     return DZ_OK;
 }
@@ -251,7 +302,16 @@ static size_t qmv_xf_bytes(const DevQMat& W, int M) {
     const int KG = W.bits == 8 ? 32 : 64;
     return (size_t)W.nkg * KG * (size_t)((M + 1) / 2) * 16;
 }
-static size_t qmv_scratch_bytes(const DevQMat& W, int M) { return r256(qmv_xf_bytes(W, M)) + r256((size_t)M * 4); }
+// Bytes of scratch the tensor-core GEMM needs for M rows: three limb planes
+// of M x (K rounded up to 128) bytes, the int64 row sums and the exponents.
+static size_t ugemm_scratch_bytes(const DevQMat& W, int M) {
+    const size_t kp = (size_t)round_up(W.K, UG_BK);
+    return r256(3 * (size_t)M * kp) + r256((size_t)M * 8) + r256((size_t)M * 4);
+}
+static size_t qmv_scratch_bytes(const DevQMat& W, int M) {
+    const size_t xf = r256(qmv_xf_bytes(W, M)) + r256((size_t)M * 4);
+    return W.kn ? std::max(xf, ugemm_scratch_bytes(W, M)) : xf;
+}
 
 template <int BITS, int NB, int NT, int W, bool XIN>
 static void launch_qms_t(const QmsArgs& a, unsigned grid, size_t smem, cudaStream_t st) {
@@ -303,6 +363,7 @@ static int qms_prepare(int device) {
     DZ_CUDA(cudaFuncSetAttribute(dz_qmv1_kernel<B, QMV1_WARPS, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
     DZ_QMV1_ATTR(4, false); DZ_QMV1_ATTR(4, true); DZ_QMV1_ATTR(8, false); DZ_QMV1_ATTR(8, true);
 #undef DZ_QMV1_ATTR
+    DZ_CUDA(cudaFuncSetAttribute(dz_ugemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UG_SMEM_BYTES));
     g_qms_ready[device] = true;
     return DZ_OK;
 }
@@ -387,8 +448,52 @@ static bool qmv1_launch(const DevQMat& W, const float* X, long long ldx, int M, 
 // `scratch` (qmv_scratch_bytes), then the streaming (M <= QMS_MAX_M) or the
 // register-blocked MMA kernel. A bulk-copy wait that gives up sets *status
 // (when given) and leaves NaN in the tile. Returns the launches (1 or 2).
+// Rows from which INT8 products go to the tensor-core GEMM.
+constexpr int UGEMM_MIN_M = QMS_MAX_M + 1;
+
+// The tensor-core GEMM (umma.cuh): limb split, then one CTA per 128 x 128
+// output tile. Returns the launches (2), or 0 when its TMA map cannot be made.
+static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
+                        cudaStream_t st, void* scratch, int* status) {
+    const int Kp = round_up(W.K, UG_BK);
+    int8_t* L = static_cast<int8_t*>(scratch);
+    long long* rowsum = reinterpret_cast<long long*>(static_cast<uint8_t*>(scratch) + r256(3 * (size_t)M * Kp));
+    int* shift = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(rowsum) + r256((size_t)M * 8));
+    CUtensorMap tmA;
+    const cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)M, (cuuint64_t)UG_LIMBS};
+    const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)Kp * M};
+    const cuuint32_t box[3] = {UG_BK, UG_BM, 1};
+    if (!encode_u8_map(&tmA, L, 3, dims, strides, box)) return 0;
+    {
+        ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 3.0 * M * Kp, 0, st);
+        dz_limb_split_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, rowsum, shift);
+    }
+    UgArgs a;
+    memset(&a, 0, sizeof(a));
+    a.M = M;
+    a.N = W.N;
+    a.K = W.K;
+    a.nkb = Kp / UG_BK;
+    a.rowsum = rowsum;
+    a.shift = shift;
+    a.code_bias = 127;
+    a.status = status;
+    a.ep = ep_in;
+    a.ep.row_shift = nullptr;
+    const dim3 grid((unsigned)((W.N + UG_BN - 1) / UG_BN), (unsigned)((M + UG_BM - 1) / UG_BM));
+    ProfScope prof(DZ_KERNEL_QMV,
+                   (double)W.K * W.N + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N,
+                   2.0 * M * W.K * W.N, st);
+    dz_ugemm_kernel<<<grid, UG_THREADS, UG_SMEM_BYTES, st>>>(tmA, W.tm_kn, a);
+    return 2;
+}
+
 static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
                       cudaStream_t st, void* scratch, int* status) {
+    if (M >= UGEMM_MIN_M && W.kn) {
+        const int n = launch_ugemm(W, X, ldx, M, ep_in, st, scratch, status);
+        if (n) return n;
+    }
     const int KG = W.bits == 8 ? 32 : 64;
     const int KT = KG / 16;
     const int Kp = W.nkg * KG;

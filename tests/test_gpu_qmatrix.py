@@ -89,6 +89,48 @@ def test_matmul_ragged_and_unaligned(gpu, oracle):
             q.close()
 
 
+@pytest.mark.parametrize("gran", [0, 1, 2])
+def test_matmul_many_rows_ragged(gpu, oracle, gran):
+    """Row counts above the matvec kernels' limit (the tensor-core GEMM for
+    INT8), ragged K / N, every granularity, against the oracle."""
+    rng = np.random.RandomState(7 + gran)
+    for (m, k, n) in [(17, 100, 77), (130, 300, 257), (200, 4104, 129), (64, 64, 16)]:
+        for bits in (8, 4):
+            w = (rng.randn(k, n) * 0.05).astype(np.float32)
+            a = rng.randn(m, k).astype(np.float32)
+            q = gpu.QuantizedWeightMatrix.encode(w, bits, gran)
+            s, p = oracle.quantize_pack(w, bits, gran)
+            ref = oracle.matmul_quantized(a, k, n, s, p, bits, gran)
+            ok, err = _tol_ok(q.matmul(a), ref)
+            assert ok, (m, k, n, bits, gran, err)
+            q.close()
+
+
+def test_matmul_many_rows_dynamic_range_and_nonfinite(gpu, oracle):
+    """Rows whose elements span 2^-30 .. 2^20, and a row holding inf / NaN
+    (which reads NaN, as the reference's fp32 sums do), at M = 40."""
+    rng = np.random.RandomState(11)
+    m, k, n = 40, 512, 300
+    w = (rng.randn(k, n) * 0.05).astype(np.float32)
+    a = (rng.randn(m, k) * np.exp2(rng.randint(-30, 20, size=(m, k)))).astype(np.float32)
+    a[5] *= 1e-30
+    for bits in (8, 4):
+        q = gpu.QuantizedWeightMatrix.encode(w, bits)
+        s, p = oracle.quantize_pack(w, bits, 2)
+        ref = oracle.matmul_quantized(a, k, n, s, p, bits, 2)
+        c = q.matmul(a)
+        for r in range(m):
+            ok, err = _tol_ok(c[r], ref[r])
+            assert ok, (bits, r, err)
+        bad = a.copy()
+        bad[3, 7] = np.inf
+        bad[9, 100] = np.nan
+        c = q.matmul(bad)
+        assert np.isnan(c[9]).all() and not np.isfinite(c[3]).any()
+        assert np.isfinite(np.delete(c, [3, 9], axis=0)).all()
+        q.close()
+
+
 def test_matmul_rejects_bad_k(gpu):
     q = gpu.QuantizedWeightMatrix.encode(np.ones((8, 4), np.float32), 8)
     with pytest.raises(gpu.DzError):
