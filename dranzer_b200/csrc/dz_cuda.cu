@@ -93,8 +93,9 @@ struct DevQMat {
     float* col_scale = nullptr;  // [Np] (COLUMN / TENSOR expanded), zero in padding
     float* k_scale = nullptr;    // [K] ROW granularity
     size_t code_bytes = 0, scale_bytes = 0;
-    // INT8 only: the codes again in the reference's k x n byte order (rows
-    // kn_ld bytes apart) with their TMA map, for the tensor-core GEMM
+    // the codes again, one byte each, in the reference's k x n order (rows
+    // kn_ld bytes apart; INT4 nibbles widened) with their TMA map, for the
+    // tensor-core GEMM
     uint8_t* kn = nullptr;
     int kn_ld = 0;
     CUtensorMap tm_kn;
@@ -216,13 +217,21 @@ static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cuda
     dz_frag_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(fs, reinterpret_cast<uint32_t*>(m.codes),
                                                                            m.K, m.bits, m.nkg, nwords);
     DZ_CUDA(cudaGetLastError());
-    if (m.bits == 8 && tensor_map_encoder()) {
+    if (tensor_map_encoder()) {
         // k x n codes for the tensor-core GEMM: the sources side by side
         m.kn_ld = round_up(N, 16);
         DZ_CUDA(cudaMalloc(&m.kn, (size_t)m.K * m.kn_ld));
-        for (size_t i = 0; i < srcs.size(); i++)
-            DZ_CUDA(cudaMemcpy2DAsync(m.kn + fs.off[i], (size_t)m.kn_ld, fs.ref[i], srcs[i]->cols, srcs[i]->cols,
-                                      (size_t)m.K, cudaMemcpyDeviceToDevice, st));
+        for (size_t i = 0; i < srcs.size(); i++) {
+            if (m.bits == 8) {
+                DZ_CUDA(cudaMemcpy2DAsync(m.kn + fs.off[i], (size_t)m.kn_ld, fs.ref[i], srcs[i]->cols,
+                                          srcs[i]->cols, (size_t)m.K, cudaMemcpyDeviceToDevice, st));
+            } else {
+                const long long total = (long long)m.K * (long long)srcs[i]->cols;
+                dz_widen_nibbles_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+                    fs.ref[i], (long long)srcs[i]->cols, total, m.kn + fs.off[i], m.kn_ld);
+                DZ_CUDA(cudaGetLastError());
+            }
+        }
         const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)m.K};
         const cuuint64_t strides[1] = {(cuuint64_t)m.kn_ld};
         const cuuint32_t box[2] = {UG_BN, UG_BK};
@@ -448,7 +457,7 @@ static bool qmv1_launch(const DevQMat& W, const float* X, long long ldx, int M, 
 // `scratch` (qmv_scratch_bytes), then the streaming (M <= QMS_MAX_M) or the
 // register-blocked MMA kernel. A bulk-copy wait that gives up sets *status
 // (when given) and leaves NaN in the tile. Returns the launches (1 or 2).
-// Rows from which INT8 products go to the tensor-core GEMM.
+// Rows from which products go to the tensor-core GEMM.
 constexpr int UGEMM_MIN_M = QMS_MAX_M + 1;
 
 // The tensor-core GEMM (umma.cuh): limb split, then one CTA per 128 x 128
@@ -476,7 +485,7 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     a.nkb = Kp / UG_BK;
     a.rowsum = rowsum;
     a.shift = shift;
-    a.code_bias = 127;
+    a.code_bias = W.bits == 8 ? 127 : 7;
     a.status = status;
     a.ep = ep_in;
     a.ep.row_shift = nullptr;

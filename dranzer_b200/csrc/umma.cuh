@@ -6,10 +6,10 @@
 // - each activation row is scaled by 2^s (exact) so that max |x 2^s| lies in
 //   [2^22, 2^23), rounded to a 24-bit integer X and cut into three 8-bit
 //   limbs X = 65536 * top + 256 * mid + low (top signed, mid / low unsigned);
-// - INT8 weights enter the tensor core as their unsigned codes c = level +
-//   127, straight from the reference's k x n byte layout (src/core/
-//   quantize.c:213-221), so there is no dequantization at all:
-//   sum_k X level = sum_k X c - 127 * sum_k X;
+// - weights enter the tensor core as their unsigned codes c = level + qmax
+//   (INT8: the reference's k x n bytes as stored, src/core/quantize.c:
+//   213-221; INT4: the nibbles widened to bytes once at upload), so there is
+//   no dequantization at all: sum_k X level = sum_k X c - qmax * sum_k X;
 // - one kind::i8 MMA per limb accumulates int32 in tensor memory (exact for
 //   K up to 33k); the epilogue combines the limbs in int64, subtracts the
 //   code bias times the row sum, converts to fp32 once and applies 2^-s and
@@ -44,12 +44,13 @@ constexpr uint32_t UG_STAGE_BYTES = UG_LIMBS * UG_A_BYTES + UG_B_BYTES;
 constexpr uint32_t UG_TMEM_COLS = 512;           // three 128-column int32 accumulators
 constexpr size_t UG_SMEM_BYTES = (size_t)UG_STAGES * UG_STAGE_BYTES + 1024 + 256;
 constexpr int UG_ROW_NONFINITE = -0x40000000;    // row exponent marking a non-finite input row
+constexpr int UG_TILE_LD = UG_BN + 4;            // staging tile row stride (floats): 16-byte rows, spread banks
 
 struct UgArgs {
     int M, N, K, nkb;             // nkb: k blocks of UG_BK
     const long long* rowsum;      // [M] sum_k X
     const int* shift;             // [M] -s, or UG_ROW_NONFINITE
-    int code_bias;                // 127 (INT8)
+    int code_bias;                // qmax: 127 (INT8) or 7 (INT4)
     int* status;                  // set to 1 when a wait gave up (may be null)
     QmvEpilogue ep;               // col_scale etc.; row_shift unused
 };
@@ -141,6 +142,19 @@ __device__ __forceinline__ void ug_tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
     for (int i = 0; i < 32; i++) v[i] = (int32_t)r[i];
 }
 
+// ------------------------------------------------------- weight bytes
+
+// INT4 codes (two per byte, even index in the low nibble, src/core/
+// quantize.c:213-221) of a k x cols matrix -> one byte per code in rows of
+// `ld` bytes.
+__global__ void dz_widen_nibbles_kernel(const uint8_t* __restrict__ packed, long long cols, long long total,
+                                        uint8_t* __restrict__ out, int ld) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const long long k = i / cols, n = i - k * cols;
+    out[k * ld + n] = (packed[i >> 1] >> ((i & 1) * 4)) & 0xF;
+}
+
 // ------------------------------------------------------- activation limbs
 
 // One block per row: X = rint(x * k_scale * 2^s) clamped to 24 bits, stored
@@ -217,6 +231,67 @@ __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restr
     }
 }
 
+// Columns [n0, n0 + UG_BN) of rows [m0, m0 + UG_BM) from the staging tile
+// through the epilogue (column scale, bias, residual, ReLU, segment routing),
+// four columns per thread with float4 accesses where the addresses allow.
+__device__ __forceinline__ void ug_store_tile(const UgArgs& a, const float* tile, int m0, int n0, bool failed) {
+    const QmvEpilogue& e = a.ep;
+    const int c4 = (threadIdx.x & 31) * 4;   // fixed per thread: blockDim.x is a multiple of 32
+    const int n = n0 + c4;
+    if (n >= a.N) return;
+    const int nv = a.N - n < 4 ? a.N - n : 4;
+    float sc[4], bi[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        sc[j] = (j < nv && e.col_scale) ? e.col_scale[n + j] : 1.0f;
+        bi[j] = (j < nv && e.bias) ? e.bias[n + j] : 0.0f;
+    }
+    int sg = 0;
+    while (sg + 1 < e.nseg && n >= e.seg_start[sg + 1]) sg++;
+    const bool one_seg = nv == 4 && (sg + 1 >= e.nseg || n + 3 < e.seg_start[sg + 1]);
+    for (int r = threadIdx.x >> 5; r < UG_BM; r += UG_THREADS / 32) {
+        const int row = m0 + r;
+        if (row >= a.M) break;
+        float4 t = *reinterpret_cast<const float4*>(tile + r * UG_TILE_LD + c4);
+        if (failed) t.x = t.y = t.z = t.w = __int_as_float(0x7fc00000);   // a failed tile reads NaN
+        float y[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            y[j] = (e.col_scale ? y[j] * sc[j] : y[j]);
+            if (e.bias) y[j] = y[j] + bi[j];
+        }
+        if (e.residual) {
+            const float* rp = e.residual + (long long)row * e.ld_res + n;
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (j < nv) y[j] = y[j] + rp[j];
+        }
+        if (e.relu) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
+        }
+        if (one_seg) {
+            long long off = (long long)row * e.seg_ld[sg] + (n - e.seg_start[sg]);
+            if (e.seg_row_off[sg]) off += e.seg_row_off[sg][row];
+            float* dst = e.seg_ptr[sg] + off;
+            if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+                continue;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; j++) dst[j] = y[j];
+            continue;
+        }
+        for (int j = 0; j < nv; j++) {
+            int s2 = 0;
+            while (s2 + 1 < e.nseg && n + j >= e.seg_start[s2 + 1]) s2++;
+            long long off = (long long)row * e.seg_ld[s2] + (n + j - e.seg_start[s2]);
+            if (e.seg_row_off[s2]) off += e.seg_row_off[s2][row];
+            e.seg_ptr[s2][off] = y[j];
+        }
+    }
+}
+
 // ------------------------------------------------------------------- GEMM
 
 __global__ void __launch_bounds__(UG_THREADS, 1)
@@ -254,7 +329,8 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
     ug_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
+    if (warp == 0) {
+      if (lane == 0) {
         // producer: TMA loads of the three limb tiles and the code tile per k block
         int kb = 0;
         for (; kb < a.nkb; kb++) {
@@ -268,7 +344,10 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
             ug_tma_2d(stage_b(s), &tmB, n0, kb * UG_BK, &full[s]);
         }
         progress[0] = kb;
-    } else if (warp == 1 && lane == 0) {
+      }
+      __syncwarp();   // the warp reconverges before the block barriers below
+    } else if (warp == 1) {
+      if (lane == 0) {
         // MMA issuer: 3 limbs x 4 k-steps of 32 per stage
         int kb = 0;
         const uint32_t id_top = ug_idesc(true), id_low = ug_idesc(false);
@@ -295,12 +374,17 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
         }
         progress[1] = kb;
         ug_commit(accum);   // completes once every MMA issued above has
+      }
+      __syncwarp();
     } else if (warp >= 4) {
-        // epilogue: thread = row, 32 columns at a time from the three accumulators
+        // epilogue, part 1: thread = row; drain the three accumulators into a
+        // [128][UG_TILE_LD] fp32 staging tile in the pipeline buffers (free
+        // once the accumulator barrier completes)
         const int ew = warp - 4;
         bool ok = dz_mbar_wait(accum, 0);
         ug_fence_after();
-        const int row = m0 + ew * 32 + lane;
+        const int rl = ew * 32 + lane;
+        const int row = m0 + rl;
         const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
         const bool live = row < a.M;
         const long long bias = live ? (long long)a.code_bias * a.rowsum[row] : 0;
@@ -308,29 +392,37 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
         if (!ok || progress[2]) {
             if (a.status && lane == 0) atomicExch(a.status, 1);
             ok = false;
+            progress[2] = 1;
         }
+        float* tile = reinterpret_cast<float*>(sm);
         for (int c0 = 0; c0 < UG_BN; c0 += 32) {
             int32_t top[32], mid[32], low[32];
             ug_tmem_ld32(tmem + lane_base + (uint32_t)c0, top);
             ug_tmem_ld32(tmem + lane_base + (uint32_t)(UG_BN + c0), mid);
             ug_tmem_ld32(tmem + lane_base + (uint32_t)(2 * UG_BN + c0), low);
-            if (!live) continue;
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const int n = n0 + c0 + j;
-                if (n >= a.N) break;
-                const long long v = (long long)top[j] * 65536 + (long long)mid[j] * 256 + (long long)low[j] - bias;
-                float y = dz_mul_pow2(__ll2float_rn(v), e);
-                if (!ok || e == UG_ROW_NONFINITE) y = __int_as_float(0x7fc00000);
-                dz_qmv_store_row(a.ep, a.M, a.N, row, n, y);
+            for (int q = 0; q < 8; q++) {
+                float y[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int c = 4 * q + j;
+                    const long long v = (long long)top[c] * 65536 + (long long)mid[c] * 256 + (long long)low[c] - bias;
+                    y[j] = dz_mul_pow2(__ll2float_rn(v), e);
+                    if (!ok || e == UG_ROW_NONFINITE) y[j] = __int_as_float(0x7fc00000);
+                }
+                *reinterpret_cast<float4*>(tile + rl * UG_TILE_LD + c0 + 4 * q) = make_float4(y[0], y[1], y[2], y[3]);
             }
         }
     }
 
-    // teardown: copies and MMAs in flight finish before the shared memory and
-    // the tensor memory are released
     ug_fence_before();
     __syncthreads();
+    // epilogue, part 2, all warps: one warp per output row, lane = 4 columns,
+    // so each store instruction writes 512 contiguous bytes
+    ug_store_tile(a, reinterpret_cast<const float*>(sm), m0, n0, progress[2] != 0);
+
+    // teardown: copies and MMAs in flight finish before the shared memory and
+    // the tensor memory are released
     if (threadIdx.x == 0 && progress[2]) {
         for (int kb = progress[1]; kb < progress[0]; kb++)
             if (!dz_mbar_wait(&full[kb % UG_STAGES], (uint32_t)((kb / UG_STAGES) & 1))) break;
