@@ -95,18 +95,31 @@ class ClockSampler:
 
 # ------------------------------------------------------------- CPU baseline
 
+def cpu_sample(wl):
+    """(sequences, prompt_len, n_new, one shared session) the CPU baseline runs."""
+    if wl.cpu_sample:
+        return wl.cpu_sample
+    return (wl.batch, wl.prompt_len, wl.n_new, False)
+
+
 def cpu_reference(wl, seqs=None, repeats=2):
     """The reference's own C path (oracle/_ref/libdzref.so: model_forward_token
-    + sample_next_token in the generation loop), sequences spread over all host
-    cores; falls back to the oracle port when the reference build is absent."""
+    + sample_next_token in the generation loop) on the host cores: either
+    sequences spread over threads (one session each, OMP 1) or, for models too
+    large to hold once per thread, one session with every thread in the
+    reference's OpenMP matmul. Falls back to the oracle port when the
+    reference build is absent."""
     sys.path.insert(0, os.path.join(ROOT, "tests"))
     from dranzer_b200 import workloads as W
     from _native_oracle import REF_SO, Oracle
     cores = os.cpu_count() or 1
-    n = wl.batch if seqs is None else seqs
-    prompts, seeds = W.prompts(wl)[:n], W.seeds(wl)[:n]
+    n, plen, n_new, shared = cpu_sample(wl)
+    if seqs is not None:
+        n = seqs
+    prompts, seeds = W.prompts(wl)[:n, :plen], W.seeds(wl)[:n]
     mk = np.array(W.MASKED, np.uint32)
-    out = np.zeros((n, wl.n_new), np.uint32)
+    out = np.zeros((n, n_new), np.uint32)
+    workers = 1 if shared else cores
     if os.path.exists(REF_SO):
         kind = "reference"
         L = ctypes.CDLL(REF_SO)
@@ -123,15 +136,15 @@ def cpu_reference(wl, seqs=None, repeats=2):
         path = f"/tmp/dz_cpu_ref_{os.getpid()}.bin".encode()
         s = wl.spec
         assert L.rh_build_bundle(path, s.vocab, s.dim, s.heads, s.layers, s.max_seq, wl.weight_seed, wl.bits, 2) == 0
-        sessions = [L.rh_load(path) for _ in range(cores)]
+        sessions = [L.rh_load(path) for _ in range(workers)]
         os.remove(path)
 
         def run(t, lo, hi):
-            L.rh_set_omp_threads(1)
+            L.rh_set_omp_threads(cores if shared else 1)
             p = np.ascontiguousarray(prompts[lo:hi])
             sd = np.ascontiguousarray(seeds[lo:hi])
-            o = np.zeros((hi - lo, wl.n_new), np.uint32)
-            L.rh_generate(sessions[t], p.ctypes.data, hi - lo, wl.prompt_len, wl.n_new, wl.strategy,
+            o = np.zeros((hi - lo, n_new), np.uint32)
+            L.rh_generate(sessions[t], p.ctypes.data, hi - lo, plen, n_new, wl.strategy,
                           wl.temperature, wl.top_k, wl.top_p, sd.ctypes.data if wl.strategy else None,
                           mk.ctypes.data, mk.size, o.ctypes.data, None)
             out[lo:hi] = o
@@ -143,18 +156,18 @@ def cpu_reference(wl, seqs=None, repeats=2):
         s = wl.spec
         spec = Spec(s.vocab, s.dim, s.heads, s.layers, s.max_seq)
         _, flat = quantize_params(o_, spec, synth_params(o_, spec, wl.weight_seed), wl.bits)
-        models = [o_.model(spec, flat) for _ in range(cores)]
+        models = [o_.model(spec, flat) for _ in range(workers)]
 
         def run(t, lo, hi):
-            toks, _ = models[t].generate(prompts[lo:hi], wl.n_new, wl.strategy, wl.temperature, wl.top_k,
-                                         wl.top_p, seeds[lo:hi] if wl.strategy else None, W.MASKED)
+            toks, _ = models[t].generate(np.ascontiguousarray(prompts[lo:hi]), n_new, wl.strategy, wl.temperature,
+                                         wl.top_k, wl.top_p, seeds[lo:hi] if wl.strategy else None, W.MASKED)
             out[lo:hi] = toks
     times = []
     for _ in range(repeats):
         t0 = time.perf_counter()
         ths = []
-        for t in range(cores):
-            lo, hi = W.shard(n, t, cores)
+        for t in range(workers):
+            lo, hi = W.shard(n, t, workers)
             if hi > lo:
                 ths.append(threading.Thread(target=run, args=(t, lo, hi)))
         for th in ths:
@@ -166,9 +179,10 @@ def cpu_reference(wl, seqs=None, repeats=2):
         for h in sessions:
             L.rh_free(h)
     best = min(times)
-    return {"value": n * wl.n_new / best, "unit": "tokens/s", "cores": cores, "kind": kind,
-            "sample": f"{n} sequences x ({wl.prompt_len} prompt + {wl.n_new} decode), best of {repeats}, "
-                      f"sequences spread over {cores} threads (OMP 1 each)",
+    how = (f"one session, {cores} OpenMP threads" if shared
+           else f"sequences spread over {cores} threads (OMP 1 each)")
+    return {"value": n * n_new / best, "unit": "tokens/s", "cores": cores, "kind": kind,
+            "sample": f"{n} sequences x ({plen} prompt + {n_new} decode), best of {repeats}, {how}",
             "seconds": best}, out
 
 
@@ -243,7 +257,7 @@ def run_dz(args, wl):
     W.write_bundle(wl, path)
     bundle = dz.Bundle(path)
     model = dz.Model.from_bundle(bundle, device=local)
-    cache = dz.KVCache(model, wl.batch, wl.spec.max_seq)
+    cache = dz.KVCache(model, wl.batch, wl.capacity or wl.spec.max_seq)
     stream = torch.cuda.Stream()
     cache.set_stream(stream.cuda_stream)
     samp = wl.sampling()
@@ -321,10 +335,13 @@ def run_dz(args, wl):
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         dev_ms, e2e_ms = float(t[0]), float(t[1])
 
-    # per-kernel-class CUDA-event timing of one eager job
+    # per-kernel-class CUDA-event timing of one eager job (a 16 + 8 token job at
+    # the full batch when the real one is too long to bracket every launch)
     nk = len(_native.KERNEL_CLASSES) + len(_native.FUSED_PHASES)
     stats = (_native.DzKernelStat * nk)()
-    _native.check(L.dz_cuda_profile_generate(cache.handle, pd.data_ptr(), wl.prompt_len, wl.n_new,
+    long_job = cache.generate_launches(wl.prompt_len, wl.n_new, samp) > 20000
+    p_plen, p_new = (16, 8) if long_job else (wl.prompt_len, wl.n_new)
+    _native.check(L.dz_cuda_profile_generate(cache.handle, pd.data_ptr(), p_plen, p_new,
                                              ctypes.byref(samp.c), seeds_ptr, od.data_ptr(), stats, nk),
                   "profile_generate")
     classes = {}
@@ -333,12 +350,16 @@ def run_dz(args, wl):
         if s.launches:
             classes[name] = {"launches": int(s.launches), "total_ms": round(s.total_ms, 4),
                              "avg_us": round(1e3 * s.total_ms / s.launches, 3),
-                             "bytes_per_launch": int(s.bytes / s.launches)}
+                             "bytes_per_launch": int(s.bytes / s.launches),
+                             "flops_per_launch": float(s.flops / s.launches)}
     phases = {name: round(stats[len(_native.KERNEL_CLASSES) + k].total_ms, 4)
               for k, name in enumerate(_native.FUSED_PHASES) if stats[len(_native.KERNEL_CLASSES) + k].total_ms}
     dom = max(classes, key=lambda n: classes[n]["total_ms"])
     d = classes[dom]
     achieved = d["bytes_per_launch"] / (d["avg_us"] * 1e-6) / 1e9
+    # arithmetic intensity above the ridge (bf16 peak / HBM peak): tensor-bound
+    tensor_bound = d["flops_per_launch"] > 0 and d["flops_per_launch"] / d["bytes_per_launch"] > bf16 * 1e3 / hbm
+    achieved_tf = d["flops_per_launch"] / (d["avg_us"] * 1e-6) / 1e12
     total_prof = sum(c["total_ms"] for c in classes.values())
     for c in classes.values():
         c["share"] = round(c["total_ms"] / total_prof, 3)
@@ -366,14 +387,22 @@ def run_dz(args, wl):
                     "h2d_bytes_per_step": int(prompts.nbytes + (seeds.nbytes if wl.strategy else 0)),
                     "d2h_bytes_per_step": int(wl.batch * wl.n_new * 4)},
             "gpu_launches": int(launches),
-            "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
+            "roofline": ({"bound": "tensor", "kernel": dom, "achieved": round(achieved_tf, 1), "peak": bf16,
+                          "unit": "TFLOP/s", "frac": round(achieved_tf / bf16, 4), "peak_source": peak_src,
+                          "traffic": None,
+                          "note": "flops = 2*M*K*N of the quantized GEMMs (useful work; the integer "
+                                  "tensor cores run three 8-bit limb passes of it); peak = measured dense "
+                                  "bf16; the profiled job is " + (f"{p_plen} + {p_new} tokens at the "
+                                  "full batch" if long_job else "the measured one")}
+                         if tensor_bound else
+                         {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                          # DRAM bytes of one dz_seqgen_kernel launch on this workload, from one ncu
                          # capture (profiles/c2_bench_launch_list.md)
                          "traffic": SEQGEN_C2_DRAM_BYTES if dom == "seqgen" and wl.name == W.C2.name else None,
                          "note": "bytes = weight codes+scales+fp32 tensors each sequence streams per step "
                                  "x steps x sequences; all of it is L2-resident for this workload, so the "
-                                 "kernel is latency/L2 bound, not HBM bound"},
+                                 "kernel is latency/L2 bound, not HBM bound"}),
             "path": "fused" if cache.uses_fused(samp) else "layered",
             "kernels": classes,
             "fused_phases_ms": phases,
@@ -383,7 +412,16 @@ def run_dz(args, wl):
         out["quant_matvec"] = quant_matvec_probe(dz, torch, stream, hbm, bf16)
         cpu, cpu_tokens = cpu_reference(wl)
         out["cpu_baseline"] = {k: v for k, v in cpu.items() if k != "seconds"}
-        out["cpu_baseline"]["tokens_match_gpu"] = bool(np.array_equal(cpu_tokens, got))
+        if wl.cpu_sample:
+            # the same sample through the device path
+            n, plen, n_new, _ = cpu_sample(wl)
+            sc = dz.KVCache(model, n, plen + n_new)
+            sp = np.ascontiguousarray(prompts[:n, :plen])
+            gs = sc.generate(sp, n_new, samp, seeds=seeds[:n] if wl.strategy else None)
+            sc.close()
+            out["cpu_baseline"]["tokens_match_gpu"] = bool(np.array_equal(cpu_tokens, gs))
+        else:
+            out["cpu_baseline"]["tokens_match_gpu"] = bool(np.array_equal(cpu_tokens, got))
     cache.close()
     model.close()
     bundle.close()

