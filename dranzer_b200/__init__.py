@@ -31,6 +31,7 @@ __all__ = ["GRAN_TENSOR", "GRAN_ROW", "GRAN_COLUMN", "GREEDY", "TOPK", "TOPP", "
 
 GRAN_TENSOR, GRAN_ROW, GRAN_COLUMN = 0, 1, 2
 GREEDY, TOPK, TOPP = 0, 1, 2
+PREFILL_AUTO, PREFILL_TOKENS, PREFILL_BATCHED = 0, 1, 2
 KIND_PROJECTION, KIND_EMBEDDING, KIND_BIAS, KIND_NORM = 0, 1, 2, 3
 STREAM_INIT = 0x9E3779B97F4A7C15
 STREAM_DROPOUT = 0xBF58476D1CE4E5B9
@@ -339,6 +340,20 @@ class KVCache:
 
     def set_path(self, path):
         check(lib().dz_cuda_cache_set_path(self.handle, path), "cache_set_path")
+
+    def set_prefill(self, mode):
+        """PREFILL_AUTO / PREFILL_TOKENS / PREFILL_BATCHED (dz_cuda_cache_set_prefill)."""
+        check(lib().dz_cuda_cache_set_prefill(self.handle, mode), "cache_set_prefill")
+
+    def prefill(self, ids, lens=None, want_logits=True):
+        """Batched prefill from empty rings: ids [batch, prompt_len], optional
+        per-sequence lengths; returns the last-position logits [batch, V]."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        assert ids.ndim == 2 and ids.shape[0] == self.batch
+        ln = None if lens is None else np.ascontiguousarray(lens, np.uint32)
+        out = np.empty((self.batch, self.vocab), np.float32) if want_logits else None
+        check(lib().dz_cuda_prefill(self.handle, _p(ids), _p(ln), ids.shape[1], _p(out)), "prefill")
+        return out
 
     def uses_fused(self, sampling=None):
         return bool(lib().dz_cuda_cache_uses_fused(self.handle, ctypes.byref(sampling.c) if sampling else None))

@@ -113,6 +113,8 @@ SIGNATURES = {
     "dz_cuda_generate_launches": (SZ, [P, SZ, SZ, P]),
     "dz_cuda_profile_generate": (I32, [P, P, SZ, SZ, P, P, P, P, SZ]),
     "dz_cuda_cache_set_path": (I32, [P, I32]),
+    "dz_cuda_cache_set_prefill": (I32, [P, I32]),
+    "dz_cuda_prefill": (I32, [P, P, P, SZ, P]),
     "dz_cuda_cache_uses_fused": (I32, [P, P]),
 }
 

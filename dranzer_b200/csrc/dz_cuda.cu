@@ -21,6 +21,7 @@
 #include "qmv.cuh"
 #include "qmma.cuh"
 #include "select.cuh"
+#include "prefill.cuh"
 #include "seqgen.cuh"
 #include "umma.cuh"
 
@@ -1085,7 +1086,31 @@ struct dz_cuda_cache {
     unsigned long long* phase_ns = nullptr;  // [SEQ_PHASES] fused-kernel phase clock (profiling)
     int* host_status = nullptr;   // pinned
     std::vector<void*> allocs;
+    // batched prefill (prefill.cuh): row buffers for up to pf_rows rows, grown on demand
+    int prefill = DZ_PREFILL_AUTO;
+    size_t pf_rows = 0;
+    float *pf_hidden = nullptr, *pf_q = nullptr, *pf_concat = nullptr, *pf_attn_raw = nullptr;
+    float *pf_attn_norm = nullptr, *pf_ff = nullptr, *pf_ff_raw = nullptr;
+    int* pf_rowoff = nullptr;
+    void* pf_scratch = nullptr;
+    uint32_t* pf_ids = nullptr;   // dz_cuda_prefill's device copies
+    int* pf_lens = nullptr;
+    size_t pf_ids_cap = 0;
 };
+
+static void free_prefill(dz_cuda_cache_t* c) {
+    for (void* p : {(void*)c->pf_hidden, (void*)c->pf_q, (void*)c->pf_concat, (void*)c->pf_attn_raw,
+                    (void*)c->pf_attn_norm, (void*)c->pf_ff, (void*)c->pf_ff_raw, (void*)c->pf_rowoff,
+                    c->pf_scratch, (void*)c->pf_ids, (void*)c->pf_lens})
+        cudaFree(p);
+    c->pf_hidden = c->pf_q = c->pf_concat = c->pf_attn_raw = c->pf_attn_norm = c->pf_ff = c->pf_ff_raw = nullptr;
+    c->pf_rowoff = nullptr;
+    c->pf_scratch = nullptr;
+    c->pf_ids = nullptr;
+    c->pf_lens = nullptr;
+    c->pf_rows = 0;
+    c->pf_ids_cap = 0;
+}
 
 static int cache_alloc(dz_cuda_cache_t* c, void** p, size_t bytes) {
     DZ_CUDA(cudaMalloc(p, bytes));
@@ -1113,6 +1138,7 @@ extern "C" void dz_cuda_cache_free(dz_cuda_cache_t* c) {
         cudaFreeHost(c->host_rng);
         cudaFreeHost(c->host_ids);
         cudaFreeHost(c->host_status);
+        free_prefill(c);
         if (c->own_stream && c->stream) cudaStreamDestroy(c->stream);
     }
     model_release(c->model);
@@ -1470,6 +1496,180 @@ static int launch_seqgen(dz_cuda_cache_t* c, const uint32_t* prompts, size_t ple
     return 1;
 }
 
+// ------------------------------------------------------------ batched prefill
+
+// Rows (sequences x prompt positions) one prefill pass holds at most; longer
+// batches run in groups of sequences.
+constexpr size_t PF_MAX_ROWS = 32768;
+
+static bool prefill_eligible(const dz_cuda_cache_t* c) {
+    const dz_cuda_model_t* m = c->model;
+    const int D = (int)m->desc.embedding_dim, H = (int)m->desc.num_heads;
+    if (H <= 0 || D % H) return false;
+    const int hd = D / H;
+    return hd == 32 || hd == 64 || hd == 128;
+}
+
+// Batched prefill under DZ_PREFILL_AUTO: models wide enough that their
+// projections run on the tensor-core GEMM at many rows.
+static bool use_batched_prefill(const dz_cuda_cache_t* c, size_t plen) {
+    if (plen < 2 || !prefill_eligible(c) || c->prefill == DZ_PREFILL_TOKENS) return false;
+    return c->prefill == DZ_PREFILL_BATCHED || c->model->desc.embedding_dim >= 512;
+}
+
+static size_t prefill_group(const dz_cuda_cache_t* c, size_t T) {
+    size_t S = PF_MAX_ROWS / T;
+    if (S < 1) S = 1;
+    return S < (size_t)c->B ? S : (size_t)c->B;
+}
+
+// Row buffers for groups of prefill_group(T) sequences of T positions
+// (allocated outside any stream capture; the attention kernel's shared
+// memory attribute is set here too).
+static int ensure_prefill(dz_cuda_cache_t* c, size_t T) {
+    const size_t rows = prefill_group(c, T) * T;
+    if (rows <= c->pf_rows) return DZ_OK;
+    clear_graphs(c);   // graphs captured earlier point at the old buffers
+    free_prefill(c);
+    dz_cuda_model_t* m = c->model;
+    const size_t D = m->desc.embedding_dim, F = 4 * D;
+    auto al = [&](void** p, size_t bytes) { return cudaMalloc(p, bytes) == cudaSuccess; };
+    size_t scratch = 0;
+    for (const DevLayer& L : m->layers)
+        for (const DevQMat* q : {&L.qkv, &L.q, &L.k, &L.v, &L.wo, &L.w1, &L.w2})
+            if (q->codes) scratch = std::max(scratch, qmv_scratch_bytes(*q, (int)rows));
+    bool ok = al((void**)&c->pf_hidden, rows * D * 4) && al((void**)&c->pf_q, rows * D * 4) &&
+              al((void**)&c->pf_concat, rows * D * 4) && al((void**)&c->pf_attn_raw, rows * D * 4) &&
+              al((void**)&c->pf_attn_norm, rows * D * 4) && al((void**)&c->pf_ff, rows * F * 4) &&
+              al((void**)&c->pf_ff_raw, rows * D * 4) && al((void**)&c->pf_rowoff, rows * 4) &&
+              al(&c->pf_scratch, scratch);
+    if (!ok) {
+        free_prefill(c);
+        return fail(DZ_E_NOMEM, "prefill buffers for %zu rows", rows);
+    }
+    c->pf_rows = rows;
+    DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)dz_prefill_att_smem(128)));
+    DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)dz_prefill_att_smem(64)));
+    return DZ_OK;
+}
+
+// Launches enqueue_prefill makes for T positions.
+static size_t prefill_launches(const dz_cuda_cache_t* c, size_t T) {
+    const dz_cuda_model_t* m = c->model;
+    const size_t S = prefill_group(c, T), groups = ((size_t)c->B + S - 1) / S;
+    size_t n = 2 + (size_t)qmv_launches(m->head, c->B);   // row offsets, ring state, head
+    for (size_t g = 0; g < groups; g++) {
+        const int R = (int)(std::min((size_t)c->B, (g + 1) * S) - g * S) * (int)T;
+        n += 2;   // embedding, gather
+        for (const auto& L : m->layers) {
+            n += L.fused_qkv ? qmv_launches(L.qkv, R)
+                             : qmv_launches(L.q, R) + qmv_launches(L.k, R) + qmv_launches(L.v, R);
+            n += qmv_launches(L.wo, R) + qmv_launches(L.w1, R) + qmv_launches(L.w2, R) + 3;   // attention, 2 LN
+        }
+    }
+    return n;
+}
+
+// Prefill of T positions of every sequence (ids_dev [B][ld], lens_dev [B]
+// positions per sequence or null for all T) into empty rings: all positions
+// of a group of sequences per layer pass, then the head on each sequence's
+// last position into c->logits. Returns the launches.
+static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long long ld, int T, const int* lens_dev) {
+    dz_cuda_model_t* m = c->model;
+    const int D = (int)m->desc.embedding_dim, F = 4 * D, V = (int)m->desc.vocab_size, H = (int)m->desc.num_heads;
+    const int hd = D / H, B = c->B, cap = c->cap;
+    cudaStream_t st = c->stream;
+    const int S = (int)prefill_group(c, (size_t)T);
+    int launches = 0;
+    {
+        const int rows = S * T;
+        dz_prefill_rowoff_kernel<<<(rows + 255) / 256, 256, 0, st>>>(c->pf_rowoff, rows, T, cap, D);
+        launches++;
+    }
+    for (int s0 = 0; s0 < B; s0 += S) {
+        const int ns = std::min(S, B - s0), R = ns * T;
+        const int* lens = lens_dev ? lens_dev + s0 : nullptr;
+        {
+            ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)R * D * 12, 0, st);
+            dz_prefill_embed_kernel<<<R, 128, 0, st>>>(ids_dev + (long long)s0 * ld, ld, T, m->emb, m->pe,
+                                                       m->pe_rows, c->pf_hidden, D, V);
+        }
+        launches++;
+        for (size_t l = 0; l < m->layers.size(); l++) {
+            DevLayer& L = m->layers[l];
+            float* Kl = c->keys + l * (size_t)B * cap * D + (size_t)s0 * cap * D;
+            float* Vl = c->values + l * (size_t)B * cap * D + (size_t)s0 * cap * D;
+            if (L.fused_qkv) {
+                QmvEpilogue ep = plain_epilogue(L.qkv, c->pf_q, D);
+                ep.nseg = 3;
+                ep.seg_start[0] = 0; ep.seg_start[1] = D; ep.seg_start[2] = 2 * D; ep.seg_start[3] = 3 * D;
+                ep.seg_ptr[1] = Kl; ep.seg_ld[1] = 0; ep.seg_row_off[1] = c->pf_rowoff;
+                ep.seg_ptr[2] = Vl; ep.seg_ld[2] = 0; ep.seg_row_off[2] = c->pf_rowoff;
+                launches += launch_qmv(L.qkv, c->pf_hidden, D, R, ep, st, c->pf_scratch, c->status);
+            } else {
+                QmvEpilogue eq = plain_epilogue(L.q, c->pf_q, D);
+                launches += launch_qmv(L.q, c->pf_hidden, D, R, eq, st, c->pf_scratch, c->status);
+                QmvEpilogue ek = plain_epilogue(L.k, Kl, 0);
+                ek.seg_row_off[0] = c->pf_rowoff;
+                launches += launch_qmv(L.k, c->pf_hidden, D, R, ek, st, c->pf_scratch, c->status);
+                QmvEpilogue ev = plain_epilogue(L.v, Vl, 0);
+                ev.seg_row_off[0] = c->pf_rowoff;
+                launches += launch_qmv(L.v, c->pf_hidden, D, R, ev, st, c->pf_scratch, c->status);
+            }
+            {
+                const double ctx_pairs = (double)ns * H * T * (T + 1) / 2.0;
+                ProfScope prof(DZ_KERNEL_ATTENTION, 8.0 * (double)R * D + 8.0 * (double)ns * T * D,
+                               4.0 * ctx_pairs * hd, st);
+                const dim3 grid((unsigned)((T + PF_QT - 1) / PF_QT), (unsigned)H, (unsigned)ns);
+                const size_t smem = dz_prefill_att_smem(hd);
+                if (hd == 128)
+                    dz_attention_prefill_kernel<4><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
+                                                                                  c->pf_concat, T, D, cap);
+                else if (hd == 64)
+                    dz_attention_prefill_kernel<2><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
+                                                                                  c->pf_concat, T, D, cap);
+                else
+                    dz_attention_prefill_kernel<1><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
+                                                                                  c->pf_concat, T, D, cap);
+            }
+            launches++;
+            QmvEpilogue eo = plain_epilogue(L.wo, c->pf_attn_raw, D);
+            launches += launch_qmv(L.wo, c->pf_concat, D, R, eo, st, c->pf_scratch, c->status);
+            {
+                ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * R * D + 8.0 * D, 0, st);
+                dz_layernorm_kernel<<<R, LN_THREADS, 0, st>>>(c->pf_attn_raw, c->pf_hidden, L.g1, L.be1,
+                                                              c->pf_attn_norm, D, 1e-6f);
+            }
+            launches++;
+            QmvEpilogue e1 = plain_epilogue(L.w1, c->pf_ff, F);
+            e1.bias = L.b1;
+            e1.relu = 1;
+            launches += launch_qmv(L.w1, c->pf_attn_norm, D, R, e1, st, c->pf_scratch, c->status);
+            QmvEpilogue e2 = plain_epilogue(L.w2, c->pf_ff_raw, D);
+            e2.bias = L.b2;
+            e2.residual = c->pf_attn_norm;
+            e2.ld_res = D;
+            launches += launch_qmv(L.w2, c->pf_ff, F, R, e2, st, c->pf_scratch, c->status);
+            {
+                ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * R * D + 8.0 * D, 0, st);
+                dz_layernorm_kernel<<<R, LN_THREADS, 0, st>>>(c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, D,
+                                                              1e-6f);
+            }
+            launches++;
+        }
+        dz_prefill_gather_kernel<<<ns, 256, 0, st>>>(c->pf_hidden, lens, T, D, c->hidden + (size_t)s0 * D);
+        launches++;
+    }
+    dz_prefill_ring_kernel<<<(B + 255) / 256, 256, 0, st>>>(c->start, c->length, c->total, lens_dev, T, B);
+    launches++;
+    QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
+    eh.bias = m->out_bias;
+    launches += launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status);
+    return launches;
+}
+
 // Generation jobs above this many launches are enqueued directly instead of
 // through a cached CUDA graph.
 constexpr size_t GRAPH_MAX_LAUNCHES = 40000;
@@ -1489,7 +1689,11 @@ static int enqueue_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t 
     }
     dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
     launches++;
-    for (size_t t = 0; t < plen; t++) launches += enqueue_step(c, prompts + t, (long long)plen);
+    if (use_batched_prefill(c, plen)) {
+        launches += enqueue_prefill(c, prompts, (long long)plen, (int)plen, nullptr);
+    } else {
+        for (size_t t = 0; t < plen; t++) launches += enqueue_step(c, prompts + t, (long long)plen);
+    }
     for (size_t i = 0; i < n_new; i++) {
         launches += enqueue_select(c, s, sampled ? c->rng : nullptr, out + i, (long long)n_new, c->tok);
         if (i + 1 < n_new) launches += enqueue_step(c, c->tok, 1);
@@ -1510,7 +1714,8 @@ extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t ple
         step += qmv_launches(L.wo, B) + qmv_launches(L.w1, B) + qmv_launches(L.w2, B) + 3;   // + attention, 2 LN
     }
     const size_t seeded = (s && s->strategy != 0 && s->temperature > 0.0f) ? 1 : 0;
-    return seeded + 1 + plen * step + n_new + (n_new ? n_new - 1 : 0) * step;
+    const size_t prefill = use_batched_prefill(c, plen) ? prefill_launches(c, plen) : plen * step;
+    return seeded + 1 + prefill + n_new + (n_new ? n_new - 1 : 0) * step;
 }
 
 extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
@@ -1521,6 +1726,7 @@ extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompt
     if (rc) return rc;
     DeviceGuard g(c->model->device);
     if ((rc = ensure_masked(c, s))) return rc;
+    if (!use_seqgen(c, s) && use_batched_prefill(c, plen) && (rc = ensure_prefill(c, plen))) return rc;
     if (s && s->n_masked)
         DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
     const bool sampled = seeds && s && s->strategy != 0 && s->temperature > 0.0f;
@@ -1594,6 +1800,57 @@ extern "C" int dz_cuda_generate(dz_cuda_cache_t* c, const uint32_t* prompts, siz
         cudaStreamSynchronize(c->stream);
         return fail(DZ_E_TIMEOUT, "generate: a weight-copy wait gave up on the device");
     }
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_cache_set_prefill(dz_cuda_cache_t* c, int mode) {
+    if (!c || mode < DZ_PREFILL_AUTO || mode > DZ_PREFILL_BATCHED) return fail(DZ_E_INVALID, "bad prefill mode");
+    if (mode == DZ_PREFILL_BATCHED && !prefill_eligible(c))
+        return fail(DZ_E_UNSUPPORTED, "batched prefill needs a head dimension of 32, 64 or 128");
+    if (mode != c->prefill) {
+        DeviceGuard g(c->model->device);
+        clear_graphs(c);
+    }
+    c->prefill = mode;
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_prefill(dz_cuda_cache_t* c, const uint32_t* ids, const uint32_t* lens, size_t prompt_len,
+                               float* logits_out) {
+    if (!c || !ids || prompt_len == 0) return fail(DZ_E_INVALID, "prefill: null ids or empty prompt");
+    if (prompt_len > (size_t)c->cap) return fail(DZ_E_INVALID, "prefill: prompt longer than the cache capacity");
+    if (!prefill_eligible(c)) return fail(DZ_E_UNSUPPORTED, "batched prefill needs a head dimension of 32, 64 or 128");
+    const size_t B = c->B;
+    std::vector<int> lv;
+    if (lens) {
+        lv.resize(B);
+        for (size_t b = 0; b < B; b++) {
+            if (lens[b] == 0 || lens[b] > prompt_len) return fail(DZ_E_INVALID, "prefill: lens must be 1..prompt_len");
+            lv[b] = (int)lens[b];
+        }
+    }
+    DeviceGuard g(c->model->device);
+    int rc = ensure_prefill(c, prompt_len);
+    if (rc) return rc;
+    if (B * prompt_len > c->pf_ids_cap) {
+        cudaFree(c->pf_ids);
+        cudaFree(c->pf_lens);
+        c->pf_ids = nullptr;
+        c->pf_lens = nullptr;
+        c->pf_ids_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->pf_ids, B * prompt_len * 4));
+        DZ_CUDA(cudaMalloc(&c->pf_lens, B * 4));
+        c->pf_ids_cap = B * prompt_len;
+    }
+    DZ_CUDA(cudaMemcpyAsync(c->pf_ids, ids, B * prompt_len * 4, cudaMemcpyHostToDevice, c->stream));
+    if (lens) DZ_CUDA(cudaMemcpyAsync(c->pf_lens, lv.data(), B * 4, cudaMemcpyHostToDevice, c->stream));
+    dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
+    enqueue_prefill(c, c->pf_ids, (long long)prompt_len, (int)prompt_len, lens ? c->pf_lens : nullptr);
+    DZ_CUDA(cudaGetLastError());
+    if (logits_out)
+        DZ_CUDA(cudaMemcpyAsync(logits_out, c->logits, B * c->model->desc.vocab_size * 4, cudaMemcpyDeviceToHost,
+                                c->stream));
+    DZ_CUDA(cudaStreamSynchronize(c->stream));
     return DZ_OK;
 }
 

@@ -180,6 +180,31 @@ typedef struct {
     double flops;
 } dz_kernel_stat_t;
 
+/* Prefill policy of the layered path (dz_cuda_generate and
+ * dz_cuda_prefill). TOKENS feeds the prompt one position per step through
+ * dz_cuda_forward_tokens' step, as the reference's generation loop does
+ * (src/cli/generation.c:231-238). BATCHED runs every prompt position of a
+ * group of sequences in one pass per layer: one GEMM over all rows per
+ * projection and a causal attention over each prompt, the arithmetic of
+ * model_forward_hidden_masked (src/core/transformer.c:392-519). AUTO picks
+ * BATCHED for models with d_model >= 512 and a head dimension of 32, 64 or
+ * 128. */
+#define DZ_PREFILL_AUTO 0
+#define DZ_PREFILL_TOKENS 1
+#define DZ_PREFILL_BATCHED 2
+int dz_cuda_cache_set_prefill(dz_cuda_cache_t *cache, int mode);
+
+/* Batched prefill of every sequence from an empty ring: ids [batch x
+ * prompt_len] (host), lens [batch] positions per sequence (1..prompt_len) or
+ * NULL for all, logits_out [batch x V] (host) of each sequence's last
+ * position or NULL. Leaves each ring holding its prompt, ready for
+ * dz_cuda_forward_tokens / dz_cuda_select. Replaces the per-token prefill
+ * loop of generation_decode_with_options (src/cli/generation.c:231-238) and
+ * model_forward_hidden_masked's full-prefix pass (src/core/transformer.c:
+ * 392-519). Synchronous. */
+int dz_cuda_prefill(dz_cuda_cache_t *cache, const uint32_t *ids, const uint32_t *lens, size_t prompt_len,
+                    float *logits_out);
+
 /* Runs one dz_cuda_generate_async loop eagerly (no graph) with CUDA events
  * around every launch on the cache's stream, synchronises, and fills
  * stats[kind] for kind < n_stats. No counterpart in the reference (its

@@ -224,3 +224,61 @@ def test_large_batch_tensor_core_path(gpu, oracle, bits):
     bad = _check_streams(toks, ref)
     assert len(bad) <= 1, bad   # at most one greedy near-tie among the 24 streams
     cache.close(); model.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("hd", [32, 64, 128])
+def test_batched_prefill_matches_token_prefill(gpu, oracle, bits, hd):
+    """dz_cuda_prefill (all prompt positions per layer pass, causal attention
+    over each prompt) against the per-token prefill and the oracle: last-position
+    logits within tolerance for full and ragged prompts, and generation through
+    both prefill policies giving the oracle's greedy streams."""
+    H = 512 // hd
+    spec = Spec(900, 512, H, 2, 64)
+    recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 50 + hd), bits)
+    model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, bits, 2) for (_, k, r, c, f, s, p) in recs])
+    B, T = 5, 21
+    rng = np.random.RandomState(hd + bits)
+    prompts = rng.randint(0, 256, size=(B, T)).astype(np.uint32)
+    lens = np.array([21, 7, 13, 1, 20], np.uint32)
+    om = oracle.model(spec, flat)
+    ref = []
+    for b in range(B):
+        om.reset()
+        for t in range(int(lens[b])):
+            r = om.forward_token(prompts[b, t])
+        ref.append(r)
+    cache = gpu.KVCache(model, B, 64)
+    got = cache.prefill(prompts, lens)
+    for b in range(B):
+        assert _rel(got[b], ref[b]) <= LOGIT_TOL, (b, _rel(got[b], ref[b]))
+    # the rings hold each prompt: one decode step continues every sequence
+    nxt = rng.randint(0, 256, size=B).astype(np.uint32)
+    step = cache.forward_tokens(nxt)
+    for b in range(B):
+        om.reset()
+        for t in range(int(lens[b])):
+            om.forward_token(prompts[b, t])
+        r = om.forward_token(nxt[b])
+        assert _rel(step[b], r) <= LOGIT_TOL, (b, _rel(step[b], r))
+    samp = gpu.Sampling(gpu.GREEDY)
+    outs = []
+    for mode in (gpu.PREFILL_TOKENS, gpu.PREFILL_BATCHED):
+        cache.set_prefill(mode)
+        outs.append(cache.generate(prompts, 6, samp))
+    gref, _ = om.generate(prompts, 6, 0, 0.0, 0, 0.0, None)
+    for o in outs:
+        assert len(_check_streams(o, gref)) <= 1
+    cache.close(); model.close()
+
+
+def test_batched_prefill_rejects_bad_lengths(gpu, oracle):
+    spec = Spec(300, 256, 4, 1, 16)
+    recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 4), 8)
+    model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, 8, 2) for (_, k, r, c, f, s, p) in recs])
+    cache = gpu.KVCache(model, 2, 16)
+    with pytest.raises(gpu.DzError):
+        cache.prefill(np.zeros((2, 5), np.uint32), np.array([0, 5], np.uint32))
+    with pytest.raises(gpu.DzError):
+        cache.prefill(np.zeros((2, 20), np.uint32))
+    cache.close(); model.close()
