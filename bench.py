@@ -335,12 +335,13 @@ def run_dz(args, wl):
         tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
         dev_ms, e2e_ms = float(t[0]), float(t[1])
 
-    # per-kernel-class CUDA-event timing of one eager job (a 16 + 8 token job at
-    # the full batch when the real one is too long to bracket every launch)
+    # per-kernel-class CUDA-event timing of one eager job (the full prompt + 8
+    # decode steps at the full batch when the real job is too long to bracket
+    # every launch)
     nk = len(_native.KERNEL_CLASSES) + len(_native.FUSED_PHASES)
     stats = (_native.DzKernelStat * nk)()
     long_job = cache.generate_launches(wl.prompt_len, wl.n_new, samp) > 20000
-    p_plen, p_new = (16, 8) if long_job else (wl.prompt_len, wl.n_new)
+    p_plen, p_new = (wl.prompt_len, 8) if long_job else (wl.prompt_len, wl.n_new)
     _native.check(L.dz_cuda_profile_generate(cache.handle, pd.data_ptr(), p_plen, p_new,
                                              ctypes.byref(samp.c), seeds_ptr, od.data_ptr(), stats, nk),
                   "profile_generate")

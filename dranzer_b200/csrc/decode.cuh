@@ -156,6 +156,109 @@ __global__ void __launch_bounds__(ATT_THREADS) dz_attention_decode_kernel(
     }
 }
 
+// attention_head_forward_token for head dimensions of 64 / 128 at long
+// contexts, streaming the K / V rows at bandwidth: one block per (head,
+// sequence), four warps; warp w takes keys w*8 .. w*8+7, then +32, ...; lanes
+// hold HDW consecutive elements of the head dimension, so every K or V row is
+// one coalesced 256- or 512-byte read, and eight keys are in flight per warp.
+// The softmax runs online per warp (running max and sum, rescaled) and the
+// four warps combine in shared memory, so rounding differs from the
+// reference's two-pass softmax within fp32 noise.
+constexpr int ATT2_THREADS = 128;
+constexpr int ATT2_KEYS = 8;
+
+template <int HDW>   // head_dim / 32: 2 or 4
+__global__ void __launch_bounds__(ATT2_THREADS) dz_attention_decode2_kernel(
+    const float* __restrict__ q, const float* __restrict__ keys, const float* __restrict__ values,
+    const int* __restrict__ start_arr, const int* __restrict__ ctx_arr, float* __restrict__ out, int dim,
+    int capacity) {
+    constexpr int HD = HDW * 32;
+    constexpr int NW = ATT2_THREADS / 32;
+    __shared__ float sm_m[NW], sm_l[NW];
+    __shared__ float sm_o[NW][HD];
+    const int h = blockIdx.x, b = blockIdx.y;
+    const int ctx = ctx_arr[b], start = start_arr[b];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* K = keys + (long long)b * capacity * dim + h * HD + lane * HDW;
+    const float* V = values + (long long)b * capacity * dim + h * HD + lane * HDW;
+    float qv[HDW];
+#pragma unroll
+    for (int c = 0; c < HDW; c++) qv[c] = q[(long long)b * dim + h * HD + lane * HDW + c];
+    const float denom = sqrtf((float)HD);
+    float m = -3.402823466e38f, l = 0.0f, o[HDW];
+#pragma unroll
+    for (int c = 0; c < HDW; c++) o[c] = 0.0f;
+    for (int j0 = warp * ATT2_KEYS; j0 < ctx; j0 += NW * ATT2_KEYS) {
+        float kv[ATT2_KEYS][HDW], sc[ATT2_KEYS];
+#pragma unroll
+        for (int u = 0; u < ATT2_KEYS; u++) {
+            const int j = j0 + u;
+            int phys = start + j;
+            if (phys >= capacity) phys -= capacity;
+            const float* kr = K + (long long)phys * dim;
+#pragma unroll
+            for (int c = 0; c < HDW; c++) kv[u][c] = j < ctx ? kr[c] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < ATT2_KEYS; u++) {
+            float d = 0.0f;
+#pragma unroll
+            for (int c = 0; c < HDW; c++) d = fmaf(qv[c], kv[u][c], d);
+            sc[u] = d;
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int u = 0; u < ATT2_KEYS; u++) sc[u] += __shfl_xor_sync(0xffffffffu, sc[u], off);
+        float tmax = m;
+#pragma unroll
+        for (int u = 0; u < ATT2_KEYS; u++) {
+            sc[u] = sc[u] / denom;
+            if (j0 + u < ctx) tmax = fmaxf(tmax, sc[u]);
+        }
+        const float corr = expf(m - tmax);
+        l *= corr;
+#pragma unroll
+        for (int c = 0; c < HDW; c++) o[c] *= corr;
+        m = tmax;
+#pragma unroll
+        for (int u = 0; u < ATT2_KEYS; u++) {
+            const int j = j0 + u;
+            if (j >= ctx) break;
+            const float p = expf(sc[u] - m);
+            l += p;
+            int phys = start + j;
+            if (phys >= capacity) phys -= capacity;
+            const float* vr = V + (long long)phys * dim;
+#pragma unroll
+            for (int c = 0; c < HDW; c++) o[c] = fmaf(p, vr[c], o[c]);
+        }
+    }
+    if (lane == 0) {
+        sm_m[warp] = m;
+        sm_l[warp] = l;
+    }
+#pragma unroll
+    for (int c = 0; c < HDW; c++) sm_o[warp][lane * HDW + c] = o[c];
+    __syncthreads();
+    if (warp == 0) {
+        float M = sm_m[0];
+        for (int w = 1; w < NW; w++) M = fmaxf(M, sm_m[w]);
+        float L = 0.0f, acc[HDW];
+#pragma unroll
+        for (int c = 0; c < HDW; c++) acc[c] = 0.0f;
+        for (int w = 0; w < NW; w++) {
+            const float f = sm_l[w] > 0.0f ? expf(sm_m[w] - M) : 0.0f;
+            L += sm_l[w] * f;
+#pragma unroll
+            for (int c = 0; c < HDW; c++) acc[c] = fmaf(sm_o[w][lane * HDW + c], f, acc[c]);
+        }
+        const float inv = 1.0f / L;
+#pragma unroll
+        for (int c = 0; c < HDW; c++) out[(long long)b * dim + h * HD + lane * HDW + c] = acc[c] * inv;
+    }
+}
+
 constexpr int LN_THREADS = 256;
 
 // layer_normalize (src/core/tensor_ops.c:88-111), eps 1e-6: mean, biased

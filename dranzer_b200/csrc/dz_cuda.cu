@@ -1311,8 +1311,15 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             // only when the profiler cannot read it) + q + output
             ProfScope prof(DZ_KERNEL_ATTENTION, c->prof_ctx_bytes_per_layer + 8.0 * B * D,
                            c->prof_ctx_flops_per_layer, st);
-            dz_attention_decode_kernel<<<dim3(H, B), ATT_THREADS, att_smem, st>>>(c->q, Kl, Vl, c->start, c->ctx,
-                                                                                 c->concat, D, hd, cap);
+            if (hd == 128)
+                dz_attention_decode2_kernel<4><<<dim3(H, B), ATT2_THREADS, 0, st>>>(c->q, Kl, Vl, c->start, c->ctx,
+                                                                                   c->concat, D, cap);
+            else if (hd == 64)
+                dz_attention_decode2_kernel<2><<<dim3(H, B), ATT2_THREADS, 0, st>>>(c->q, Kl, Vl, c->start, c->ctx,
+                                                                                   c->concat, D, cap);
+            else
+                dz_attention_decode_kernel<<<dim3(H, B), ATT_THREADS, att_smem, st>>>(c->q, Kl, Vl, c->start,
+                                                                                     c->ctx, c->concat, D, hd, cap);
         }
         launches++;
         QmvEpilogue eo = plain_epilogue(L.wo, c->attn_raw, D);

@@ -48,105 +48,187 @@ __global__ void dz_prefill_rowoff_kernel(int* __restrict__ row_off, int rows, in
 
 constexpr int PF_QT = 64;        // queries per block
 constexpr int PF_KT = 32;        // keys per tile
-constexpr int PF_THREADS = 256;  // 8 warps x 8 queries
-constexpr int PF_QW = PF_QT / (PF_THREADS / 32);
+constexpr int PF_THREADS = 256;
+constexpr int PF_PLD = PF_QT + 4;   // transposed probability tile row stride
 
-// Shared memory of dz_attention_prefill_kernel for head dimension hd.
+// Shared memory of dz_attention_prefill_kernel for head dimension hd: the
+// query tile, two K / V tile buffers, the probability tile, softmax state.
 __host__ __device__ constexpr size_t dz_prefill_att_smem(int hd) {
-    return ((size_t)PF_QT * hd + 2 * (size_t)PF_KT * (hd + 1)) * sizeof(float);
+    return ((size_t)PF_QT * (hd + 4) + 4 * (size_t)PF_KT * (hd + 4) + (size_t)PF_KT * PF_PLD + 3 * PF_QT) *
+           sizeof(float);
 }
 
+__device__ __forceinline__ void pf_cp_async16(void* dst, const void* src, bool valid) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    const int n = valid ? 16 : 0;   // zero-fill rows past the block's last query
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void pf_cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void pf_cp_wait_all_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+__device__ __forceinline__ void pf_cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Causal attention over one prompt, for queries [q0, q0 + PF_QT) of one
-// (head, sequence): score_j = (q . k_j) / sqrtf(hd) for j <= t, softmax, o =
-// sum_j p_j v_j, with the keys and values read from ring slots 0..T-1. The
-// softmax runs online over key tiles (running max and sum, rescaled), so its
-// rounding differs from the reference's two-pass form within fp32 noise.
-// Warp w owns queries q0 + w*PF_QW .. +PF_QW; lane = key within a tile for the
-// scores, lane = head-dimension element (hd/32 each) for the output.
+// (head, sequence): score_j = (q . k_j) / sqrtf(hd) for j <= t, softmax,
+// o = sum_j p_j v_j, keys and values read from ring slots 0..T-1. K / V tiles
+// of 32 rows are double-buffered with cp.async (the next tile loads while the
+// current one is used). The score and P.V products of each tile are
+// register-tiled SIMT GEMMs on shared memory (scores: 4 queries x 2 keys per
+// thread, four head elements per 128-bit load; P.V: 8 queries x hd/32
+// elements per thread), and the softmax runs online over the tiles (running
+// max and sum, rescaled), so its rounding differs from the reference's
+// two-pass form within fp32 noise.
 template <int HDW>   // head_dim / 32
 __global__ void __launch_bounds__(PF_THREADS) dz_attention_prefill_kernel(
     const float* __restrict__ q, const float* __restrict__ keys, const float* __restrict__ values,
     const int* __restrict__ lens, float* __restrict__ out, int T, int dim, int capacity) {
     constexpr int HD = HDW * 32;
-    extern __shared__ float pf_smem[];
-    float* qs = pf_smem;                         // [PF_QT][HD]
-    float* ks = qs + PF_QT * HD;                 // [PF_KT][HD + 1]
-    float* vs = ks + PF_KT * (HD + 1);           // [PF_KT][HD + 1]
+    constexpr int LD = HD + 4;               // row stride of the Q / K / V tiles (floats)
+    constexpr int CH = HD / 4;               // 16-byte chunks per row
+    extern __shared__ __align__(16) float pf_smem[];
+    float* qs = pf_smem;                     // [PF_QT][LD]
+    float* kb = qs + PF_QT * LD;             // [2][PF_KT][LD]
+    float* vb = kb + 2 * PF_KT * LD;         // [2][PF_KT][LD]
+    float* pt = vb + 2 * PF_KT * LD;         // [PF_KT][PF_PLD] probabilities transposed
+    float* corr_s = pt + PF_KT * PF_PLD;     // [PF_QT]
+    float* m_s = corr_s + PF_QT;             // [PF_QT]
+    float* l_s = m_s + PF_QT;                // [PF_QT]
     const int q0 = blockIdx.x * PF_QT, h = blockIdx.y, s = blockIdx.z;
     const int len = lens ? lens[s] : T;
     if (q0 >= len) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tid = threadIdx.x;
     const float* K = keys + (long long)s * capacity * dim + h * HD;
     const float* Vv = values + (long long)s * capacity * dim + h * HD;
     const long long row0 = (long long)s * T;
-    for (int i = threadIdx.x; i < PF_QT * HD; i += PF_THREADS) {
-        const int qi = i / HD, e = i - qi * HD;
-        const int t = q0 + qi;
-        qs[i] = t < len ? q[(row0 + t) * dim + h * HD + e] : 0.0f;
-    }
-    const float denom = sqrtf((float)HD);
-    float m[PF_QW], l[PF_QW], o[PF_QW][HDW];
-#pragma unroll
-    for (int i = 0; i < PF_QW; i++) {
-        m[i] = -3.402823466e38f;
-        l[i] = 0.0f;
-#pragma unroll
-        for (int c = 0; c < HDW; c++) o[i][c] = 0.0f;
-    }
-    const int tq_last = min(q0 + PF_QT, len) - 1;   // last query of this block
-    for (int j0 = 0; j0 <= tq_last; j0 += PF_KT) {
-        __syncthreads();   // previous tile consumed (and qs written, first time)
-        for (int i = threadIdx.x; i < PF_KT * HD; i += PF_THREADS) {
-            const int kj = i / HD, e = i - kj * HD;
+    const int tq_last = min(q0 + PF_QT, len) - 1;
+    auto load_tile = [&](int j0, int buf) {
+        for (int i = tid; i < PF_KT * CH; i += PF_THREADS) {
+            const int kj = i / CH, c = i - kj * CH;
             const int j = j0 + kj;
             const bool in = j <= tq_last;
-            ks[kj * (HD + 1) + e] = in ? K[(long long)j * dim + e] : 0.0f;
-            vs[kj * (HD + 1) + e] = in ? Vv[(long long)j * dim + e] : 0.0f;
+            const int jj = in ? j : 0;
+            pf_cp_async16(kb + (buf * PF_KT + kj) * LD + 4 * c, K + (long long)jj * dim + 4 * c, in);
+            pf_cp_async16(vb + (buf * PF_KT + kj) * LD + 4 * c, Vv + (long long)jj * dim + 4 * c, in);
         }
-        __syncthreads();
+        pf_cp_commit();
+    };
+    load_tile(0, 0);
+    for (int i = tid; i < PF_QT * CH; i += PF_THREADS) {
+        const int qi = i / CH, c = i - qi * CH;
+        const int t = q0 + qi;
+        const float4 v = t < len ? *reinterpret_cast<const float4*>(q + (row0 + t) * dim + h * HD + 4 * c)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(qs + qi * LD + 4 * c) = v;
+    }
+    if (tid < PF_QT) {
+        m_s[tid] = -3.402823466e38f;
+        l_s[tid] = 0.0f;
+    }
+    const float denom = sqrtf((float)HD);
+    const int sqg = tid >> 4, skg = tid & 15;          // scores: 16 x 4 queries, 16 x 2 keys
+    const int oqg = tid >> 5, oe = (tid & 31) * HDW;   // P.V: 8 x 8 queries, 32 x HDW elements
+    float o[8][HDW];
 #pragma unroll
-        for (int i = 0; i < PF_QW; i++) {
-            const int qi = warp * PF_QW + i;
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int c = 0; c < HDW; c++) o[i][c] = 0.0f;
+    int buf = 0;
+    for (int j0 = 0; j0 <= tq_last; j0 += PF_KT, buf ^= 1) {
+        if (j0 + PF_KT <= tq_last) {
+            load_tile(j0 + PF_KT, buf ^ 1);   // prefetch the next tile
+            pf_cp_wait_all_but_one();
+        } else {
+            pf_cp_wait_all();
+        }
+        __syncthreads();   // tile `buf` landed for everyone; qs, m_s, l_s written
+        const float* ks = kb + buf * PF_KT * LD;
+        const float* vs = vb + buf * PF_KT * LD;
+        float sc[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) sc[i][0] = sc[i][1] = 0.0f;
+#pragma unroll 4
+        for (int e = 0; e < HD; e += 4) {
+            float4 qv[4], kv[2];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const float4*>(qs + (sqg * 4 + i) * LD + e);
+#pragma unroll
+            for (int kk = 0; kk < 2; kk++) kv[kk] = *reinterpret_cast<const float4*>(ks + (skg * 2 + kk) * LD + e);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int kk = 0; kk < 2; kk++) {
+                    float a2 = sc[i][kk];
+                    a2 = fmaf(qv[i].x, kv[kk].x, a2);
+                    a2 = fmaf(qv[i].y, kv[kk].y, a2);
+                    a2 = fmaf(qv[i].z, kv[kk].z, a2);
+                    a2 = fmaf(qv[i].w, kv[kk].w, a2);
+                    sc[i][kk] = a2;
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int qi = sqg * 4 + i;
             const int t = q0 + qi;
-            if (t >= len || j0 > t) continue;   // warp-uniform
-            // score of key j0 + lane
-            const float* qr = qs + qi * HD;
-            const float* kr = ks + lane * (HD + 1);
-            float sc = 0.0f;
-#pragma unroll 8
-            for (int e = 0; e < HD; e++) sc = fmaf(qr[e], kr[e], sc);
-            sc = sc / denom;
-            const bool valid = j0 + lane <= t;
-            float tmax = valid ? sc : -3.402823466e38f;
+            float tmax = -3.402823466e38f;
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-            const float mnew = fmaxf(m[i], tmax);
-            const float corr = expf(m[i] - mnew);
-            const float p = valid ? expf(sc - mnew) : 0.0f;
-            float psum = p;
+            for (int kk = 0; kk < 2; kk++) {
+                const int j = j0 + skg * 2 + kk;
+                sc[i][kk] = sc[i][kk] / denom;
+                if (j <= t && t < len) tmax = fmaxf(tmax, sc[i][kk]);
+            }
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-            l[i] = l[i] * corr + psum;
-            m[i] = mnew;
+            for (int off = 8; off >= 1; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+            const float mold = m_s[qi];
+            const float mnew = fmaxf(mold, tmax);
+            float ps = 0.0f;
 #pragma unroll
-            for (int c = 0; c < HDW; c++) o[i][c] *= corr;
-            const int nk = min(PF_KT, t - j0 + 1);
-            for (int kj = 0; kj < nk; kj++) {
-                const float pk = __shfl_sync(0xffffffffu, p, kj);
-                const float* vr = vs + kj * (HD + 1);
+            for (int kk = 0; kk < 2; kk++) {
+                const int j = j0 + skg * 2 + kk;
+                const float p = (j <= t && t < len) ? expf(sc[i][kk] - mnew) : 0.0f;
+                pt[(skg * 2 + kk) * PF_PLD + qi] = p;
+                ps += p;
+            }
 #pragma unroll
-                for (int c = 0; c < HDW; c++) o[i][c] = fmaf(pk, vr[lane + 32 * c], o[i][c]);
+            for (int off = 8; off >= 1; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+            __syncwarp();
+            if (skg == 0) {
+                const float cf = expf(mold - mnew);
+                corr_s[qi] = cf;
+                l_s[qi] = l_s[qi] * cf + ps;
+                m_s[qi] = mnew;
             }
         }
+        __syncthreads();
+        float cf[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) cf[i] = corr_s[oqg * 8 + i];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int c = 0; c < HDW; c++) o[i][c] *= cf[i];
+        const int nk = min(PF_KT, tq_last - j0 + 1);
+        for (int k = 0; k < nk; k++) {
+            const float4 pa = *reinterpret_cast<const float4*>(pt + k * PF_PLD + oqg * 8);
+            const float4 pb = *reinterpret_cast<const float4*>(pt + k * PF_PLD + oqg * 8 + 4);
+            const float pr[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+            float vv[HDW];
+#pragma unroll
+            for (int c = 0; c < HDW; c++) vv[c] = vs[k * LD + oe + c];
+#pragma unroll
+            for (int i = 0; i < 8; i++)
+#pragma unroll
+                for (int c = 0; c < HDW; c++) o[i][c] = fmaf(pr[i], vv[c], o[i][c]);
+        }
+        __syncthreads();   // pt, corr_s and tile `buf` consumed before they are rewritten
     }
 #pragma unroll
-    for (int i = 0; i < PF_QW; i++) {
-        const int t = q0 + warp * PF_QW + i;
+    for (int i = 0; i < 8; i++) {
+        const int qi = oqg * 8 + i;
+        const int t = q0 + qi;
         if (t >= len) continue;
-        const float inv = 1.0f / l[i];
+        const float inv = 1.0f / l_s[qi];
         float* orow = out + (row0 + t) * dim + h * HD;
 #pragma unroll
-        for (int c = 0; c < HDW; c++) orow[lane + 32 * c] = o[i][c] * inv;
+        for (int c = 0; c < HDW; c++) orow[oe + c] = o[i][c] * inv;
     }
 }
 
