@@ -25,7 +25,7 @@ from ._native import (DzBundleInfo, DzBundleMeta, DzError, DzModelDesc, DzSampli
 __all__ = ["GRAN_TENSOR", "GRAN_ROW", "GRAN_COLUMN", "GREEDY", "TOPK", "TOPP", "STREAM_INIT",
            "STREAM_DROPOUT", "STREAM_SAMPLING", "STREAM_TESTING", "DzError", "available",
            "rng_stream", "synth_gaussian", "synth_prompt_ids", "quantized_scale_count",
-           "quantized_packed_size", "quantize_pack", "quantize_unpack", "positional_encoding", "fnv1a",
+           "quantized_packed_size", "quantize_pack", "quantize_unpack", "quantized_slice", "positional_encoding", "fnv1a",
            "QuantizedWeightMatrix", "matmul_quantized_weight", "Bundle", "save_quantized_bundle",
            "minimal_tokenizer", "model_tensor_layout", "Sampling", "Model", "KVCache"]
 
@@ -103,6 +103,20 @@ def quantize_pack(values, bits, granularity=GRAN_COLUMN):
     if lib().dz_quantize_pack(_p(w), rows, cols, bits, granularity, _p(scales), ns, _p(packed), nb) != 0:
         raise ValueError("quantize_pack rejected the input (non-finite value or bad arguments)")
     return scales, packed
+
+
+def quantized_slice(scales, packed, rows, cols, bits, granularity, axis, start, count):
+    """Rows (axis 0) or columns (axis 1) [start, start + count) of a quantized
+    matrix as (scales, packed) of its own (dz_quantized_slice)."""
+    s = np.ascontiguousarray(scales, np.float32)
+    p = np.ascontiguousarray(packed, np.uint8)
+    r2, c2 = (count, cols) if axis == 0 else (rows, count)
+    so = np.empty(quantized_scale_count(r2, c2, granularity), np.float32)
+    po = np.empty(quantized_packed_size(r2 * c2, bits), np.uint8)
+    if lib().dz_quantized_slice(_p(s), s.size, _p(p), p.size, rows, cols, bits, granularity, axis, start, count,
+                                _p(so), _p(po)) != 0:
+        raise ValueError("quantized_slice: bad arguments")
+    return so, po
 
 
 def quantize_unpack(scales, packed, rows, cols, bits, granularity=GRAN_COLUMN):
@@ -282,22 +296,37 @@ class Sampling:
 class Model:
     """A bundle's parameters as codes on one device (dz_cuda_model_create)."""
 
-    def __init__(self, desc, blobs, device=0, keepalive=None):
+    def __init__(self, desc, blobs, device=0, keepalive=None, tp=None):
+        """tp: None, or (rank, world, nccl_id bytes) for one tensor-parallel
+        shard (dz_cuda_model_create_tp; collective over the ranks)."""
         self.desc = _desc(desc)
         self.device = device
         self._keep = keepalive
         arr = (DzTensorBlob * len(blobs))(*blobs)
         h = ctypes.c_void_p()
-        check(lib().dz_cuda_model_create(ctypes.byref(self.desc), arr, len(blobs), device, ctypes.byref(h)),
-              "model_create")
+        if tp is None:
+            check(lib().dz_cuda_model_create(ctypes.byref(self.desc), arr, len(blobs), device, ctypes.byref(h)),
+                  "model_create")
+        else:
+            rank, world, uid = tp
+            idb = (ctypes.c_uint8 * 128).from_buffer_copy(bytes(uid))
+            check(lib().dz_cuda_model_create_tp(ctypes.byref(self.desc), arr, len(blobs), device, rank, world, idb,
+                                                ctypes.byref(h)), "model_create_tp")
         self.handle = h.value
 
-    @classmethod
-    def from_bundle(cls, bundle, device=0):
-        return cls(bundle.desc, list(bundle.tensors), device, keepalive=bundle)
+    @staticmethod
+    def tp_unique_id():
+        """NCCL unique id (128 bytes) for dz_cuda_model_create_tp, made on one rank."""
+        buf = (ctypes.c_uint8 * 128)()
+        check(lib().dz_cuda_tp_unique_id(buf), "tp_unique_id")
+        return bytes(buf)
 
     @classmethod
-    def from_arrays(cls, desc, tensors, device=0):
+    def from_bundle(cls, bundle, device=0, tp=None):
+        return cls(bundle.desc, list(bundle.tensors), device, keepalive=bundle, tp=tp)
+
+    @classmethod
+    def from_arrays(cls, desc, tensors, device=0, tp=None):
         """tensors: per tensor (kind, rows, cols, f32 | None, scales | None, packed | None, bits, gran)."""
         keep, blobs = [], []
         for kind, rows, cols, f32, scales, packed, bits, gran in tensors:
@@ -310,7 +339,7 @@ class Model:
                 packed = np.ascontiguousarray(packed, np.uint8)
                 keep += [scales, packed]
                 blobs.append(_blob(kind, rows, cols, bits, gran, scales, packed))
-        return cls(desc, blobs, device, keepalive=keep)
+        return cls(desc, blobs, device, keepalive=keep, tp=tp)
 
     @property
     def step_bytes(self):

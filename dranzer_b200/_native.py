@@ -68,6 +68,7 @@ SIGNATURES = {
     "dz_rng_next": (U64, [P]),
     "dz_rng_unit": (F64, [P]),
     "dz_synth_gaussian": (None, [P, P, SZ, F64]),
+    "dz_quantized_slice": (I32, [P, SZ, P, SZ, SZ, SZ, I32, I32, I32, SZ, SZ, P, P]),
     "dz_synth_prompt_ids": (None, [P, P, SZ, U32, P, SZ]),
     "dz_quantized_scale_count": (I32, [SZ, SZ, I32, P]),
     "dz_quantized_packed_size": (I32, [SZ, I32, P]),
@@ -114,6 +115,8 @@ SIGNATURES = {
     "dz_cuda_profile_generate": (I32, [P, P, SZ, SZ, P, P, P, P, SZ]),
     "dz_cuda_cache_set_path": (I32, [P, I32]),
     "dz_cuda_cache_set_prefill": (I32, [P, I32]),
+    "dz_cuda_tp_unique_id": (I32, [P]),
+    "dz_cuda_model_create_tp": (I32, [P, P, SZ, I32, I32, I32, P, P]),
     "dz_cuda_prefill": (I32, [P, P, P, SZ, P]),
     "dz_cuda_cache_uses_fused": (I32, [P, P]),
 }

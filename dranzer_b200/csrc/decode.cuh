@@ -25,7 +25,7 @@ struct RingState {
 // in the exp(-x ln 10000) form the host table uses.
 __global__ void dz_step_begin_kernel(RingState rs, const uint32_t* __restrict__ tokens, long long tok_stride,
                                      const float* __restrict__ emb, const float* __restrict__ pe,
-                                     long long pe_rows, float* __restrict__ hidden, int dim, int vocab,
+                                     long long pe_rows, float* __restrict__ hidden, int dim, int kv_dim, int vocab,
                                      int capacity) {
     const int b = blockIdx.x;
     const int len = rs.length[b], start = rs.start[b];
@@ -58,7 +58,7 @@ __global__ void dz_step_begin_kernel(RingState rs, const uint32_t* __restrict__ 
     if (threadIdx.x == 0) {
         rs.slot[b] = slot;
         rs.ctx[b] = ctx;
-        rs.row_off[b] = slot * dim;
+        rs.row_off[b] = slot * kv_dim;   // this rank's K / V row width
         rs.start[b] = new_start;
         rs.length[b] = len < capacity ? len + 1 : len;
         rs.total[b] = pos + 1;

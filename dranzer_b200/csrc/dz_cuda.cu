@@ -4,6 +4,8 @@
 #include "dz_host.h"
 
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <atomic>
 #include <cstdarg>
@@ -799,11 +801,43 @@ struct dz_cuda_model {
     SeqLayer* seq_layers = nullptr;   // device array [L]
     SeqMat seq_head{};
     std::vector<void*> seq_blobs;
+    // tensor parallelism over heads / FFN columns (1 rank: the whole model)
+    int tp_rank = 0, tp_world = 1;
+    int Hl = 0, dl = 0, Fl = 0;   // local heads, attention width Hl*hd, FFN width F/world
+    ncclComm_t comm = nullptr;
 };
+
+// NCCL, loaded at run time (the copy the process already holds, else the
+// system's libnccl.so.2), so the library has no link-time dependency on it.
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*);
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    const char* (*error_string)(ncclResult_t);
+};
+static const NcclApi* nccl_api() {
+    static NcclApi api;
+    static bool ok = false;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.get_unique_id = reinterpret_cast<decltype(api.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+        api.comm_init_rank = reinterpret_cast<decltype(api.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+        api.all_reduce = reinterpret_cast<decltype(api.all_reduce)>(dlsym(h, "ncclAllReduce"));
+        api.comm_destroy = reinterpret_cast<decltype(api.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+        api.error_string = reinterpret_cast<decltype(api.error_string)>(dlsym(h, "ncclGetErrorString"));
+        ok = api.get_unique_id && api.comm_init_rank && api.all_reduce && api.comm_destroy && api.error_string;
+    });
+    return ok ? &api : nullptr;
+}
 
 static void model_release(dz_cuda_model_t* m) {
     if (!m || --m->refs > 0) return;
     DeviceGuard g(m->device);
+    if (m->comm && nccl_api()) nccl_api()->comm_destroy(m->comm);
     for (auto& L : m->layers) {
         free_qmat(L.qkv); free_qmat(L.q); free_qmat(L.k); free_qmat(L.v);
         free_qmat(L.wo); free_qmat(L.w1); free_qmat(L.w2);
@@ -936,8 +970,85 @@ static void prepare_seqgen(dz_cuda_model_t* m) {
     m->seq_ok = true;
 }
 
+// A quantized projection blob owned by the host while a shard is built.
+struct SliceBlob {
+    dz_tensor_blob_t blob;
+    std::vector<float> scales;
+    std::vector<uint8_t> packed;
+};
+
+// Rows (axis 0) or columns (axis 1) [start, start + count) of a projection blob.
+static int slice_blob(const dz_tensor_blob_t& t, int axis, size_t start, size_t count, SliceBlob* out) {
+    const size_t r2 = axis == 0 ? count : t.rows, c2 = axis == 0 ? t.cols : count;
+    size_t ns = 0, nb = 0;
+    dz_quantized_scale_count(r2, c2, t.granularity, &ns);
+    dz_quantized_packed_size(r2 * c2, t.bits, &nb);
+    out->scales.resize(ns);
+    out->packed.resize(nb);
+    if (dz_quantized_slice(t.scales, t.scale_count, t.packed, t.packed_size, t.rows, t.cols, t.bits,
+                           t.granularity, axis, start, count, out->scales.data(), out->packed.data()) != DZ_OK)
+        return fail(DZ_E_INVALID, "tensor-parallel slice of a %zux%zu projection", t.rows, t.cols);
+    out->blob = t;
+    out->blob.rows = r2;
+    out->blob.cols = c2;
+    out->blob.scales = out->scales.data();
+    out->blob.scale_count = ns;
+    out->blob.packed = out->packed.data();
+    out->blob.packed_size = nb;
+    return DZ_OK;
+}
+
+static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tensors, size_t n, int device,
+                       int tp_rank, int tp_world, ncclComm_t comm, dz_cuda_model_t** out);
+
 extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor_blob_t* tensors, size_t n,
                                     int device, dz_cuda_model_t** out) {
+    return build_model(desc, tensors, n, device, 0, 1, nullptr, out);
+}
+
+extern "C" int dz_cuda_tp_unique_id(uint8_t* id) {
+    if (!id) return fail(DZ_E_INVALID, "null id buffer");
+    const NcclApi* api = nccl_api();
+    if (!api) return fail(DZ_E_UNSUPPORTED, "NCCL (libnccl.so.2) not found");
+    ncclUniqueId u;
+    ncclResult_t r = api->get_unique_id(&u);
+    if (r != ncclSuccess) return fail(DZ_E_DEVICE, "ncclGetUniqueId: %s", api->error_string(r));
+    static_assert(sizeof(ncclUniqueId) == DZ_TP_ID_BYTES, "NCCL unique id size");
+    memcpy(id, &u, sizeof(u));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_model_create_tp(const dz_model_desc_t* desc, const dz_tensor_blob_t* tensors, size_t n,
+                                       int device, int tp_rank, int tp_world, const uint8_t* id,
+                                       dz_cuda_model_t** out) {
+    if (!out) return fail(DZ_E_INVALID, "null output handle");
+    *out = nullptr;
+    if (!desc || tp_world < 1 || tp_rank < 0 || tp_rank >= tp_world || (tp_world > 1 && !id))
+        return fail(DZ_E_INVALID, "tensor-parallel rank %d of %d", tp_rank, tp_world);
+    if (desc->num_heads % (size_t)tp_world || (4 * desc->embedding_dim) % (size_t)tp_world)
+        return fail(DZ_E_INVALID, "heads and FFN width must divide by the %d ranks", tp_world);
+    if (tp_world == 1) return build_model(desc, tensors, n, device, 0, 1, nullptr, out);
+    const NcclApi* api = nccl_api();
+    if (!api) return fail(DZ_E_UNSUPPORTED, "NCCL (libnccl.so.2) not found");
+    ncclComm_t comm = nullptr;
+    {
+        DeviceGuard g(device);
+        if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", device);
+        ncclUniqueId u;
+        memcpy(&u, id, sizeof(u));
+        ncclResult_t r = api->comm_init_rank(&comm, tp_world, u, tp_rank);
+        if (r != ncclSuccess) return fail(DZ_E_DEVICE, "ncclCommInitRank: %s", api->error_string(r));
+    }
+    int rc = build_model(desc, tensors, n, device, tp_rank, tp_world, comm, out);
+    if (rc) {
+        DeviceGuard g(device);
+        api->comm_destroy(comm);
+    }
+    return rc;
+}
+
+static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tensors, size_t n, int device,
+                       int tp_rank, int tp_world, ncclComm_t comm, dz_cuda_model_t** out) {
     if (!out) return fail(DZ_E_INVALID, "null output handle");
     *out = nullptr;
     if (!desc || !tensors) return fail(DZ_E_INVALID, "null argument");
@@ -965,6 +1076,11 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
     if (!m) return fail(DZ_E_NOMEM, "host allocation");
     m->device = device;
     m->desc = *desc;
+    m->tp_rank = tp_rank;
+    m->tp_world = tp_world;
+    m->Hl = (int)(H / tp_world);
+    m->dl = (int)(D / tp_world);
+    m->Fl = (int)(F / tp_world);
     cudaStream_t st;
     if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
         delete m;
@@ -983,6 +1099,18 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
         for (size_t l = 0; l < desc->num_layers && !rc; l++, ti += 12) {
             DevLayer& L = m->layers[l];
             const dz_tensor_blob_t *tq = &t[ti], *tk = &t[ti + 1], *tv = &t[ti + 2];
+            const dz_tensor_blob_t *two = &t[ti + 3], *tw1 = &t[ti + 6], *tw2 = &t[ti + 8];
+            SliceBlob sq, sk, sv, swo, sw1, sw2;
+            if (tp_world > 1) {
+                // this rank's heads (columns of Q, K, V; rows of W_o) and FFN columns (W1) / rows (W2)
+                const size_t d0 = (size_t)tp_rank * m->dl, f0 = (size_t)tp_rank * m->Fl;
+                if ((rc = slice_blob(*tq, 1, d0, m->dl, &sq)) || (rc = slice_blob(*tk, 1, d0, m->dl, &sk)) ||
+                    (rc = slice_blob(*tv, 1, d0, m->dl, &sv)) || (rc = slice_blob(*two, 0, d0, m->dl, &swo)) ||
+                    (rc = slice_blob(*tw1, 1, f0, m->Fl, &sw1)) || (rc = slice_blob(*tw2, 0, f0, m->Fl, &sw2)))
+                    break;
+                tq = &sq.blob; tk = &sk.blob; tv = &sv.blob;
+                two = &swo.blob; tw1 = &sw1.blob; tw2 = &sw2.blob;
+            }
             L.fused_qkv = tq->granularity != DZ_GRAN_ROW;
             if (L.fused_qkv) {
                 if ((rc = make_qmat({tq, tk, tv}, st, &L.qkv))) break;
@@ -993,12 +1121,13 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
                     break;
                 step += 3 * (L.q.code_bytes + L.q.scale_bytes);
             }
-            if ((rc = make_qmat({&t[ti + 3]}, st, &L.wo))) break;
+            if ((rc = make_qmat({two}, st, &L.wo))) break;
             if ((rc = upload_f32(m, t[ti + 4], D, &L.g1, st)) || (rc = upload_f32(m, t[ti + 5], D, &L.be1, st)))
                 break;
-            if ((rc = make_qmat({&t[ti + 6]}, st, &L.w1))) break;
+            if ((rc = make_qmat({tw1}, st, &L.w1))) break;
             if ((rc = upload_f32(m, t[ti + 7], F, &L.b1, st))) break;
-            if ((rc = make_qmat({&t[ti + 8]}, st, &L.w2))) break;
+            if (tp_world > 1) L.b1 += (size_t)tp_rank * m->Fl;   // this rank's FFN columns
+            if ((rc = make_qmat({tw2}, st, &L.w2))) break;
             if ((rc = upload_f32(m, t[ti + 9], D, &L.b2, st)) || (rc = upload_f32(m, t[ti + 10], D, &L.g2, st)) ||
                 (rc = upload_f32(m, t[ti + 11], D, &L.be2, st)))
                 break;
@@ -1028,7 +1157,8 @@ extern "C" int dz_cuda_model_create(const dz_model_desc_t* desc, const dz_tensor
         return rc;
     }
     m->step_bytes = step;
-    prepare_seqgen(m);
+    m->comm = comm;
+    if (tp_world == 1) prepare_seqgen(m);
     *out = m;
     return DZ_OK;
 }
@@ -1157,7 +1287,7 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     c->model = m;
     c->B = (int)batch;
     c->cap = (int)capacity;
-    const size_t D = m->desc.embedding_dim, F = 4 * D, V = m->desc.vocab_size, Lr = m->desc.num_layers;
+    const size_t D = m->desc.embedding_dim, V = m->desc.vocab_size, Lr = m->desc.num_layers;
     const size_t B = batch;
     int rc = DZ_OK;
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
@@ -1165,8 +1295,9 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     } else {
         c->own_stream = true;
     }
-    if (!rc) rc = cache_alloc(c, (void**)&c->keys, Lr * B * capacity * D * 4);
-    if (!rc) rc = cache_alloc(c, (void**)&c->values, Lr * B * capacity * D * 4);
+    const size_t dl = m->dl, Fl = m->Fl;   // this rank's attention and FFN widths
+    if (!rc) rc = cache_alloc(c, (void**)&c->keys, Lr * B * capacity * dl * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->values, Lr * B * capacity * dl * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->start, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->length, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->slot, B * 4);
@@ -1174,11 +1305,11 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     if (!rc) rc = cache_alloc(c, (void**)&c->row_off, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->total, B * 8);
     if (!rc) rc = cache_alloc(c, (void**)&c->hidden, B * D * 4);
-    if (!rc) rc = cache_alloc(c, (void**)&c->q, B * D * 4);
-    if (!rc) rc = cache_alloc(c, (void**)&c->concat, B * D * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->q, B * dl * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->concat, B * dl * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->attn_raw, B * D * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->attn_norm, B * D * 4);
-    if (!rc) rc = cache_alloc(c, (void**)&c->ff, B * F * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->ff, B * Fl * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->ff_raw, B * D * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->logits, B * V * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->tok, B * 4);
@@ -1270,38 +1401,44 @@ extern "C" int dz_cuda_cache_reset(dz_cuda_cache_t* c, const uint8_t* seq_mask) 
 }
 
 // One decode step for all sequences; returns the number of kernel launches.
+// Sum of every rank's partial [rows x D] product, in place (tensor parallelism).
+static void tp_allreduce(dz_cuda_model_t* m, float* buf, size_t count, cudaStream_t st) {
+    if (m->tp_world > 1) nccl_api()->all_reduce(buf, buf, count, ncclFloat32, ncclSum, m->comm, st);
+}
+
 static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long tok_stride) {
     dz_cuda_model_t* m = c->model;
-    const int D = (int)m->desc.embedding_dim, F = 4 * D, V = (int)m->desc.vocab_size, H = (int)m->desc.num_heads;
-    const int hd = D / H, B = c->B, cap = c->cap;
+    const int D = (int)m->desc.embedding_dim, V = (int)m->desc.vocab_size;
+    const int H = m->Hl, dl = m->dl, F = m->Fl;   // this rank's heads, attention width, FFN width
+    const int hd = D / (int)m->desc.num_heads, B = c->B, cap = c->cap;
     cudaStream_t st = c->stream;
     int launches = 0;
     RingState rs{c->start, c->length, c->total, c->slot, c->ctx, c->row_off};
     {
         ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)B * D * 12, 0, st);
         dz_step_begin_kernel<<<B, 128, 0, st>>>(rs, tokens, tok_stride, m->emb, m->pe, m->pe_rows, c->hidden, D,
-                                                V, cap);
+                                                dl, V, cap);
     }
     launches++;
     const size_t att_smem = (size_t)(cap + hd + ATT_THREADS) * 4;
     for (size_t l = 0; l < m->layers.size(); l++) {
         DevLayer& L = m->layers[l];
-        float* Kl = c->keys + l * (size_t)B * cap * D;
-        float* Vl = c->values + l * (size_t)B * cap * D;
+        float* Kl = c->keys + l * (size_t)B * cap * dl;
+        float* Vl = c->values + l * (size_t)B * cap * dl;
         if (L.fused_qkv) {
-            QmvEpilogue ep = plain_epilogue(L.qkv, c->q, D);
+            QmvEpilogue ep = plain_epilogue(L.qkv, c->q, dl);
             ep.nseg = 3;
-            ep.seg_start[0] = 0; ep.seg_start[1] = D; ep.seg_start[2] = 2 * D; ep.seg_start[3] = 3 * D;
-            ep.seg_ptr[1] = Kl; ep.seg_ld[1] = (long long)cap * D; ep.seg_row_off[1] = c->row_off;
-            ep.seg_ptr[2] = Vl; ep.seg_ld[2] = (long long)cap * D; ep.seg_row_off[2] = c->row_off;
+            ep.seg_start[0] = 0; ep.seg_start[1] = dl; ep.seg_start[2] = 2 * dl; ep.seg_start[3] = 3 * dl;
+            ep.seg_ptr[1] = Kl; ep.seg_ld[1] = (long long)cap * dl; ep.seg_row_off[1] = c->row_off;
+            ep.seg_ptr[2] = Vl; ep.seg_ld[2] = (long long)cap * dl; ep.seg_row_off[2] = c->row_off;
             launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st, c->xs_scratch, c->status);
         } else {
-            QmvEpilogue eq = plain_epilogue(L.q, c->q, D);
+            QmvEpilogue eq = plain_epilogue(L.q, c->q, dl);
             launches += launch_qmv(L.q, c->hidden, D, B, eq, st, c->xs_scratch, c->status);
-            QmvEpilogue ek = plain_epilogue(L.k, Kl, (long long)cap * D);
+            QmvEpilogue ek = plain_epilogue(L.k, Kl, (long long)cap * dl);
             ek.seg_row_off[0] = c->row_off;
             launches += launch_qmv(L.k, c->hidden, D, B, ek, st, c->xs_scratch, c->status);
-            QmvEpilogue ev = plain_epilogue(L.v, Vl, (long long)cap * D);
+            QmvEpilogue ev = plain_epilogue(L.v, Vl, (long long)cap * dl);
             ev.seg_row_off[0] = c->row_off;
             launches += launch_qmv(L.v, c->hidden, D, B, ev, st, c->xs_scratch, c->status);
         }
@@ -1309,21 +1446,22 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             // bytes: the K and V rows of every sequence's context (ctx <= cap; the
             // exact per-step context is device state, so the capacity bound is used
             // only when the profiler cannot read it) + q + output
-            ProfScope prof(DZ_KERNEL_ATTENTION, c->prof_ctx_bytes_per_layer + 8.0 * B * D,
+            ProfScope prof(DZ_KERNEL_ATTENTION, c->prof_ctx_bytes_per_layer + 8.0 * B * dl,
                            c->prof_ctx_flops_per_layer, st);
             if (hd == 128)
                 dz_attention_decode2_kernel<4><<<dim3(H, B), ATT2_THREADS, 0, st>>>(c->q, Kl, Vl, c->start, c->ctx,
-                                                                                   c->concat, D, cap);
+                                                                                   c->concat, dl, cap);
             else if (hd == 64)
                 dz_attention_decode2_kernel<2><<<dim3(H, B), ATT2_THREADS, 0, st>>>(c->q, Kl, Vl, c->start, c->ctx,
-                                                                                   c->concat, D, cap);
+                                                                                   c->concat, dl, cap);
             else
                 dz_attention_decode_kernel<<<dim3(H, B), ATT_THREADS, att_smem, st>>>(c->q, Kl, Vl, c->start,
-                                                                                     c->ctx, c->concat, D, hd, cap);
+                                                                                     c->ctx, c->concat, dl, hd, cap);
         }
         launches++;
         QmvEpilogue eo = plain_epilogue(L.wo, c->attn_raw, D);
-        launches += launch_qmv(L.wo, c->concat, D, B, eo, st, c->xs_scratch, c->status);
+        launches += launch_qmv(L.wo, c->concat, dl, B, eo, st, c->xs_scratch, c->status);
+        tp_allreduce(m, c->attn_raw, (size_t)B * D, st);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D, 0, st);
             dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, D,
@@ -1335,10 +1473,13 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         e1.relu = 1;
         launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st, c->xs_scratch, c->status);
         QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
-        e2.bias = L.b2;
-        e2.residual = c->attn_norm;
-        e2.ld_res = D;
+        if (m->tp_rank == 0) {   // bias and residual once, before the sum over ranks
+            e2.bias = L.b2;
+            e2.residual = c->attn_norm;
+            e2.ld_res = D;
+        }
         launches += launch_qmv(L.w2, c->ff, F, B, e2, st, c->xs_scratch, c->status);
+        tp_allreduce(m, c->ff_raw, (size_t)B * D, st);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D, 0, st);
             dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->ff_raw, nullptr, L.g2, L.be2, c->hidden, D, 1e-6f);
@@ -1585,14 +1726,15 @@ static size_t prefill_launches(const dz_cuda_cache_t* c, size_t T) {
 // last position into c->logits. Returns the launches.
 static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long long ld, int T, const int* lens_dev) {
     dz_cuda_model_t* m = c->model;
-    const int D = (int)m->desc.embedding_dim, F = 4 * D, V = (int)m->desc.vocab_size, H = (int)m->desc.num_heads;
-    const int hd = D / H, B = c->B, cap = c->cap;
+    const int D = (int)m->desc.embedding_dim, V = (int)m->desc.vocab_size;
+    const int H = m->Hl, dl = m->dl, F = m->Fl;   // this rank's heads, attention width, FFN width
+    const int hd = D / (int)m->desc.num_heads, B = c->B, cap = c->cap;
     cudaStream_t st = c->stream;
     const int S = (int)prefill_group(c, (size_t)T);
     int launches = 0;
     {
         const int rows = S * T;
-        dz_prefill_rowoff_kernel<<<(rows + 255) / 256, 256, 0, st>>>(c->pf_rowoff, rows, T, cap, D);
+        dz_prefill_rowoff_kernel<<<(rows + 255) / 256, 256, 0, st>>>(c->pf_rowoff, rows, T, cap, dl);
         launches++;
     }
     for (int s0 = 0; s0 < B; s0 += S) {
@@ -1606,17 +1748,17 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
         launches++;
         for (size_t l = 0; l < m->layers.size(); l++) {
             DevLayer& L = m->layers[l];
-            float* Kl = c->keys + l * (size_t)B * cap * D + (size_t)s0 * cap * D;
-            float* Vl = c->values + l * (size_t)B * cap * D + (size_t)s0 * cap * D;
+            float* Kl = c->keys + l * (size_t)B * cap * dl + (size_t)s0 * cap * dl;
+            float* Vl = c->values + l * (size_t)B * cap * dl + (size_t)s0 * cap * dl;
             if (L.fused_qkv) {
-                QmvEpilogue ep = plain_epilogue(L.qkv, c->pf_q, D);
+                QmvEpilogue ep = plain_epilogue(L.qkv, c->pf_q, dl);
                 ep.nseg = 3;
-                ep.seg_start[0] = 0; ep.seg_start[1] = D; ep.seg_start[2] = 2 * D; ep.seg_start[3] = 3 * D;
+                ep.seg_start[0] = 0; ep.seg_start[1] = dl; ep.seg_start[2] = 2 * dl; ep.seg_start[3] = 3 * dl;
                 ep.seg_ptr[1] = Kl; ep.seg_ld[1] = 0; ep.seg_row_off[1] = c->pf_rowoff;
                 ep.seg_ptr[2] = Vl; ep.seg_ld[2] = 0; ep.seg_row_off[2] = c->pf_rowoff;
                 launches += launch_qmv(L.qkv, c->pf_hidden, D, R, ep, st, c->pf_scratch, c->status);
             } else {
-                QmvEpilogue eq = plain_epilogue(L.q, c->pf_q, D);
+                QmvEpilogue eq = plain_epilogue(L.q, c->pf_q, dl);
                 launches += launch_qmv(L.q, c->pf_hidden, D, R, eq, st, c->pf_scratch, c->status);
                 QmvEpilogue ek = plain_epilogue(L.k, Kl, 0);
                 ek.seg_row_off[0] = c->pf_rowoff;
@@ -1627,23 +1769,24 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
             }
             {
                 const double ctx_pairs = (double)ns * H * T * (T + 1) / 2.0;
-                ProfScope prof(DZ_KERNEL_ATTENTION, 8.0 * (double)R * D + 8.0 * (double)ns * T * D,
+                ProfScope prof(DZ_KERNEL_ATTENTION, 8.0 * (double)R * dl + 8.0 * (double)ns * T * dl,
                                4.0 * ctx_pairs * hd, st);
                 const dim3 grid((unsigned)((T + PF_QT - 1) / PF_QT), (unsigned)H, (unsigned)ns);
                 const size_t smem = dz_prefill_att_smem(hd);
                 if (hd == 128)
                     dz_attention_prefill_kernel<4><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
-                                                                                  c->pf_concat, T, D, cap);
+                                                                                  c->pf_concat, T, dl, cap);
                 else if (hd == 64)
                     dz_attention_prefill_kernel<2><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
-                                                                                  c->pf_concat, T, D, cap);
+                                                                                  c->pf_concat, T, dl, cap);
                 else
                     dz_attention_prefill_kernel<1><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
-                                                                                  c->pf_concat, T, D, cap);
+                                                                                  c->pf_concat, T, dl, cap);
             }
             launches++;
             QmvEpilogue eo = plain_epilogue(L.wo, c->pf_attn_raw, D);
-            launches += launch_qmv(L.wo, c->pf_concat, D, R, eo, st, c->pf_scratch, c->status);
+            launches += launch_qmv(L.wo, c->pf_concat, dl, R, eo, st, c->pf_scratch, c->status);
+            tp_allreduce(m, c->pf_attn_raw, (size_t)R * D, st);
             {
                 ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * R * D + 8.0 * D, 0, st);
                 dz_layernorm_kernel<<<R, LN_THREADS, 0, st>>>(c->pf_attn_raw, c->pf_hidden, L.g1, L.be1,
@@ -1655,10 +1798,13 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
             e1.relu = 1;
             launches += launch_qmv(L.w1, c->pf_attn_norm, D, R, e1, st, c->pf_scratch, c->status);
             QmvEpilogue e2 = plain_epilogue(L.w2, c->pf_ff_raw, D);
-            e2.bias = L.b2;
-            e2.residual = c->pf_attn_norm;
-            e2.ld_res = D;
+            if (m->tp_rank == 0) {
+                e2.bias = L.b2;
+                e2.residual = c->pf_attn_norm;
+                e2.ld_res = D;
+            }
             launches += launch_qmv(L.w2, c->pf_ff, F, R, e2, st, c->pf_scratch, c->status);
+            tp_allreduce(m, c->pf_ff_raw, (size_t)R * D, st);
             {
                 ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * R * D + 8.0 * D, 0, st);
                 dz_layernorm_kernel<<<R, LN_THREADS, 0, st>>>(c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, D,
@@ -1893,7 +2039,7 @@ extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prom
     // eager launches, each bracketed by events; the attention byte count uses
     // the mean context of the run (prefill then decode, all sequences in step)
     const dz_cuda_model_t* m = c->model;
-    const double D = (double)m->desc.embedding_dim;
+    const double D = (double)m->dl;   // this rank's K / V width
     const double total_steps = (double)plen + (double)(n_new - 1);
     const double mean_ctx = (total_steps + 1.0) / 2.0 < c->cap ? (total_steps + 1.0) / 2.0 : c->cap;
     c->prof_ctx_bytes_per_layer = 8.0 * D * mean_ctx * c->B;

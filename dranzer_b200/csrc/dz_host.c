@@ -191,6 +191,60 @@ int dz_quantize_pack(const float *src, size_t rows, size_t cols, int bits, int g
     return 0;
 }
 
+static uint32_t code_at(const uint8_t *packed, size_t idx, int bits) {
+    if (bits == 8) return packed[idx];
+    if (bits == 4) return (uint32_t)((packed[idx >> 1] >> ((idx & 1) * 4)) & 0xF);
+    /* other widths: LSB-first bit stream */
+    uint32_t v = 0;
+    for (int b = 0; b < bits; b++) {
+        const size_t bit = idx * (size_t)bits + (size_t)b;
+        v |= (uint32_t)((packed[bit >> 3] >> (bit & 7)) & 1) << b;
+    }
+    return v;
+}
+
+static void code_put(uint8_t *packed, size_t idx, int bits, uint32_t v) {
+    if (bits == 8) {
+        packed[idx] = (uint8_t)v;
+        return;
+    }
+    for (int b = 0; b < bits; b++) {
+        const size_t bit = idx * (size_t)bits + (size_t)b;
+        if ((v >> b) & 1) packed[bit >> 3] |= (uint8_t)(1u << (bit & 7));
+    }
+}
+
+int dz_quantized_slice(const float *scales, size_t scales_count, const uint8_t *packed, size_t packed_size,
+                       size_t rows, size_t cols, int bits, int granularity, int axis, size_t start,
+                       size_t count, float *scales_out, uint8_t *packed_out) {
+    size_t ns = 0, nb = 0, ns2 = 0, nb2 = 0;
+    if (!scales || !packed || !scales_out || !packed_out || (axis != 0 && axis != 1) || count == 0 ||
+        bits < 2 || bits > 16)
+        return DZ_E_INVALID;
+    const size_t lim = axis == 0 ? rows : cols;
+    if (start > lim || count > lim - start) return DZ_E_INVALID;
+    if (dz_quantized_scale_count(rows, cols, granularity, &ns) || dz_quantized_packed_size(rows * cols, bits, &nb) ||
+        ns != scales_count || nb != packed_size)
+        return DZ_E_INVALID;
+    const size_t r2 = axis == 0 ? count : rows, c2 = axis == 0 ? cols : count;
+    if (dz_quantized_scale_count(r2, c2, granularity, &ns2) || dz_quantized_packed_size(r2 * c2, bits, &nb2))
+        return DZ_E_INVALID;
+    memset(packed_out, 0, nb2);
+    for (size_t r = 0; r < r2; r++)
+        for (size_t c = 0; c < c2; c++) {
+            const size_t sr = axis == 0 ? start + r : r, sc = axis == 0 ? c : start + c;
+            code_put(packed_out, r * c2 + c, bits, code_at(packed, sr * cols + sc, bits));
+        }
+    if (granularity == DZ_GRAN_COLUMN) {
+        for (size_t c = 0; c < c2; c++) scales_out[c] = scales[axis == 1 ? start + c : c];
+    } else if (granularity == DZ_GRAN_ROW) {
+        for (size_t r = 0; r < r2; r++) scales_out[r] = scales[axis == 0 ? start + r : r];
+    } else {
+        scales_out[0] = scales[0];
+    }
+    return DZ_OK;
+}
+
 int dz_quantize_unpack(const float *scales, size_t scales_count, const uint8_t *packed,
                        size_t packed_size, size_t rows, size_t cols, int bits, int granularity,
                        float *dst) {

@@ -180,6 +180,27 @@ typedef struct {
     double flops;
 } dz_kernel_stat_t;
 
+/* Tensor parallelism across GPUs (one process or thread per rank), the
+ * layout of the large configuration: each rank holds the Q/K/V columns and
+ * the W_o rows of num_heads/world heads, and the W1 columns (with their b1)
+ * and W2 rows of 4*d_model/world FFN columns; embeddings, LayerNorms, the
+ * head and its bias are replicated. Per layer and step, the attention-out and
+ * FFN-down partial products [rows x d_model] are summed over the ranks with
+ * an fp32 NCCL all-reduce (b2 and the residual are added once, before it),
+ * so every rank ends each layer with the full hidden state and computes the
+ * same logits and tokens. Shards are exact: a column (row) slice of a
+ * per-column quantized matrix keeps its codes and scales
+ * (dz_quantized_slice). Rank 0 makes the NCCL unique id with
+ * dz_cuda_tp_unique_id and the host hands it to every rank; every rank
+ * calls dz_cuda_model_create_tp (collective) and then makes the same calls
+ * with the same arguments (generate, forward, select). With world = 1 this is
+ * dz_cuda_model_create. The fused one-CTA-per-sequence path is not used.
+ * No counterpart in the reference (its backend runs on one device). */
+#define DZ_TP_ID_BYTES 128
+int dz_cuda_tp_unique_id(uint8_t *id);
+int dz_cuda_model_create_tp(const dz_model_desc_t *desc, const dz_tensor_blob_t *tensors, size_t n_tensors,
+                            int device, int tp_rank, int tp_world, const uint8_t *id, dz_cuda_model_t **out);
+
 /* Prefill policy of the layered path (dz_cuda_generate and
  * dz_cuda_prefill). TOKENS feeds the prompt one position per step through
  * dz_cuda_forward_tokens' step, as the reference's generation loop does

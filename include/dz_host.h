@@ -42,6 +42,20 @@ int dz_quantize_unpack(const float *scales, size_t scales_count, const uint8_t *
                        size_t packed_size, size_t rows, size_t cols, int bits, int granularity,
                        float *dst);
 
+/* Rows [start, start + count) (axis 0) or columns (axis 1) of a quantized
+ * rows x cols matrix as a quantized matrix of its own: the same codes (the
+ * reference's layout, INT4 nibbles LSB-first with a zero pad nibble) and the
+ * scales of the kept rows / columns (COLUMN scales follow a column slice and
+ * stay whole for a row slice, ROW scales the other way round, TENSOR keeps
+ * its one scale). Exact: a slice of a matrix quantized per column (or row)
+ * is what quantize_pack gives for that slice of the float matrix. Used to
+ * shard projections across tensor-parallel ranks; no counterpart in the
+ * reference. scales_out / packed_out hold dz_quantized_scale_count /
+ * dz_quantized_packed_size of the slice. */
+int dz_quantized_slice(const float *scales, size_t scales_count, const uint8_t *packed, size_t packed_size,
+                       size_t rows, size_t cols, int bits, int granularity, int axis, size_t start,
+                       size_t count, float *scales_out, uint8_t *packed_out);
+
 /* ---- Sinusoidal positions, compute_positional_encoding (src/core/tensor_ops.c:227-248):
  * PE[pos][i] = sin/cos(pos / 10000^(2i/d)), even i -> sin, odd i -> cos. */
 int dz_positional_encoding(float *out, size_t rows, size_t dim);
