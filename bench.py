@@ -222,6 +222,11 @@ def quant_matvec_probe(dz, torch, stream, hbm, bf16=None):
             reps = 24 if M <= 64 else 8
             evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
             torch.cuda.synchronize()
+            # a bounded device-side delay lets the host enqueue the whole burst
+            # first, so the events see device time rather than launch cadence
+            if hasattr(torch.cuda, "_sleep"):
+                with torch.cuda.stream(stream):
+                    torch.cuda._sleep(8_000_000)
             for i in range(reps):
                 evs[i][0].record(stream)
                 mats[i % copies].matmul_async(xd.data_ptr(), yd.data_ptr(), M, stream.cuda_stream)

@@ -96,11 +96,10 @@ struct DevQMat {
     float* col_scale = nullptr;  // [Np] (COLUMN / TENSOR expanded), zero in padding
     float* k_scale = nullptr;    // [K] ROW granularity
     size_t code_bytes = 0, scale_bytes = 0;
-    // the codes again, one byte each, in the reference's k x n order (rows
-    // kn_ld bytes apart; INT4 nibbles widened) with their TMA map, for the
-    // tensor-core GEMM
-    uint8_t* kn = nullptr;
-    int kn_ld = 0;
+    // the levels again, one signed byte each, in K-major 16 KB blocks
+    // [n / 128][k / 128][n % 128][k % 128], with their TMA map, for the
+    // tensor-core kernels
+    int8_t* kn = nullptr;
     CUtensorMap tm_kn;
 };
 
@@ -135,7 +134,7 @@ static bool encode_u8_map(CUtensorMap* tm, void* base, int rank, const cuuint64_
                           const cuuint32_t* box) {
     TensorMapEncodeFn enc = tensor_map_encoder();
     if (!enc) return false;
-    const cuuint32_t es[3] = {1, 1, 1};
+    const cuuint32_t es[5] = {1, 1, 1, 1, 1};
     return enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank, base, dims, strides, box, es,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -220,25 +219,22 @@ static int make_qmat_into(const std::vector<const dz_tensor_blob_t*>& srcs, cuda
     dz_frag_repack_kernel<<<(unsigned)((nwords + 255) / 256), 256, 0, st>>>(fs, reinterpret_cast<uint32_t*>(m.codes),
                                                                            m.K, m.bits, m.nkg, nwords);
     DZ_CUDA(cudaGetLastError());
-    if (tensor_map_encoder()) {
-        // k x n codes for the tensor-core GEMM: the sources side by side
-        m.kn_ld = round_up(N, 16);
-        DZ_CUDA(cudaMalloc(&m.kn, (size_t)m.K * m.kn_ld));
+    if (tensor_map_encoder() && m.K <= UG_MAX_K) {
+        // K-major level blocks for the tensor-core kernels
+        const int nt = (N + UG_BN - 1) / UG_BN, nkb = (m.K + UG_BK - 1) / UG_BK;
+        const size_t blk = (size_t)UG_BN * UG_BK, bytes = (size_t)nt * nkb * blk;
+        DZ_CUDA(cudaMalloc(&m.kn, bytes));
+        DZ_CUDA(cudaMemsetAsync(m.kn, 0, bytes, st));
         for (size_t i = 0; i < srcs.size(); i++) {
-            if (m.bits == 8) {
-                DZ_CUDA(cudaMemcpy2DAsync(m.kn + fs.off[i], (size_t)m.kn_ld, fs.ref[i], srcs[i]->cols,
-                                          srcs[i]->cols, (size_t)m.K, cudaMemcpyDeviceToDevice, st));
-            } else {
-                const long long total = (long long)m.K * (long long)srcs[i]->cols;
-                dz_widen_nibbles_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
-                    fs.ref[i], (long long)srcs[i]->cols, total, m.kn + fs.off[i], m.kn_ld);
-                DZ_CUDA(cudaGetLastError());
-            }
+            const long long total = (long long)m.K * (long long)srcs[i]->cols;
+            dz_code_blocks_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(
+                fs.ref[i], m.bits, (long long)srcs[i]->cols, total, m.kn, nkb, fs.off[i]);
+            DZ_CUDA(cudaGetLastError());
         }
-        const cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)m.K};
-        const cuuint64_t strides[1] = {(cuuint64_t)m.kn_ld};
-        const cuuint32_t box[2] = {UG_BN, UG_BK};
-        if (!encode_u8_map(&m.tm_kn, m.kn, 2, dims, strides, box)) {
+        const cuuint64_t dims[4] = {(cuuint64_t)UG_BK, (cuuint64_t)UG_BN, (cuuint64_t)nkb, (cuuint64_t)nt};
+        const cuuint64_t strides[3] = {(cuuint64_t)UG_BK, (cuuint64_t)blk, (cuuint64_t)blk * nkb};
+        const cuuint32_t box[4] = {UG_BK, UG_BN, 1, 1};
+        if (!encode_u8_map(&m.tm_kn, m.kn, 4, dims, strides, box)) {
             cudaFree(m.kn);
             m.kn = nullptr;
         }
@@ -318,11 +314,31 @@ static size_t qmv_xf_bytes(const DevQMat& W, int M) {
 // of M x (K rounded up to 128) bytes, the int64 row sums and the exponents.
 static size_t ugemm_scratch_bytes(const DevQMat& W, int M) {
     const size_t kp = (size_t)round_up(W.K, UG_BK);
-    return r256(3 * (size_t)M * kp) + r256((size_t)M * 8) + r256((size_t)M * 4);
+    return r256(3 * (size_t)M * kp) + r256((size_t)M * 4);
+}
+// Every scratch buffer starts with the GEMV's per-tile counters, shared by
+// all matrices that use the buffer (each launch leaves the counters it used
+// at zero; the scratch is zeroed when allocated); the kernels' own scratch
+// follows.
+constexpr int UGEMV_MAX_TILES = 4096;
+constexpr size_t SCRATCH_COUNTERS = (size_t)UGEMV_MAX_TILES * 4;
+// CTAs of the GEMV: one per SM, fewer when the matrix has fewer than
+// UV_MIN_STAGES_PER_CTA stages for each.
+static int ugemv_grid(const DevQMat& W) {
+    const long long total = (long long)((W.N + UG_BN - 1) / UG_BN) * ((W.K + UG_BK - 1) / UG_BK);
+    return (int)std::max(1LL, std::min((long long)g_num_sms, total / UV_MIN_STAGES_PER_CTA));
+}
+// Scratch of the tensor-core GEMV for M <= 16 rows: limbs, exponents and two
+// int64 partial slots per CTA.
+static size_t ugemv_scratch_bytes(const DevQMat& W, int M) {
+    const size_t kp = (size_t)round_up(W.K, UG_BK);
+    return r256(3 * (size_t)M * kp) + r256((size_t)M * 4) + r256((size_t)ugemv_grid(W) * 2 * UV_SLOT_ELEMS * 8);
 }
 static size_t qmv_scratch_bytes(const DevQMat& W, int M) {
     const size_t xf = r256(qmv_xf_bytes(W, M)) + r256((size_t)M * 4);
-    return W.kn ? std::max(xf, ugemm_scratch_bytes(W, M)) : xf;
+    if (!W.kn) return SCRATCH_COUNTERS + xf;
+    return SCRATCH_COUNTERS +
+           std::max({xf, ugemm_scratch_bytes(W, M), M <= UV_N ? ugemv_scratch_bytes(W, M) : (size_t)0});
 }
 
 template <int BITS, int NB, int NT, int W, bool XIN>
@@ -376,6 +392,11 @@ static int qms_prepare(int device) {
     DZ_QMV1_ATTR(4, false); DZ_QMV1_ATTR(4, true); DZ_QMV1_ATTR(8, false); DZ_QMV1_ATTR(8, true);
 #undef DZ_QMV1_ATTR
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UG_SMEM_BYTES));
+    DZ_CUDA(cudaFuncSetAttribute(dz_ugemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UV_SMEM_BYTES));
+    // the split runs right before the GEMV (and may share SMs with it): the
+    // same shared-memory carve-out spares a reconfiguration between them
+    DZ_CUDA(cudaFuncSetAttribute(dz_limb_split_chunk_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 (int)cudaSharedmemCarveoutMaxShared));
     g_qms_ready[device] = true;
     return DZ_OK;
 }
@@ -460,6 +481,19 @@ static bool qmv1_launch(const DevQMat& W, const float* X, long long ldx, int M, 
 // `scratch` (qmv_scratch_bytes), then the streaming (M <= QMS_MAX_M) or the
 // register-blocked MMA kernel. A bulk-copy wait that gives up sets *status
 // (when given) and leaves NaN in the tile. Returns the launches (1 or 2).
+
+// The tensor-core GEMV takes M <= 16 rows where it measured faster than the
+// CUDA-core matvec kernels (B200, K x N from 2048 x 2048 to 4096 x 32000):
+// from 8 rows on every matrix of at least 2^20 codes, from 3 rows on matrices
+// of at least 2^25 codes. Below that the matvec kernels' lower fixed cost wins.
+constexpr size_t UGEMV_MIN_WEIGHTS = (size_t)1 << 20;
+constexpr size_t UGEMV_LARGE_WEIGHTS = (size_t)1 << 25;
+static bool use_ugemv(const DevQMat& W, int M) {
+    const size_t kn = (size_t)W.K * W.N;
+    if (!W.kn || kn < UGEMV_MIN_WEIGHTS || M > UV_N || (W.N + UG_BN - 1) / UG_BN > UGEMV_MAX_TILES) return false;
+    return M >= 8 || (M >= 3 && kn >= UGEMV_LARGE_WEIGHTS);
+}
+
 // Rows and matrix size from which products go to the tensor-core GEMM.
 constexpr int UGEMM_MIN_M = QMS_MAX_M + 1;
 constexpr size_t UGEMM_MIN_WEIGHTS = (size_t)1 << 20;
@@ -470,8 +504,7 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
                         cudaStream_t st, void* scratch, int* status) {
     const int Kp = round_up(W.K, UG_BK);
     int8_t* L = static_cast<int8_t*>(scratch);
-    long long* rowsum = reinterpret_cast<long long*>(static_cast<uint8_t*>(scratch) + r256(3 * (size_t)M * Kp));
-    int* shift = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(rowsum) + r256((size_t)M * 8));
+    int* shift = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + r256(3 * (size_t)M * Kp));
     CUtensorMap tmA;
     const cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)M, (cuuint64_t)UG_LIMBS};
     const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)Kp * M};
@@ -479,7 +512,7 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     if (!encode_u8_map(&tmA, L, 3, dims, strides, box)) return 0;
     {
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 3.0 * M * Kp, 0, st);
-        dz_limb_split_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, rowsum, shift);
+        dz_limb_split_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
     }
     UgArgs a;
     memset(&a, 0, sizeof(a));
@@ -487,9 +520,7 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     a.N = W.N;
     a.K = W.K;
     a.nkb = Kp / UG_BK;
-    a.rowsum = rowsum;
     a.shift = shift;
-    a.code_bias = W.bits == 8 ? 127 : 7;
     a.status = status;
     a.ep = ep_in;
     a.ep.row_shift = nullptr;
@@ -501,8 +532,74 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     return 2;
 }
 
+// The tensor-core GEMV for M <= 16 (umma.cuh): chunked limb split, then the
+// stream-K kernel on ugemv_grid CTAs. Returns the launches (2), or 0 when its
+// TMA map cannot be made.
+static int launch_ugemv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
+                        cudaStream_t st, void* scratch, int* counter, int* status) {
+    const int Kp = round_up(W.K, UG_BK);
+    const int nch = (Kp + UG_SPLIT_CHUNK - 1) / UG_SPLIT_CHUNK;
+    const int ntiles = (W.N + UG_BN - 1) / UG_BN;
+    uint8_t* p = static_cast<uint8_t*>(scratch);
+    int8_t* L = reinterpret_cast<int8_t*>(p);
+    p += r256(3 * (size_t)M * Kp);
+    int* shift = reinterpret_cast<int*>(p);
+    p += r256((size_t)M * 4);
+    long long* partial = reinterpret_cast<long long*>(p);
+    CUtensorMap tmL;
+    const cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)M, (cuuint64_t)UG_LIMBS};
+    const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)Kp * M};
+    const cuuint32_t box[3] = {UG_BK, UV_N, 1};
+    if (!encode_u8_map(&tmL, L, 3, dims, strides, box)) return 0;
+    {
+        ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K * nch + 3.0 * M * Kp, 0, st);
+        dz_limb_split_chunk_kernel<<<dim3((unsigned)nch, (unsigned)M), 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp,
+                                                                                      L, shift);
+    }
+    UvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.M = M;
+    a.N = W.N;
+    a.K = W.K;
+    a.nkb = Kp / UG_BK;
+    a.ntiles = ntiles;
+    a.total = (long long)ntiles * a.nkb;
+    a.shift = shift;
+    a.partial = partial;
+    a.counter = counter;
+    a.status = status;
+    a.ep = ep_in;
+    a.ep.row_shift = nullptr;
+    ProfScope prof(DZ_KERNEL_QMV, (double)W.K * W.N + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N,
+                   2.0 * M * W.K * W.N, st);
+    // programmatic dependent of the split: weight streaming starts before the
+    // split grid completes (the kernel waits for it before reading limbs)
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)ugemv_grid(W));
+    cfg.blockDim = dim3(UG_THREADS);
+    cfg.dynamicSmemBytes = UV_SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, dz_ugemv_kernel, W.tm_kn, tmL, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        dz_ugemv_kernel<<<cfg.gridDim, UG_THREADS, UV_SMEM_BYTES, st>>>(W.tm_kn, tmL, a);
+    }
+    return 2;
+}
+
 static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
                       cudaStream_t st, void* scratch, int* status) {
+    int* counters = static_cast<int*>(scratch);
+    scratch = static_cast<uint8_t*>(scratch) + SCRATCH_COUNTERS;
+    if (M <= UV_N && use_ugemv(W, M)) {
+        const int n = launch_ugemv(W, X, ldx, M, ep_in, st, scratch, counters, status);
+        if (n) return n;
+    }
     // small matrices stay on the register-blocked kernel: the GEMM's fixed
     // cost per tile (pipeline fill, tensor-memory drain) would dominate
     if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) {
@@ -606,6 +703,7 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
 // The launches launch_qmv makes for this matrix at M rows (mirrors its choices).
 static int qmv_launches(const DevQMat& W, int M) {
     if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) return 2;
+    if (M <= UV_N && use_ugemv(W, M)) return 2;
     const int KG = W.bits == 8 ? 32 : 64;
     const int Kp = W.nkg * KG;
     bool xin = M <= QMS_MAX_M && qmv_xf_bytes(W, M) <= QMS_XF_SMEM_MAX;
@@ -647,6 +745,7 @@ static int qmatrix_scratch(dz_cuda_qmatrix_t* q, int M) {
     q->scratch = nullptr;
     q->scratch_bytes = 0;
     DZ_CUDA(cudaMalloc(&q->scratch, need));
+    DZ_CUDA(cudaMemset(q->scratch, 0, need));   // the GEMV's per-tile counters start at zero
     q->scratch_bytes = need;
     return DZ_OK;
 }
@@ -1322,6 +1421,7 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
                 if (q->codes) xs = std::max(xs, qmv_scratch_bytes(*q, (int)B));
         xs = std::max(xs, qmv_scratch_bytes(m->head, (int)B));
         rc = cache_alloc(c, (void**)&c->xs_scratch, xs);
+        if (!rc && cudaMemset(c->xs_scratch, 0, xs) != cudaSuccess) rc = fail(DZ_E_DEVICE, "scratch memset");
     }
     if (!rc) rc = cache_alloc(c, (void**)&c->status, 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->phase_ns, SEQ_PHASES * 8);
@@ -1696,6 +1796,7 @@ static int ensure_prefill(dz_cuda_cache_t* c, size_t T) {
         return fail(DZ_E_NOMEM, "prefill buffers for %zu rows", rows);
     }
     c->pf_rows = rows;
+    DZ_CUDA(cudaMemset(c->pf_scratch, 0, scratch));
     DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dz_prefill_att_smem(128)));
     DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,

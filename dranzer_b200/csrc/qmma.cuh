@@ -512,8 +512,13 @@ __device__ __forceinline__ bool dz_mbar_test(uint64_t* bar, uint32_t parity) {
         : "memory");
     return done != 0;
 }
-// Bounded wait (about one second). False when it gave up.
+// Bounded wait (about one second). False when it gave up. The timer is read
+// only once the phase has not completed on the first tries (a global-timer
+// read costs far more than a try_wait that succeeds).
 __device__ __forceinline__ bool dz_mbar_wait(uint64_t* bar, uint32_t parity) {
+#pragma unroll 1
+    for (int i = 0; i < 4; i++)
+        if (dz_mbar_test(bar, parity)) return true;
     const uint64_t t0 = dz_global_ns();
     for (unsigned i = 0;; i++) {
         if (dz_mbar_test(bar, parity)) return true;

@@ -127,8 +127,13 @@ struct SeqClock {
     }
 };
 
-// Bounded wait (about one second); returns false when the limit ran out.
+// Bounded wait (about one second); returns false when the limit ran out. The
+// timer is read only after the first tries fail (a global-timer read costs far
+// more than a try_wait that succeeds).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+#pragma unroll 1
+    for (int i = 0; i < 4; i++)
+        if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (unsigned i = 0; i < SEQ_WAIT_LIMIT; i++) {
         if (mbar_try_wait(bar, parity)) return true;

@@ -4,23 +4,23 @@
 //
 // Integer formulation, exact in every product and sum:
 // - each activation row is scaled by 2^s (exact) so that max |x 2^s| lies in
-//   [2^22, 2^23), rounded to a 24-bit integer X and cut into three 8-bit
-//   limbs X = 65536 * top + 256 * mid + low (top signed, mid / low unsigned);
-// - weights enter the tensor core as their unsigned codes c = level + qmax
-//   (INT8: the reference's k x n bytes as stored, src/core/quantize.c:
-//   213-221; INT4: the nibbles widened to bytes once at upload), so there is
-//   no dequantization at all: sum_k X level = sum_k X c - qmax * sum_k X;
+//   [2^21, 2^22), rounded to an integer X (|X| <= 2^22) and cut into three
+//   signed 8-bit limbs X = 65536 * top + 256 * mid + low (balanced base-256
+//   digits: mid, low in [-128, 127], top in [-64, 64]);
+// - weights enter the tensor core as their signed levels q = code - qmax
+//   (src/core/quantize.c:213-221 stores code = level + qmax; INT4 nibbles are
+//   widened to bytes), converted once at upload, so there is no
+//   dequantization at all;
 // - one kind::i8 MMA per limb accumulates int32 in tensor memory (exact for
-//   K up to 33k); the epilogue combines the limbs in int64, subtracts the
-//   code bias times the row sum, converts to fp32 once and applies 2^-s and
-//   the column scale.
+//   K <= UG_MAX_K); the epilogue combines the limbs in int64, converts to
+//   fp32 once and applies 2^-s and the column scale.
 // Rounding differs from the reference's fp32 multiply-add only in the
 // activation's 24-bit fixed-point representation (relative to the row's
 // largest element) and the final conversions.
 //
 // Tiles: 128 rows x 128 columns per CTA, k in steps of 128 bytes. A (the
-// limbs) is K-major and B (the codes) MN-major, both loaded by TMA with the
-// 128-byte swizzle; a 3-stage ring of 64 KB stages. Warp 0 issues the TMA
+// limbs) and B (the codes, 16 KB blocks) are K-major, both loaded by TMA with
+// the 128-byte swizzle; a 3-stage ring of 64 KB stages. Warp 0 issues the TMA
 // loads, warp 1 (one thread) the MMAs and commits, warps 4-7 drain the
 // accumulators (tcgen05.ld) and run the epilogue. Every wait is bounded.
 #pragma once
@@ -45,12 +45,14 @@ constexpr uint32_t UG_TMEM_COLS = 512;           // three 128-column int32 accum
 constexpr size_t UG_SMEM_BYTES = (size_t)UG_STAGES * UG_STAGE_BYTES + 1024 + 256;
 constexpr int UG_ROW_NONFINITE = -0x40000000;    // row exponent marking a non-finite input row
 constexpr int UG_TILE_LD = UG_BN + 4;            // staging tile row stride (floats): 16-byte rows, spread banks
+// Largest K for which the int32 limb sums are exact: |q| <= 127, |limb| <=
+// 128, and 131072 * 128 * 127 < 2^31.
+constexpr int UG_MAX_K = 131072;
+constexpr int UG_X_BITS = 22;                    // |X| <= 2^22 after scaling
 
 struct UgArgs {
     int M, N, K, nkb;             // nkb: k blocks of UG_BK
-    const long long* rowsum;      // [M] sum_k X
     const int* shift;             // [M] -s, or UG_ROW_NONFINITE
-    int code_bias;                // qmax: 127 (INT8) or 7 (INT4)
     int* status;                  // set to 1 when a wait gave up (may be null)
     QmvEpilogue ep;               // col_scale etc.; row_shift unused
 };
@@ -71,25 +73,13 @@ __device__ __forceinline__ uint64_t ug_desc_kmajor(uint32_t saddr) {
     return d;
 }
 
-// MN-major operand, 128-byte swizzle: 128 consecutive n per 128-byte row, one
-// row per k; 8-row groups 1024 bytes apart along k (stride byte offset);
-// 128-column atoms `lbo` bytes apart along n (a single atom here).
-__device__ __forceinline__ uint64_t ug_desc_mnmajor(uint32_t saddr, uint32_t lbo) {
-    uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-    d |= (uint64_t)(1024u >> 4) << 32;
-    d |= (uint64_t)1u << 46;
-    d |= (uint64_t)2u << 61;
-    return d;
-}
-
-// Instruction descriptor for kind::i8, int32 accumulate, A K-major (s8 or
-// u8), B MN-major u8, M = UG_BM, N = UG_BN.
+// Instruction descriptor for kind::i8, int32 accumulate, A = limb K-major
+// (s8), B = codes K-major s8, M = UG_BM, N = UG_BN.
 __device__ __forceinline__ uint32_t ug_idesc(bool a_signed) {
     uint32_t d = 2u << 4;                   // D format S32
     d |= (a_signed ? 1u : 0u) << 7;         // A: 1 = s8, 0 = u8
-    d |= 0u << 10;                          // B: u8
-    d |= 1u << 16;                          // B MN-major
+    d |= 1u << 10;                          // B: s8 (signed codes)
+    d |= 0u << 16;                          // B K-major
     d |= (uint32_t)(UG_BN >> 3) << 17;
     d |= (uint32_t)(UG_BM >> 4) << 24;
     return d;
@@ -126,6 +116,25 @@ __device__ __forceinline__ void ug_tma_3d(void* dst, const CUtensorMap* tm, int 
         : "memory");
 }
 
+__device__ __forceinline__ void ug_tma_4d(void* dst, const CUtensorMap* tm, int c0, int c1, int c2, int c3,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(dz_smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(dz_smem_addr(bar))
+        : "memory");
+}
+
+// The same with an L2 cache policy (createpolicy), for streamed weights.
+__device__ __forceinline__ void ug_tma_4d_hint(void* dst, const CUtensorMap* tm, int c0, int c1, int c2, int c3,
+                                               uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dz_smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(dz_smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 // 32 consecutive int32 columns of this warp's 32 TMEM lanes (one per thread).
 __device__ __forceinline__ void ug_tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
     uint32_t r[32];
@@ -147,24 +156,52 @@ __device__ __forceinline__ void ug_tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
 // INT4 codes (two per byte, even index in the low nibble, src/core/
 // quantize.c:213-221) of a k x cols matrix -> one byte per code in rows of
 // `ld` bytes.
-__global__ void dz_widen_nibbles_kernel(const uint8_t* __restrict__ packed, long long cols, long long total,
-                                        uint8_t* __restrict__ out, int ld) {
+// The code copy for the tensor-core kernels: the signed levels q = code - qmax
+// (in [-qmax, qmax]: loaded blobs hold no code above 2 * qmax) as s8 in
+// K-major 16 KB blocks, codes[tile][kb][n % 128][k % 128] with tile = n / 128
+// and kb = k / 128, so one TMA box (128 n x 128 k) is one contiguous read and
+// lands as the K-major operand the 8-bit MMA reads at full rate. Source: the
+// reference's k x cols order (INT8 bytes or packed nibbles, low nibble first)
+// placed at columns [off, off + cols). Padding (n >= N, k >= K) stays as the
+// caller zeroed it (q = 0).
+__global__ void dz_code_blocks_kernel(const uint8_t* __restrict__ packed, int bits, long long cols, long long total,
+                                      int8_t* __restrict__ codes, int nkb, int off) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= total) return;
-    const long long k = i / cols, n = i - k * cols;
-    out[k * ld + n] = (packed[i >> 1] >> ((i & 1) * 4)) & 0xF;
+    const long long k = i / cols, n = off + (i - k * cols);
+    const int c = bits == 8 ? (int)packed[i] - 127 : (int)((packed[i >> 1] >> ((i & 1) * 4)) & 0xF) - 7;
+    const long long blk = (n / UG_BN) * nkb + k / UG_BK;
+    codes[(blk * UG_BN + n % UG_BN) * UG_BK + k % UG_BK] = (int8_t)c;
 }
 
 // ------------------------------------------------------- activation limbs
 
-// One block per row: X = rint(x * k_scale * 2^s) clamped to 24 bits, stored
-// as three limb planes L[limb][M][Kp] (zero past K), the row sum of X and -s.
+// X of one element: rint(v * 2^s) (|X| <= 2^22 for finite v), 0 for a
+// non-finite v (the row is flagged separately).
+__device__ __forceinline__ int ug_fixed(float v, int s) {
+    if (!(fabsf(v) <= 3.402823466e38f)) return 0;
+    const float f = rintf(dz_mul_pow2(v, s));
+    const float lim = (float)(1 << UG_X_BITS);
+    return f >= lim ? (1 << UG_X_BITS) : f <= -lim ? -(1 << UG_X_BITS) : (int)f;
+}
+// Balanced base-256 digits of X: X = 65536 * t + 256 * m + l, l, m in
+// [-128, 127], |t| <= 64; each returned as its byte.
+__device__ __forceinline__ void ug_digits(int X, uint32_t& t, uint32_t& m, uint32_t& l) {
+    const int d0 = (int)(int8_t)(X & 0xFF);
+    const int x1 = (X - d0) >> 8;
+    const int d1 = (int)(int8_t)(x1 & 0xFF);
+    const int d2 = (x1 - d1) >> 8;
+    l = (uint32_t)d0 & 0xFFu;
+    m = (uint32_t)d1 & 0xFFu;
+    t = (uint32_t)d2 & 0xFFu;
+}
+
+// One block per row: X = rint(x * k_scale * 2^s), stored as three signed limb
+// planes L[limb][M][Kp] (zero past K), and -s.
 __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restrict__ X, long long ldx,
                                                             const float* __restrict__ k_scale, int M, int K, int Kp,
-                                                            int8_t* __restrict__ L, long long* __restrict__ rowsum,
-                                                            int* __restrict__ shift) {
+                                                            int8_t* __restrict__ L, int* __restrict__ shift) {
     __shared__ float wred[8];
-    __shared__ long long wsum[8];
     __shared__ int wbad[8];
     const int r = blockIdx.x;
     const float* x = X + (long long)r * ldx;
@@ -192,8 +229,7 @@ __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restr
         amax = fmaxf(amax, wred[w]);
         bad |= wbad[w];
     }
-    const int s = amax > 0.0f ? 22 - ilogbf(amax) : 0;
-    long long sum = 0;
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
     const size_t plane = (size_t)M * Kp;
     for (int k0 = threadIdx.x * 4; k0 < Kp; k0 += blockDim.x * 4) {
         uint32_t t4 = 0, m4 = 0, l4 = 0;
@@ -204,31 +240,20 @@ __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restr
             if (k < K) {
                 float v = x[k];
                 if (k_scale) v *= k_scale[k];
-                if (fabsf(v) <= 3.402823466e38f) {
-                    const float f = rintf(dz_mul_pow2(v, s));
-                    xi = f >= 8388607.0f ? 8388607 : f <= -8388608.0f ? -8388608 : (int)f;
-                }
+                xi = ug_fixed(v, s);
             }
-            sum += xi;
-            t4 |= ((uint32_t)(xi >> 16) & 0xFFu) << (8 * j);
-            m4 |= ((uint32_t)(xi >> 8) & 0xFFu) << (8 * j);
-            l4 |= ((uint32_t)xi & 0xFFu) << (8 * j);
+            uint32_t dt, dm, dl;
+            ug_digits(xi, dt, dm, dl);
+            t4 |= dt << (8 * j);
+            m4 |= dm << (8 * j);
+            l4 |= dl << (8 * j);
         }
         const size_t at = (size_t)r * Kp + k0;
         *reinterpret_cast<uint32_t*>(L + at) = t4;
         *reinterpret_cast<uint32_t*>(L + plane + at) = m4;
         *reinterpret_cast<uint32_t*>(L + 2 * plane + at) = l4;
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = sum;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        long long t = 0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += wsum[w];
-        rowsum[r] = t;
-        shift[r] = bad ? UG_ROW_NONFINITE : -s;
-    }
+    if (threadIdx.x == 0) shift[r] = bad ? UG_ROW_NONFINITE : -s;
 }
 
 // Columns [n0, n0 + UG_BN) of rows [m0, m0 + UG_BM) from the staging tile
@@ -292,6 +317,101 @@ __device__ __forceinline__ void ug_store_tile(const UgArgs& a, const float* tile
     }
 }
 
+constexpr int UG_SPLIT_CHUNK = 1024;   // k per block of dz_limb_split_chunk_kernel
+
+// The limb split for few rows: grid (ceil(Kp / UG_SPLIT_CHUNK), M). Every
+// block reads its whole row once (thread t holds elements c * 1024 + 4t ..
+// + 3 of every chunk c; float4 loads when the row and k_scale are 16-byte
+// aligned and K % 4 == 0), keeps its own chunk's four in registers, finds the
+// row's maximum (the same exponent in every block) and converts those four:
+// one global round trip. It lets the GEMV launched after it start at once
+// (programmatic dependent launch): the GEMV streams weights and waits for
+// this grid only before it reads the limbs.
+__global__ void __launch_bounds__(256) dz_limb_split_chunk_kernel(const float* __restrict__ X, long long ldx,
+                                                                  const float* __restrict__ k_scale, int M, int K,
+                                                                  int Kp, int8_t* __restrict__ L,
+                                                                  int* __restrict__ shift) {
+    __shared__ float wred[8];
+    __shared__ int wbad[8];
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int r = blockIdx.y, ch = blockIdx.x;
+    const float* x = X + (long long)r * ldx;
+    const bool vec = (K & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(k_scale)) & 15u) == 0;
+    const int nch = (K + UG_SPLIT_CHUNK - 1) / UG_SPLIT_CHUNK;
+    float mine[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float m = 0.0f;
+    int bad = 0;
+#pragma unroll 4
+    for (int c = 0; c < nch; c++) {
+        const int k0 = c * UG_SPLIT_CHUNK + threadIdx.x * 4;
+        float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        if (vec) {
+            if (k0 < K) {
+                const float4 q = *reinterpret_cast<const float4*>(x + k0);
+                v[0] = q.x;
+                v[1] = q.y;
+                v[2] = q.z;
+                v[3] = q.w;
+                if (k_scale) {
+                    const float4 w = *reinterpret_cast<const float4*>(k_scale + k0);
+                    v[0] *= w.x;
+                    v[1] *= w.y;
+                    v[2] *= w.z;
+                    v[3] *= w.w;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+                if (k0 + j < K) {
+                    v[j] = x[k0 + j];
+                    if (k_scale) v[j] *= k_scale[k0 + j];
+                }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (!(fabsf(v[j]) <= 3.402823466e38f)) bad = 1;
+            else m = fmaxf(m, fabsf(v[j]));
+            if (c == ch) mine[j] = v[j];
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        wred[threadIdx.x >> 5] = m;
+        wbad[threadIdx.x >> 5] = bad;
+    }
+    __syncthreads();
+    float amax = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+        amax = fmaxf(amax, wred[w]);
+        bad |= wbad[w];
+    }
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
+    const size_t plane = (size_t)M * Kp;
+    const int k0 = ch * UG_SPLIT_CHUNK + threadIdx.x * 4;
+    if (k0 < Kp) {
+        uint32_t t4 = 0, m4 = 0, l4 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint32_t dt, dm, dl;
+            ug_digits(ug_fixed(mine[j], s), dt, dm, dl);   // zero past K
+            t4 |= dt << (8 * j);
+            m4 |= dm << (8 * j);
+            l4 |= dl << (8 * j);
+        }
+        const size_t at = (size_t)r * Kp + k0;
+        *reinterpret_cast<uint32_t*>(L + at) = t4;
+        *reinterpret_cast<uint32_t*>(L + plane + at) = m4;
+        *reinterpret_cast<uint32_t*>(L + 2 * plane + at) = l4;
+    }
+    if (threadIdx.x == 0 && ch == 0) shift[r] = bad ? UG_ROW_NONFINITE : -s;
+}
+
 // ------------------------------------------------------------------- GEMM
 
 __global__ void __launch_bounds__(UG_THREADS, 1)
@@ -341,7 +461,7 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
             }
             dz_mbar_expect_tx(&full[s], UG_STAGE_BYTES);
             for (int limb = 0; limb < UG_LIMBS; limb++) ug_tma_3d(stage_a(s, limb), &tmA, kb * UG_BK, m0, limb, &full[s]);
-            ug_tma_2d(stage_b(s), &tmB, n0, kb * UG_BK, &full[s]);
+            ug_tma_4d(stage_b(s), &tmB, 0, 0, kb, blockIdx.x, &full[s]);
         }
         progress[0] = kb;
       }
@@ -350,7 +470,7 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
       if (lane == 0) {
         // MMA issuer: 3 limbs x 4 k-steps of 32 per stage
         int kb = 0;
-        const uint32_t id_top = ug_idesc(true), id_low = ug_idesc(false);
+        const uint32_t idesc = ug_idesc(true);
         for (; kb < a.nkb; kb++) {
             const int s = kb % UG_STAGES;
             if (!dz_mbar_wait(&full[s], (uint32_t)((kb / UG_STAGES) & 1))) {
@@ -365,9 +485,8 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
 #pragma unroll
                 for (int kk = 0; kk < UG_BK / 32; kk++) {
                     const uint64_t ad = ug_desc_kmajor(a_addr + kk * 32);
-                    const uint64_t bd = ug_desc_mnmajor(b_addr + kk * 32 * UG_BN, UG_B_BYTES);
-                    ug_mma(tmem + (uint32_t)(limb * UG_BN), ad, bd, limb == 0 ? id_top : id_low,
-                           (kb > 0 || kk > 0) ? 1u : 0u);
+                    const uint64_t bd = ug_desc_kmajor(b_addr + kk * 32);
+                    ug_mma(tmem + (uint32_t)(limb * UG_BN), ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                 }
             }
             ug_commit(&empty[s]);
@@ -387,7 +506,6 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
         const int row = m0 + rl;
         const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
         const bool live = row < a.M;
-        const long long bias = live ? (long long)a.code_bias * a.rowsum[row] : 0;
         const int e = live ? a.shift[row] : 0;
         if (!ok || progress[2]) {
             if (a.status && lane == 0) atomicExch(a.status, 1);
@@ -406,7 +524,7 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int c = 4 * q + j;
-                    const long long v = (long long)top[c] * 65536 + (long long)mid[c] * 256 + (long long)low[c] - bias;
+                    const long long v = (long long)top[c] * 65536 + (long long)mid[c] * 256 + (long long)low[c];
                     y[j] = dz_mul_pow2(__ll2float_rn(v), e);
                     if (!ok || e == UG_ROW_NONFINITE) y[j] = __int_as_float(0x7fc00000);
                 }
@@ -432,6 +550,353 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
     if (warp == 1) {
         ug_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(UG_TMEM_COLS) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------- GEMV
+
+// The same integer formulation for M <= 16 rows (decode matvecs), with the
+// roles turned round so the tensor core's 128-row side holds output columns:
+// D[128 n x 48] += codes[128 n x k] . limbs[k x 48], the code blocks as the
+// K-major A operand (no dequantization) and the three limbs' 16 rows each
+// (rows past M zero-filled by TMA) as one 48-row K-major B operand, so one
+// MMA per 32 k serves all three limbs.
+//
+// Work is split stream-K: the ntiles x nkb (n-tile, k block) stages, tile
+// major, are cut into gridDim.x equal contiguous ranges, one per CTA, so every
+// CTA streams the same number of weight bytes. A CTA's range holds whole tiles
+// and at most two pieces of tiles shared with its neighbours. A piece's three
+// limb accumulators become int64 partials (exact, so order does not matter),
+// stored in the CTA's slot 0 (the first segment of its range) or slot 1 (the
+// last); the per-tile counter adds k blocks and the piece that completes the
+// tile (counter reaches nkb) adds the other pieces and finishes: convert to
+// fp32 once, apply 2^-s and the epilogue. That CTA resets the counter for the
+// next launch. The codes are signed levels, so the products need no offset
+// correction.
+//
+// The kernel is launched as a programmatic dependent of the limb split: the
+// weight loads of the first UV_STAGES stages go out at once, and only the
+// limb loads and the row exponents wait for the split grid
+// (griddepcontrol.wait); every output store comes after that wait.
+constexpr int UV_N = 16;                          // rows (tokens) per UMMA
+constexpr int UV_STAGES = 9;
+constexpr uint32_t UV_A_BYTES = UG_BN * UG_BK;    // 128 n x 128 k codes
+constexpr uint32_t UV_B_BYTES = UV_N * UG_BK;     // 16 rows x 128 k, one limb
+constexpr uint32_t UV_B_PITCH = (UV_B_BYTES + 1023) & ~1023u;
+static_assert(UV_B_PITCH == UV_B_BYTES, "the three limb boxes of a stage form one 48-row operand");
+constexpr uint32_t UV_STAGE_BYTES = UV_A_BYTES + UG_LIMBS * UV_B_PITCH;
+constexpr uint32_t UV_ACC_COLS = UG_LIMBS * UV_N; // one accumulator set: 48 columns
+constexpr uint32_t UV_TMEM_COLS = 128;            // two sets
+constexpr size_t UV_SMEM_BYTES = (size_t)UV_STAGES * UV_STAGE_BYTES + 1024 + 512;
+constexpr size_t UV_SLOT_ELEMS = (size_t)UG_BN * UV_N;   // int64 per partial slot
+constexpr int UV_MIN_STAGES_PER_CTA = 4;
+
+struct UvArgs {
+    int M, N, K, nkb;             // nkb: k blocks of UG_BK per tile
+    int ntiles;
+    long long total;              // ntiles * nkb
+    const int* shift;             // [M] -s, or UG_ROW_NONFINITE
+    long long* partial;           // [gridDim.x][2][UV_SLOT_ELEMS]
+    int* counter;                 // [ntiles], zero between launches
+    int* status;
+    QmvEpilogue ep;               // row_shift unused
+};
+
+// First stage of CTA c's range, and the CTA whose range holds stage p.
+__device__ __forceinline__ long long uv_range_start(long long total, int c, int G) {
+    return total * c / G;
+}
+__device__ __forceinline__ int uv_owner(long long total, long long p, int G) {
+    return (int)(((p + 1) * G - 1) / total);
+}
+
+// Next segment of a CTA's range: the tile holding stage `pos`, its first k
+// block and the k blocks up to the tile's or the range's end.
+struct UvSeg {
+    int tile, kb0, nk;
+};
+__device__ __forceinline__ UvSeg uv_segment(long long pos, long long end, int nkb) {
+    UvSeg g;
+    g.tile = (int)(pos / nkb);
+    g.kb0 = (int)(pos - (long long)g.tile * nkb);
+    g.nk = (int)min((long long)(nkb - g.kb0), end - pos);
+    return g;
+}
+
+// Epilogue of one output column for rows 0..M-1 (M <= R): the column's scale,
+// bias and output segment are looked up once and the residuals are loaded
+// before any store, so the rows do not wait on one another.
+template <int R>
+__device__ __forceinline__ void dz_qmv_store_col(const QmvEpilogue& e, int M, int N, int n, const float (&acc)[R]) {
+    if (n >= N) return;
+    const float cs = e.col_scale ? e.col_scale[n] : 0.0f;
+    const float bi = e.bias ? e.bias[n] : 0.0f;
+    int s = 0;
+    while (s + 1 < e.nseg && n >= e.seg_start[s + 1]) s++;
+    float res[R];
+#pragma unroll
+    for (int m = 0; m < R; m++) res[m] = (e.residual && m < M) ? e.residual[(long long)m * e.ld_res + n] : 0.0f;
+    int roff[R];
+#pragma unroll
+    for (int m = 0; m < R; m++) roff[m] = (e.seg_row_off[s] && m < M) ? e.seg_row_off[s][m] : 0;
+#pragma unroll
+    for (int m = 0; m < R; m++) {
+        if (m >= M) break;
+        float y = e.col_scale ? acc[m] * cs : acc[m];
+        if (e.bias) y = y + bi;
+        if (e.residual) y = y + res[m];
+        if (e.relu) y = y > 0.0f ? y : 0.0f;
+        e.seg_ptr[s][(long long)m * e.seg_ld[s] + (n - e.seg_start[s]) + roff[m]] = y;
+    }
+}
+
+__device__ __forceinline__ void ug_tmem_ld16(uint32_t taddr, int32_t (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = (int32_t)r[i];
+}
+
+// Instruction descriptor: A = codes (s8, K-major), B = the three limbs' rows
+// (s8, K-major), M = 128 output columns, N = 3 x 16 limb rows, int32
+// accumulate.
+__device__ __forceinline__ uint32_t uv_idesc() {
+    uint32_t d = 2u << 4;                 // D format S32
+    d |= 1u << 7;                         // A: s8
+    d |= 1u << 10;                        // B: s8
+    d |= 0u << 15;                        // A K-major
+    d |= 0u << 16;                        // B K-major
+    d |= (uint32_t)((UG_LIMBS * UV_N) >> 3) << 17;
+    d |= (uint32_t)(UG_BN >> 4) << 24;
+    return d;
+}
+
+// Warp 0 lane 0 streams the stages by TMA through a UV_STAGES ring that runs
+// across segments; warp 1 lane 0 issues the MMAs into one of two accumulator
+// sets (segments alternate, so a segment's epilogue overlaps the next
+// segment's MMAs); warps 4-7 drain a set (one output column per thread).
+__global__ void __launch_bounds__(UG_THREADS, 1)
+    dz_ugemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmL, UvArgs a) {
+    extern __shared__ __align__(1024) uint8_t uv_raw[];
+    const uint32_t raw = dz_smem_addr(uv_raw);
+    uint8_t* sm = uv_raw + ((1024u - (raw & 1023u)) & 1023u);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + (size_t)UV_STAGES * UV_STAGE_BYTES);
+    uint64_t* empty = full + UV_STAGES;
+    uint64_t* tfull = empty + UV_STAGES;      // [2] accumulator set ready
+    uint64_t* tempty = tfull + 2;             // [2] accumulator set drained (4 epilogue warps arrive)
+    int* row_e = reinterpret_cast<int*>(tempty + 2);   // [UV_N] -s or UG_ROW_NONFINITE
+    int* pend_kb = row_e + UV_N;                        // [UV_STAGES] k block of a stage whose limbs wait
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pend_kb + UV_STAGES);
+    int* flags = reinterpret_cast<int*>(tmem_slot + 1);   // [0] stages issued, [1] consumed, [2] failed, [3] last
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = gridDim.x;
+    const long long s0 = uv_range_start(a.total, blockIdx.x, G), s1 = uv_range_start(a.total, blockIdx.x + 1, G);
+    auto stage_a = [&](int s) { return sm + (size_t)s * UV_STAGE_BYTES; };
+    auto stage_b = [&](int s, int limb) { return sm + (size_t)s * UV_STAGE_BYTES + UV_A_BYTES + (size_t)limb * UV_B_PITCH; };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < UV_STAGES; s++) {
+            dz_mbar_init(&full[s]);
+            dz_mbar_init(&empty[s]);
+        }
+        for (int b = 0; b < 2; b++) {
+            dz_mbar_init(&tfull[b]);
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 4;" ::"r"(dz_smem_addr(&tempty[b])) : "memory");
+        }
+        flags[0] = flags[1] = flags[2] = flags[3] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dz_smem_addr(tmem_slot)),
+                     "r"(UV_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    ug_fence_before();
+    __syncthreads();
+    ug_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // the weights are read once per product: they should not push
+            // the activations and other reused data out of L2
+            const uint64_t wpol = dz_policy_evict_first();
+            int i = 0;   // stage counter over the range
+            bool stop = false, limbs_ready = false;
+            auto load_limbs = [&](int s, int kb) {
+                for (int limb = 0; limb < UG_LIMBS; limb++)
+                    ug_tma_3d(stage_b(s, limb), &tmL, kb * UG_BK, 0, limb, &full[s]);
+            };
+            auto release_pending = [&]() {   // the split grid is done: its limbs can be read
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                for (int q = 0; q < i && q < UV_STAGES; q++) load_limbs(q, pend_kb[q]);
+                limbs_ready = true;
+            };
+            for (long long pos = s0; pos < s1 && !stop;) {
+                const UvSeg g = uv_segment(pos, s1, a.nkb);
+                for (int j = 0; j < g.nk; j++, i++) {
+                    const int s = i % UV_STAGES;
+                    if (i >= UV_STAGES) {
+                        if (!limbs_ready) release_pending();
+                        if (!dz_mbar_wait(&empty[s], (uint32_t)(((i / UV_STAGES) - 1) & 1))) {
+                            flags[2] = 1;
+                            stop = true;
+                            break;
+                        }
+                    }
+                    const int kb = g.kb0 + j;
+                    dz_mbar_expect_tx(&full[s], UV_A_BYTES + UG_LIMBS * UV_B_BYTES);
+                    ug_tma_4d_hint(stage_a(s), &tmW, 0, 0, kb, g.tile, &full[s], wpol);
+                    if (limbs_ready) load_limbs(s, kb);
+                    else pend_kb[s] = kb;
+                }
+                pos += g.nk;
+            }
+            if (!limbs_ready) release_pending();
+            flags[0] = i;
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t idesc = uv_idesc();
+            int i = 0, t = 0;   // stage counter, segment counter
+            bool stop = false;
+            for (long long pos = s0; pos < s1 && !stop; t++) {
+                const UvSeg g = uv_segment(pos, s1, a.nkb);
+                pos += g.nk;
+                const int buf = t & 1;
+                // the accumulator set of segment t-2 has been drained
+                if (t >= 2 && !dz_mbar_wait(&tempty[buf], (uint32_t)(((t >> 1) - 1) & 1))) {
+                    flags[2] = 1;
+                    break;
+                }
+                ug_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(buf * UV_ACC_COLS);
+                for (int j = 0; j < g.nk; j++, i++) {
+                    const int s = i % UV_STAGES;
+                    if (!dz_mbar_wait(&full[s], (uint32_t)((i / UV_STAGES) & 1))) {
+                        flags[2] = 1;
+                        stop = true;
+                        break;
+                    }
+                    ug_fence_after();
+                    // one MMA per 32 k covers the three limbs: B is the
+                    // stage's 48 limb rows (limb-major, 16 rows each)
+                    const uint32_t a_addr = dz_smem_addr(stage_a(s)), b_addr = dz_smem_addr(stage_b(s, 0));
+#pragma unroll
+                    for (int kk = 0; kk < UG_BK / 32; kk++) {
+                        const uint64_t ad = ug_desc_kmajor(a_addr + kk * 32);
+                        const uint64_t bd = ug_desc_kmajor(b_addr + kk * 32);
+                        ug_mma(acc, ad, bd, idesc, (j > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    ug_commit(&empty[s]);
+                }
+                ug_commit(&tfull[buf]);   // this segment's accumulator set is complete
+            }
+            flags[1] = i;
+        }
+        __syncwarp();
+    } else if (warp == 2) {
+        // row exponents: written by the split grid, read after it completed
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        if (lane < UV_N) row_e[lane] = lane < a.M ? a.shift[lane] : 0;
+        __syncwarp();
+        asm volatile("bar.arrive 2, 160;" ::: "memory");
+    } else if (warp >= 4) {
+        // thread = output column n0 + nl: 16 rows x 3 limbs -> int64
+        asm volatile("bar.sync 2, 160;" ::: "memory");   // row exponents are in place
+        const int ew = warp - 4;
+        const int nl = ew * 32 + lane;
+        const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+        int t = 0;
+        for (long long pos = s0; pos < s1; t++) {
+            const bool first = pos == s0;
+            const UvSeg g = uv_segment(pos, s1, a.nkb);
+            pos += g.nk;
+            const int buf = t & 1;
+            bool ok = dz_mbar_wait(&tfull[buf], (uint32_t)((t >> 1) & 1));
+            ug_fence_after();
+            if (!ok || flags[2]) {
+                ok = false;
+                flags[2] = 1;
+                if (a.status && lane == 0) atomicExch(a.status, 1);
+            }
+            const uint32_t acc = tmem + lane_base + (uint32_t)(buf * UV_ACC_COLS);
+            int32_t top[UV_N], mid[UV_N], low[UV_N];
+            ug_tmem_ld16(acc, top);
+            ug_tmem_ld16(acc + UV_N, mid);
+            ug_tmem_ld16(acc + 2 * UV_N, low);
+            ug_fence_before();
+            __syncwarp();
+            if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(dz_smem_addr(&tempty[buf])) : "memory");
+            long long v[UV_N];
+#pragma unroll
+            for (int r = 0; r < UV_N; r++) v[r] = (long long)top[r] * 65536 + (long long)mid[r] * 256 + (long long)low[r];
+            bool finish = true;
+            if (g.nk < a.nkb) {   // a piece of a tile shared with neighbouring ranges
+                long long* mine = a.partial + ((size_t)blockIdx.x * 2 + (first ? 0 : 1)) * UV_SLOT_ELEMS + (size_t)nl * UV_N;
+#pragma unroll
+                for (int r = 0; r < UV_N; r++) __stcg(mine + r, v[r]);
+                // one release by one thread after the barrier covers the
+                // group's stores; its acquire covers the reads below
+                dz_named_sync(1, 128);
+                if (threadIdx.x == 128) {
+                    int prev;
+                    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+                                 : "=r"(prev)
+                                 : "l"(a.counter + g.tile), "r"(g.nk)
+                                 : "memory");
+                    flags[3] = prev + g.nk == a.nkb ? 1 : 0;
+                    if (flags[3]) a.counter[g.tile] = 0;   // ready for the next launch
+                }
+                dz_named_sync(1, 128);
+                finish = flags[3] != 0;
+                dz_named_sync(1, 128);   // everyone read flags[3] before the next piece rewrites it
+                if (finish) {
+                    const long long t0 = (long long)g.tile * a.nkb;
+                    const int c0 = uv_owner(a.total, t0, G), c1 = uv_owner(a.total, t0 + a.nkb - 1, G);
+                    for (int c = c0; c <= c1; c++) {
+                        if (c == (int)blockIdx.x) continue;
+                        const int slot = uv_range_start(a.total, c, G) >= t0 ? 0 : 1;
+                        const long long* pp = a.partial + ((size_t)c * 2 + slot) * UV_SLOT_ELEMS + (size_t)nl * UV_N;
+                        long long q[UV_N];
+#pragma unroll
+                        for (int r = 0; r < UV_N; r++) q[r] = __ldcg(pp + r);
+#pragma unroll
+                        for (int r = 0; r < UV_N; r++) v[r] += q[r];
+                    }
+                }
+            }
+            if (finish) {
+                float y[UV_N];
+#pragma unroll
+                for (int r = 0; r < UV_N; r++) {
+                    const int e = row_e[r];
+                    y[r] = dz_mul_pow2(__ll2float_rn(v[r]), e);
+                    if (!ok || e == UG_ROW_NONFINITE) y[r] = __int_as_float(0x7fc00000);
+                }
+                dz_qmv_store_col<UV_N>(a.ep, a.M, a.N, g.tile * UG_BN + nl, y);
+            }
+        }
+    }
+
+    ug_fence_before();
+    __syncthreads();
+    if (threadIdx.x == 0 && flags[2]) {
+        // copies in flight land before the shared memory goes away
+        for (int i = flags[1]; i < flags[0]; i++)
+            if (!dz_mbar_wait(&full[i % UV_STAGES], (uint32_t)((i / UV_STAGES) & 1))) break;
+    }
+    __syncthreads();
+    if (warp == 1) {
+        ug_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(UV_TMEM_COLS) : "memory");
     }
 }
 

@@ -136,3 +136,78 @@ def test_matmul_rejects_bad_k(gpu):
     with pytest.raises(gpu.DzError):
         q.matmul(np.ones((2, 7), np.float32))
     q.close()
+
+
+@pytest.mark.parametrize("gran", [0, 1, 2])
+def test_matmul_tensor_core_gemv_ragged(gpu, oracle, gran):
+    """8..16 rows on matrices of at least 2^20 codes (the tcgen05 GEMV):
+    ragged K and N, every granularity, activations from an aligned buffer and
+    from a device buffer off the 16-byte grid (the split's scalar path),
+    against the oracle."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.RandomState(23 + gran)
+    for (m, k, n) in [(8, 1100, 1000), (16, 4104, 300), (13, 2048, 1031)]:
+        for bits in (8, 4):
+            w = (rng.randn(k, n) * 0.05).astype(np.float32)
+            buf = rng.randn(m * k + 1).astype(np.float32)
+            q = gpu.QuantizedWeightMatrix.encode(w, bits, gran)
+            s, p = oracle.quantize_pack(w, bits, gran)
+            a = np.ascontiguousarray(buf[1:].reshape(m, k))
+            ref = oracle.matmul_quantized(a, k, n, s, p, bits, gran)
+            ok, err = _tol_ok(q.matmul(a), ref)
+            assert ok, (m, k, n, bits, gran, err)
+            # the same rows from a device buffer 4 bytes past a 16-byte boundary
+            xd = torch.from_numpy(buf).cuda()
+            cd = torch.empty((m, n), dtype=torch.float32, device="cuda")
+            q.matmul_async(xd.data_ptr() + 4, cd.data_ptr(), m, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            ok, err = _tol_ok(cd.cpu().numpy(), ref)
+            assert ok, ("unaligned", m, k, n, bits, gran, err)
+            q.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_matmul_tensor_core_gemv_large(gpu, oracle, bits):
+    """3..16 rows on a matrix of more than 2^25 codes (the GEMV from 3 rows),
+    K = 4096, N = 8300 (not a multiple of the 128-column tile); the oracle
+    checks a seeded sample of columns."""
+    st = np.array([gpu.rng_stream(5, gpu.STREAM_TESTING)], np.uint64)
+    K, N = 4096, 8300
+    x = gpu.synth_gaussian(st, 16 * K, 1.0).reshape(16, K)
+    w = gpu.synth_gaussian(st, K * N, 0.02).reshape(K, N)
+    q = gpu.QuantizedWeightMatrix.encode(w, bits)
+    cols = np.sort(np.random.RandomState(bits).choice(N, 128, replace=False))
+    cols[-1] = N - 1
+    s_sub, p_sub = oracle.quantize_pack(np.ascontiguousarray(w[:, cols]), bits, 2)
+    for M in (3, 5, 8, 11, 16):
+        c = q.matmul(x[:M])
+        assert c.shape == (M, N) and np.isfinite(c).all()
+        ref = oracle.matmul_quantized(np.ascontiguousarray(x[:M]), K, len(cols), s_sub, p_sub, bits, 2)
+        ok, err = _tol_ok(c[:, cols], ref)
+        assert ok, (M, err)
+    q.close()
+
+
+def test_matmul_tensor_core_gemv_dynamic_range_and_nonfinite(gpu, oracle):
+    """The GEMV at M = 12: rows spanning 2^-30 .. 2^20, a tiny row, and rows
+    holding inf / NaN (NaN out, the other rows unaffected)."""
+    rng = np.random.RandomState(12)
+    m, k, n = 12, 1536, 1000
+    w = (rng.randn(k, n) * 0.05).astype(np.float32)
+    a = (rng.randn(m, k) * np.exp2(rng.randint(-30, 20, size=(m, k)))).astype(np.float32)
+    a[5] *= 1e-30
+    for bits in (8, 4):
+        q = gpu.QuantizedWeightMatrix.encode(w, bits)
+        s, p = oracle.quantize_pack(w, bits, 2)
+        ref = oracle.matmul_quantized(a, k, n, s, p, bits, 2)
+        c = q.matmul(a)
+        for r in range(m):
+            ok, err = _tol_ok(c[r], ref[r])
+            assert ok, (bits, r, err)
+        bad = a.copy()
+        bad[3, 7] = np.inf
+        bad[9, 100] = np.nan
+        c = q.matmul(bad)
+        assert np.isnan(c[9]).all() and not np.isfinite(c[3]).any()
+        assert np.isfinite(np.delete(c, [3, 9], axis=0)).all()
+        q.close()
