@@ -1028,6 +1028,8 @@ static size_t seq_smem_for(const dz_cuda_model_t* m, int cap) {
 static void prepare_seqgen(dz_cuda_model_t* m) {
     m->seq_ok = false;
     if (m->layers.empty() || m->desc.embedding_dim % 4 != 0) return;  // 16-byte aligned activations
+    // the fused attention keeps a head's output in four registers per lane
+    if (m->desc.num_heads == 0 || m->desc.embedding_dim / m->desc.num_heads > 128) return;
     const int bits = m->head.bits;
     if (bits != 4 && bits != 8 || m->head.k_scale) return;
     for (auto& L : m->layers) {

@@ -303,6 +303,142 @@ __device__ __forceinline__ void seq_split_block(const float* src, int n, __half*
     if (threadIdx.x == 0) *shift_slot = -sh;
 }
 
+// Attention of one decode position over ctx ring rows (transformer.c:686-713)
+// followed by the fp16 split of its output (the input of W_o). The warps of a
+// head (up to four) split its keys: a lane takes one key and computes its
+// whole q.k (float4 reads in a lane-rotated order, so the lanes' rows do not
+// fall into one bank), the warp keeps an online softmax (running max m and
+// sum l), and accumulates p.v with its lanes over the head dimension. After
+// one barrier the warps of each head merge (m, l, vector); the merged output
+// goes straight into the split. exp is expf of the difference to the running
+// maximum, as in the reference's softmax; the normalisation divides the
+// accumulated vector once. `scratch` holds wph x D floats, `red` 48.
+__device__ __forceinline__ void seq_attention(int H, int hd, int D, int cap, int ctx, int start, const float* Ksrc,
+                                              const float* Vsrc, const float* q, float denom, float* scratch,
+                                              float* red, float* att, __half* xs, int xs_stride, int* shift_slot) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float NEG_INF = __int_as_float(0xff800000);
+    const int wph = H >= SEQ_WARPS ? 1 : min(4, SEQ_WARPS / H);   // warps per head
+    const int hpr = SEQ_WARPS / wph;                                // heads per round
+    const bool vec = (hd & 3) == 0 && (D & 3) == 0;
+    const int nv = vec ? hd / 4 : hd;                               // float4s (or floats) per row
+    const int rot = lane % nv;
+    float* mw = red;               // [SEQ_WARPS] running max per warp
+    float* lw = red + SEQ_WARPS;   // [SEQ_WARPS] running sum per warp
+    const bool fused_split = H <= hpr && D <= SEQ_THREADS;
+    float out = 0.0f;
+    for (int h0 = 0; h0 < H; h0 += hpr) {
+        const int h = h0 + warp / wph, w = warp % wph;
+        if (warp < hpr * wph && h < H) {
+            const int j0 = w * ctx / wph, j1 = (w + 1) * ctx / wph;
+            const float* qh = q + h * hd;
+            float m = NEG_INF, l = 0.0f;
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int c0 = j0; c0 < j1; c0 += 32) {
+                const int j = c0 + lane;
+                float sc = NEG_INF;
+                if (j < j1) {
+                    int phys = start + j;
+                    if (phys >= cap) phys -= cap;
+                    const float* kr = Ksrc + (long long)phys * D + h * hd;
+                    float dot = 0.0f;
+                    if (vec) {
+                        const float4* k4 = reinterpret_cast<const float4*>(kr);
+                        const float4* q4 = reinterpret_cast<const float4*>(qh);
+                        for (int c = 0; c < nv; c++) {
+                            int cc = rot + c;
+                            if (cc >= nv) cc -= nv;
+                            const float4 kv = k4[cc], qv = q4[cc];
+                            dot = fmaf(qv.x, kv.x, dot);
+                            dot = fmaf(qv.y, kv.y, dot);
+                            dot = fmaf(qv.z, kv.z, dot);
+                            dot = fmaf(qv.w, kv.w, dot);
+                        }
+                    } else {
+                        for (int c = 0; c < nv; c++) {
+                            int cc = rot + c;
+                            if (cc >= nv) cc -= nv;
+                            dot = fmaf(qh[cc], kr[cc], dot);
+                        }
+                    }
+                    sc = dot / denom;
+                }
+                float cmax = sc;
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
+                const float mn = fmaxf(m, cmax);
+                const float pj = j < j1 ? expf(sc - mn) : 0.0f;
+                const float corr = expf(m - mn);
+                float ps = pj;
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+                l = l * corr + ps;
+#pragma unroll
+                for (int i = 0; i < 4; i++) acc[i] *= corr;
+                const int n = min(32, j1 - c0);
+                for (int u = 0; u < n; u++) {
+                    const float pu = __shfl_sync(0xffffffffu, pj, u);
+                    int phys = start + c0 + u;
+                    if (phys >= cap) phys -= cap;
+                    const float* vr = Vsrc + (long long)phys * D + h * hd;
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const int e = lane + 32 * i;
+                        if (e < hd) acc[i] = fmaf(pu, vr[e], acc[i]);
+                    }
+                }
+                m = mn;
+            }
+            if (lane == 0) {
+                mw[warp] = m;
+                lw[warp] = l;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int e = lane + 32 * i;
+                if (e < hd) scratch[w * D + h * hd + e] = acc[i];
+            }
+        }
+        __syncthreads();
+        // merge the warps of each head of this round
+        for (int i = threadIdx.x; i < D; i += SEQ_THREADS) {
+            const int h = i / hd;
+            if (h < h0 || h >= h0 + hpr) continue;
+            const int wb = (h - h0) * wph;
+            float M = NEG_INF;
+            for (int w = 0; w < wph; w++) M = fmaxf(M, mw[wb + w]);
+            float num = 0.0f, den = 0.0f;
+            for (int w = 0; w < wph; w++) {
+                const float f = expf(mw[wb + w] - M);
+                num = fmaf(f, scratch[w * D + i], num);
+                den = fmaf(f, lw[wb + w], den);
+            }
+            const float o = num / den;
+            if (fused_split) out = o;
+            else att[i] = o;
+        }
+        if (!fused_split) __syncthreads();   // the next round reuses mw / lw / scratch
+    }
+    if (!fused_split) {
+        seq_split_block(att, D, xs, xs_stride, shift_slot, red + 2 * SEQ_WARPS);
+        return;
+    }
+    // split of the merged output (held by threads 0..D-1): block max, then
+    // each thread stores its element's hi / mid / lo
+    float mx = threadIdx.x < D ? fabsf(out) : 0.0f;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float* wred = red + 2 * SEQ_WARPS;
+    if (lane == 0) wred[warp] = mx;
+    __syncthreads();
+    float amax = 0.0f;
+#pragma unroll
+    for (int w = 0; w < SEQ_WARPS; w++) amax = fmaxf(amax, wred[w]);
+    const int sh = dz_row_shift(amax);
+    if (threadIdx.x < D) seq_split_store(xs, xs_stride, threadIdx.x, out, sh);
+    if (threadIdx.x == 0) *shift_slot = -sh;
+}
+
 // LayerNorm (src/core/tensor_ops.c:88-111) of D values in shared memory, by
 // warp 0 (shuffle reductions, no block barrier until the output is written).
 __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const float* gamma, const float* beta,
@@ -648,96 +784,10 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
             kv_pending = false;
             const float* Ksrc = ksm ? ksm : Kl;
             const float* Vsrc = vsm ? vsm : Vl;
-            // attention over the ring (transformer.c:686-713). Scores: one warp
-            // per (head, key row), lanes across the head dimension (coalesced
-            // row reads), four rows in flight per warp.
-            {
-                const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-                const int rows = H * ctx;
-                for (int r0 = warp; r0 < rows; r0 += SEQ_WARPS * 4) {
-                    float part[4];
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        const int r = r0 + u * SEQ_WARPS;
-                        part[u] = 0.0f;
-                        if (r < rows) {
-                            const int h = r / ctx, j = r - (r / ctx) * ctx;
-                            int phys = start + j;
-                            if (phys >= cap) phys -= cap;
-                            const float* kr = Ksrc + (long long)phys * D + h * hd;
-                            const float* qh = s.q + h * hd;
-                            for (int e2 = lane; e2 < hd; e2 += 32) part[u] = fmaf(qh[e2], kr[e2], part[u]);
-                        }
-                    }
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-#pragma unroll
-                        for (int off = 16; off >= 1; off >>= 1)
-                            part[u] += __shfl_xor_sync(0xffffffffu, part[u], off);
-                    }
-                    if (lane == 0) {
-#pragma unroll
-                        for (int u = 0; u < 4; u++) {
-                            const int r = r0 + u * SEQ_WARPS;
-                            if (r < rows) {
-                                const int h = r / ctx, j = r - (r / ctx) * ctx;
-                                s.scores[h * cap + j] = part[u] / denom;
-                            }
-                        }
-                    }
-                }
-            }
-            __syncthreads();
-            {
-                const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-                for (int h = warp; h < H; h += SEQ_WARPS) {
-                    float* sc = s.scores + h * cap;
-                    float mx = -3.402823466e38f;
-                    for (int j = lane; j < ctx; j += 32) mx = fmaxf(mx, sc[j]);
-#pragma unroll
-                    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-                    float sum = 0.0f;
-                    for (int j = lane; j < ctx; j += 32) {
-                        const float ev = expf(sc[j] - mx);
-                        sc[j] = ev;
-                        sum += ev;
-                    }
-#pragma unroll
-                    for (int off = 16; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                    const float inv = 1.0f / sum;
-                    for (int j = lane; j < ctx; j += 32) sc[j] = sc[j] * inv;
-                }
-            }
-            __syncthreads();
-            // o = sum_j p_j v_j: thread (g, t) sums rows j = g, g + G, ...
-            // (coalesced across t), groups combine through shared memory.
-            {
-                const int groups = D <= SEQ_THREADS ? SEQ_THREADS / D : 1;
-                for (int t0 = 0; t0 < D; t0 += SEQ_THREADS) {
-                    const int t = t0 + (threadIdx.x % (D < SEQ_THREADS ? D : SEQ_THREADS));
-                    const int g = D < SEQ_THREADS ? threadIdx.x / D : 0;
-                    float acc = 0.0f;
-                    if (g < groups && t < D) {
-                        const float* sc = s.scores + (t / hd) * cap;
-#pragma unroll 4
-                        for (int j = g; j < ctx; j += groups) {
-                            int phys = start + j;
-                            if (phys >= cap) phys -= cap;
-                            acc = fmaf(sc[j], Vsrc[(long long)phys * D + t], acc);
-                        }
-                    }
-                    s.part[threadIdx.x] = acc;
-                    __syncthreads();
-                    if (threadIdx.x < (D < SEQ_THREADS ? D : SEQ_THREADS) && t0 + threadIdx.x < D) {
-                        const int w = D < SEQ_THREADS ? D : SEQ_THREADS;
-                        float o = 0.0f;
-                        for (int gg = 0; gg < groups; gg++) o += s.part[gg * w + threadIdx.x];
-                        s.att[t0 + threadIdx.x] = o;
-                    }
-                    __syncthreads();
-                }
-            }
-            seq_split_block(s.att, D, s.xs[1], xs_stride, &s.xsh[1], s.red);
+            // attention over the ring (transformer.c:686-713), then the fp16
+            // split of its output for W_o
+            seq_attention(H, hd, D, cap, ctx, start, Ksrc, Vsrc, s.q, denom, s.hid, s.red, s.att, s.xs[1],
+                          xs_stride, &s.xsh[1]);
             clk.mark(SEQ_PH_ATTENTION);
             // W_o, + residual, then LayerNorm with the gamma/beta carried in W_o's blob
             if (!acquire()) return false;

@@ -156,14 +156,18 @@ def test_batched_against_oracle_with_reset_mask(gpu, oracle):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
-def test_fused_matches_layered_random_model(gpu, oracle, bits):
-    """Both paths on a model off the golden shapes (d=80, 5 heads of 16, F=320, V=700, L=3),
-    batch 7, greedy and top-k: identical token streams."""
-    spec = Spec(700, 80, 5, 3, 48)
+@pytest.mark.parametrize("shape", [(700, 80, 5, 3, 48, 9), (600, 128, 2, 2, 40, 30), (500, 128, 1, 2, 70, 12),
+                                   (400, 128, 16, 1, 64, 50)])
+def test_fused_matches_layered_random_model(gpu, oracle, bits, shape):
+    """Both paths on models off the golden shapes: d=80 with 5 heads of 16
+    (F=320, V=700, L=3), d=128 with 2 heads of 64, 1 head of 128 and 16 heads
+    of 8 (one warp per head over 2 chunks of keys, the ring wrapping); batch 7,
+    greedy and top-k: identical token streams, equal to the oracle's."""
+    spec = Spec(*shape[:5])
     recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, 33), bits)
     model = gpu.Model.from_arrays(spec, [(k, r, c, f, s, p, bits, 2) for (_, k, r, c, f, s, p) in recs])
     rng = np.random.RandomState(bits)
-    prompts = rng.randint(0, 256, size=(7, 9)).astype(np.uint32)
+    prompts = rng.randint(0, min(256, shape[0]), size=(7, shape[5])).astype(np.uint32)
     assert gpu.KVCache(model, 7).uses_fused(gpu.Sampling(gpu.GREEDY))
     seeds = np.arange(7, dtype=np.uint64) + 100
     om = oracle.model(spec, flat)
