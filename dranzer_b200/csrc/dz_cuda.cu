@@ -2183,11 +2183,14 @@ extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prom
 
 // ------------------------------------------------ allocation-free matmul
 
-// Scratch of dz_cuda_matmul_quantized_noalloc: the bf16 hi/mid/lo split of the
-// activation rows (m x 3 x padded k). Every GPU that loads this library holds
-// it until the process exits. It is shared by all calls on a device and keeps
-// the last call's contents; the split kernel overwrites every byte a call then
-// reads, so nothing needs clearing between calls.
+// Scratch of dz_cuda_matmul_quantized_noalloc, laid out as every product
+// scratch (qmv_scratch_bytes): the tensor-core GEMV's per-tile counters, then
+// the activation split or limbs and the GEMV's partial sums. Every GPU that
+// loads this library holds it until the process exits. It is shared by all
+// calls on a device and keeps the last call's contents: the kernels overwrite
+// every byte of split, limbs and partials that they then read, and each call
+// zeroes the counter block before its kernels run, since the GEMV relies on
+// counters that start at zero.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[DZ_NOALLOC_SCRATCH_BYTES];
 
 static std::mutex g_noalloc_mutex;
@@ -2219,13 +2222,15 @@ extern "C" int dz_cuda_matmul_quantized_noalloc(const float* A, const dz_cuda_qm
     if (need > (size_t)DZ_NOALLOC_SCRATCH_BYTES)
         return fail(DZ_E_INVALID,
                     "matmul_quantized_noalloc: m=%zu rows x k=%zu need %zu bytes of scratch, above the static "
-                    "limit of %u bytes (ceil(m/2) * 16 * k padded to 32/64, + 4m)",
+                    "limit of %u bytes",
                     m, k, need, (unsigned)DZ_NOALLOC_SCRATCH_BYTES);
     DeviceGuard g(q->device);
     if (!g.ok) return fail(DZ_E_DEVICE, "cannot select device %d", q->device);
     void* scratch = nullptr;
     int rc = noalloc_scratch(q->device, &scratch);
     if (rc) return rc;
+    // counters from an earlier call that stopped part-way must not leak into this one
+    DZ_CUDA(cudaMemsetAsync(scratch, 0, SCRATCH_COUNTERS, (cudaStream_t)stream));
     QmvEpilogue ep = plain_epilogue(q->m, C, q->m.N);
     launch_qmv(q->m, A, (long long)k, (int)m, ep, (cudaStream_t)stream, scratch, q->status);
     DZ_CUDA(cudaGetLastError());

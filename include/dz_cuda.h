@@ -68,21 +68,25 @@ int dz_cuda_matmul_quantized(const float *A, const dz_cuda_qmatrix_t *weights, f
 int dz_cuda_matmul_quantized_async(const float *A_dev, const dz_cuda_qmatrix_t *weights,
                                    float *C_dev, size_t m, size_t k, void *stream);
 
-/* Same product as dz_cuda_matmul_quantized_async, for callers that cannot
- * allocate device memory when they call: code recording a CUDA graph (a stream
- * capture forbids cudaMalloc) and hosts that hand the library no allocation
- * rights after start-up. The async entry point grows a per-matrix scratch
+/* Same product as dz_cuda_matmul_quantized_async, for callers that cannot call
+ * cudaMalloc when they multiply: hosts that budget all device memory at
+ * start-up and hand the library no allocation rights afterwards, or that run
+ * it where an allocation could stall or fail mid-step. The async entry point
+ * grows a per-matrix scratch
  * buffer with cudaMalloc the first time it sees a larger m; this one allocates
- * nothing and uses a fixed DZ_NOALLOC_SCRATCH_BYTES array that every GPU which
- * loads the library holds until exit. ceil(m / 2) * 16 * kp bytes of split
- * activations (kp = k rounded up to 32 for INT8, 64 for INT4) plus 4 * m bytes
- * of row exponents, each rounded up to 256, must fit in it (e.g. m <= 126 at
- * k = 4096); larger calls return DZ_E_INVALID.
+ * nothing and uses a fixed DZ_NOALLOC_SCRATCH_BYTES (8 MiB) array that every
+ * GPU which loads the library holds until exit. The call's scratch must fit in
+ * it: 16 KB of tensor-core GEMV tile counters plus the largest of the split
+ * activations (ceil(m / 2) * 16 * kp bytes, kp = k rounded up to 32 for INT8,
+ * 64 for INT4, + 4 * m), the tensor-core limbs (3 * m * k rounded up to 128,
+ * + 4 * m) and, for m <= 16, the GEMV's partial sums (up to 148 x 32 KB).
+ * That allows m <= 254 at k = 4096; larger calls return DZ_E_INVALID.
  * The first call on a device looks up the array's device address (make that
  * call before any stream capture). All calls on a device share the array, so
- * calls whose work overlaps on the GPU (different streams, no ordering) race.
+ * calls whose work overlaps on the GPU (different streams, no ordering) race;
+ * each call zeroes the counters it relies on before its kernels run.
  * No counterpart in the reference. */
-#define DZ_NOALLOC_SCRATCH_BYTES (4u << 20)
+#define DZ_NOALLOC_SCRATCH_BYTES (8u << 20)
 int dz_cuda_matmul_quantized_noalloc(const float *A_dev, const dz_cuda_qmatrix_t *weights, float *C_dev,
                                      size_t m, size_t k, void *stream);
 

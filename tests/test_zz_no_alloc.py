@@ -1,8 +1,12 @@
 """The allocation-free quantized matmul (dz_cuda_matmul_quantized_noalloc).
 
-Callers that cannot allocate device memory when they call - code recording a
-CUDA graph, hosts with no allocation rights after start-up - get the same
-product as dz_cuda_matmul_quantized_async from a fixed static scratch array.
+Some hosts budget all device memory at start-up and give the library no right
+to call cudaMalloc afterwards; they multiply through this entry point, which
+takes its scratch from a fixed static device array instead of growing a buffer.
+These tests check that it gives the product of dz_cuda_matmul_quantized_async,
+on two calls in a row (the array keeps the previous call's contents), on the
+CUDA-core matvec path and on the tensor-core GEMV path (whose tile counters
+live in the array), and that calls too large for the array are refused.
 This file is collected last on purpose: a failure here leaves every other test
 already run."""
 import numpy as np
@@ -17,16 +21,17 @@ def _tol_ok(c, ref):
 
 
 @pytest.mark.parametrize("bits", [4, 8])
-def test_noalloc_matches_allocating_entry_point(gpu, bits):
+@pytest.mark.parametrize("shape", [(1000, 3000, (5, 3)), (4096, 8300, (12, 9))])
+def test_noalloc_matches_allocating_entry_point(gpu, bits, shape):
     import torch
     from dranzer_b200 import _native
     L = _native.lib()
-    K, N = 1000, 3000
+    K, N, ms = shape
     rng = np.random.RandomState(bits)
     w = (rng.randn(K, N) * 0.02).astype(np.float32)
     q = gpu.QuantizedWeightMatrix.encode(w, bits)
     stream = torch.cuda.Stream()
-    for call, m in enumerate((5, 3)):   # two calls in a row on the shared array
+    for call, m in enumerate(ms):   # two calls in a row on the shared array
         a = torch.from_numpy(rng.randn(m, K).astype(np.float32)).cuda()
         c_ref = torch.zeros((m, N), dtype=torch.float32, device="cuda")
         c_new = torch.full((m, N), float("nan"), dtype=torch.float32, device="cuda")
@@ -47,10 +52,10 @@ def test_noalloc_rejects_oversized_calls(gpu):
     L = _native.lib()
     import torch
     q = gpu.QuantizedWeightMatrix.encode(np.ones((4096, 16), np.float32), 8)
-    a = torch.zeros((171, 4096), dtype=torch.float32, device="cuda")
-    c = torch.zeros((171, 16), dtype=torch.float32, device="cuda")
-    # 86 row pairs x 16 x 4096 bytes of split activations are above the 4 MiB array
-    st = L.dz_cuda_matmul_quantized_noalloc(a.data_ptr(), q.handle, c.data_ptr(), 171, 4096, None)
+    a = torch.zeros((300, 4096), dtype=torch.float32, device="cuda")
+    c = torch.zeros((300, 16), dtype=torch.float32, device="cuda")
+    # 150 row pairs x 16 x 4096 bytes of split activations are above the 8 MiB array
+    st = L.dz_cuda_matmul_quantized_noalloc(a.data_ptr(), q.handle, c.data_ptr(), 300, 4096, None)
     assert st == -1
     assert "static" in _native.last_error()[1]
     q.close()
