@@ -1010,7 +1010,7 @@ static size_t seq_smem_bytes(const dz_cuda_model_t* m, int cap, bool kv_smem) {
     auto r4 = [](size_t n) { return (n + 3) & ~(size_t)3; };
     const size_t table = (sizeof(SeqLayer) * m->layers.size() + 15) & ~(size_t)15;
     const size_t xs_stride = (F + 63) / 64 * 64;
-    return 2 * (size_t)m->seq_buf_bytes + 64 + table + 8 * (P > (size_t)SEQ_WARPS ? P : (size_t)SEQ_WARPS) +
+    return 2 * (size_t)m->seq_buf_bytes + 64 + table + 8 * (P > (size_t)SEQ_THREADS ? P : (size_t)SEQ_THREADS) +
            4 * (5 * r4(D) + r4(F) + 2 * r4(V) + r4(H * (size_t)cap) + 64 + 2 * r4(pv)) +
            (kv_smem ? 8 * r4((size_t)cap * D) : 0) + 2 * 4 * r4(3 * xs_stride / 2);
 }

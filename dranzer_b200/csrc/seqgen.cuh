@@ -186,6 +186,7 @@ __device__ __forceinline__ const SeqMat& seq_mat(const SeqParams& p, const SeqLa
 // buffer seq & 1; its barrier phase is (seq >> 1) & 1.
 struct SeqPipe {
     int per_step;      // matrices per step: 4L + 1
+    int in_step;       // issued % per_step, kept incrementally
     long long issued;  // next matrix to issue
     long long total;   // matrices the job consumes
 };
@@ -193,7 +194,7 @@ struct SeqPipe {
 __device__ __forceinline__ void seq_issue(const SeqParams& p, SeqSmem& s, SeqPipe& pipe) {
     // thread 0 only; buffer (issued & 1) must be free
     if (pipe.issued >= pipe.total) return;
-    const SeqMat& m = seq_mat(p, s.layers, (int)(pipe.issued % pipe.per_step));
+    const SeqMat& m = seq_mat(p, s.layers, pipe.in_step);
     const int b = (int)(pipe.issued & 1);
     mbar_expect_tx(&s.bar[b], m.bytes);
     const uint8_t* src = m.blob;
@@ -203,6 +204,7 @@ __device__ __forceinline__ void seq_issue(const SeqParams& p, SeqSmem& s, SeqPip
         bulk_g2s(dst + off, src + off, n, &s.bar[b]);
     }
     pipe.issued++;
+    if (++pipe.in_step == pipe.per_step) pipe.in_step = 0;
 }
 
 // Block-level quantized matvec on the tensor cores from the shared-memory copy
@@ -473,6 +475,70 @@ __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const
     __syncthreads();
 }
 
+// Ascending bitonic sort of the n keys of a (n a power of two), the network of
+// dz_bitonic_sort with its keys held in registers for n <= 2 * SEQ_THREADS:
+// element i = e * SEQ_THREADS + threadIdx.x, padded to SEQ_THREADS with the
+// largest key (a holds at least SEQ_THREADS entries). Partners closer than 32
+// are exchanged by warp shuffles, partners up to SEQ_THREADS / 2 apart through
+// a[] (two barriers per stage), the partner SEQ_THREADS away sits in the same
+// thread. Larger n go to dz_bitonic_sort.
+__device__ void seq_sort_keys(uint64_t* a, int n) {
+    if (n > 2 * SEQ_THREADS) {
+        dz_bitonic_sort(a, n);
+        return;
+    }
+    const int m = n < SEQ_THREADS ? SEQ_THREADS : n;
+    const int E = m / SEQ_THREADS;   // keys per thread: 1 or 2
+    const int tid = threadIdx.x;
+    uint64_t v[2];
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int i = e * SEQ_THREADS + tid;
+        v[e] = (e < E && i < n) ? a[i] : ~0ull;
+    }
+    for (int size = 2; size <= m; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= SEQ_THREADS) {   // E == 2: elements tid and tid + SEQ_THREADS
+                const bool up = (tid & size) == 0;
+                if ((v[0] > v[1]) == up) {
+                    const uint64_t t = v[0];
+                    v[0] = v[1];
+                    v[1] = t;
+                }
+                continue;
+            }
+            uint64_t w[2];
+            if (stride >= 32) {
+                __syncthreads();   // earlier readers of a[] are done
+#pragma unroll
+                for (int e = 0; e < 2; e++)
+                    if (e < E) a[e * SEQ_THREADS + tid] = v[e];
+                __syncthreads();
+#pragma unroll
+                for (int e = 0; e < 2; e++) w[e] = e < E ? a[(e * SEQ_THREADS + tid) ^ stride] : 0ull;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 2; e++) w[e] = __shfl_xor_sync(0xffffffffu, v[e], stride);
+            }
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                if (e >= E) continue;
+                const int i = e * SEQ_THREADS + tid;
+                const bool take_min = ((i & stride) == 0) == ((i & size) == 0);
+                const bool less = v[e] < w[e];
+                v[e] = take_min ? (less ? v[e] : w[e]) : (less ? w[e] : v[e]);
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        const int i = e * SEQ_THREADS + tid;
+        if (e < E && i < n) a[i] = v[e];
+    }
+    __syncthreads();
+}
+
 // Selection over the logits in shared memory; returns the token on every thread.
 __device__ uint32_t seq_select(const SeqParams& p, SeqSmem& s, uint64_t* rng) {
     const int V = p.V;
@@ -516,7 +582,7 @@ __device__ uint32_t seq_select(const SeqParams& p, SeqSmem& s, uint64_t* rng) {
     for (int i = threadIdx.x; i < P; i += SEQ_THREADS)
         s.keys[i] = i < V ? dz_desc_key(lg[i] * inv_t, (uint32_t)i) : ~0ull;
     __syncthreads();
-    dz_bitonic_sort(s.keys, P);
+    seq_sort_keys(s.keys, P);
     const int nexp = p.strategy == 1 ? (p.top_k < V ? p.top_k : V) : V;
     const float top = dz_key_value(s.keys[0]);
     for (int i = threadIdx.x; i < nexp; i += SEQ_THREADS) s.ev[i] = dz_expf(dz_key_value(s.keys[i]) - top);
@@ -612,7 +678,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
     s.layers = reinterpret_cast<SeqLayer*>(cur); cur += (sizeof(SeqLayer) * p.L + 15) & ~(size_t)15;
     int P = 1;
     while (P < V) P <<= 1;
-    s.keys = reinterpret_cast<uint64_t*>(cur); cur += 8 * (P > SEQ_WARPS ? P : SEQ_WARPS);
+    s.keys = reinterpret_cast<uint64_t*>(cur); cur += 8 * (P > SEQ_THREADS ? P : SEQ_THREADS);
     // float arrays, each rounded up to 16 bytes (bulk-copy destinations and
     // float4 activation reads need the alignment); seq_smem_bytes mirrors this
     float* f = reinterpret_cast<float*>(cur);
@@ -660,6 +726,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
     const long long steps = (long long)p.plen + (p.n_new > 0 ? p.n_new - 1 : 0);
     pipe.total = steps * pipe.per_step;
     pipe.issued = 0;
+    pipe.in_step = 0;
     if (threadIdx.x == 0) {
         seq_issue(p, s, pipe);
         seq_issue(p, s, pipe);
