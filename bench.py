@@ -34,7 +34,7 @@ METRIC = "INT4/INT8 decode tokens/s at 1/2/4/8 B200; quant-matvec HBM GB/s vs pe
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one dz_seqgen_kernel launch on the
 # C2 job (64 sequences x (32 + 32), INT4 d128 L4 V512), one ncu capture
-SEQGEN_C2_DRAM_BYTES = 1047296 + 30208
+SEQGEN_C2_DRAM_BYTES = 1025280 + 60672
 
 
 def peaks():
@@ -404,7 +404,7 @@ def run_dz(args, wl):
                          {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4), "peak_source": peak_src,
                          # DRAM bytes of one dz_seqgen_kernel launch on this workload, from one ncu
-                         # capture (profiles/c2_bench_launch_list.md)
+                         # capture (profiles/seqgen_c2_int4.md)
                          "traffic": SEQGEN_C2_DRAM_BYTES if dom == "seqgen" and wl.name == W.C2.name else None,
                          "note": "bytes = weight codes+scales+fp32 tensors each sequence streams per step "
                                  "x steps x sequences; all of it is L2-resident for this workload, so the "
