@@ -196,6 +196,78 @@ __device__ __forceinline__ void ug_digits(int X, uint32_t& t, uint32_t& m, uint3
     t = (uint32_t)d2 & 0xFFu;
 }
 
+// One pass over a row of K <= UG_SPLIT_REG_K elements (K % 4 == 0, row and
+// k_scale 16-byte aligned): thread t holds the float4s 4 (j * 256 + t) of the
+// row in registers, so the row is read once; the maximum, exponent and limbs
+// are those of the two-pass form below.
+constexpr int UG_SPLIT_REG_V = 8;                          // float4s per thread
+constexpr int UG_SPLIT_REG_K = 256 * 4 * UG_SPLIT_REG_V;   // 8192
+__device__ __forceinline__ void ug_limb_split_row_regs(const float* __restrict__ x, const float* __restrict__ k_scale,
+                                                       int r, int M, int K, int Kp, int8_t* __restrict__ L,
+                                                       int* __restrict__ shift, float* wred, int* wbad) {
+    float4 v[UG_SPLIT_REG_V];
+    float m = 0.0f;
+    int bad = 0;
+#pragma unroll
+    for (int j = 0; j < UG_SPLIT_REG_V; j++) {
+        const int k0 = (j * 256 + (int)threadIdx.x) * 4;
+        v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (k0 < K) {
+            v[j] = *reinterpret_cast<const float4*>(x + k0);
+            if (k_scale) {
+                const float4 w = *reinterpret_cast<const float4*>(k_scale + k0);
+                v[j].x *= w.x;
+                v[j].y *= w.y;
+                v[j].z *= w.z;
+                v[j].w *= w.w;
+            }
+        }
+        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            if (!(fabsf(e[c]) <= 3.402823466e38f)) bad = 1;
+            else m = fmaxf(m, fabsf(e[c]));
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        wred[threadIdx.x >> 5] = m;
+        wbad[threadIdx.x >> 5] = bad;
+    }
+    __syncthreads();
+    float amax = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
+        amax = fmaxf(amax, wred[w]);
+        bad |= wbad[w];
+    }
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
+    const size_t plane = (size_t)M * Kp;
+#pragma unroll
+    for (int j = 0; j < UG_SPLIT_REG_V; j++) {
+        const int k0 = (j * 256 + (int)threadIdx.x) * 4;
+        if (k0 >= Kp) continue;
+        const float e[4] = {v[j].x, v[j].y, v[j].z, v[j].w};   // zero past K
+        uint32_t t4 = 0, m4 = 0, l4 = 0;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            uint32_t dt, dm, dl;
+            ug_digits(ug_fixed(e[c], s), dt, dm, dl);
+            t4 |= dt << (8 * c);
+            m4 |= dm << (8 * c);
+            l4 |= dl << (8 * c);
+        }
+        const size_t at = (size_t)r * Kp + k0;
+        *reinterpret_cast<uint32_t*>(L + at) = t4;
+        *reinterpret_cast<uint32_t*>(L + plane + at) = m4;
+        *reinterpret_cast<uint32_t*>(L + 2 * plane + at) = l4;
+    }
+    if (threadIdx.x == 0) shift[r] = bad ? UG_ROW_NONFINITE : -s;
+}
+
 // One block per row: X = rint(x * k_scale * 2^s), stored as three signed limb
 // planes L[limb][M][Kp] (zero past K), and -s.
 __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restrict__ X, long long ldx,
@@ -205,6 +277,11 @@ __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restr
     __shared__ int wbad[8];
     const int r = blockIdx.x;
     const float* x = X + (long long)r * ldx;
+    if (blockDim.x == 256 && K <= UG_SPLIT_REG_K && (K & 3) == 0 &&
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(k_scale)) & 15u) == 0) {
+        ug_limb_split_row_regs(x, k_scale, r, M, K, Kp, L, shift, wred, wbad);
+        return;
+    }
     float m = 0.0f;
     int bad = 0;
 #pragma unroll 8
