@@ -233,12 +233,26 @@ def quant_matvec_probe(dz, torch, stream, hbm, bf16=None):
                 evs[i][1].record(stream)
             torch.cuda.synchronize()
             ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+            # the same launches back to back, as a decode stream issues them:
+            # one event pair around the burst
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            if hasattr(torch.cuda, "_sleep"):
+                with torch.cuda.stream(stream):
+                    torch.cuda._sleep(8_000_000)
+            b0.record(stream)
+            for i in range(reps):
+                mats[i % copies].matmul_async(xd.data_ptr(), yd.data_ptr(), M, stream.cuda_stream)
+            b1.record(stream)
+            torch.cuda.synchronize()
+            ms_stream = b0.elapsed_time(b1) / reps
             nbytes = 4096 * 32000 * bits / 8 + 32000 * 4 + M * 4096 * 4 + M * 32000 * 4
             gbs = nbytes / (ms * 1e-3) / 1e9
             tflops = 2.0 * M * 4096 * 32000 / (ms * 1e-3) / 1e12
             r = {"bits": bits, "M": M, "K": 4096, "N": 32000, "us": round(ms * 1e3, 2),
                  "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "TFLOP/s": round(tflops, 1),
-                 "bytes": int(nbytes)}
+                 "bytes": int(nbytes), "us_stream": round(ms_stream * 1e3, 2),
+                 "frac_stream": round(nbytes / (ms_stream * 1e-3) / 1e9 / hbm, 3)}
             if bf16:
                 r["tensor_frac_of_bf16"] = round(tflops / bf16, 4)
             res.append(r)

@@ -465,12 +465,25 @@ static bool qmv1_launch(const DevQMat& W, const float* X, long long ldx, int M, 
     a.pk = (int)std::min<size_t>(16, ((size_t)g_smem_optin - fixed) / ((size_t)WP * QMS_STAGES * 512));
     const size_t smem = dz_qmv1_smem_bytes(a.pk, WP, xf_bytes, a.max_tiles, a.max_parts);
     ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
-    if (W.bits == 8) {
-        if (xf_bytes) dz_qmv1_kernel<8, WP, true><<<G, WP * 32, smem, st>>>(a);
-        else dz_qmv1_kernel<8, WP, false><<<G, WP * 32, smem, st>>>(a);
-    } else {
-        if (xf_bytes) dz_qmv1_kernel<4, WP, true><<<G, WP * 32, smem, st>>>(a);
-        else dz_qmv1_kernel<4, WP, false><<<G, WP * 32, smem, st>>>(a);
+    // programmatic dependent launch: weight streaming may start while the
+    // previous kernel in the stream drains (the kernel waits for it before
+    // touching activations or outputs)
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)G);
+    cfg.blockDim = dim3(WP * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void (*k)(Qmv1Args) = W.bits == 8 ? (xf_bytes ? dz_qmv1_kernel<8, WP, true> : dz_qmv1_kernel<8, WP, false>)
+                                      : (xf_bytes ? dz_qmv1_kernel<4, WP, true> : dz_qmv1_kernel<4, WP, false>);
+    if (cudaLaunchKernelEx(&cfg, k, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        k<<<G, WP * 32, smem, st>>>(a);
     }
     return true;
 }

@@ -900,6 +900,12 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1_kernel(Qmv1Args a) {
     }
     __syncwarp();
 
+    // Launched as a programmatic dependent of the previous kernel, and lets the
+    // next one launch: its CTAs take SMs as this kernel's CTAs finish. Only
+    // the weight copies (constant for the launch) go out before
+    // griddepcontrol.wait; activations are read and every global write made
+    // after it, i.e. after the previous kernel completed.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // lane 0 keeps two pieces in flight: piece i -> stage i % QMS_STAGES
     Cursor ic = cursor_at(my0);
     int issued = 0, istage = 0;
@@ -914,15 +920,17 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1_kernel(Qmv1Args a) {
         issued++;
         istage = istage == QMS_STAGES - 1 ? 0 : istage + 1;
     };
-    // the activation rows are requested before the first weight pieces, so
-    // they do not queue behind them
+    // the first weight piece goes out before the wait; the activation rows
+    // are requested before the second, so they do not queue behind both
+    if (lane == 0 && ic.pos < my1) issue();
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     float xr[2][QMS_XIN_PAIRS][2];
     if (XIN) {
         dz_split_row_load<QMS_XIN_PAIRS>(a.X, a.k_scale, a.K, xr[0]);
         if (a.M > 1) dz_split_row_load<QMS_XIN_PAIRS>(a.X + a.ldx, a.k_scale, a.K, xr[1]);
     }
     if (lane == 0)
-        for (int i = 0; i < QMS_STAGES - 1 && ic.pos < my1; i++) issue();
+        for (int i = 1; i < QMS_STAGES - 1 && ic.pos < my1; i++) issue();
 
     const int* shifts = a.row_shift;
     if (XIN) {
