@@ -566,8 +566,23 @@ static int launch_ugemv(const DevQMat& W, const float* X, long long ldx, int M, 
     if (!encode_u8_map(&tmL, L, 3, dims, strides, box)) return 0;
     {
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K * nch + 3.0 * M * Kp, 0, st);
-        dz_limb_split_chunk_kernel<<<dim3((unsigned)nch, (unsigned)M), 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp,
-                                                                                      L, shift);
+        // programmatic dependent of the previous kernel: its blocks wait
+        // (griddepcontrol.wait) before reading X or writing the limbs
+        cudaLaunchConfig_t sc;
+        memset(&sc, 0, sizeof(sc));
+        sc.gridDim = dim3((unsigned)nch, (unsigned)M);
+        sc.blockDim = dim3(256);
+        sc.stream = st;
+        cudaLaunchAttribute sa[1];
+        sa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        sa[0].val.programmaticStreamSerializationAllowed = 1;
+        sc.attrs = sa;
+        sc.numAttrs = 1;
+        if (cudaLaunchKernelEx(&sc, dz_limb_split_chunk_kernel, X, ldx, W.k_scale, M, W.K, Kp, L, shift) !=
+            cudaSuccess) {
+            (void)cudaGetLastError();
+            dz_limb_split_chunk_kernel<<<sc.gridDim, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
+        }
     }
     UvArgs a;
     memset(&a, 0, sizeof(a));

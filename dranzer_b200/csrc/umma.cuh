@@ -411,6 +411,10 @@ __global__ void __launch_bounds__(256) dz_limb_split_chunk_kernel(const float* _
     __shared__ float wred[8];
     __shared__ int wbad[8];
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    // launched as a programmatic dependent of the previous kernel (a GEMV
+    // that may still read this scratch's limbs): nothing is read or written
+    // before that kernel completed
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int r = blockIdx.y, ch = blockIdx.x;
     const float* x = X + (long long)r * ldx;
     const bool vec = (K & 3) == 0 &&
@@ -759,6 +763,9 @@ __device__ __forceinline__ uint32_t uv_idesc() {
 // segment's MMAs); warps 4-7 drain a set (one output column per thread).
 __global__ void __launch_bounds__(UG_THREADS, 1)
     dz_ugemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmL, UvArgs a) {
+    // the next kernel (the next call's limb split) may launch now; it waits
+    // for this grid before touching memory
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(1024) uint8_t uv_raw[];
     const uint32_t raw = dz_smem_addr(uv_raw);
     uint8_t* sm = uv_raw + ((1024u - (raw & 1023u)) & 1023u);
