@@ -445,7 +445,56 @@ __device__ __forceinline__ void seq_attention(int H, int hd, int D, int cap, int
 // warp 0 (shuffle reductions, no block barrier until the output is written).
 __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const float* gamma, const float* beta,
                                               int D, __half* xs, int xs_stride, int* shift_slot) {
-    if (threadIdx.x < 32) {
+    constexpr int R = 8;   // elements per lane kept in registers (D <= 256)
+    if (threadIdx.x < 32 && D <= 32 * R) {
+        // the same arithmetic, with the lane's inputs, gamma and beta loaded
+        // once up front instead of re-read from shared memory per pass
+        const int lane = threadIdx.x;
+        float xv[R], gv[R], bv[R], yv[R];
+#pragma unroll
+        for (int j = 0; j < R; j++) {
+            const int i = lane + 32 * j;
+            xv[j] = i < D ? in[i] : 0.0f;
+            gv[j] = i < D ? gamma[i] : 0.0f;
+            bv[j] = i < D ? beta[i] : 0.0f;
+        }
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < R; j++)
+            if (lane + 32 * j < D) s += xv[j];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+        const float mean = s / (float)D;
+        float v = 0.0f;
+#pragma unroll
+        for (int j = 0; j < R; j++)
+            if (lane + 32 * j < D) {
+                const float d = xv[j] - mean;
+                v = fmaf(d, d, v);
+            }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+        const float sd = sqrtf(v / (float)D + 1e-6f);
+        float mx = 0.0f;
+#pragma unroll
+        for (int j = 0; j < R; j++) {
+            const int i = lane + 32 * j;
+            yv[j] = 0.0f;
+            if (i < D) {
+                const float y = gv[j] * ((xv[j] - mean) / sd) + bv[j];
+                out[i] = y;
+                yv[j] = y;
+                mx = fmaxf(mx, fabsf(y));
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        const int sh = dz_row_shift(mx);
+#pragma unroll
+        for (int j = 0; j < R; j++)
+            if (lane + 32 * j < D) seq_split_store(xs, xs_stride, lane + 32 * j, yv[j], sh);
+        if (lane == 0) *shift_slot = -sh;
+    } else if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float s = 0.0f;
         for (int i = lane; i < D; i += 32) s += in[i];
@@ -758,10 +807,11 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         return s.flag[0] == 0;
     };
     // matrix `consumed` no longer read: refill its buffer with the one after next
-    auto release = [&]() {
+    auto release = [&](bool after_barrier = false) {
         // every thread is past its reads of this buffer; the next TMA write
-        // into it is issued after the barrier
-        __syncthreads();
+        // into it is issued after the barrier (the LayerNorm that ends W_o's
+        // and W2's phases ends with one already)
+        if (!after_barrier) __syncthreads();
         if (threadIdx.x == 0) seq_issue(p, s, pipe);
         consumed++;
         clk.mark(SEQ_PH_QMV);
@@ -866,7 +916,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
                 const float* g = reinterpret_cast<const float*>(wb + Ly.wo.gamma_off);
                 seq_layernorm(s.fr, s.an, g, g + D, D, s.xs[0], xs_stride, &s.xsh[0]);
             }
-            release();
+            release(true);
             clk.mark(SEQ_PH_NORM);
             // FFN up + bias + ReLU
             if (!acquire()) return false;
@@ -891,7 +941,7 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
                 const float* g = reinterpret_cast<const float*>(wb + Ly.w2.gamma_off);
                 seq_layernorm(s.fr, s.x, g, g + D, D, s.xs[0], xs_stride, &s.xsh[0]);
             }
-            release();
+            release(true);
             clk.mark(SEQ_PH_NORM);
         }
         if (!acquire()) return false;
