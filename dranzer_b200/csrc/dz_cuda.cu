@@ -311,7 +311,7 @@ static size_t qmv_xf_bytes(const DevQMat& W, int M) {
     return (size_t)W.nkg * KG * (size_t)((M + 1) / 2) * 16;
 }
 // Bytes of scratch the tensor-core GEMM needs for M rows: three limb planes
-// of M x (K rounded up to 128) bytes, the int64 row sums and the exponents.
+// of M x (K rounded up to 128) bytes and the row exponents.
 static size_t ugemm_scratch_bytes(const DevQMat& W, int M) {
     const size_t kp = (size_t)round_up(W.K, UG_BK);
     return r256(3 * (size_t)M * kp) + r256((size_t)M * 4);

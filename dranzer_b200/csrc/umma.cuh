@@ -75,9 +75,9 @@ __device__ __forceinline__ uint64_t ug_desc_kmajor(uint32_t saddr) {
 
 // Instruction descriptor for kind::i8, int32 accumulate, A = limb K-major
 // (s8), B = codes K-major s8, M = UG_BM, N = UG_BN.
-__device__ __forceinline__ uint32_t ug_idesc(bool a_signed) {
+__device__ __forceinline__ uint32_t ug_idesc() {
     uint32_t d = 2u << 4;                   // D format S32
-    d |= (a_signed ? 1u : 0u) << 7;         // A: 1 = s8, 0 = u8
+    d |= 1u << 7;                           // A: s8 (balanced limbs)
     d |= 1u << 10;                          // B: s8 (signed codes)
     d |= 0u << 16;                          // B K-major
     d |= (uint32_t)(UG_BN >> 3) << 17;
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(UG_THREADS, 1)
       if (lane == 0) {
         // MMA issuer: 3 limbs x 4 k-steps of 32 per stage
         int kb = 0;
-        const uint32_t idesc = ug_idesc(true);
+        const uint32_t idesc = ug_idesc();
         for (; kb < a.nkb; kb++) {
             const int s = kb % UG_STAGES;
             if (!dz_mbar_wait(&full[s], (uint32_t)((kb / UG_STAGES) & 1))) {
