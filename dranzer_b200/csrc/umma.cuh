@@ -100,14 +100,6 @@ __device__ __forceinline__ void ug_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void ug_tma_2d(void* dst, const CUtensorMap* tm, int c0, int c1, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            dz_smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(tm)), "r"(c0), "r"(c1), "r"(dz_smem_addr(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ void ug_tma_3d(void* dst, const CUtensorMap* tm, int c0, int c1, int c2, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
