@@ -18,6 +18,7 @@ sys.path.insert(0, os.path.dirname(HERE))
 
 from _native_oracle import (GREEDY, STREAM_DROPOUT, STREAM_INIT, STREAM_SAMPLING,  # noqa: E402
                             STREAM_TESTING, TOPP, TOPK, FLT_MAX, RefHarness)
+from _margins import stream_margins, unit_draws  # noqa: E402
 
 ref = RefHarness()
 L = ref.L
@@ -159,8 +160,13 @@ def gen_qmm():
     np.savez_compressed(os.path.join(HERE, "qmm.npz"), **out)
 
 
+def units_for(seeds, n_new):
+    return unit_draws(lambda s, st: L.dranzer_rng_stream(s, st),
+                      lambda st: L.dranzer_rng_unit(st.ctypes.data), seeds, n_new, STREAM_SAMPLING)
+
+
 def gen_model(name, vocab, dim, heads, layers, max_seq, wseed, bits, prompt_seed, n_seq, plen,
-              n_new, strategy, temperature, top_k, top_p, seeds, logits_seqs):
+              n_new, strategy, temperature, top_k, top_p, seeds, logits_seqs, prompt_logits=True):
     path = f"/tmp/dz_golden_{name}.bin"
     rc = L.rh_build_bundle(path.encode(), vocab, dim, heads, layers, max_seq, wseed, bits, 2)
     assert rc == 0, rc
@@ -175,18 +181,22 @@ def gen_model(name, vocab, dim, heads, layers, max_seq, wseed, bits, prompt_seed
                        top_p, sd.ctypes.data if sd is not None else None, mk.ctypes.data, 4,
                        toks.ctypes.data, lg.ctypes.data)
     assert rc == 0
+    # decision margin of every draw (tests/_margins.py)
+    units = units_for(seeds, n_new) if seeds is not None else None
+    margins = stream_margins(lg, toks, strategy, temperature, top_k, top_p, units)
     # prompt-position logits of sequence 0 (prefill parity)
-    L.rh_reset(h)
-    pl = np.empty((plen, vocab), np.float32)
-    for i in range(plen):
-        L.rh_forward_token(h, int(prompts[0, i]), pl[i].ctypes.data)
+    pl = np.empty((plen if prompt_logits else 0, vocab), np.float32)
+    if prompt_logits:
+        L.rh_reset(h)
+        for i in range(plen):
+            L.rh_forward_token(h, int(prompts[0, i]), pl[i].ctypes.data)
     L.rh_free(h)
     with open(path, "rb") as f:
         blob = np.frombuffer(f.read(), np.uint8)
     os.remove(path)
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"),
                         spec=np.array([vocab, dim, heads, layers, max_seq, wseed, bits], np.int64),
-                        prompts=prompts, tokens=toks, logits=lg[:logits_seqs],
+                        prompts=prompts, tokens=toks, logits=lg[:logits_seqs], margins=margins,
                         prompt_logits=pl, bundle_fnv=np.array([fnv(blob)], np.uint64),
                         bundle_size=np.array([blob.size], np.int64),
                         sampling=np.array([strategy, top_k], np.int64),
@@ -210,17 +220,37 @@ def gen_pe():
     np.savez_compressed(os.path.join(HERE, "pe.npz"), pe_64x128=t)
 
 
-if __name__ == "__main__":
-    gen_rng()
-    gen_quant()
-    gen_qmm()
-    gen_pe()
-    gen_bundle_small()
+def gen_c1():
     # config 1: INT8 greedy, batch 1, 16 prompt + 48 decode
     gen_model("c1", 512, 128, 4, 4, 64, 0, 8, 1, 1, 16, 48, GREEDY, 0.0, 0, 0.0, None, 1)
+
+
+def gen_c2():
     # config 2: INT4 top-p 0.9 at temperature 0.8, 64 x (32 + 32), seed 2*1000+i
     gen_model("c2", 512, 128, 4, 4, 64, 0, 4, 2, 64, 32, 32, TOPP, 0.8, 0, 0.9,
               [2000 + i for i in range(64)], 4)
+
+
+def gen_ring():
     # a ring-eviction case: capacity 32 (max_seq 32), 24 prompt + 40 decode, top-k 5
     gen_model("ring", 400, 64, 2, 2, 32, 7, 8, 3, 2, 24, 40, TOPK, 0.8, 5, 0.0, [70, 71], 2)
-    print("golden fixtures written to", HERE)
+
+
+def gen_c4():
+    # config 4 sample: the full model (d 2048, 16 heads, 24 layers, V 32000,
+    # context 2048, INT8, weights seed 4), the first 2 of its prompts (seed 4,
+    # 512 tokens each), then 8 greedy draws; every draw's logits are kept
+    # (the first is the last prompt position's)
+    gen_model("c4s", 32000, 2048, 16, 24, 2048, 4, 8, 4, 2, 512, 8, GREEDY, 0.0, 0, 0.0, None, 2,
+              prompt_logits=False)
+
+
+GENERATORS = {"rng": gen_rng, "quant": gen_quant, "qmm": gen_qmm, "pe": gen_pe, "bundle": gen_bundle_small,
+              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "c4": gen_c4}
+
+if __name__ == "__main__":
+    # no argument: every fixture except the config-4 sample (minutes of CPU)
+    names = sys.argv[1:] or [n for n in GENERATORS if n != "c4"]
+    for n in names:
+        GENERATORS[n]()
+    print("golden fixtures written to", HERE, ":", " ".join(names))

@@ -5,15 +5,17 @@ Logit parity metric (the normalized form of src/tests/core/
 test_quantized_matmul.c:79): max_i |g_i - r_i| / max(max_i |r_i|, 1e-6),
 target <= 1e-3 per position. Token streams: identical; a divergence is
 accepted only at a documented near-tie (the reference's own top-2 gap or
-sampling boundary margin within 10x the observed logit error), after which the
-sequence is not compared further."""
+sampling boundary margin within 10x the observed logit error, tests/_margins.py),
+after which the sequence is not compared further."""
 import os
 
 import numpy as np
 import pytest
 
 from conftest import golden
+from _margins import check_streams, stream_margins, unit_draws
 from _models import Spec, quantize_params, synth_params
+from _native_oracle import STREAM_SAMPLING
 
 pytestmark = pytest.mark.gpu
 
@@ -56,14 +58,45 @@ def test_c1_logits_every_position(gpu, oracle, tmp_path):
     cache.close(); model.close()
 
 
-def _check_streams(got, ref, ref_logits=None):
-    """Identical streams, or a first divergence at a near-tie of the reference."""
-    bad = []
-    for q in range(ref.shape[0]):
-        diff = np.nonzero(got[q] != ref[q])[0]
-        if diff.size:
-            bad.append((q, int(diff[0])))
-    return bad
+MASKED = [256, 257, 258, 259]
+
+
+def _abs_err(got, ref):
+    """Max absolute logit error, masked ids excluded (the reference holds
+    -FLT_MAX there, the device the raw logit)."""
+    g = np.array(got, np.float32, copy=True)
+    r = np.array(ref, np.float32, copy=True)
+    g[..., MASKED] = 0
+    r[..., MASKED] = 0
+    return float(np.abs(g - r).max())
+
+
+def _golden_logit_err(gpu, model, g, capacity=None):
+    """The device's observed logit error on the golden sequences whose
+    reference logits are stored: their prompts and reference tokens fed
+    through the step API, logits compared at every draw."""
+    lg = g["logits"]
+    n = lg.shape[0]
+    cache = gpu.KVCache(model, n, capacity)
+    prompts, toks = g["prompts"][:n], g["tokens"][:n]
+    for t in range(prompts.shape[1]):
+        out = cache.forward_tokens(prompts[:, t])
+    err = _abs_err(out, lg[:, 0])
+    for i in range(1, lg.shape[1]):
+        out = cache.forward_tokens(toks[:, i - 1])
+        err = max(err, _abs_err(out, lg[:, i]))
+    cache.close()
+    return err
+
+
+def _oracle_margins(oracle, om, prompts, n_new, strategy=0, temperature=0.0, top_k=0, top_p=0.0, seeds=None):
+    """The oracle's tokens, logits and decision margins for a generation."""
+    toks, lg = om.generate(prompts, n_new, strategy, temperature, top_k, top_p, seeds, want_logits=True)
+    units = None
+    if seeds is not None:
+        units = unit_draws(oracle.rng_stream, lambda st: oracle.L.or_rng_unit(st.ctypes.data), seeds, n_new,
+                           STREAM_SAMPLING)
+    return toks, lg, stream_margins(lg, toks, strategy, temperature, top_k, top_p, units)
 
 
 PATHS = {"layered": 1, "fused": 2}
@@ -82,7 +115,7 @@ def test_c1_greedy_stream(gpu, oracle, tmp_path, path):
     samp = gpu.Sampling(gpu.GREEDY)
     cache = _cache(gpu, model, 1, path, samp)
     toks = cache.generate(g["prompts"], 48, samp)
-    assert _check_streams(toks, g["tokens"]) == []
+    check_streams(toks, g["tokens"], g["margins"], _golden_logit_err(gpu, model, g))
     cache.close(); model.close()
 
 
@@ -93,8 +126,9 @@ def test_c2_top_p_streams(gpu, oracle, tmp_path, path):
     samp = gpu.Sampling(gpu.TOPP, 0.8, 0, 0.9)
     cache = _cache(gpu, model, 64, path, samp)
     toks = cache.generate(g["prompts"], 32, samp, seeds=g["seeds"])
-    bad = _check_streams(toks, g["tokens"])
-    assert len(bad) <= 1, bad
+    err = _golden_logit_err(gpu, model, g)
+    bad = check_streams(toks, g["tokens"], g["margins"], err)
+    print(f"c2 {path}: observed logit error {err:.3g}, near-tie divergences {bad}")
     # repeated launches of the cached graph give the same streams
     np.testing.assert_array_equal(cache.generate(g["prompts"], 32, samp, seeds=g["seeds"]), toks)
     cache.close(); model.close()
@@ -107,7 +141,7 @@ def test_ring_eviction_top_k(gpu, oracle, tmp_path, path):
     samp = gpu.Sampling(gpu.TOPK, 0.8, 5, 0.0)
     cache = _cache(gpu, model, 2, path, samp)
     toks = cache.generate(g["prompts"], 40, samp, seeds=g["seeds"])
-    assert _check_streams(toks, g["tokens"]) == []
+    check_streams(toks, g["tokens"], g["margins"], _golden_logit_err(gpu, model, g))
     cache.close(); model.close()
 
 
@@ -217,16 +251,17 @@ def test_large_batch_tensor_core_path(gpu, oracle, bits):
     om = oracle.model(spec, flat)
     for t in range(10):
         got = cache.forward_tokens(prompts[:, t])
+    err = 0.0
     for b in (0, 17):
         om.reset()
         for t in range(10):
             r = om.forward_token(prompts[b, t])
         assert _rel(got[b], r) <= LOGIT_TOL, (b, _rel(got[b], r))
+        err = max(err, _abs_err(got[b], r))
     cache.reset()
     toks = cache.generate(prompts, 8, gpu.Sampling(gpu.GREEDY))
-    ref, _ = om.generate(prompts, 8, 0, 0.0, 0, 0.0, None)
-    bad = _check_streams(toks, ref)
-    assert len(bad) <= 1, bad   # at most one greedy near-tie among the 24 streams
+    ref, _, margins = _oracle_margins(oracle, om, prompts, 8)
+    check_streams(toks, ref, margins, err)
     cache.close(); model.close()
 
 
@@ -254,8 +289,10 @@ def test_batched_prefill_matches_token_prefill(gpu, oracle, bits, hd):
         ref.append(r)
     cache = gpu.KVCache(model, B, 64)
     got = cache.prefill(prompts, lens)
+    err = 0.0
     for b in range(B):
         assert _rel(got[b], ref[b]) <= LOGIT_TOL, (b, _rel(got[b], ref[b]))
+        err = max(err, _abs_err(got[b], ref[b]))
     # the rings hold each prompt: one decode step continues every sequence
     nxt = rng.randint(0, 256, size=B).astype(np.uint32)
     step = cache.forward_tokens(nxt)
@@ -265,14 +302,15 @@ def test_batched_prefill_matches_token_prefill(gpu, oracle, bits, hd):
             om.forward_token(prompts[b, t])
         r = om.forward_token(nxt[b])
         assert _rel(step[b], r) <= LOGIT_TOL, (b, _rel(step[b], r))
+        err = max(err, _abs_err(step[b], r))
     samp = gpu.Sampling(gpu.GREEDY)
     outs = []
     for mode in (gpu.PREFILL_TOKENS, gpu.PREFILL_BATCHED):
         cache.set_prefill(mode)
         outs.append(cache.generate(prompts, 6, samp))
-    gref, _ = om.generate(prompts, 6, 0, 0.0, 0, 0.0, None)
+    gref, _, margins = _oracle_margins(oracle, om, prompts, 6)
     for o in outs:
-        assert len(_check_streams(o, gref)) <= 1
+        check_streams(o, gref, margins, err)
     cache.close(); model.close()
 
 
