@@ -9,6 +9,7 @@
 #include <errno.h>
 #include <fcntl.h>
 #include <math.h>
+#include <pthread.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -43,15 +44,95 @@ double dz_rng_unit(uint64_t *state) {
     return (double)(dz_rng_next(state) >> 11) * (1.0 / 9007199254740992.0);
 }
 
-void dz_synth_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+/* The xorshift state update is linear over GF(2): the state n draws ahead is
+ * a 64 x 64 bit matrix (the update's n-th power) applied to the state. A
+ * matrix is held as the images of the 64 basis vectors. */
+typedef struct { uint64_t col[64]; } gf2_map;
+
+static uint64_t gf2_apply(const gf2_map *m, uint64_t x) {
+    uint64_t y = 0;
+    for (int j = 0; j < 64; j++)
+        if ((x >> j) & 1) y ^= m->col[j];
+    return y;
+}
+
+static void gf2_compose(gf2_map *out, const gf2_map *a, const gf2_map *b) {
+    gf2_map t;
+    for (int j = 0; j < 64; j++) t.col[j] = gf2_apply(a, b->col[j]);
+    *out = t;
+}
+
+/* The state after n draws from `state`. */
+static uint64_t rng_jump(uint64_t state, uint64_t n) {
+    if (n == 0) return state;
+    gf2_map step, acc;
+    for (int j = 0; j < 64; j++) {
+        uint64_t x = UINT64_C(1) << j;
+        x ^= x >> 12;
+        x ^= x << 25;
+        x ^= x >> 27;
+        step.col[j] = x;
+        acc.col[j] = UINT64_C(1) << j;
+    }
+    while (n) {
+        if (n & 1) gf2_compose(&acc, &step, &acc);
+        gf2_compose(&step, &step, &step);
+        n >>= 1;
+    }
+    return gf2_apply(&acc, state ? state : UINT64_C(0x9e3779b97f4a7c15));
+}
+
+static void gaussian_run(uint64_t state, float *out, size_t count, double sd) {
     const double two_pi = 6.283185307179586476925286766559;
     const double floor_u = 1.0 / 9007199254740992.0;
     for (size_t i = 0; i < count; i++) {
-        double u1 = dz_rng_unit(state);
+        double u1 = dz_rng_unit(&state);
         if (u1 < floor_u) u1 = floor_u;
-        double u2 = dz_rng_unit(state);
+        double u2 = dz_rng_unit(&state);
         out[i] = (float)(sd * sqrt(-2.0 * log(u1)) * cos(two_pi * u2));
     }
+}
+
+typedef struct { uint64_t state; float *out; size_t count; double sd; } gaussian_part;
+
+static void *gaussian_thread(void *arg) {
+    gaussian_part *p = (gaussian_part *)arg;
+    gaussian_run(p->state, p->out, p->count, p->sd);
+    return NULL;
+}
+
+/* One value per two draws (Box-Muller). Long fills are cut into pieces, each
+ * started from the state that the draws before it leave (rng_jump), and run
+ * on the host's cores; the values and the final state are those of one
+ * sequential pass. */
+void dz_synth_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+    enum { MAX_PARTS = 64 };
+    const size_t min_part = (size_t)1 << 22;
+    long cores = sysconf(_SC_NPROCESSORS_ONLN);
+    size_t parts = count / min_part;
+    if (parts > (size_t)(cores > 0 ? cores : 1)) parts = (size_t)(cores > 0 ? cores : 1);
+    if (parts > MAX_PARTS) parts = MAX_PARTS;
+    if (parts < 2) {
+        gaussian_run(*state, out, count, sd);
+        *state = rng_jump(*state, 2 * (uint64_t)count);
+        return;
+    }
+    gaussian_part job[MAX_PARTS];
+    pthread_t th[MAX_PARTS];
+    int started[MAX_PARTS] = {0};
+    const size_t per = (count + parts - 1) / parts;
+    for (size_t t = 0; t < parts; t++) {
+        const size_t lo = t * per < count ? t * per : count, hi = lo + per < count ? lo + per : count;
+        job[t].state = rng_jump(*state, 2 * (uint64_t)lo);
+        job[t].out = out + lo;
+        job[t].count = hi - lo;
+        job[t].sd = sd;
+        started[t] = pthread_create(&th[t], NULL, gaussian_thread, &job[t]) == 0;
+        if (!started[t]) gaussian_thread(&job[t]);
+    }
+    for (size_t t = 0; t < parts; t++)
+        if (started[t]) pthread_join(th[t], NULL);
+    *state = rng_jump(*state, 2 * (uint64_t)count);
 }
 
 void dz_synth_prompt_ids(uint64_t *state, uint32_t *out, size_t count, uint32_t vocab,

@@ -41,14 +41,65 @@ double or_rng_unit(uint64_t *state) {
     return (double)(or_rng_next(state) >> 11) * (1.0 / 9007199254740992.0);
 }
 
-void or_fill_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+/* The xorshift state update is linear over GF(2), so the state n draws
+ * ahead is the update's n-th power (a 64 x 64 bit matrix, held as the images
+ * of the basis vectors) applied to the state. Long fills are cut into pieces
+ * started from their own jumped states and generated in parallel; values and
+ * final state equal one sequential pass. */
+typedef struct { uint64_t col[64]; } or_gf2_map;
+
+static uint64_t or_gf2_apply(const or_gf2_map *m, uint64_t x) {
+    uint64_t y = 0;
+    for (int j = 0; j < 64; j++)
+        if ((x >> j) & 1) y ^= m->col[j];
+    return y;
+}
+
+static void or_gf2_compose(or_gf2_map *out, const or_gf2_map *a, const or_gf2_map *b) {
+    or_gf2_map t;
+    for (int j = 0; j < 64; j++) t.col[j] = or_gf2_apply(a, b->col[j]);
+    *out = t;
+}
+
+static uint64_t or_rng_jump(uint64_t state, uint64_t n) {
+    if (n == 0) return state;
+    or_gf2_map step, acc;
+    for (int j = 0; j < 64; j++) {
+        uint64_t x = UINT64_C(1) << j;
+        x ^= x >> 12;
+        x ^= x << 25;
+        x ^= x >> 27;
+        step.col[j] = x;
+        acc.col[j] = UINT64_C(1) << j;
+    }
+    while (n) {
+        if (n & 1) or_gf2_compose(&acc, &step, &acc);
+        or_gf2_compose(&step, &step, &step);
+        n >>= 1;
+    }
+    return or_gf2_apply(&acc, state ? state : UINT64_C(0x9e3779b97f4a7c15));
+}
+
+static void or_gaussian_run(uint64_t state, float *out, size_t count, double sd) {
     const double two_pi = 6.283185307179586476925286766559;
     for (size_t i = 0; i < count; i++) {
-        double u1 = or_rng_unit(state);
+        double u1 = or_rng_unit(&state);
         if (u1 < 1.0 / 9007199254740992.0) u1 = 1.0 / 9007199254740992.0;
-        double u2 = or_rng_unit(state);
+        double u2 = or_rng_unit(&state);
         out[i] = (float)(sd * sqrt(-2.0 * log(u1)) * cos(two_pi * u2));
     }
+}
+
+void or_fill_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+    const size_t piece = (size_t)1 << 22;
+    const long long parts = (long long)((count + piece - 1) / piece);
+    const uint64_t s0 = *state;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (long long t = 0; t < parts; t++) {
+        const size_t lo = (size_t)t * piece, hi = lo + piece < count ? lo + piece : count;
+        or_gaussian_run(or_rng_jump(s0, 2 * (uint64_t)lo), out + lo, hi - lo, sd);
+    }
+    *state = or_rng_jump(s0, 2 * (uint64_t)count);
 }
 
 void or_prompt_ids(uint64_t *state, uint32_t *out, size_t count, uint32_t vocab,

@@ -39,23 +39,96 @@ float rh_gaussian(uint64_t *state, double sd) {
     return (float)(sd * sqrt(-2.0 * log(u1)) * cos(RH_TWO_PI * u2));
 }
 
-void rh_fill_gaussian(uint64_t *state, float *out, size_t count, double sd) {
-    for (size_t i = 0; i < count; i++) out[i] = rh_gaussian(state, sd);
+/* The xorshift state update is linear over GF(2), so the state n draws
+ * ahead is the update's n-th power (a 64 x 64 bit matrix, held as the images
+ * of the basis vectors) applied to the state. Long fills are cut into pieces
+ * started from their own jumped states and generated in parallel; values and
+ * final state equal one sequential pass. */
+typedef struct { uint64_t col[64]; } rh_gf2_map;
+
+static uint64_t rh_gf2_apply(const rh_gf2_map *m, uint64_t x) {
+    uint64_t y = 0;
+    for (int j = 0; j < 64; j++)
+        if ((x >> j) & 1) y ^= m->col[j];
+    return y;
 }
 
-/* Build a model with the reference's allocator, overwrite its parameters with
- * N(0, 0.02) for embeddings/projections (model_param_tensors order), 1/0 for
- * LayerNorm gamma/beta and 0 for biases, then write a quantized bundle with the
- * reference's own writer (projections only, per the default policy). */
-int rh_build_bundle(const char *path, size_t vocab, size_t dim, size_t heads,
-                    size_t layers, size_t max_seq, uint64_t weight_seed,
-                    int bits, int granularity) {
+static void rh_gf2_compose(rh_gf2_map *out, const rh_gf2_map *a, const rh_gf2_map *b) {
+    rh_gf2_map t;
+    for (int j = 0; j < 64; j++) t.col[j] = rh_gf2_apply(a, b->col[j]);
+    *out = t;
+}
+
+static uint64_t rh_rng_jump(uint64_t state, uint64_t n) {
+    if (n == 0) return state;
+    rh_gf2_map step, acc;
+    for (int j = 0; j < 64; j++) {
+        uint64_t x = UINT64_C(1) << j;
+        x ^= x >> 12;
+        x ^= x << 25;
+        x ^= x >> 27;
+        step.col[j] = x;
+        acc.col[j] = UINT64_C(1) << j;
+    }
+    while (n) {
+        if (n & 1) rh_gf2_compose(&acc, &step, &acc);
+        rh_gf2_compose(&step, &step, &step);
+        n >>= 1;
+    }
+    return rh_gf2_apply(&acc, state ? state : UINT64_C(0x9e3779b97f4a7c15));
+}
+
+/* Same values and final state as rh_gaussian called count times. */
+void rh_fill_gaussian(uint64_t *state, float *out, size_t count, double sd) {
+    const size_t piece = (size_t)1 << 22;
+    const long long parts = (long long)((count + piece - 1) / piece);
+    const uint64_t s0 = *state;
+#pragma omp parallel for schedule(dynamic, 1)
+    for (long long t = 0; t < parts; t++) {
+        const size_t lo = (size_t)t * piece, hi = lo + piece < count ? lo + piece : count;
+        uint64_t st = rh_rng_jump(s0, 2 * (uint64_t)lo);
+        for (size_t i = lo; i < hi; i++) out[i] = rh_gaussian(&st, sd);
+    }
+    *state = rh_rng_jump(s0, 2 * (uint64_t)count);
+}
+
+/* Parameter count of a model of this shape and architecture, as
+ * model_new lays it out (src/core/model.c:37-72, 120-124): embeddings (and
+ * the untied output projection), output bias, then per layer 4 d^2, the
+ * norms (beta only for LayerNorm), W_ff1 + b_ff1, the SwiGLU gate branch,
+ * W_ff2 + b_ff2. */
+size_t rh_arch_param_count(size_t vocab, size_t dim, size_t layers, uint32_t flags) {
+    const size_t F = 4 * dim, norms = (flags & MODEL_ARCH_RMSNORM) ? dim : 2 * dim;
+    size_t per = 4 * dim * dim + 2 * norms + dim * F + F + F * dim + dim;
+    if (flags & MODEL_ARCH_SWIGLU) per += dim * F + F;
+    return vocab * dim * ((flags & MODEL_ARCH_TIED_EMBEDDINGS) ? 1 : 2) + vocab + layers * per;
+}
+
+/* Build a model over a parameter buffer of our own (no initialisation pass),
+ * fill it with N(0, 0.02) for embeddings/projections (model_param_tensors
+ * order), 1/0 for norm gamma/beta and 0 for biases, then write a quantized
+ * bundle with the reference's own writer (projections only, per the default
+ * policy). */
+int rh_build_bundle_arch(const char *path, size_t vocab, size_t dim, size_t heads,
+                         size_t layers, size_t max_seq, uint64_t weight_seed,
+                         int bits, int granularity, uint32_t flags) {
     neural_model_t model = {0};
-    if (model_new_seeded(&model, vocab, dim, heads, layers, max_seq, 0) != MODEL_SUCCESS)
+    const size_t total = rh_arch_param_count(vocab, dim, layers, flags);
+    float *params = calloc(total, sizeof(float));
+    if (!params) return -2;
+    if (model_new_external_parameters_architecture(&model, vocab, dim, heads, layers, max_seq, flags,
+                                                   params) != MODEL_SUCCESS) {
+        free(params);
         return -1;
+    }
+    if (model.total_param_count != total) {
+        model_free(&model);
+        free(params);
+        return -4;
+    }
     size_t count = model_param_tensor_count(&model);
     param_tensor_t *tensors = calloc(count, sizeof(*tensors));
-    if (!tensors) { model_free(&model); return -2; }
+    if (!tensors) { model_free(&model); free(params); return -2; }
     model_param_tensors(&model, tensors, count);
     uint64_t state = dranzer_rng_stream(weight_seed, DRANZER_RNG_STREAM_TESTING);
     for (size_t t = 0; t < count; t++) {
@@ -79,6 +152,7 @@ int rh_build_bundle(const char *path, size_t vocab, size_t dim, size_t heads,
     if (bpe_encoder_new_with_special_tokens(&encoder, vocab) != BPE_SUCCESS ||
         bpe_encoder_freeze(&encoder) != BPE_SUCCESS) {
         model_free(&model);
+        free(params);
         return -3;
     }
     model_bundle_metadata_t meta = {0};
@@ -91,7 +165,15 @@ int rh_build_bundle(const char *path, size_t vocab, size_t dim, size_t heads,
     bundle_errors_t rc = model_bundle_save_quantized(&model, &encoder, &meta, &config, NULL, path);
     bpe_encoder_free(&encoder);
     model_free(&model);
+    free(params);
     return rc == BUNDLE_SUCCESS ? 0 : -10 - (int)rc;
+}
+
+int rh_build_bundle(const char *path, size_t vocab, size_t dim, size_t heads,
+                    size_t layers, size_t max_seq, uint64_t weight_seed,
+                    int bits, int granularity) {
+    return rh_build_bundle_arch(path, vocab, dim, heads, layers, max_seq, weight_seed, bits,
+                                granularity, 0);
 }
 
 typedef struct {

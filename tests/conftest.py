@@ -10,6 +10,8 @@ ROOT = os.path.dirname(HERE)
 sys.path.insert(0, HERE)
 sys.path.insert(0, ROOT)
 GOLDEN = os.path.join(HERE, "golden")
+# the DRANZER source tree the checker builds from, where it is present
+REF_TREE = os.environ.get("DRANZER_REF", "/root/reference")
 
 
 def pytest_configure(config):
@@ -49,8 +51,8 @@ def golden(name):
 def ref():
     from _native_oracle import REF_SO, RefHarness
     if not os.path.exists(REF_SO):
-        if os.path.isdir("/root/reference"):
-            subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref"], check=True)
+        if os.path.isdir(os.path.join(REF_TREE, "src")):
+            subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", f"REF={REF_TREE}"], check=True)
         else:
             pytest.skip("reference build not present (tests/golden pins the oracle instead)")
     return RefHarness()

@@ -181,3 +181,18 @@ def test_quantized_slice_equals_quantizing_the_slice(dz, bits, gran):
             np.testing.assert_array_equal(po, p2)
     with pytest.raises(ValueError):
         dz.quantized_slice(s, p, rows, cols, bits, gran, 1, 50, 10)
+
+
+def test_synth_gaussian_in_parallel_pieces_is_one_sequential_pass(dz, oracle):
+    """dz_synth_gaussian cuts long fills into pieces started from jumped RNG
+    states; values and final state equal the oracle's sequential pass and a
+    fill split across two calls."""
+    from _native_oracle import STREAM_TESTING
+    n = 3 * (1 << 22) + 77
+    s1 = np.array([oracle.rng_stream(9, STREAM_TESTING)], np.uint64)
+    s2, s3 = s1.copy(), s1.copy()
+    a = oracle.gaussian(s1, n, 0.02)
+    b = dz.synth_gaussian(s2, n, 0.02)
+    c = np.concatenate([dz.synth_gaussian(s3, 10, 0.02), dz.synth_gaussian(s3, n - 10, 0.02)])
+    assert np.array_equal(a, b) and np.array_equal(a, c)
+    assert s1[0] == s2[0] == s3[0]
