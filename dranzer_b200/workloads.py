@@ -37,7 +37,7 @@ class Workload:
     bits: int
     weight_seed: int
     prompt_seed: int
-    batch: int             # sequences per GPU
+    batch: int             # sequences of the whole job (split over the GPUs)
     prompt_len: int
     n_new: int
     strategy: int = dz.GREEDY
@@ -63,10 +63,11 @@ C2 = Workload("c2-int4-topp0.9-64x(32+32)", Spec(512, 128, 4, 4, 64), 4, 0, 2, 6
 # config 4: the scaled architecture (24 layers, d 2048, 16 heads, F 8192, V
 # 32000, context 2048), INT8, weights seed 4; 256 prompts of 512 tokens
 # (seed 4) prefilled, then 128 greedy steps; the ring holds the 640 tokens a
-# sequence uses. The CPU baseline times one sequence of 16 + 8 tokens with
-# every host thread in the reference's OpenMP matmul.
+# sequence uses. The CPU baseline times one sequence of 16 + 4 tokens (the
+# job's 4:1 prompt-to-decode ratio) with every host thread in the
+# reference's OpenMP matmul.
 C4 = Workload("c4-int8-greedy-256x(512+128)", Spec(32000, 2048, 16, 24, 2048), 8, 4, 4, 256, 512, 128,
-              capacity=640, cpu_sample=(1, 16, 8, True))
+              capacity=640, cpu_sample=(1, 16, 4, True))
 WORKLOADS = {"c1": C1, "c2": C2, "c4": C4}
 
 
@@ -92,16 +93,19 @@ def model_params(spec, seed):
     return flat
 
 
-def prompts(wl, rank=0):
-    """[batch, prompt_len] ids for the sequences of `rank` (sequence index
-    rank*batch + i of one stream)."""
+def prompts(wl, lo=0, hi=None):
+    """[hi - lo, prompt_len] ids of the job's sequences lo..hi-1 (sequence i
+    takes ids [i * prompt_len, (i + 1) * prompt_len) of one stream)."""
+    hi = wl.batch if hi is None else hi
     state = np.array([dz.rng_stream(wl.prompt_seed, dz.STREAM_TESTING)], np.uint64)
-    ids = dz.synth_prompt_ids(state, (rank + 1) * wl.batch * wl.prompt_len, wl.spec.vocab, MASKED)
-    return ids[rank * wl.batch * wl.prompt_len:].reshape(wl.batch, wl.prompt_len)
+    ids = dz.synth_prompt_ids(state, hi * wl.prompt_len, wl.spec.vocab, MASKED)
+    return ids[lo * wl.prompt_len:].reshape(hi - lo, wl.prompt_len)
 
 
-def seeds(wl, rank=0):
-    return np.array([wl.seed_base + rank * wl.batch + i for i in range(wl.batch)], np.uint64)
+def seeds(wl, lo=0, hi=None):
+    """Per-sequence sampling seeds of the job's sequences lo..hi-1."""
+    hi = wl.batch if hi is None else hi
+    return np.array([wl.seed_base + i for i in range(lo, hi)], np.uint64)
 
 
 def shard(n_items, rank, world):
