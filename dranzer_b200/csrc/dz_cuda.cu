@@ -10,6 +10,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <algorithm>
 #include <map>
@@ -26,6 +27,7 @@
 #include "prefill.cuh"
 #include "seqgen.cuh"
 #include "umma.cuh"
+#include "qmvi.cuh"
 
 using namespace dz;
 
@@ -391,6 +393,10 @@ static int qms_prepare(int device) {
     DZ_CUDA(cudaFuncSetAttribute(dz_qmv1_kernel<B, QMV1_WARPS, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
     DZ_QMV1_ATTR(4, false); DZ_QMV1_ATTR(4, true); DZ_QMV1_ATTR(8, false); DZ_QMV1_ATTR(8, true);
 #undef DZ_QMV1_ATTR
+#define DZ_QMV1I_ATTR(B, R) \
+    DZ_CUDA(cudaFuncSetAttribute(dz_qmv1i_kernel<B, QMV1_WARPS, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
+    DZ_QMV1I_ATTR(4, 1); DZ_QMV1I_ATTR(4, 2); DZ_QMV1I_ATTR(8, 1); DZ_QMV1I_ATTR(8, 2);
+#undef DZ_QMV1I_ATTR
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UG_SMEM_BYTES));
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UV_SMEM_BYTES));
     // the split runs right before the GEMV (and may share SMs with it): the
@@ -429,6 +435,90 @@ static int qms_kparts(int n_groups, int nkg, int W, int* nrounds_out, unsigned* 
     *nrounds_out = (int)rounds;
     *grid_out = (unsigned)std::min<long long>(rounds, g_num_sms);
     return best;
+}
+
+// Which M <= 2 matvec kernel runs: the integer dot-product kernel
+// (dz_qmv1i_kernel, the default) or the fp16 tensor-core one
+// (dz_qmv1_kernel). DZ_MATVEC_KERNEL=mma in the environment selects the
+// latter, for comparison; both compute the same product.
+static bool matvec_int_kernel() {
+    static const bool v = [] {
+        const char* e = getenv("DZ_MATVEC_KERNEL");
+        return !(e && strcmp(e, "mma") == 0);
+    }();
+    return v;
+}
+
+// Launch geometry of the integer dot-product matvec (qmvi.cuh): grid, tiles
+// per CTA, parts per tile, chunks per piece and shared memory. False when it
+// is not selected, K is above its exact range, or its limb table and one
+// stage per warp do not fit shared memory.
+struct Qmv1iPlan {
+    int G, max_tiles, max_parts, pk;
+    unsigned tab_bytes;
+    size_t smem;
+};
+static bool qmv1i_plan(const DevQMat& W, int M, Qmv1iPlan* p) {
+    constexpr int WP = QMV1_WARPS;
+    if (W.K > QI_MAX_K || M < 1 || M > 2 || !matvec_int_kernel()) return false;
+    const int KT = W.bits == 8 ? 2 : 4;
+    p->tab_bytes = dz_qmv1i_tab_bytes(W.nkg, KT, M);
+    p->G = std::min(g_num_sms, W.ntiles);
+    p->max_tiles = (W.ntiles + p->G - 1) / p->G;
+    // a tile meets at most (nkg - 2) / shortest range + 2 non-empty warp ranges
+    const long long per_min = (long long)(W.ntiles / p->G) * W.nkg / WP;
+    p->max_parts =
+        per_min >= 1 ? (int)std::min<long long>(WP, std::max<long long>(1, (W.nkg - 2) / per_min + 2)) : WP;
+    const size_t fixed = dz_qmv1i_smem_bytes(0, WP, p->tab_bytes, p->max_tiles, p->max_parts);
+    if (fixed + (size_t)WP * QMS_STAGES * 512 > (size_t)g_smem_optin) return false;
+    p->pk = (int)std::min<size_t>(16, ((size_t)g_smem_optin - fixed) / ((size_t)WP * QMS_STAGES * 512));
+    p->smem = dz_qmv1i_smem_bytes(p->pk, WP, p->tab_bytes, p->max_tiles, p->max_parts);
+    return true;
+}
+
+static bool qmv1i_launch(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep,
+                         cudaStream_t st, int* status, double qmv_bytes) {
+    constexpr int WP = QMV1_WARPS;
+    Qmv1iPlan pl;
+    if (!qmv1i_plan(W, M, &pl)) return false;
+    Qmv1iArgs a;
+    memset(&a, 0, sizeof(a));
+    a.codes = W.codes;
+    a.N = W.N;
+    a.nkg = W.nkg;
+    a.ntiles = W.ntiles;
+    a.X = X;
+    a.ldx = ldx;
+    a.k_scale = W.k_scale;
+    a.K = W.K;
+    a.M = M;
+    a.status = status;
+    a.ep = ep;
+    a.ep.row_shift = nullptr;
+    a.tab_bytes = pl.tab_bytes;
+    a.max_tiles = pl.max_tiles;
+    a.max_parts = pl.max_parts;
+    a.pk = pl.pk;
+    ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
+    // programmatic dependent launch, as the tensor-core matvec below
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)pl.G);
+    cfg.blockDim = dim3(WP * 32);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void (*k)(Qmv1iArgs) = W.bits == 8 ? (M == 2 ? dz_qmv1i_kernel<8, WP, 2> : dz_qmv1i_kernel<8, WP, 1>)
+                                       : (M == 2 ? dz_qmv1i_kernel<4, WP, 2> : dz_qmv1i_kernel<4, WP, 1>);
+    if (cudaLaunchKernelEx(&cfg, k, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        k<<<pl.G, WP * 32, pl.smem, st>>>(a);
+    }
+    return true;
 }
 
 // The stream-K matvec for M <= 2 (dz_qmv1_kernel). False when its shared
@@ -647,6 +737,10 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
         qms_shape(M, &NB, &NT, &WP);
         xin = (long long)Kp / 2 <= (long long)QMS_XIN_PAIRS * WP * 32;
     }
+    if (M <= 2 &&
+        qmv1i_launch(W, X, ldx, M, ep_in, st, status,
+                     (double)W.K * W.N * W.bits / 8 + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N))
+        return 1;
     int launches = 1;
     if (!xin) {
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 16.0 * nbt * Kp, 0, st);
@@ -732,6 +826,8 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
 static int qmv_launches(const DevQMat& W, int M) {
     if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) return 2;
     if (M <= UV_N && use_ugemv(W, M)) return 2;
+    Qmv1iPlan pl;
+    if (qmv1i_plan(W, M, &pl)) return 1;
     const int KG = W.bits == 8 ? 32 : 64;
     const int Kp = W.nkg * KG;
     bool xin = M <= QMS_MAX_M && qmv_xf_bytes(W, M) <= QMS_XF_SMEM_MAX;
@@ -2167,12 +2263,15 @@ extern "C" int dz_cuda_profile_generate(dz_cuda_cache_t* c, const uint32_t* prom
     std::vector<ProfRec> recs;
     DZ_CUDA(cudaMemsetAsync(c->phase_ns, 0, SEQ_PHASES * 8, c->stream));
     g_prof = &recs;
-    // eager launches, each bracketed by events; the attention byte count uses
-    // the mean context of the run (prefill then decode, all sequences in step)
+    // eager launches, each bracketed by events; the decode attention's byte
+    // count uses the mean context of the decode steps it serves: every step
+    // of a token-by-token run, or the draws after a batched prefill (contexts
+    // plen + 1 .. plen + n_new - 1); all sequences move in step
     const dz_cuda_model_t* m = c->model;
     const double D = (double)m->dl;   // this rank's K / V width
     const double total_steps = (double)plen + (double)(n_new - 1);
-    const double mean_ctx = (total_steps + 1.0) / 2.0 < c->cap ? (total_steps + 1.0) / 2.0 : c->cap;
+    double mean_ctx = use_batched_prefill(c, plen) ? (double)plen + (double)n_new / 2.0 : (total_steps + 1.0) / 2.0;
+    if (mean_ctx > c->cap) mean_ctx = c->cap;
     c->prof_ctx_bytes_per_layer = 8.0 * D * mean_ctx * c->B;
     c->prof_ctx_flops_per_layer = 4.0 * D * mean_ctx * c->B;
     enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out);
