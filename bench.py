@@ -316,7 +316,8 @@ def quant_matvec_probe(dz, torch, stream, hbm, bf16=None, cpu=False, Ns=(4096, 1
             mats = [dz.QuantizedWeightMatrix(s, p, 4096, N, bits) for _ in range(copies)]
             rh = ref.qmat(w, bits, 2) if ref is not None else None
             for M in Ms:
-                for i in range(6):
+                # every copy once first: a copy grows its scratch on its first call at a new M
+                for i in range(max(6, copies)):
                     mats[i % copies].matmul_async(xd.data_ptr(), yd.data_ptr(), M, stream.cuda_stream)
                 reps = 24 if M <= 64 else 8
                 evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -641,6 +642,43 @@ def run_dz(args, wl):
     return out
 
 
+def decode_probe(dz, torch, hbm, layers=2, batch=64, steps=8):
+    """The config-4 layer shapes (d 2048, 16 heads of 128, F 8192, V 32000,
+    INT8) with a few layers and a smaller batch: a 512-token batched prefill,
+    then `steps` decode steps, each step timed with CUDA events (a profiling
+    target for the decode kernels at the job's contexts, a few GB on the
+    device)."""
+    from dranzer_b200 import workloads as W
+    spec = W.Spec(32000, 2048, 16, layers, 2048)
+    wl = W.Workload("decode-probe", spec, 8, 4, 4, batch, 512, steps + 1, capacity=640)
+    path = f"/tmp/dz_probe_{os.getpid()}.bin"
+    W.write_bundle(wl, path)
+    bundle = dz.Bundle(path)
+    os.remove(path)
+    model = dz.Model.from_bundle(bundle)
+    cache = dz.KVCache(model, batch, 640)
+    prompts = W.prompts(wl)
+    cache.prefill(prompts, want_logits=False)
+    ids = prompts[:, -1].copy()
+    times = []
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        cache.forward_tokens(ids, want_logits=False)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    kv = 2.0 * layers * batch * 516 * 2048 * 4
+    ms = statistics.median(times)
+    cache.close()
+    model.close()
+    bundle.close()
+    return {"decode_probe": {"layers": layers, "batch": batch, "context": "513-520", "step_ms": round(ms, 4),
+                             "kv_gb_per_step": round(kv / 1e9, 3),
+                             "kv_frac_of_hbm_if_alone": round(kv / (ms * 1e-3) / 1e9 / hbm, 3)}}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -651,7 +689,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-2 line after config 4")
     ap.add_argument("--no-probe", action="store_true", help="skip the config-3 quantized-matmul rows")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline and the CPU matmul column")
-    ap.add_argument("--probe", choices=["qmv"], help="run only the C3 quantized-matmul rows (profiling target)")
+    ap.add_argument("--probe", choices=["qmv", "decode"],
+                    help="run only the C3 quantized-matmul rows, or a few config-4 decode steps (profiling targets)")
     ap.add_argument("--probe-n", type=int, default=0, help="with --probe: one N instead of all three")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -664,6 +703,11 @@ def main():
         hbm, bf16, _ = peaks()
         Ns = (args.probe_n,) if args.probe_n else (4096, 11008, 32000)
         out = {"quant_matvec": quant_matvec_probe(dz, torch, stream, hbm, bf16, Ns=Ns)}
+    elif args.probe == "decode":
+        import torch
+        import dranzer_b200 as dz
+        hbm, _, _ = peaks()
+        out = decode_probe(dz, torch, hbm)
     else:
         from dranzer_b200 import workloads as W
         out = run_dz(args, W.WORKLOADS[args.workload])

@@ -393,10 +393,7 @@ static int qms_prepare(int device) {
     DZ_CUDA(cudaFuncSetAttribute(dz_qmv1_kernel<B, QMV1_WARPS, X>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
     DZ_QMV1_ATTR(4, false); DZ_QMV1_ATTR(4, true); DZ_QMV1_ATTR(8, false); DZ_QMV1_ATTR(8, true);
 #undef DZ_QMV1_ATTR
-#define DZ_QMV1I_ATTR(B, R) \
-    DZ_CUDA(cudaFuncSetAttribute(dz_qmv1i_kernel<B, QMV1_WARPS, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin))
-    DZ_QMV1I_ATTR(4, 1); DZ_QMV1I_ATTR(4, 2); DZ_QMV1I_ATTR(8, 1); DZ_QMV1I_ATTR(8, 2);
-#undef DZ_QMV1I_ATTR
+    DZ_CUDA(dz_qmv1i_set_smem(optin));
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UG_SMEM_BYTES));
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UV_SMEM_BYTES));
     // the split runs right before the GEMV (and may share SMs with it): the
@@ -459,10 +456,10 @@ struct Qmv1iPlan {
     size_t smem;
 };
 static bool qmv1i_plan(const DevQMat& W, int M, Qmv1iPlan* p) {
-    constexpr int WP = QMV1_WARPS;
+    constexpr int WP = QMV1I_WARPS;
     if (W.K > QI_MAX_K || M < 1 || M > 2 || !matvec_int_kernel()) return false;
     const int KT = W.bits == 8 ? 2 : 4;
-    p->tab_bytes = dz_qmv1i_tab_bytes(W.nkg, KT, M);
+    p->tab_bytes = dz_qmv1i_tab_bytes(W.nkg, KT);
     p->G = std::min(g_num_sms, W.ntiles);
     p->max_tiles = (W.ntiles + p->G - 1) / p->G;
     // a tile meets at most (nkg - 2) / shortest range + 2 non-empty warp ranges
@@ -478,7 +475,6 @@ static bool qmv1i_plan(const DevQMat& W, int M, Qmv1iPlan* p) {
 
 static bool qmv1i_launch(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep,
                          cudaStream_t st, int* status, double qmv_bytes) {
-    constexpr int WP = QMV1_WARPS;
     Qmv1iPlan pl;
     if (!qmv1i_plan(W, M, &pl)) return false;
     Qmv1iArgs a;
@@ -500,24 +496,7 @@ static bool qmv1i_launch(const DevQMat& W, const float* X, long long ldx, int M,
     a.max_parts = pl.max_parts;
     a.pk = pl.pk;
     ProfScope prof(DZ_KERNEL_QMV, qmv_bytes, 2.0 * M * W.K * W.N, st);
-    // programmatic dependent launch, as the tensor-core matvec below
-    cudaLaunchConfig_t cfg;
-    memset(&cfg, 0, sizeof(cfg));
-    cfg.gridDim = dim3((unsigned)pl.G);
-    cfg.blockDim = dim3(WP * 32);
-    cfg.dynamicSmemBytes = pl.smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    void (*k)(Qmv1iArgs) = W.bits == 8 ? (M == 2 ? dz_qmv1i_kernel<8, WP, 2> : dz_qmv1i_kernel<8, WP, 1>)
-                                       : (M == 2 ? dz_qmv1i_kernel<4, WP, 2> : dz_qmv1i_kernel<4, WP, 1>);
-    if (cudaLaunchKernelEx(&cfg, k, a) != cudaSuccess) {
-        (void)cudaGetLastError();
-        k<<<pl.G, WP * 32, pl.smem, st>>>(a);
-    }
+    (void)dz_qmv1i_launch(a, W.bits, pl.G, pl.smem, st);
     return true;
 }
 
@@ -615,7 +594,12 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     if (!encode_u8_map(&tmA, L, 3, dims, strides, box)) return 0;
     {
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 3.0 * M * Kp, 0, st);
-        dz_limb_split_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
+        // a warp per row from one wave of rows on (fewer block barriers per byte)
+        if (M >= 2 * g_num_sms)
+            dz_limb_split_warp_kernel<<<(unsigned)((M + UG_SPLIT_WARP_ROWS - 1) / UG_SPLIT_WARP_ROWS), 256, 0, st>>>(
+                X, ldx, W.k_scale, M, W.K, Kp, L, shift);
+        else
+            dz_limb_split_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
     }
     UgArgs a;
     memset(&a, 0, sizeof(a));

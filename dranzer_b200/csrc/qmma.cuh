@@ -35,6 +35,13 @@
 
 #include "qmv.cuh"
 
+// Linkage of the non-template kernels defined in these headers: external in
+// the translation unit that launches them (dz_cuda.cu); a unit that includes
+// the headers only for their device helpers (qmvi.cu) defines it as static.
+#ifndef DZ_KERNEL_LINKAGE
+#define DZ_KERNEL_LINKAGE
+#endif
+
 namespace dz {
 
 // k rows covered by one 512-byte chunk
@@ -54,7 +61,7 @@ struct FragSources {
     int nsrc;
 };
 
-__global__ void dz_frag_repack_kernel(FragSources src, uint32_t* __restrict__ out, int K, int bits, int nkg,
+DZ_KERNEL_LINKAGE __global__ void dz_frag_repack_kernel(FragSources src, uint32_t* __restrict__ out, int K, int bits, int nkg,
                                       long long nwords) {
     const long long wid = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (wid >= nwords) return;
@@ -106,7 +113,7 @@ __device__ __forceinline__ uint32_t dz_frag_code(const uint8_t* codes, int bits,
 }
 
 // Fragment layout -> reference storage (bit-exact inverse), one thread per byte.
-__global__ void dz_frag_unrepack_kernel(const uint8_t* __restrict__ codes, uint8_t* __restrict__ ref, int K, int N,
+DZ_KERNEL_LINKAGE __global__ void dz_frag_unrepack_kernel(const uint8_t* __restrict__ codes, uint8_t* __restrict__ ref, int K, int N,
                                         int bits, int nkg, long long nbytes) {
     const long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= nbytes) return;
@@ -122,7 +129,7 @@ __global__ void dz_frag_unrepack_kernel(const uint8_t* __restrict__ codes, uint8
 }
 
 // quantize_unpack (src/core/quantize.c:290-295) from the fragment layout.
-__global__ void dz_frag_dequant_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ scales, int gran,
+DZ_KERNEL_LINKAGE __global__ void dz_frag_dequant_kernel(const uint8_t* __restrict__ codes, const float* __restrict__ scales, int gran,
                                        float* __restrict__ dst, int K, int N, int bits, int nkg) {
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (long long)K * N) return;
@@ -173,11 +180,20 @@ __device__ __forceinline__ void dz_mma_f16(float (&d)[4], const uint32_t (&a)[4]
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// floor(log2 |v|) of a finite non-zero float, read from its bit fields
+// (normal: biased exponent - 127; subnormal: the mantissa's top bit - 149).
+// Kept inline so that no kernel depends on how a library call is inlined.
+__device__ __forceinline__ int dz_ilogb(float v) {
+    const uint32_t u = __float_as_uint(v) & 0x7fffffffu;
+    const int e = (int)(u >> 23);
+    return e ? e - 127 : (31 - __clz((int)u)) - 149;
+}
+
 // Exponent shift s for a row whose largest magnitude is amax: max |x 2^s| in
 // [2^14, 2^15). Zero, inf and NaN rows take s = 0.
 __device__ __forceinline__ int dz_row_shift(float amax) {
     if (!(amax > 0.0f) || !(amax <= 3.402823466e38f)) return 0;
-    return 14 - ilogbf(amax);
+    return 14 - dz_ilogb(amax);
 }
 
 // v * 2^e, exact unless the result is subnormal (e in [-300, 300]).

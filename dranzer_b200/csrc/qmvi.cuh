@@ -1,37 +1,44 @@
-// The decode matvec (M <= 2 activation rows) on CUDA cores with integer dot
-// products: the weights stream from HBM in the MMA-fragment layout of
-// qmma.cuh (16-byte loads per lane out of bulk-copied shared-memory stages),
-// the codes are unpacked in registers and multiplied against the activation
-// limbs with dp4a, and the partial sums of a column meet through warp
-// shuffles. No tensor-core instruction is issued per chunk, so the loop is
-// bound by the weight stream, not by MMA issue.
+// The decode matvec (M <= 2 activation rows) with the codes as they are: the
+// weights stream from HBM in the MMA-fragment layout of qmma.cuh (bulk-copied
+// shared-memory stages, one 16-byte load per lane per chunk), are widened to
+// bytes in registers with one logic op per word (no dequantization), and
+// meet the activation limbs in the 8-bit integer MMA (m16n8k32, u8 codes x
+// s8 limbs, int32 accumulate): two MMAs per INT4 chunk and one per INT8
+// chunk, half and a quarter of the fp16 kernel's per-chunk MMA count.
 //
 // Integer formulation (the same as the tensor-core GEMM of umma.cuh):
 // - each activation row is scaled by 2^s (exact) so that max |x 2^s| lies in
 //   [2^21, 2^22), rounded to an integer X and cut into three balanced
 //   base-256 digits X = 65536 * top + 256 * mid + low (signed bytes);
-// - codes enter as the reference's biased bytes c = level + qmax
+// - codes enter as the reference's biased values c = level + qmax
 //   (src/core/quantize.c:213-221): sum_k c X = sum_k level X + qmax sum_k X,
 //   and qmax sum_k X is subtracted once per column;
-// - dp4a.u32.s32 of four codes (unsigned) and four limb bytes (signed) adds
-//   exactly into int32 (|sum| <= K * 254 * 128 < 2^31 for K <= 65536); the
-//   three limb sums combine in int64, convert to fp32 once, and 2^-s and the
-//   column scale are applied after.
+// - the int32 sums are exact (|sum| <= K * 254 * 128 < 2^31 for INT8, and
+//   16 * K * 14 * 128 < 2^31 for INT4, K <= 65536); the three limb sums
+//   combine in int64, convert to fp32 once, and 2^-s and the column scale
+//   are applied after.
 //
-// Which four k a lane's codes cover: in the fragment layout lane l = 4g + t
-// holds, per 16-row k-tile, columns g and g + 8 at k in {2t, 2t+1, 2t+8,
-// 2t+9}. INT4: (w & 0x0F0F0F0F) is column g and ((w >> 4) & 0x0F0F0F0F)
-// column g + 8, bytes in the k order (2t, 2t+8, 2t+1, 2t+9). INT8: the two
-// words of a k-tile give column g with one byte permute (0x5140) and column
-// g + 8 with another (0x7362), in the same k order. The limb table in shared
-// memory stores, per (k-tile, t, row), the three limb words in that order.
+// Operand mapping. In the fragment layout lane l = 4g + t holds, per 16-row
+// k-tile, columns g and g + 8 at k in {2t, 2t+1, 2t+8, 2t+9}. INT4:
+// (w & 0x0F0F0F0F) is column g and (w & 0xF0F0F0F0) is 16x column g + 8,
+// bytes in the k order (2t, 2t+8, 2t+1, 2t+9); INT8: the two words of a
+// k-tile give column g with one byte permute (0x5140) and column g + 8 with
+// another (0x7362), in the same order. Those four words are exactly the A
+// fragment of m16n8k32 (rows = output columns) for two k-tiles, with the
+// MMA's k indices 4t..4t+3 standing for that lane's four k; the MMA sums over
+// k, so any permutation shared with B is the same sum. B column j is limb
+// j % 3 of row j / 3 (columns 3M..7 zero); the limb table holds, per pair of
+// k-tiles and lane, the B fragment words in the same k order.
 #pragma once
 #include <cstdint>
+#include <cstring>
 #include <cuda_runtime.h>
 
 #include "umma.cuh"
 
 namespace dz {
+
+constexpr int QMV1I_WARPS = 16;
 
 struct Qmv1iArgs {
     const uint8_t* codes;     // fragment layout
@@ -52,8 +59,9 @@ struct Qmv1iArgs {
 // Largest K for which the int32 limb sums of biased codes are exact.
 constexpr int QI_MAX_K = 65536;
 
-__host__ __device__ constexpr unsigned dz_qmv1i_tab_bytes(int nkg, int KT, int MR) {
-    return (unsigned)nkg * KT * 4 * MR * 16;
+// The B-fragment table: per pair of k-tiles, 32 lanes x two words.
+__host__ __device__ constexpr unsigned dz_qmv1i_tab_bytes(int nkg, int KT) {
+    return (unsigned)nkg * KT / 2 * 256;
 }
 
 __host__ __device__ constexpr size_t dz_qmv1i_smem_bytes(int pk, int W, unsigned tab_bytes, int max_tiles,
@@ -63,18 +71,22 @@ __host__ __device__ constexpr size_t dz_qmv1i_smem_bytes(int pk, int W, unsigned
            32 * 8;
 }
 
-__device__ __forceinline__ int dz_dp4a_us(uint32_t codes, uint32_t limbs, int acc) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(codes), "r"(limbs), "r"(acc));
-    return d;
+// D += A (16 x 32, u8 codes, row) . B (32 x 8, s8 limbs, col), int32.
+__device__ __forceinline__ void dz_imma(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint2 b) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
 }
 
-// Limbs of row r into the table: entry (kt, t) holds the limb words of
-// k = 16 kt + (2t, 2t+8, 2t+1, 2t+9) (zero past K); sets rsh[r] (-s, or
-// UG_ROW_NONFINITE) and sumx[r] = sum_k X.
-template <int MR>
+// Limbs of row r of M into the B-fragment table: for k-tile kt and t, the
+// limb words of k = 16 kt + (2t, 2t+8, 2t+1, 2t+9) (zero past K) go to lanes
+// g = 3r + limb, word kt & 1 of pair kt / 2; the last row also zeroes lanes
+// g >= 3M. Sets rsh[r] (-s, or UG_ROW_NONFINITE) and sumx[r] = sum_k X.
 __device__ __forceinline__ void dz_qmv1i_split_row(const float* __restrict__ x, const float* __restrict__ k_scale,
-                                                   int K, int nkt, int r, uint4* __restrict__ tab,
+                                                   int K, int nkt, int r, int M, uint32_t* __restrict__ tab,
                                                    int* __restrict__ rsh, long long* __restrict__ sumx, float* wred,
                                                    int* wbad, long long* wsum) {
     float m = 0.0f;
@@ -102,7 +114,7 @@ __device__ __forceinline__ void dz_qmv1i_split_row(const float* __restrict__ x, 
         amax = fmaxf(amax, wred[w]);
         bad |= wbad[w];
     }
-    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(amax) : 0;
     long long sx = 0;
     for (int e = threadIdx.x; e < nkt * 4; e += blockDim.x) {
         const int k0 = (e >> 2) * 16 + 2 * (e & 3);
@@ -123,7 +135,13 @@ __device__ __forceinline__ void dz_qmv1i_split_row(const float* __restrict__ x, 
             m4 |= dm << (8 * b);
             t4 |= dt << (8 * b);
         }
-        tab[e * MR + r] = make_uint4(l4, m4, t4, 0u);
+        const int kt = e >> 2, t = e & 3;
+        uint32_t* base = tab + (size_t)(kt >> 1) * 64 + t * 2 + (kt & 1);
+        base[(3 * r + 0) * 8] = l4;
+        base[(3 * r + 1) * 8] = m4;
+        base[(3 * r + 2) * 8] = t4;
+        if (r == M - 1)
+            for (int g = 3 * M; g < 8; g++) base[g * 8] = 0u;
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, off);
@@ -153,7 +171,7 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
     const int g = lane >> 2, t = lane & 3;
     const int stage_bytes = a.pk * 512;
     uint8_t* ring = qmv1i_smem + (size_t)warp * QMS_STAGES * stage_bytes;
-    uint4* tab = reinterpret_cast<uint4*>(qmv1i_smem + (size_t)W * QMS_STAGES * stage_bytes);
+    uint32_t* tab = reinterpret_cast<uint32_t*>(qmv1i_smem + (size_t)W * QMS_STAGES * stage_bytes);
     long long* slots = reinterpret_cast<long long*>(reinterpret_cast<uint8_t*>(tab) + a.tab_bytes);
     int* cnt = reinterpret_cast<int*>(slots + (size_t)a.max_tiles * a.max_parts * 32);
     uint64_t* bars = reinterpret_cast<uint64_t*>(cnt + ((a.max_tiles + 3) & ~3)) + warp * QMS_STAGES;
@@ -218,8 +236,8 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
 
     const int nkt = a.nkg * KT;
     for (int r = 0; r < a.M; r++)
-        dz_qmv1i_split_row<MR>(a.X + (long long)r * a.ldx, a.k_scale, a.K, nkt, r, tab, rsh, sumx, wred, wbad,
-                               wsum);
+        dz_qmv1i_split_row(a.X + (long long)r * a.ldx, a.k_scale, a.K, nkt, r, a.M, tab, rsh, sumx, wred, wbad,
+                           wsum);
     __syncthreads();   // counters zeroed, limb table, shifts and sums written
 
     auto owner_of = [&](int x) {
@@ -241,13 +259,12 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
     Cursor cc = cursor_at(my0);
     int consumed = 0, cstage = 0;
     uint32_t cphase = 0;
-    int acc[MR][2][3];
+    // two accumulator chains (alternate k-tile pairs)
+    int acc[2][4];
 #pragma unroll
-    for (int r = 0; r < MR; r++)
+    for (int c = 0; c < 2; c++)
 #pragma unroll
-        for (int c = 0; c < 2; c++)
-#pragma unroll
-            for (int l = 0; l < 3; l++) acc[r][c][l] = 0;
+        for (int q = 0; q < 4; q++) acc[c][q] = 0;
     while (cc.pos < my1) {
         const int n = piece_len(cc);
         if (!failed && lane == 0 && ic.pos < my1) issue();
@@ -266,31 +283,21 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
         const int kg0 = cc.kg;
         if (!failed) {
             const uint4* w4 = reinterpret_cast<const uint4*>(ring + stage * stage_bytes) + lane;
-            const uint4* tk = tab + ((size_t)kg0 * KT * 4 + t) * MR;
+            // B fragments of this lane: one uint2 per pair of k-tiles
+            const uint2* tb = reinterpret_cast<const uint2*>(tab) + (size_t)kg0 * (KT / 2) * 32 + lane;
 #pragma unroll 2
-            for (int c = 0; c < n; c++, tk += KT * 4 * MR) {
+            for (int c = 0; c < n; c++, tb += (KT / 2) * 32) {
                 const uint4 w = w4[c * 32];
-                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                for (int j = 0; j < KT; j++) {
-                    uint32_t c0, c1;
-                    if (BITS == 4) {
-                        c0 = ww[j] & 0x0F0F0F0Fu;
-                        c1 = (ww[j] >> 4) & 0x0F0F0F0Fu;
-                    } else {
-                        c0 = __byte_perm(ww[2 * j], ww[2 * j + 1], 0x5140);
-                        c1 = __byte_perm(ww[2 * j], ww[2 * j + 1], 0x7362);
-                    }
-#pragma unroll
-                    for (int r = 0; r < MR; r++) {
-                        const uint4 lb = tk[j * 4 * MR + r];
-                        acc[r][0][0] = dz_dp4a_us(c0, lb.x, acc[r][0][0]);
-                        acc[r][0][1] = dz_dp4a_us(c0, lb.y, acc[r][0][1]);
-                        acc[r][0][2] = dz_dp4a_us(c0, lb.z, acc[r][0][2]);
-                        acc[r][1][0] = dz_dp4a_us(c1, lb.x, acc[r][1][0]);
-                        acc[r][1][1] = dz_dp4a_us(c1, lb.y, acc[r][1][1]);
-                        acc[r][1][2] = dz_dp4a_us(c1, lb.z, acc[r][1][2]);
-                    }
+                if (BITS == 4) {
+                    dz_imma(acc[0], w.x & 0x0F0F0F0Fu, w.x & 0xF0F0F0F0u, w.y & 0x0F0F0F0Fu, w.y & 0xF0F0F0F0u,
+                            tb[0]);
+                    dz_imma(acc[1], w.z & 0x0F0F0F0Fu, w.z & 0xF0F0F0F0u, w.w & 0x0F0F0F0Fu, w.w & 0xF0F0F0F0u,
+                            tb[32]);
+                } else {
+                    const uint32_t a0 = __byte_perm(w.x, w.y, 0x5140), a1 = __byte_perm(w.x, w.y, 0x7362);
+                    const uint32_t a2 = __byte_perm(w.z, w.w, 0x5140), a3 = __byte_perm(w.z, w.w, 0x7362);
+                    if (c & 1) dz_imma(acc[1], a0, a1, a2, a3, tb[0]);
+                    else dz_imma(acc[0], a0, a1, a2, a3, tb[0]);
                 }
             }
         }
@@ -304,24 +311,36 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
         const int tile_start = tile * a.nkg, tile_end = tile_start + a.nkg;
         if (cc.pos != tile_end && cc.pos != my1) continue;
 
-        // this warp's share of the n-tile: limb sums over the four t lanes,
-        // combined in int64 (exact)
+        // this warp's share of the n-tile. Lane (g, t) holds B columns 2t and
+        // 2t + 1 of output columns g (d0, d1) and g + 8 (d2, d3; 16x for
+        // INT4); B column j is limb j % 3 of row j / 3. Gather them, combine
+        // the limbs in int64 (exact).
+        int d[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            d[q] = acc[0][q] + acc[1][q];
+            acc[0][q] = acc[1][q] = 0;
+        }
+        if (BITS == 4) {
+            d[2] >>= 4;   // exact: every term was 16x
+            d[3] >>= 4;
+        }
+        int bc[2][6];
+#pragma unroll
+        for (int q = 0; q < 3; q++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int src = (lane & ~3) | q;
+                bc[h][2 * q] = __shfl_sync(0xffffffffu, d[2 * h], src);
+                bc[h][2 * q + 1] = __shfl_sync(0xffffffffu, d[2 * h + 1], src);
+            }
         long long tot[MR][2];
 #pragma unroll
         for (int r = 0; r < MR; r++)
 #pragma unroll
-            for (int c = 0; c < 2; c++) {
-                int s[3];
-#pragma unroll
-                for (int l = 0; l < 3; l++) {
-                    int v = acc[r][c][l];
-                    v += __shfl_xor_sync(0xffffffffu, v, 1);
-                    v += __shfl_xor_sync(0xffffffffu, v, 2);
-                    s[l] = v;
-                    acc[r][c][l] = 0;
-                }
-                tot[r][c] = (long long)s[0] + 256LL * (long long)s[1] + 65536LL * (long long)s[2];
-            }
+            for (int h = 0; h < 2; h++)
+                tot[r][h] = (long long)bc[h][3 * r] + 256LL * (long long)bc[h][3 * r + 1] +
+                            65536LL * (long long)bc[h][3 * r + 2];
         const int n0 = tile * 16 + g;
         const bool whole = my0 <= tile_start && my1 >= tile_end;
         if (whole) {
@@ -394,5 +413,10 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
             if (!dz_mbar_wait(&bars[i % QMS_STAGES], (uint32_t)((i / QMS_STAGES) & 1))) break;
     }
 }
+
+// Host side (qmvi.cu): the dynamic shared-memory limit of every
+// instantiation, and one launch of the instantiation for (bits, a.M).
+cudaError_t dz_qmv1i_set_smem(int bytes);
+cudaError_t dz_qmv1i_launch(const Qmv1iArgs& a, int bits, int grid, size_t smem, cudaStream_t st);
 
 }  // namespace dz

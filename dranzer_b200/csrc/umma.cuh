@@ -156,7 +156,7 @@ __device__ __forceinline__ void ug_tmem_ld32(uint32_t taddr, int32_t (&v)[32]) {
 // reference's k x cols order (INT8 bytes or packed nibbles, low nibble first)
 // placed at columns [off, off + cols). Padding (n >= N, k >= K) stays as the
 // caller zeroed it (q = 0).
-__global__ void dz_code_blocks_kernel(const uint8_t* __restrict__ packed, int bits, long long cols, long long total,
+DZ_KERNEL_LINKAGE __global__ void dz_code_blocks_kernel(const uint8_t* __restrict__ packed, int bits, long long cols, long long total,
                                       int8_t* __restrict__ codes, int nkb, int off) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= total) return;
@@ -236,7 +236,7 @@ __device__ __forceinline__ void ug_limb_split_row_regs(const float* __restrict__
         amax = fmaxf(amax, wred[w]);
         bad |= wbad[w];
     }
-    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(amax) : 0;
     const size_t plane = (size_t)M * Kp;
 #pragma unroll
     for (int j = 0; j < UG_SPLIT_REG_V; j++) {
@@ -262,7 +262,7 @@ __device__ __forceinline__ void ug_limb_split_row_regs(const float* __restrict__
 
 // One block per row: X = rint(x * k_scale * 2^s), stored as three signed limb
 // planes L[limb][M][Kp] (zero past K), and -s.
-__global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restrict__ X, long long ldx,
+DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restrict__ X, long long ldx,
                                                             const float* __restrict__ k_scale, int M, int K, int Kp,
                                                             int8_t* __restrict__ L, int* __restrict__ shift) {
     __shared__ float wred[8];
@@ -298,7 +298,7 @@ __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restr
         amax = fmaxf(amax, wred[w]);
         bad |= wbad[w];
     }
-    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(amax) : 0;
     const size_t plane = (size_t)M * Kp;
     for (int k0 = threadIdx.x * 4; k0 < Kp; k0 += blockDim.x * 4) {
         uint32_t t4 = 0, m4 = 0, l4 = 0;
@@ -323,6 +323,81 @@ __global__ void __launch_bounds__(256) dz_limb_split_kernel(const float* __restr
         *reinterpret_cast<uint32_t*>(L + 2 * plane + at) = l4;
     }
     if (threadIdx.x == 0) shift[r] = bad ? UG_ROW_NONFINITE : -s;
+}
+
+// The limb split for many rows: one warp per row, eight rows per block, no
+// block barriers. Pass 1 finds the row's maximum (and non-finite elements)
+// with 16-byte loads; pass 2 reads the row again (from L1/L2) and writes the
+// three limb planes, 4 bytes per lane per plane per step (128-byte coalesced
+// stores), zero past K. The same limbs and exponents as dz_limb_split_kernel.
+constexpr int UG_SPLIT_WARP_ROWS = 8;
+DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_warp_kernel(const float* __restrict__ X, long long ldx,
+                                                                 const float* __restrict__ k_scale, int M, int K,
+                                                                 int Kp, int8_t* __restrict__ L,
+                                                                 int* __restrict__ shift) {
+    const int lane = threadIdx.x & 31;
+    const int r = blockIdx.x * UG_SPLIT_WARP_ROWS + (threadIdx.x >> 5);
+    if (r >= M) return;
+    const float* x = X + (long long)r * ldx;
+    const bool vec = (K & 3) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(k_scale)) & 15u) == 0;
+    auto load4 = [&](int k0, float (&v)[4]) {
+        if (vec && k0 + 3 < K) {
+            const float4 q = *reinterpret_cast<const float4*>(x + k0);
+            v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+            if (k_scale) {
+                const float4 w = *reinterpret_cast<const float4*>(k_scale + k0);
+                v[0] *= w.x; v[1] *= w.y; v[2] *= w.z; v[3] *= w.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                v[j] = 0.0f;
+                if (k0 + j < K) {
+                    v[j] = x[k0 + j];
+                    if (k_scale) v[j] *= k_scale[k0 + j];
+                }
+            }
+        }
+    };
+    float m = 0.0f;
+    int bad = 0;
+#pragma unroll 4
+    for (int k0 = lane * 4; k0 < K; k0 += 128) {
+        float v[4];
+        load4(k0, v);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (!(fabsf(v[j]) <= 3.402823466e38f)) bad = 1;
+            else m = fmaxf(m, fabsf(v[j]));
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        bad |= __shfl_xor_sync(0xffffffffu, bad, off);
+    }
+    const int s = m > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(m) : 0;
+    const size_t plane = (size_t)M * Kp;
+#pragma unroll 4
+    for (int k0 = lane * 4; k0 < Kp; k0 += 128) {
+        float v[4];
+        load4(k0, v);   // zero past K
+        uint32_t t4 = 0, m4 = 0, l4 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            uint32_t dt, dm, dl;
+            ug_digits(ug_fixed(v[j], s), dt, dm, dl);
+            t4 |= dt << (8 * j);
+            m4 |= dm << (8 * j);
+            l4 |= dl << (8 * j);
+        }
+        const size_t at = (size_t)r * Kp + k0;
+        *reinterpret_cast<uint32_t*>(L + at) = t4;
+        *reinterpret_cast<uint32_t*>(L + plane + at) = m4;
+        *reinterpret_cast<uint32_t*>(L + 2 * plane + at) = l4;
+    }
+    if (lane == 0) shift[r] = bad ? UG_ROW_NONFINITE : -s;
 }
 
 // Columns [n0, n0 + UG_BN) of rows [m0, m0 + UG_BM) from the staging tile
@@ -396,7 +471,7 @@ constexpr int UG_SPLIT_CHUNK = 1024;   // k per block of dz_limb_split_chunk_ker
 // one global round trip. It lets the GEMV launched after it start at once
 // (programmatic dependent launch): the GEMV streams weights and waits for
 // this grid only before it reads the limbs.
-__global__ void __launch_bounds__(256) dz_limb_split_chunk_kernel(const float* __restrict__ X, long long ldx,
+DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_chunk_kernel(const float* __restrict__ X, long long ldx,
                                                                   const float* __restrict__ k_scale, int M, int K,
                                                                   int Kp, int8_t* __restrict__ L,
                                                                   int* __restrict__ shift) {
@@ -464,7 +539,7 @@ __global__ void __launch_bounds__(256) dz_limb_split_chunk_kernel(const float* _
         amax = fmaxf(amax, wred[w]);
         bad |= wbad[w];
     }
-    const int s = amax > 0.0f ? (UG_X_BITS - 1) - ilogbf(amax) : 0;
+    const int s = amax > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(amax) : 0;
     const size_t plane = (size_t)M * Kp;
     const int k0 = ch * UG_SPLIT_CHUNK + threadIdx.x * 4;
     if (k0 < Kp) {
@@ -487,7 +562,7 @@ __global__ void __launch_bounds__(256) dz_limb_split_chunk_kernel(const float* _
 
 // ------------------------------------------------------------------- GEMM
 
-__global__ void __launch_bounds__(UG_THREADS, 1)
+DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
     dz_ugemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, UgArgs a) {
     extern __shared__ __align__(1024) uint8_t ug_raw[];
     const uint32_t raw = dz_smem_addr(ug_raw);
@@ -753,7 +828,7 @@ __device__ __forceinline__ uint32_t uv_idesc() {
 // across segments; warp 1 lane 0 issues the MMAs into one of two accumulator
 // sets (segments alternate, so a segment's epilogue overlaps the next
 // segment's MMAs); warps 4-7 drain a set (one output column per thread).
-__global__ void __launch_bounds__(UG_THREADS, 1)
+DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
     dz_ugemv_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmL, UvArgs a) {
     // the next kernel (the next call's limb split) may launch now; it waits
     // for this grid before touching memory
