@@ -19,15 +19,15 @@ import ctypes
 
 import numpy as np
 
-from ._native import (DzBundleInfo, DzBundleMeta, DzError, DzModelDesc, DzSampling, DzTensorBlob,
-                      check, lib)
+from ._native import (DzBundleInfo, DzBundleMeta, DzError, DzGenerationControls, DzGenerationResult,
+                      DzModelDesc, DzSampling, DzTensorBlob, check, lib)
 
 __all__ = ["GRAN_TENSOR", "GRAN_ROW", "GRAN_COLUMN", "GREEDY", "TOPK", "TOPP", "STREAM_INIT",
            "STREAM_DROPOUT", "STREAM_SAMPLING", "STREAM_TESTING", "DzError", "available",
            "rng_stream", "synth_gaussian", "synth_prompt_ids", "quantized_scale_count",
            "quantized_packed_size", "quantize_pack", "quantize_unpack", "quantized_slice", "positional_encoding", "fnv1a",
            "QuantizedWeightMatrix", "matmul_quantized_weight", "Bundle", "save_quantized_bundle",
-           "minimal_tokenizer", "model_tensor_layout", "Sampling", "Model", "KVCache"]
+           "minimal_tokenizer", "model_tensor_layout", "Sampling", "Controls", "Model", "KVCache"]
 
 GRAN_TENSOR, GRAN_ROW, GRAN_COLUMN = 0, 1, 2
 GREEDY, TOPK, TOPP = 0, 1, 2
@@ -293,6 +293,24 @@ class Sampling:
         self.c.n_masked = self.masked.size
 
 
+class Controls:
+    """dz_generation_controls_t: the generation loop's controls beyond token
+    selection (generation_options_t, src/include/cli/generation.h):
+    repetition penalty, EOS id and minimum new tokens, the first masked id of
+    the tokenizer's unassigned range, stop sequences (lists of ids)."""
+
+    def __init__(self, penalty=1.0, eos_id=259, min_new=0, mask_from=0xFFFFFFFF, stops=()):
+        self.stops = [list(int(t) for t in q) for q in stops]
+        self._tok = np.array([t for q in self.stops for t in q] or [0], np.uint32)
+        self._len = np.array([len(q) for q in self.stops] or [0], np.uint64)
+        self.c = DzGenerationControls()
+        self.c.repetition_penalty, self.c.eos_id = penalty, eos_id
+        self.c.minimum_new_tokens, self.c.mask_from = min_new, mask_from
+        self.c.stop_tokens = self._tok.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32))
+        self.c.stop_lengths = self._len.ctypes.data_as(ctypes.POINTER(ctypes.c_size_t))
+        self.c.n_stops = len(self.stops)
+
+
 class Model:
     """A bundle's parameters as codes on one device (dz_cuda_model_create)."""
 
@@ -423,6 +441,34 @@ class KVCache:
                                      ctypes.byref(sampling.c) if sampling else None, _p(sd), _p(out)),
               "generate")
         return out
+
+    def generate_ex(self, prompts, n_new, sampling=None, controls=None, seeds=None):
+        """generation_decode_with_options for every sequence: tokens [batch,
+        n_new] (0xffffffff after a sequence's end) and results [batch, 5]
+        (new_count, emitted_count, stopped_on_eos, stopped_on_stop_sequence,
+        stop_sequence_index)."""
+        pr = np.ascontiguousarray(prompts, np.uint32)
+        assert pr.shape[0] == self.batch
+        sd = None if seeds is None else np.ascontiguousarray(seeds, np.uint64)
+        out = np.empty((self.batch, n_new), np.uint32)
+        res = (DzGenerationResult * self.batch)()
+        check(lib().dz_cuda_generate_ex(self.handle, _p(pr), pr.shape[1], n_new,
+                                        ctypes.byref(sampling.c) if sampling else None,
+                                        ctypes.byref(controls.c) if controls else None, _p(sd), _p(out), res),
+              "generate_ex")
+        r = np.array([[x.new_count, x.emitted_count, x.stopped_on_eos, x.stopped_on_stop_sequence,
+                       x.stop_sequence_index] for x in res], np.uint32)
+        return out, r
+
+    def select_ex(self, sampling=None, controls=None, rng_states=None):
+        ids = np.empty(self.batch, np.uint32)
+        st = None if rng_states is None else np.ascontiguousarray(rng_states, np.uint64)
+        check(lib().dz_cuda_select_ex(self.handle, ctypes.byref(sampling.c) if sampling else None,
+                                      ctypes.byref(controls.c) if controls else None, _p(st), _p(ids)),
+              "select_ex")
+        if rng_states is not None:
+            rng_states[...] = st
+        return ids
 
     def generate_async(self, prompts_ptr, prompt_len, n_new, sampling, seeds_ptr, out_ptr):
         check(lib().dz_cuda_generate_async(self.handle, prompts_ptr, prompt_len, n_new,

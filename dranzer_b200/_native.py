@@ -61,6 +61,16 @@ class DzSampling(ctypes.Structure):
                 ("masked_ids", ctypes.POINTER(U32)), ("n_masked", SZ)]
 
 
+class DzGenerationControls(ctypes.Structure):
+    _fields_ = [("repetition_penalty", F32), ("eos_id", U32), ("minimum_new_tokens", SZ), ("mask_from", U32),
+                ("stop_tokens", ctypes.POINTER(U32)), ("stop_lengths", ctypes.POINTER(SZ)), ("n_stops", SZ)]
+
+
+class DzGenerationResult(ctypes.Structure):
+    _fields_ = [("new_count", U32), ("emitted_count", U32), ("stopped_on_eos", U32),
+                ("stopped_on_stop_sequence", U32), ("stop_sequence_index", U32)]
+
+
 # name -> (restype, argtypes); every exported symbol of include/dz_host.h and include/dz_cuda.h
 SIGNATURES = {
     # dz_host.h
@@ -119,6 +129,8 @@ SIGNATURES = {
     "dz_cuda_model_create_tp": (I32, [P, P, SZ, I32, I32, I32, P, P]),
     "dz_cuda_prefill": (I32, [P, P, P, SZ, P]),
     "dz_cuda_cache_uses_fused": (I32, [P, P]),
+    "dz_cuda_generate_ex": (I32, [P, P, SZ, SZ, P, P, P, P, P]),
+    "dz_cuda_select_ex": (I32, [P, P, P, P, P]),
 }
 
 _lib = None

@@ -16,6 +16,8 @@ struct RingState {
     int* slot;        // this step: slot the new K/V row is written to
     int* ctx;         // this step: context length attended over
     int* row_off;     // this step: slot * dim (epilogue scatter offset)
+    uint32_t* seen;   // [B][seen_words]: a bit per token id fed since reset (the
+    int seen_words;   // sequence the repetition penalty looks at)
 };
 
 // One block per sequence: the ring bookkeeping of model_forward_token
@@ -41,6 +43,8 @@ __global__ void dz_step_begin_kernel(RingState rs, const uint32_t* __restrict__ 
     }
     uint32_t tok = tokens[(long long)b * tok_stride];
     if (tok >= (uint32_t)vocab) tok = 0;
+    else if (rs.seen && threadIdx.x == 0)
+        rs.seen[(long long)b * rs.seen_words + (tok >> 5)] |= 1u << (tok & 31);
     const float* e = emb + (long long)tok * dim;
     float* h = hidden + (long long)b * dim;
     if (pos < pe_rows) {

@@ -1378,19 +1378,35 @@ extern "C" size_t dz_cuda_model_step_bytes(const dz_cuda_model_t* m) { return m 
 
 // ------------------------------------------------------------------ cache
 
+// The generation loop's controls as one generation uses them (host copy of
+// dz_generation_controls_t, stop sequences flattened).
+struct GenControls {
+    bool on = false;
+    float penalty = 1.0f;
+    uint32_t eos_id = 0xffffffffu, mask_from = 0xffffffffu;
+    int min_new = 0;
+    std::vector<uint32_t> stop_tok;
+    std::vector<int> stop_off;   // n_stops + 1 offsets
+    bool operator<(const GenControls& o) const {
+        return std::tie(on, penalty, eos_id, mask_from, min_new, stop_tok, stop_off) <
+               std::tie(o.on, o.penalty, o.eos_id, o.mask_from, o.min_new, o.stop_tok, o.stop_off);
+    }
+};
+
 struct GenKey {
     size_t plen, n_new;
     int strategy;
     float temperature, top_p;
     uint32_t top_k;
     std::vector<uint32_t> masked;
+    GenControls ctl;
     const void* prompts;
     const void* seeds;
     const void* out;
     bool operator<(const GenKey& o) const {
-        return std::tie(plen, n_new, strategy, temperature, top_p, top_k, masked, prompts, seeds, out) <
-               std::tie(o.plen, o.n_new, o.strategy, o.temperature, o.top_p, o.top_k, o.masked, o.prompts, o.seeds,
-                        o.out);
+        return std::tie(plen, n_new, strategy, temperature, top_p, top_k, masked, ctl, prompts, seeds, out) <
+               std::tie(o.plen, o.n_new, o.strategy, o.temperature, o.top_p, o.top_k, o.masked, o.ctl, o.prompts,
+                        o.seeds, o.out);
     }
 };
 
@@ -1407,6 +1423,16 @@ struct dz_cuda_cache {
     uint32_t* tok = nullptr;
     uint64_t* rng = nullptr;
     uint32_t* masked = nullptr;   // device copy of the masked ids (grown)
+    // token history for the repetition penalty: a bit per id fed through the
+    // model since reset, per sequence; invalid after a fused-path generation
+    uint32_t* seen = nullptr;
+    int seen_words = 0;
+    bool seen_valid = true;
+    uint32_t* gen_state = nullptr;   // [B][DZ_GEN_WORDS] (dz_cuda_generate_ex)
+    uint32_t* stop_tok = nullptr;    // device copy of the stop sequences (grown)
+    int* stop_off = nullptr;
+    size_t stop_tok_cap = 0, stop_off_cap = 0;
+    uint32_t* host_gen = nullptr;    // pinned copy of gen_state
     size_t masked_cap = 0;
     // device buffers of the host-facing generate()
     uint32_t* gen_prompts = nullptr;
@@ -1474,6 +1500,9 @@ extern "C" void dz_cuda_cache_free(dz_cuda_cache_t* c) {
         cudaFree(c->gen_prompts);
         cudaFree(c->gen_out);
         cudaFree(c->masked);
+        cudaFree(c->stop_tok);
+        cudaFree(c->stop_off);
+        cudaFreeHost(c->host_gen);
         cudaFreeHost(c->host_rng);
         cudaFreeHost(c->host_ids);
         cudaFreeHost(c->host_status);
@@ -1524,6 +1553,11 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     if (!rc) rc = cache_alloc(c, (void**)&c->tok, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->rng, B * 8);
     if (!rc) rc = cache_alloc(c, (void**)&c->gen_seeds, B * 8);
+    c->seen_words = (int)((V + 31) / 32);
+    if (!rc) rc = cache_alloc(c, (void**)&c->seen, B * (size_t)c->seen_words * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->gen_state, B * DZ_GEN_WORDS * 4);
+    if (!rc && cudaMallocHost(&c->host_gen, B * DZ_GEN_WORDS * 4) != cudaSuccess)
+        rc = fail(DZ_E_NOMEM, "pinned host");
     if (!rc) {
         size_t xs = 0;
         for (const auto& L : m->layers)
@@ -1563,6 +1597,7 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
         cudaMemsetAsync(c->start, 0, B * 4, c->stream);
         cudaMemsetAsync(c->length, 0, B * 4, c->stream);
         cudaMemsetAsync(c->total, 0, B * 8, c->stream);
+        cudaMemsetAsync(c->seen, 0, B * (size_t)c->seen_words * 4, c->stream);
         if (cudaStreamSynchronize(c->stream) != cudaSuccess) rc = fail(DZ_E_DEVICE, "cache init");
     }
     if (rc) {
@@ -1603,6 +1638,9 @@ extern "C" int dz_cuda_cache_reset(dz_cuda_cache_t* c, const uint8_t* seq_mask) 
         DZ_CUDA(cudaMemcpyAsync(dmask, seq_mask, c->B, cudaMemcpyHostToDevice, c->stream));
     }
     dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, dmask, c->B);
+    dz_seen_clear_kernel<<<dim3((unsigned)((c->seen_words + 255) / 256), (unsigned)c->B), 256, 0, c->stream>>>(
+        c->seen, c->seen_words, dmask);
+    if (!seq_mask) c->seen_valid = true;
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
     cudaFree(dmask);
@@ -1623,7 +1661,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
     const int hd = D / (int)m->desc.num_heads, B = c->B, cap = c->cap;
     cudaStream_t st = c->stream;
     int launches = 0;
-    RingState rs{c->start, c->length, c->total, c->slot, c->ctx, c->row_off};
+    RingState rs{c->start, c->length, c->total, c->slot, c->ctx, c->row_off, c->seen, c->seen_words};
     {
         ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)B * D * 12, 0, st);
         dz_step_begin_kernel<<<B, 128, 0, st>>>(rs, tokens, tok_stride, m->emb, m->pe, m->pe_rows, c->hidden, D,
@@ -1727,9 +1765,40 @@ static int check_sampling(const dz_cuda_cache_t* c, const dz_sampling_t* s) {
     return DZ_OK;
 }
 
+// The device form of a generation's controls: penalty over the token
+// history, the unassigned range, and (with `state`) EOS, the minimum length
+// and stop sequences from the cache's device copies.
+static SelectControls select_controls(const dz_cuda_cache_t* c, const GenControls* g, bool with_state) {
+    SelectControls k;
+    memset(&k, 0, sizeof(k));
+    k.mask_from = 0xffffffffu;
+    k.eos_id = 0xffffffffu;
+    if (!g || !g->on) return k;
+    k.seen = g->penalty > 1.0f ? c->seen : nullptr;
+    k.seen_words = c->seen_words;
+    k.penalty = g->penalty;
+    k.mask_from = g->mask_from;
+    if (with_state) {
+        k.state = c->gen_state;
+        k.eos_id = g->eos_id;
+        k.min_new = g->min_new;
+        k.stop_tok = c->stop_tok;
+        k.stop_off = c->stop_off;
+        k.n_stops = (int)g->stop_off.size() - 1;
+    }
+    return k;
+}
+
 static int enqueue_select(dz_cuda_cache_t* c, const dz_sampling_t* s, uint64_t* rng, uint32_t* out,
-                          long long out_stride, uint32_t* out2) {
+                          long long out_stride, uint32_t* out2, const SelectControls* ctl = nullptr) {
     SelectArgs a;
+    if (ctl) {
+        a.ctl = *ctl;
+    } else {
+        memset(&a.ctl, 0, sizeof(a.ctl));
+        a.ctl.mask_from = 0xffffffffu;
+        a.ctl.eos_id = 0xffffffffu;
+    }
     a.logits = c->logits;
     a.V = (int)c->model->desc.vocab_size;
     a.ld = a.V;
@@ -1788,6 +1857,41 @@ extern "C" int dz_cuda_select(dz_cuda_cache_t* c, const dz_sampling_t* s, uint64
         DZ_CUDA(cudaMemcpyAsync(c->rng, c->host_rng, B * 8, cudaMemcpyHostToDevice, c->stream));
     }
     enqueue_select(c, s, rng_states ? c->rng : nullptr, c->tok, 1, nullptr);
+    DZ_CUDA(cudaGetLastError());
+    DZ_CUDA(cudaMemcpyAsync(c->host_ids, c->tok, B * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (rng_states) DZ_CUDA(cudaMemcpyAsync(c->host_rng, c->rng, B * 8, cudaMemcpyDeviceToHost, c->stream));
+    DZ_CUDA(cudaStreamSynchronize(c->stream));
+    memcpy(out_ids, c->host_ids, B * 4);
+    if (rng_states) memcpy(rng_states, c->host_rng, B * 8);
+    return DZ_OK;
+}
+
+static int prepare_controls(dz_cuda_cache_t* c, const dz_generation_controls_t* in, GenControls* out);
+
+extern "C" int dz_cuda_select_ex(dz_cuda_cache_t* c, const dz_sampling_t* s, const dz_generation_controls_t* controls,
+                                 uint64_t* rng_states, uint32_t* out_ids) {
+    if (!c || !out_ids) return fail(DZ_E_INVALID, "null argument");
+    int rc = check_sampling(c, s);
+    if (rc) return rc;
+    DeviceGuard g(c->model->device);
+    GenControls ctl;
+    if ((rc = prepare_controls(c, controls, &ctl))) return rc;
+    if (ctl.on && ctl.penalty > 1.0f && !c->seen_valid)
+        return fail(DZ_E_UNSUPPORTED,
+                    "repetition penalty: the last generation ran on the fused path, which keeps no token history; "
+                    "reset the cache or generate on the layered path");
+    if ((rc = ensure_masked(c, s))) return rc;
+    const size_t B = c->B;
+    if (s && s->n_masked)
+        DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
+    if (rng_states) {
+        memcpy(c->host_rng, rng_states, B * 8);
+        DZ_CUDA(cudaMemcpyAsync(c->rng, c->host_rng, B * 8, cudaMemcpyHostToDevice, c->stream));
+    }
+    // penalty and unassigned range only: EOS, the minimum length and stop
+    // sequences stay with the caller's loop, as in the reference
+    const SelectControls sc = select_controls(c, &ctl, false);
+    enqueue_select(c, s, rng_states ? c->rng : nullptr, c->tok, 1, nullptr, &sc);
     DZ_CUDA(cudaGetLastError());
     DZ_CUDA(cudaMemcpyAsync(c->host_ids, c->tok, B * 4, cudaMemcpyDeviceToHost, c->stream));
     if (rng_states) DZ_CUDA(cudaMemcpyAsync(c->host_rng, c->rng, B * 8, cudaMemcpyDeviceToHost, c->stream));
@@ -1954,7 +2058,8 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
         {
             ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)R * D * 12, 0, st);
             dz_prefill_embed_kernel<<<R, 128, 0, st>>>(ids_dev + (long long)s0 * ld, ld, T, m->emb, m->pe,
-                                                       m->pe_rows, c->pf_hidden, D, V);
+                                                       m->pe_rows, c->pf_hidden, D, V, lens,
+                                                       c->seen + (long long)s0 * c->seen_words, c->seen_words);
         }
         launches++;
         for (size_t l = 0; l < m->layers.size(); l++) {
@@ -2040,10 +2145,13 @@ constexpr size_t GRAPH_MAX_LAUNCHES = 40000;
 
 // The whole generation loop, enqueued on the cache's stream. Returns launches.
 static int enqueue_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
-                            const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
+                            const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out,
+                            const GenControls* ctl = nullptr) {
     int launches = 0;
-    if (use_seqgen(c, s)) {
+    const bool controls = ctl && ctl->on;
+    if (!controls && use_seqgen(c, s)) {
         dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
+        c->seen_valid = false;   // the fused kernel keeps no token history
         return 1 + launch_seqgen(c, prompts, plen, n_new, s, seeds, out);
     }
     const bool sampled = seeds != nullptr;
@@ -2052,14 +2160,23 @@ static int enqueue_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t 
         launches++;
     }
     dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
-    launches++;
+    dz_seen_clear_kernel<<<dim3((unsigned)((c->seen_words + 255) / 256), (unsigned)c->B), 256, 0, c->stream>>>(
+        c->seen, c->seen_words, nullptr);
+    c->seen_valid = true;
+    launches += 2;
+    SelectControls sc = select_controls(c, ctl, true);
+    if (controls) {
+        dz_gen_init_kernel<<<(c->B + 127) / 128, 128, 0, c->stream>>>(c->gen_state, c->B);
+        launches++;
+    }
     if (use_batched_prefill(c, plen)) {
         launches += enqueue_prefill(c, prompts, (long long)plen, (int)plen, nullptr);
     } else {
         for (size_t t = 0; t < plen; t++) launches += enqueue_step(c, prompts + t, (long long)plen);
     }
     for (size_t i = 0; i < n_new; i++) {
-        launches += enqueue_select(c, s, sampled ? c->rng : nullptr, out + i, (long long)n_new, c->tok);
+        launches += enqueue_select(c, s, sampled ? c->rng : nullptr, out + i, (long long)n_new, c->tok,
+                                   controls ? &sc : nullptr);
         if (i + 1 < n_new) launches += enqueue_step(c, c->tok, 1);
     }
     return launches;
@@ -2079,18 +2196,20 @@ extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t ple
     }
     const size_t seeded = (s && s->strategy != 0 && s->temperature > 0.0f) ? 1 : 0;
     const size_t prefill = use_batched_prefill(c, plen) ? prefill_launches(c, plen) : plen * step;
-    return seeded + 1 + prefill + n_new + (n_new ? n_new - 1 : 0) * step;
+    return seeded + 2 + prefill + n_new + (n_new ? n_new - 1 : 0) * step;   // + ring reset, history clear
 }
 
-extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
-                                      const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
+static int generate_async(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                          const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out, const GenControls* ctl) {
     if (!c || !prompts || !out || plen == 0 || n_new == 0)
         return fail(DZ_E_INVALID, "generate: null buffer or empty prompt/decode length");
     int rc = check_sampling(c, s);
     if (rc) return rc;
     DeviceGuard g(c->model->device);
     if ((rc = ensure_masked(c, s))) return rc;
-    if (!use_seqgen(c, s) && use_batched_prefill(c, plen) && (rc = ensure_prefill(c, plen))) return rc;
+    const bool fused = !(ctl && ctl->on) && use_seqgen(c, s);
+    if (!fused && use_batched_prefill(c, plen) && (rc = ensure_prefill(c, plen))) return rc;
+    c->seen_valid = !fused;   // the fused kernel keeps no token history
     if (s && s->n_masked)
         DZ_CUDA(cudaMemcpyAsync(c->masked, s->masked_ids, s->n_masked * 4, cudaMemcpyHostToDevice, c->stream));
     const bool sampled = seeds && s && s->strategy != 0 && s->temperature > 0.0f;
@@ -2103,12 +2222,13 @@ extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompt
     key.top_k = s ? s->top_k : 0;
     key.masked = s && s->n_masked ? std::vector<uint32_t>(s->masked_ids, s->masked_ids + s->n_masked)
                                   : std::vector<uint32_t>();
+    if (ctl) key.ctl = *ctl;
     key.prompts = prompts;
     key.seeds = sampled ? seeds : nullptr;
     key.out = out;
     if (dz_cuda_generate_launches(c, plen, n_new, s) > GRAPH_MAX_LAUNCHES) {
         // jobs this long launch directly: a graph of this many nodes costs more to build than it saves
-        enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out);
+        enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out, ctl);
         DZ_CUDA(cudaGetLastError());
         return DZ_OK;
     }
@@ -2116,7 +2236,7 @@ extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompt
     if (it == c->gen_graphs.end()) {
         cudaGraph_t graph;
         DZ_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-        enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out);
+        enqueue_generate(c, prompts, plen, n_new, s, sampled ? seeds : nullptr, out, ctl);
         cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
         if (e != cudaSuccess) return fail(DZ_E_DEVICE, "capture: %s", cudaGetErrorString(e));
         cudaGraphExec_t exec;
@@ -2129,8 +2249,69 @@ extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompt
     return DZ_OK;
 }
 
+extern "C" int dz_cuda_generate_async(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                                      const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out) {
+    return generate_async(c, prompts, plen, n_new, s, seeds, out, nullptr);
+}
+
+// The controls of a generation on the host (validated the way
+// options_are_valid does, src/cli/generation.c:84-112) and their stop
+// sequences copied to the device (buffers grown outside any capture).
+static int prepare_controls(dz_cuda_cache_t* c, const dz_generation_controls_t* in, GenControls* out) {
+    out->on = false;
+    if (!in) return DZ_OK;
+    const uint32_t V = (uint32_t)c->model->desc.vocab_size;
+    if (!(in->repetition_penalty >= 1.0f) || !(in->repetition_penalty <= 3.402823466e38f))
+        return fail(DZ_E_INVALID, "repetition penalty must be finite and >= 1");
+    if (in->n_stops > 64 || (in->n_stops && (!in->stop_tokens || !in->stop_lengths)))
+        return fail(DZ_E_INVALID, "stop sequences: at most 64, with their tokens and lengths");
+    if (in->minimum_new_tokens > (size_t)1 << 30) return fail(DZ_E_INVALID, "minimum_new_tokens too large");
+    out->on = true;
+    out->penalty = in->repetition_penalty;
+    out->eos_id = in->eos_id;
+    out->mask_from = in->mask_from;
+    out->min_new = (int)in->minimum_new_tokens;
+    out->stop_tok.clear();
+    out->stop_off.assign(1, 0);
+    for (size_t q = 0; q < in->n_stops; q++) {
+        const size_t len = in->stop_lengths[q];
+        if (len == 0 || len > 256) return fail(DZ_E_INVALID, "stop sequence %zu: length must be 1..256", q);
+        for (size_t j = 0; j < len; j++) {
+            const uint32_t t = in->stop_tokens[out->stop_tok.size()];
+            if (t >= V) return fail(DZ_E_INVALID, "stop sequence %zu: token %u out of the vocabulary", q, t);
+            out->stop_tok.push_back(t);
+        }
+        out->stop_off.push_back((int)out->stop_tok.size());
+    }
+    const size_t nt = std::max<size_t>(1, out->stop_tok.size()), no = out->stop_off.size();
+    if (nt > c->stop_tok_cap || no > c->stop_off_cap) {
+        clear_graphs(c);   // captured graphs hold the old pointers
+        cudaFree(c->stop_tok);
+        cudaFree(c->stop_off);
+        c->stop_tok = nullptr;
+        c->stop_off = nullptr;
+        c->stop_tok_cap = c->stop_off_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->stop_tok, std::max<size_t>(nt, 64) * 4));
+        DZ_CUDA(cudaMalloc(&c->stop_off, std::max<size_t>(no, 65) * 4));
+        c->stop_tok_cap = std::max<size_t>(nt, 64);
+        c->stop_off_cap = std::max<size_t>(no, 65);
+    }
+    if (!out->stop_tok.empty())
+        DZ_CUDA(cudaMemcpyAsync(c->stop_tok, out->stop_tok.data(), out->stop_tok.size() * 4, cudaMemcpyHostToDevice,
+                                c->stream));
+    DZ_CUDA(cudaMemcpyAsync(c->stop_off, out->stop_off.data(), out->stop_off.size() * 4, cudaMemcpyHostToDevice,
+                            c->stream));
+    return DZ_OK;
+}
+
 extern "C" int dz_cuda_generate(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
                                 const dz_sampling_t* s, const uint64_t* seeds, uint32_t* out_tokens) {
+    return dz_cuda_generate_ex(c, prompts, plen, n_new, s, nullptr, seeds, out_tokens, nullptr);
+}
+
+extern "C" int dz_cuda_generate_ex(dz_cuda_cache_t* c, const uint32_t* prompts, size_t plen, size_t n_new,
+                                   const dz_sampling_t* s, const dz_generation_controls_t* controls,
+                                   const uint64_t* seeds, uint32_t* out_tokens, dz_generation_result_t* results) {
     if (!c || !prompts || !out_tokens || plen == 0 || n_new == 0)
         return fail(DZ_E_INVALID, "generate: null buffer or empty prompt/decode length");
     if (plen > (size_t)c->cap) return fail(DZ_E_INVALID, "prompt longer than the cache capacity");
@@ -2154,15 +2335,38 @@ extern "C" int dz_cuda_generate(dz_cuda_cache_t* c, const uint32_t* prompts, siz
     }
     DZ_CUDA(cudaMemcpyAsync(c->gen_prompts, prompts, B * plen * 4, cudaMemcpyHostToDevice, c->stream));
     if (seeds) DZ_CUDA(cudaMemcpyAsync(c->gen_seeds, seeds, B * 8, cudaMemcpyHostToDevice, c->stream));
-    int rc = dz_cuda_generate_async(c, c->gen_prompts, plen, n_new, s, seeds ? c->gen_seeds : nullptr, c->gen_out);
+    GenControls ctl;
+    int rc = prepare_controls(c, controls, &ctl);
+    if (rc) return rc;
+    rc = generate_async(c, c->gen_prompts, plen, n_new, s, seeds ? c->gen_seeds : nullptr, c->gen_out,
+                        ctl.on ? &ctl : nullptr);
     if (rc) return rc;
     DZ_CUDA(cudaMemcpyAsync(out_tokens, c->gen_out, B * n_new * 4, cudaMemcpyDeviceToHost, c->stream));
+    if (ctl.on && results)
+        DZ_CUDA(cudaMemcpyAsync(c->host_gen, c->gen_state, B * DZ_GEN_WORDS * 4, cudaMemcpyDeviceToHost, c->stream));
     DZ_CUDA(cudaMemcpyAsync(c->host_status, c->status, 4, cudaMemcpyDeviceToHost, c->stream));
     DZ_CUDA(cudaStreamSynchronize(c->stream));
     if (*c->host_status != 0) {
         cudaMemsetAsync(c->status, 0, 4, c->stream);
         cudaStreamSynchronize(c->stream);
         return fail(DZ_E_TIMEOUT, "generate: a weight-copy wait gave up on the device");
+    }
+    if (results) {
+        for (size_t b = 0; b < B; b++) {
+            dz_generation_result_t& r = results[b];
+            if (ctl.on) {
+                const uint32_t* gsv = c->host_gen + b * DZ_GEN_WORDS;
+                r.new_count = gsv[GEN_NEW];
+                r.emitted_count = gsv[GEN_EMITTED];
+                r.stopped_on_eos = gsv[GEN_EOS];
+                r.stopped_on_stop_sequence = gsv[GEN_STOP];
+                r.stop_sequence_index = gsv[GEN_STOP_INDEX];
+            } else {
+                r.new_count = r.emitted_count = (uint32_t)n_new;
+                r.stopped_on_eos = r.stopped_on_stop_sequence = 0;
+                r.stop_sequence_index = 0xffffffffu;
+            }
+        }
     }
     return DZ_OK;
 }
@@ -2209,6 +2413,9 @@ extern "C" int dz_cuda_prefill(dz_cuda_cache_t* c, const uint32_t* ids, const ui
     DZ_CUDA(cudaMemcpyAsync(c->pf_ids, ids, B * prompt_len * 4, cudaMemcpyHostToDevice, c->stream));
     if (lens) DZ_CUDA(cudaMemcpyAsync(c->pf_lens, lv.data(), B * 4, cudaMemcpyHostToDevice, c->stream));
     dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
+    dz_seen_clear_kernel<<<dim3((unsigned)((c->seen_words + 255) / 256), (unsigned)c->B), 256, 0, c->stream>>>(
+        c->seen, c->seen_words, nullptr);
+    c->seen_valid = true;
     enqueue_prefill(c, c->pf_ids, (long long)prompt_len, (int)prompt_len, lens ? c->pf_lens : nullptr);
     DZ_CUDA(cudaGetLastError());
     if (logits_out)

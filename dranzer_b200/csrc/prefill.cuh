@@ -17,11 +17,15 @@ namespace dz {
 // table as compute_positional_encoding_at, src/core/tensor_ops.c:250-260).
 __global__ void dz_prefill_embed_kernel(const uint32_t* __restrict__ tokens, long long ld_tok, int T,
                                         const float* __restrict__ emb, const float* __restrict__ pe,
-                                        long long pe_rows, float* __restrict__ hidden, int dim, int vocab) {
+                                        long long pe_rows, float* __restrict__ hidden, int dim, int vocab,
+                                        const int* __restrict__ lens, uint32_t* __restrict__ seen,
+                                        int seen_words) {
     const long long r = blockIdx.x;
     const int s = (int)(r / T), t = (int)(r % T);
     uint32_t tok = tokens[(long long)s * ld_tok + t];
     if (tok >= (uint32_t)vocab) tok = 0;
+    else if (seen && threadIdx.x == 0 && (!lens || t < lens[s]))   // the sequence's token history
+        atomicOr(&seen[(long long)s * seen_words + (tok >> 5)], 1u << (tok & 31));
     const float* e = emb + (long long)tok * dim;
     float* h = hidden + r * dim;
     if (t < pe_rows) {

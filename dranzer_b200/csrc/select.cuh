@@ -22,6 +22,25 @@ constexpr int SEL_THREADS = 512;
 constexpr int SEL_SORT_CAP = 8192;   // vocabularies sorted whole in shared memory
 constexpr int SEL_TOPK_CAP = 1024;   // top-k bound for larger vocabularies
 
+// Per-sequence state of the generation loop's controls (dz_cuda_generate_ex):
+// words of one sequence's row of DZ_GEN_WORDS.
+enum { GEN_NEW = 0, GEN_EMITTED = 1, GEN_EOS = 2, GEN_STOP = 3, GEN_STOP_INDEX = 4, GEN_DONE = 5, DZ_GEN_WORDS = 8 };
+
+// The generation loop's controls beyond sample_next_token
+// (src/cli/generation.c:52-72, 31-46, 250-280), all optional.
+struct SelectControls {
+    const uint32_t* seen;     // [B][seen_words] bit per id fed through the model since reset, or null
+    int seen_words;
+    float penalty;            // > 1: the sign-aware repetition penalty on the seen ids
+    uint32_t mask_from;       // ids >= mask_from masked (the tokenizer's unassigned ids)
+    uint32_t* state;          // [B][DZ_GEN_WORDS] loop state, or null: no EOS, stops or end
+    uint32_t eos_id;          // a draw of it ends the sequence (>= V: none)
+    int min_new;              // EOS masked and stops unmatched before this many new tokens
+    const uint32_t* stop_tok; // the stop sequences' ids, concatenated
+    const int* stop_off;      // [n_stops + 1] offsets into stop_tok
+    int n_stops;
+};
+
 struct SelectArgs {
     const float* logits;   // [B][ld]
     long long ld;
@@ -36,6 +55,7 @@ struct SelectArgs {
     uint32_t* out;         // out[b * out_stride]
     long long out_stride;
     uint32_t* out2;        // optional second copy, [B]
+    SelectControls ctl;    // zero: plain selection
 };
 
 __device__ __forceinline__ uint64_t dz_rng_next(uint64_t* s) {
@@ -81,10 +101,22 @@ __device__ void dz_bitonic_sort(uint64_t* a, int n) {  // n power of two, ascend
     }
 }
 
-__device__ __forceinline__ float dz_masked_logit(const SelectArgs& a, const float* lg, int i) {
+// Logit i as the draw sees it: repetition penalty on an id the sequence
+// holds (generation_apply_repetition_penalty: multiplied when negative,
+// divided otherwise), then the masked ids, the unassigned range and EOS
+// under the minimum length set to -FLT_MAX.
+struct SelRow {
+    const uint32_t* seen;   // this sequence's bits, or null
+    bool eos_masked;
+};
+__device__ __forceinline__ float dz_masked_logit(const SelectArgs& a, const SelRow& row, const float* lg, int i) {
     float v = lg[i];
+    if (row.seen && ((row.seen[i >> 5] >> (i & 31)) & 1u))
+        v = v < 0.0f ? v * a.ctl.penalty : __fdiv_rn(v, a.ctl.penalty);
     for (int m = 0; m < a.n_masked; m++)
         if (a.masked[m] == (uint32_t)i) v = -3.402823466e38f;
+    if ((uint32_t)i >= a.ctl.mask_from) v = -3.402823466e38f;
+    if (row.eos_masked && (uint32_t)i == a.ctl.eos_id) v = -3.402823466e38f;
     return v;
 }
 
@@ -97,6 +129,17 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
     const int b = blockIdx.x;
     const float* lg = a.logits + (long long)b * a.ld;
     const int V = a.V;
+    uint32_t* gst = a.ctl.state ? a.ctl.state + (long long)b * DZ_GEN_WORDS : nullptr;
+    if (gst && gst[GEN_DONE]) {   // the sequence has ended: no draw (uniform over the block)
+        if (threadIdx.x == 0) {
+            a.out[(long long)b * a.out_stride] = 0xffffffffu;
+            if (a.out2) a.out2[b] = 0u;
+        }
+        return;
+    }
+    SelRow row;
+    row.seen = a.ctl.seen && a.ctl.penalty > 1.0f ? a.ctl.seen + (long long)b * a.ctl.seen_words : nullptr;
+    row.eos_masked = gst && (int)gst[GEN_NEW] < a.ctl.min_new && a.ctl.eos_id < (uint32_t)V;
     const bool greedy = a.strategy == 0 || !(a.temperature > 0.0f) || a.rng == nullptr ||
                         (a.strategy == 1 && a.top_k == 0) ||
                         (a.strategy == 2 && (a.top_p <= 0.0f || a.top_p > 1.0f)) ||
@@ -107,7 +150,7 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
         // first index of the strict maximum: smallest descending key
         uint64_t best = ~0ull;
         for (int i = threadIdx.x; i < V; i += SEL_THREADS) {
-            const uint64_t k = dz_desc_key(dz_masked_logit(a, lg, i), (uint32_t)i);
+            const uint64_t k = dz_desc_key(dz_masked_logit(a, row, lg, i), (uint32_t)i);
             best = k < best ? k : best;
         }
 #pragma unroll
@@ -131,7 +174,7 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
             int P = 1;
             while (P < V) P <<= 1;
             for (int i = threadIdx.x; i < P; i += SEL_THREADS)
-                keys[i] = i < V ? dz_desc_key(dz_masked_logit(a, lg, i) * inv_t, (uint32_t)i) : ~0ull;
+                keys[i] = i < V ? dz_desc_key(dz_masked_logit(a, row, lg, i) * inv_t, (uint32_t)i) : ~0ull;
             __syncthreads();
             dz_bitonic_sort(keys, P);
             n_sorted = V;
@@ -151,7 +194,7 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
                 const int shift = pass * 8;
                 const unsigned long long hi_mask = pass == 7 ? 0ull : (~0ull << (shift + 8));
                 for (int i = threadIdx.x; i < V; i += SEL_THREADS) {
-                    const uint64_t key = dz_desc_key(dz_masked_logit(a, lg, i) * inv_t, (uint32_t)i);
+                    const uint64_t key = dz_desc_key(dz_masked_logit(a, row, lg, i) * inv_t, (uint32_t)i);
                     if ((key & hi_mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xff], 1u);
                 }
                 __syncthreads();
@@ -169,7 +212,7 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
             }
             const unsigned long long kth = prefix_s;
             for (int i = threadIdx.x; i < V; i += SEL_THREADS) {
-                const uint64_t key = dz_desc_key(dz_masked_logit(a, lg, i) * inv_t, (uint32_t)i);
+                const uint64_t key = dz_desc_key(dz_masked_logit(a, row, lg, i) * inv_t, (uint32_t)i);
                 if (key <= kth) {
                     const unsigned int slot = atomicAdd(&count_s, 1u);
                     if (slot < (unsigned)SEL_TOPK_CAP) keys[slot] = key;
@@ -224,9 +267,57 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
         __syncthreads();
     }
     if (threadIdx.x == 0) {
-        a.out[(long long)b * a.out_stride] = sel_result;
-        if (a.out2) a.out2[b] = sel_result;
+        const uint32_t tok = sel_result;
+        uint32_t* o = a.out + (long long)b * a.out_stride;
+        *o = tok;
+        if (a.out2) a.out2[b] = tok;
+        if (gst) {
+            // the end of a sequence (src/cli/generation.c:262-280): EOS, or the
+            // generated tail equal to a stop sequence that starts at or after
+            // the minimum length; `o` is column new_count - 1 of the row
+            const uint32_t nc = gst[GEN_NEW] + 1;
+            gst[GEN_NEW] = nc;
+            uint32_t done = 0;
+            if (tok == a.ctl.eos_id) {
+                gst[GEN_EMITTED] = nc - 1;
+                gst[GEN_EOS] = 1;
+                done = 1;
+            } else {
+                for (int q = 0; q < a.ctl.n_stops && !done; q++) {
+                    const int len = a.ctl.stop_off[q + 1] - a.ctl.stop_off[q];
+                    if ((uint32_t)len > nc || (int)(nc - (uint32_t)len) < a.ctl.min_new) continue;
+                    bool eq = true;
+                    for (int j = 0; j < len && eq; j++)
+                        eq = o[-(long long)(len - 1 - j)] == a.ctl.stop_tok[a.ctl.stop_off[q] + j];
+                    if (eq) {
+                        gst[GEN_EMITTED] = nc - (uint32_t)len;
+                        gst[GEN_STOP] = 1;
+                        gst[GEN_STOP_INDEX] = (uint32_t)q;
+                        done = 1;
+                    }
+                }
+                if (!done) gst[GEN_EMITTED] = nc;
+            }
+            gst[GEN_DONE] = done;
+        }
     }
+}
+
+// Fresh loop state for every sequence of a generation.
+__global__ void dz_gen_init_kernel(uint32_t* __restrict__ state, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    uint32_t* s = state + (long long)b * DZ_GEN_WORDS;
+    for (int w = 0; w < DZ_GEN_WORDS; w++) s[w] = 0u;
+    s[GEN_STOP_INDEX] = 0xffffffffu;
+}
+
+// Clears the token history of the sequences whose mask byte is set (all
+// when mask is null): grid (ceil(words / 256), B).
+__global__ void dz_seen_clear_kernel(uint32_t* __restrict__ seen, int words, const uint8_t* __restrict__ mask) {
+    const int b = blockIdx.y;
+    const int w = blockIdx.x * blockDim.x + threadIdx.x;
+    if (w < words && (!mask || mask[b])) seen[(long long)b * words + w] = 0u;
 }
 
 inline size_t dz_select_smem_bytes(int V, int strategy, int top_k) {

@@ -145,6 +145,53 @@ int dz_cuda_generate(dz_cuda_cache_t *cache, const uint32_t *prompts, size_t pro
 int dz_cuda_generate_async(dz_cuda_cache_t *cache, const uint32_t *prompts_dev, size_t prompt_len,
                            size_t n_new, const dz_sampling_t *sampling, const uint64_t *seeds_dev,
                            uint32_t *out_tokens_dev);
+/* The generation loop's controls beyond token selection, the fields of
+ * generation_options_t (src/include/cli/generation.h) that
+ * generation_decode_with_options (src/cli/generation.c:198-308) applies per
+ * draw: the sign-aware repetition penalty over every id the sequence holds
+ * (prompt and generated, :52-72), the tokenizer's unassigned ids masked
+ * (ids >= mask_from, :43-45), EOS masked until minimum_new_tokens tokens are
+ * drawn (:250-254), and the end of a sequence at a draw of EOS (:262-269)
+ * or when its generated tail equals a stop sequence starting at or after
+ * minimum_new_tokens (:120-138, :271-280). The control ids PAD/UNK/BOS go in
+ * dz_sampling_t.masked_ids as before. */
+typedef struct {
+    float repetition_penalty;     /* >= 1; 1 leaves the logits as they are */
+    uint32_t eos_id;              /* >= vocab: no EOS */
+    size_t minimum_new_tokens;
+    uint32_t mask_from;           /* >= vocab: nothing masked */
+    const uint32_t *stop_tokens;  /* the stop sequences' ids, concatenated */
+    const size_t *stop_lengths;   /* [n_stops], each 1..256 */
+    size_t n_stops;               /* <= 64 */
+} dz_generation_controls_t;
+
+/* generation_result_t (src/include/cli/generation.h) per sequence. */
+typedef struct {
+    uint32_t new_count;                /* tokens drawn, the ending one included */
+    uint32_t emitted_count;            /* tokens delivered: before EOS or the matched stop sequence */
+    uint32_t stopped_on_eos;
+    uint32_t stopped_on_stop_sequence;
+    uint32_t stop_sequence_index;      /* 0xffffffff: none */
+} dz_generation_result_t;
+
+/* dz_cuda_generate with the loop's controls (NULL: none): the loop of
+ * generation_decode_with_options for every sequence at once. A sequence that
+ * ends draws no more tokens; out_tokens after its end hold 0xffffffff.
+ * results[batch] (host, or NULL) as generation_result_t. Runs on the layered
+ * path (the fused kernel has no controls). Host buffers, synchronous. */
+int dz_cuda_generate_ex(dz_cuda_cache_t *cache, const uint32_t *prompts, size_t prompt_len, size_t n_new,
+                        const dz_sampling_t *sampling, const dz_generation_controls_t *controls,
+                        const uint64_t *seeds, uint32_t *out_tokens, dz_generation_result_t *results);
+
+/* dz_cuda_select with the repetition penalty (over the tokens each sequence
+ * was fed since its reset) and the unassigned-id mask of `controls`; EOS,
+ * the minimum length and stop sequences stay with the caller's loop, as in
+ * the reference (src/cli/generation.c:246-280). DZ_E_UNSUPPORTED for a
+ * penalty after a generation on the fused path (it keeps no token history)
+ * until the cache is reset. */
+int dz_cuda_select_ex(dz_cuda_cache_t *cache, const dz_sampling_t *sampling, const dz_generation_controls_t *controls,
+                      uint64_t *rng_states, uint32_t *out_ids);
+
 /* Execution path of dz_cuda_generate(_async). AUTO runs the fused kernel (one
  * thread block per sequence runs the whole generation, weights streamed into
  * shared memory by TMA bulk copies) whenever the model fits it (every

@@ -605,6 +605,100 @@ int or_generate(const or_model_t *m, or_cache_t *c, const uint32_t *prompts, siz
     return 0;
 }
 
+/* src/cli/generation.c:52-72: the sign-aware penalty, once per token id
+ * present in sequence[0..count). */
+static void or_repetition_penalty(float *logits, size_t vocab, const uint32_t *sequence, size_t count,
+                                  float penalty) {
+    if (penalty <= 1.0f) return;
+    for (size_t i = 0; i < count; i++) {
+        uint32_t id = sequence[i];
+        if (id >= vocab) continue;
+        int seen = 0;
+        for (size_t j = 0; j < i; j++)
+            if (sequence[j] == id) { seen = 1; break; }
+        if (seen) continue;
+        if (logits[id] < 0.0f) logits[id] *= penalty;
+        else logits[id] /= penalty;
+    }
+}
+
+/* The decode loop of generation_decode_with_options (src/cli/generation.c:
+ * 198-308) with its controls: repetition penalty over prompt + generated ids,
+ * control masking (the ids in `masked` and every id >= mask_from, :31-46),
+ * EOS masked until min_new tokens are drawn (:250-254), a draw of EOS ends
+ * the sequence (:262-269), and the generated tail matching a stop sequence
+ * that starts at or after min_new ends it (:120-138, :271-280). results[5 *
+ * q] = new_count, emitted_count, stopped_on_eos, stopped_on_stop_sequence,
+ * stop_sequence_index (UINT32_MAX when none). Tokens after the end are
+ * UINT32_MAX. out_logits, when not NULL, receives the logits of every draw
+ * after penalty and masking ([n_seq][n_new][V]). */
+int or_generate_ex(const or_model_t *m, or_cache_t *c, const uint32_t *prompts, size_t n_seq,
+                   size_t prompt_len, size_t n_new, int strategy, float temperature, size_t top_k,
+                   float top_p, const uint64_t *seeds, float penalty, uint32_t eos_id, size_t min_new,
+                   uint32_t mask_from, const uint32_t *masked, size_t n_masked, const uint32_t *stop_tokens,
+                   const size_t *stop_lengths, size_t n_stops, uint32_t *out_tokens, uint32_t *results,
+                   float *out_logits) {
+    const size_t V = m->vocab;
+    float *logits = malloc(V * sizeof(float));
+    uint32_t *seq = malloc((prompt_len + n_new) * sizeof(uint32_t));
+    if (!logits || !seq) { free(logits); free(seq); return -1; }
+    for (size_t q = 0; q < n_seq; q++) {
+        or_cache_reset(c);
+        memcpy(seq, prompts + q * prompt_len, prompt_len * sizeof(uint32_t));
+        for (size_t i = 0; i < prompt_len; i++) or_forward_token(m, c, seq[i], logits);
+        uint64_t rng = seeds ? or_rng_stream(seeds[q], OR_STREAM_SAMPLING) : 0;
+        size_t total = prompt_len, new_count = 0, emitted = 0;
+        uint32_t on_eos = 0, on_stop = 0, stop_index = UINT32_MAX;
+        for (size_t i = 0; i < n_new; i++) out_tokens[q * n_new + i] = UINT32_MAX;
+        int ended = 0;
+        for (size_t i = 0; i < n_new && !ended; i++) {
+            or_repetition_penalty(logits, V, seq, total, penalty);
+            for (size_t k = 0; k < n_masked; k++)
+                if (masked[k] < V) logits[masked[k]] = -FLT_MAX;
+            for (size_t k = mask_from; k < V; k++) logits[k] = -FLT_MAX;
+            if (new_count < min_new && eos_id < V) logits[eos_id] = -FLT_MAX;
+            if (out_logits) memcpy(out_logits + (q * n_new + i) * V, logits, V * sizeof(float));
+            uint32_t next = or_sample_next_token(logits, V, strategy, temperature, top_k, top_p,
+                                                 seeds ? &rng : NULL);
+            seq[total++] = next;
+            new_count++;
+            out_tokens[q * n_new + i] = next;
+            if (next == eos_id) {
+                emitted = new_count - 1;
+                on_eos = 1;
+                ended = 1;
+                break;
+            }
+            const uint32_t *gen = seq + prompt_len;
+            size_t off = 0;
+            for (size_t s = 0; s < n_stops; s++) {
+                const size_t len = stop_lengths[s];
+                if (len <= new_count && new_count - len >= min_new &&
+                    memcmp(gen + new_count - len, stop_tokens + off, len * sizeof(uint32_t)) == 0) {
+                    emitted = new_count - len;
+                    on_stop = 1;
+                    stop_index = (uint32_t)s;
+                    ended = 1;
+                    break;
+                }
+                off += len;
+            }
+            if (ended) break;
+            if (i + 1 < n_new) or_forward_token(m, c, next, logits);
+        }
+        if (!on_eos && !on_stop) emitted = new_count;
+        uint32_t *r = results + 5 * q;
+        r[0] = (uint32_t)new_count;
+        r[1] = (uint32_t)emitted;
+        r[2] = on_eos;
+        r[3] = on_stop;
+        r[4] = stop_index;
+    }
+    free(logits);
+    free(seq);
+    return 0;
+}
+
 /* src/core/fingerprint.c:14-20 */
 uint64_t or_fnv1a(uint64_t running, const void *data, size_t size) {
     const uint8_t *b = data;

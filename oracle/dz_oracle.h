@@ -80,6 +80,15 @@ int or_generate(const or_model_t *m, or_cache_t *c, const uint32_t *prompts, siz
                 const uint32_t *masked, size_t n_masked,
                 uint32_t *out_tokens, float *out_logits);
 
+/* generation_decode_with_options (src/cli/generation.c:198-308) with its
+ * controls; see dz_oracle.c for the contract. */
+int or_generate_ex(const or_model_t *m, or_cache_t *c, const uint32_t *prompts, size_t n_seq,
+                   size_t prompt_len, size_t n_new, int strategy, float temperature, size_t top_k,
+                   float top_p, const uint64_t *seeds, float penalty, uint32_t eos_id, size_t min_new,
+                   uint32_t mask_from, const uint32_t *masked, size_t n_masked, const uint32_t *stop_tokens,
+                   const size_t *stop_lengths, size_t n_stops, uint32_t *out_tokens, uint32_t *results,
+                   float *out_logits);
+
 /* src/core/fingerprint.c:14-20 */
 uint64_t or_fnv1a(uint64_t running, const void *data, size_t size);
 

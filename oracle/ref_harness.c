@@ -22,6 +22,7 @@
 #include "core/rng.h"
 #include "core/transformer.h"
 #include "cli/sampling.h"
+#include "cli/generation.h"
 #include "byte_pair_encoding.h"
 #include <float.h>
 #include <math.h>
@@ -248,6 +249,67 @@ int rh_generate(void *handle, const uint32_t *prompts, size_t n_seq,
     }
     return 0;
 }
+
+/* The reference's own generation loop, generation_decode_with_options
+ * (src/cli/generation.c:198-308), per sequence with its controls: sampling
+ * strategy, repetition penalty, minimum new tokens and stop sequences
+ * (token ids, concatenated, with their lengths), the bundle's tokenizer for
+ * control masking and EOS. out_tokens [n_seq][n_new] receives the drawn
+ * tokens (UINT32_MAX after the end); results [n_seq][5] = new_count,
+ * emitted_count, stopped_on_eos, stopped_on_stop_sequence,
+ * stop_sequence_index (UINT32_MAX when none). Returns the first non-zero
+ * generation_errors_t, or 0. */
+int rh_generate_ex(void *handle, const uint32_t *prompts, size_t n_seq, size_t prompt_len,
+                   size_t n_new, int strategy, float temperature, size_t top_k, float top_p,
+                   const uint64_t *seeds, float penalty, size_t min_new,
+                   const uint32_t *stop_tokens, const size_t *stop_lengths, size_t n_stops,
+                   uint32_t *out_tokens, uint32_t *results) {
+    rh_session_t *s = handle;
+    generation_stop_sequence_t stops[16];
+    if (n_stops > 16) return -100;
+    size_t off = 0;
+    for (size_t i = 0; i < n_stops; i++) {
+        stops[i].token_ids = stop_tokens + off;
+        stops[i].token_count = stop_lengths[i];
+        off += stop_lengths[i];
+    }
+    uint32_t *seq = malloc((prompt_len + n_new) * sizeof(uint32_t));
+    if (!seq) return -101;
+    for (size_t q = 0; q < n_seq; q++) {
+        memcpy(seq, prompts + q * prompt_len, prompt_len * sizeof(uint32_t));
+        uint64_t rng = seeds ? dranzer_rng_stream(seeds[q], DRANZER_RNG_STREAM_SAMPLING) : 0;
+        generation_options_t opt;
+        generation_options_init(&opt);
+        opt.strategy = (sampling_strategy_t)strategy;
+        opt.temperature = temperature;
+        opt.top_k = top_k;
+        opt.top_p = top_p;
+        opt.repetition_penalty = penalty;
+        opt.minimum_new_tokens = min_new;
+        opt.sequence_capacity = prompt_len + n_new;
+        opt.stop_sequences = n_stops ? stops : NULL;
+        opt.stop_sequence_count = n_stops;
+        opt.rng_state = seeds ? &rng : NULL;
+        generation_result_t res;
+        generation_errors_t rc = generation_decode_with_options(&s->model, s->encoder, seq, prompt_len,
+                                                                n_new, &opt, &res);
+        if (rc != GENERATION_SUCCESS) { free(seq); return (int)rc; }
+        for (size_t i = 0; i < n_new; i++)
+            out_tokens[q * n_new + i] = i < res.new_count ? seq[prompt_len + i] : UINT32_MAX;
+        uint32_t *r = results + 5 * q;
+        r[0] = (uint32_t)res.new_count;
+        r[1] = (uint32_t)res.emitted_count;
+        r[2] = (uint32_t)res.stopped_on_eos;
+        r[3] = (uint32_t)res.stopped_on_stop_sequence;
+        r[4] = res.stop_sequence_index == SIZE_MAX ? UINT32_MAX : (uint32_t)res.stop_sequence_index;
+    }
+    free(seq);
+    return 0;
+}
+
+/* The tokenizer's assigned vocabulary size (ids at or above it are masked
+ * by generation_mask_control_logits, src/cli/generation.c:43-45). */
+size_t rh_tokenizer_vocab(void *handle) { return ((rh_session_t *)handle)->encoder->vocab_size; }
 
 /* Quantized weight matrix through the reference's encoder and INT8/INT4
  * matmul (src/core/quantized_matmul.c). */

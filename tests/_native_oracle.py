@@ -77,6 +77,8 @@ class Oracle:
         _sig(L, "or_sample_next_token", U32, P, SZ, I32, F32, SZ, F32, P)
         _sig(L, "or_generate", I32, P, P, P, SZ, SZ, SZ, I32, F32, SZ, F32, P, P, SZ, P, P)
         _sig(L, "or_fnv1a", U64, U64, P, SZ)
+        _sig(L, "or_generate_ex", I32, P, P, P, SZ, SZ, SZ, I32, F32, SZ, F32, P, F32, U32, SZ, U32, P, SZ, P, P,
+             SZ, P, P, P)
 
     # --- rng / synthetic inputs
     def rng_stream(self, seed, stream):
@@ -167,6 +169,27 @@ class OracleModel:
                              temperature, top_k, top_p, _ptr(sd), _ptr(mk), len(mk), _ptr(toks), _ptr(lg))
         return toks, lg
 
+    def generate_ex(self, prompts, n_new, controls, strategy=GREEDY, temperature=0.0, top_k=0, top_p=0.0,
+                    seeds=None, want_logits=False):
+        """generation_decode_with_options with its controls (Controls):
+        tokens [n_seq, n_new] (UINT32_MAX after the end), results [n_seq, 5]
+        and, when asked, the logits of every draw after penalty and masking."""
+        prompts = np.ascontiguousarray(prompts, np.uint32)
+        n_seq, plen = prompts.shape
+        toks = np.empty((n_seq, n_new), np.uint32)
+        res = np.empty((n_seq, 5), np.uint32)
+        lg = np.empty((n_seq, n_new, self.spec.vocab), np.float32) if want_logits else None
+        sd = np.ascontiguousarray(seeds, np.uint64) if seeds is not None else None
+        c = controls
+        mk = np.array(c.masked, np.uint32)
+        st, sl = c.stop_arrays()
+        rc = self.o.L.or_generate_ex(self.h, self.cache, _ptr(prompts), n_seq, plen, n_new, strategy, temperature,
+                                     top_k, top_p, _ptr(sd), c.penalty, c.eos_id, c.min_new, c.mask_from,
+                                     _ptr(mk), len(mk), _ptr(st), _ptr(sl), len(c.stops), _ptr(toks), _ptr(res),
+                                     _ptr(lg))
+        assert rc == 0
+        return toks, res, lg
+
     def close(self):
         if self.h:
             self.o.L.or_cache_free(self.cache)
@@ -174,6 +197,24 @@ class OracleModel:
             self.h = None
 
     __del__ = close
+
+
+class Controls:
+    """The generation loop's controls beyond sample_next_token
+    (generation_options_t, src/include/cli/generation.h): repetition
+    penalty, EOS id and minimum new tokens, control ids masked and the first
+    masked id of the tokenizer's unassigned range, stop sequences."""
+
+    def __init__(self, penalty=1.0, eos_id=259, min_new=0, masked=(256, 257, 258), mask_from=1 << 31,
+                 stops=()):
+        self.penalty, self.eos_id, self.min_new = float(penalty), int(eos_id), int(min_new)
+        self.masked, self.mask_from = tuple(masked), int(mask_from)
+        self.stops = [tuple(int(t) for t in s) for s in stops]
+
+    def stop_arrays(self):
+        toks = np.array([t for s in self.stops for t in s] or [0], np.uint32)
+        lens = np.array([len(s) for s in self.stops] or [0], np.uint64)
+        return toks, lens
 
 
 class RefHarness:
@@ -206,6 +247,8 @@ class RefHarness:
         _sig(L, "quantize_unpack", I32, P, SZ, P, SZ, SZ, SZ, I32, I32, P)
         _sig(L, "sample_next_token", U32, P, SZ, I32, F32, SZ, F32, P)
         _sig(L, "compute_positional_encoding", I32, P, SZ, SZ)
+        _sig(L, "rh_generate_ex", I32, P, P, SZ, SZ, SZ, I32, F32, SZ, F32, P, F32, SZ, P, P, SZ, P, P)
+        _sig(L, "rh_tokenizer_vocab", SZ, P)
 
     def quantize_pack(self, w, bits, gran):
         w = np.ascontiguousarray(w, np.float32)

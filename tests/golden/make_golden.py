@@ -245,8 +245,75 @@ def gen_c4():
               prompt_logits=False)
 
 
+def gen_controls():
+    """The reference's own generation loop (generation_decode_with_options via
+    rh_generate_ex) with repetition penalty, minimum length, EOS and stop
+    sequences, on a 2-layer INT8 model whose tokenizer assigns ids 0..259
+    (so ids >= 260 are masked, src/cli/generation.c:43-45). Stop sequences
+    are picked from a first run without them, so that they occur."""
+    from _native_oracle import Controls, Oracle
+    vocab, dim, heads, layers, max_seq, wseed, bits = 512, 128, 4, 2, 64, 12, 8
+    path = "/tmp/dz_golden_controls.bin"
+    assert L.rh_build_bundle(path.encode(), vocab, dim, heads, layers, max_seq, wseed, bits, 2) == 0
+    h = L.rh_load(path.encode())
+    tok_vocab = int(L.rh_tokenizer_vocab(h))
+    with open(path, "rb") as f:
+        blob = np.frombuffer(f.read(), np.uint8)
+    os.remove(path)
+    st = np.array([rng_stream(13, STREAM_TESTING)], np.uint64)
+    n_seq, plen, n_new = 6, 10, 24
+    prompts = prompt_ids(st, n_seq * plen, vocab).reshape(n_seq, plen)
+    seeds = np.array([500 + i for i in range(n_seq)], np.uint64)
+    cases = [(GREEDY, 0.0, 0, 0.0, 1.3, 4, False), (TOPK, 0.9, 6, 0.0, 1.15, 2, True),
+             (TOPP, 0.8, 0, 0.85, 1.0, 0, True), (TOPK, 1.1, 40, 0.0, 1.4, 6, True)]
+    out = {"spec": np.array([vocab, dim, heads, layers, max_seq, wseed, bits], np.int64), "prompts": prompts,
+           "seeds": seeds, "tokenizer_vocab": np.array([tok_vocab], np.int64),
+           "bundle_fnv": np.array([fnv(blob)], np.uint64), "count": np.array([len(cases)], np.int64)}
+
+    def run(strategy, temperature, top_k, top_p, penalty, min_new, stops):
+        st_t = np.array([t for q in stops for t in q] or [0], np.uint32)
+        st_l = np.array([len(q) for q in stops] or [0], np.uint64)
+        toks = np.empty((n_seq, n_new), np.uint32)
+        res = np.empty((n_seq, 5), np.uint32)
+        sd = seeds if strategy else None
+        rc = L.rh_generate_ex(h, prompts.ctypes.data, n_seq, plen, n_new, strategy, temperature, top_k, top_p,
+                              sd.ctypes.data if sd is not None else None, penalty, min_new, st_t.ctypes.data,
+                              st_l.ctypes.data, len(stops), toks.ctypes.data, res.ctypes.data)
+        assert rc == 0, rc
+        return toks, res
+
+    # a near-flat draw (top-p 1 at temperature 4): seeds scanned, in order,
+    # for a set whose draws include EOS, so that EOS ends some sequences
+    base = 600
+    while True:
+        seeds = np.array([base + i for i in range(n_seq)], np.uint64)
+        t, r = run(TOPP, 4.0, 0, 1.0, 1.0, 2, [])
+        if r[:, 2].any():
+            break
+        base += n_seq
+    out["eos_seeds"] = seeds.copy()
+    cases.append((TOPP, 4.0, 0, 1.0, 1.0, 2, False))
+    out["count"] = np.array([len(cases)], np.int64)
+    for i, (strategy, temperature, top_k, top_p, penalty, min_new, with_stops) in enumerate(cases):
+        seeds = out["eos_seeds"] if i == len(cases) - 1 else out["seeds"]
+        out[f"c{i}_seeds"] = seeds
+        stops = []
+        if with_stops:
+            t0, _ = run(strategy, temperature, top_k, top_p, penalty, min_new, [])
+            stops = [(int(t0[0, min_new + 3]),), (int(t0[1, min_new + 5]), int(t0[1, min_new + 6]))]
+        toks, res = run(strategy, temperature, top_k, top_p, penalty, min_new, stops)
+        out[f"c{i}_params"] = np.array([strategy, top_k, min_new], np.int64)
+        out[f"c{i}_params_f"] = np.array([temperature, top_p, penalty], np.float32)
+        out[f"c{i}_stop_tokens"] = np.array([t for q in stops for t in q], np.uint32)
+        out[f"c{i}_stop_lengths"] = np.array([len(q) for q in stops], np.int64)
+        out[f"c{i}_tokens"] = toks
+        out[f"c{i}_results"] = res
+    L.rh_free(h)
+    np.savez_compressed(os.path.join(HERE, "controls.npz"), **out)
+
+
 GENERATORS = {"rng": gen_rng, "quant": gen_quant, "qmm": gen_qmm, "pe": gen_pe, "bundle": gen_bundle_small,
-              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "c4": gen_c4}
+              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "controls": gen_controls, "c4": gen_c4}
 
 if __name__ == "__main__":
     # no argument: every fixture except the config-4 sample (minutes of CPU)

@@ -137,3 +137,30 @@ def test_model_generation_golden(oracle, name):
     pl = np.stack([m.forward_token(t) for t in g["prompts"][0]])
     ref_pl = g["prompt_logits"]
     assert (np.abs(pl - ref_pl).max(axis=-1) / np.abs(ref_pl).max(axis=-1)).max() <= 1e-4
+
+
+def test_generation_controls_match_reference(oracle):
+    """or_generate_ex against the reference's own generation loop
+    (generation_decode_with_options, tests/golden/controls.npz): repetition
+    penalty, minimum length, EOS, stop sequences and the tokenizer's masking
+    give identical tokens and identical result fields."""
+    from _native_oracle import Controls
+    g = golden("controls.npz")
+    V, d, H, L, T, wseed, bits = (int(x) for x in g["spec"])
+    spec = Spec(V, d, H, L, T)
+    _, flat = quantize_params(oracle, spec, synth_params(oracle, spec, wseed), bits)
+    om = oracle.model(spec, flat)
+    for i in range(int(g["count"][0])):
+        strategy, top_k, min_new = (int(x) for x in g[f"c{i}_params"])
+        temperature, top_p, penalty = (float(x) for x in g[f"c{i}_params_f"])
+        st, sl = g[f"c{i}_stop_tokens"], g[f"c{i}_stop_lengths"]
+        stops, off = [], 0
+        for n in sl:
+            stops.append(tuple(st[off:off + n]))
+            off += n
+        c = Controls(penalty=penalty, min_new=min_new, mask_from=int(g["tokenizer_vocab"][0]), stops=stops)
+        toks, res, _ = om.generate_ex(g["prompts"], g[f"c{i}_tokens"].shape[1], c, strategy, temperature, top_k,
+                                      top_p, g[f"c{i}_seeds"] if strategy else None)
+        np.testing.assert_array_equal(toks, g[f"c{i}_tokens"], err_msg=f"case {i}")
+        np.testing.assert_array_equal(res, g[f"c{i}_results"], err_msg=f"case {i}")
+    om.close()
