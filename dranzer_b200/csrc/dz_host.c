@@ -426,10 +426,24 @@ int dz_positional_encoding(float *out, size_t rows, size_t dim) {
 
 /* --------------------------------------------------------- model layout */
 
+/* Architecture bits (src/include/core/model_types.h:26-36). */
+#define ARCH_TIED 1u
+#define ARCH_ROPE 2u
+#define ARCH_RMSNORM 4u
+#define ARCH_GELU 8u
+#define ARCH_SWIGLU 16u
+#define ARCH_ALL 31u
+
+/* A supported combination: known bits, GELU and SwiGLU not both
+ * (src/core/bundle.c:142-144). */
+static int arch_valid(uint32_t f) { return (f & ~ARCH_ALL) == 0 && !((f & ARCH_GELU) && (f & ARCH_SWIGLU)); }
+
 size_t dz_model_param_count(const dz_model_desc_t *d) {
-    if (!d) return 0;
+    if (!d || !arch_valid(d->architecture_flags)) return 0;
+    const uint32_t f = d->architecture_flags;
     size_t D = d->embedding_dim, V = d->vocab_size;
-    return 2 * V * D + V + d->num_layers * (12 * D * D + 9 * D);
+    size_t per = ((f & ARCH_SWIGLU) ? 16 : 12) * D * D + (((f & ARCH_RMSNORM) ? 7 : 9) + ((f & ARCH_SWIGLU) ? 4 : 0)) * D;
+    return ((f & ARCH_TIED) ? 1 : 2) * V * D + V + d->num_layers * per;
 }
 
 static void put_layout(dz_tensor_blob_t *out, size_t cap, size_t *n, uint32_t kind, size_t r,
@@ -445,21 +459,27 @@ static void put_layout(dz_tensor_blob_t *out, size_t cap, size_t *n, uint32_t ki
 
 /* src/core/model_params.c:39-103, default architecture (flags 0). */
 size_t dz_model_tensor_layout(const dz_model_desc_t *d, dz_tensor_blob_t *out, size_t cap) {
-    if (!d || d->architecture_flags != 0) return 0;
+    if (!d || !arch_valid(d->architecture_flags)) return 0;
+    const uint32_t f = d->architecture_flags;
+    const int tied = (f & ARCH_TIED) != 0, rms = (f & ARCH_RMSNORM) != 0, swiglu = (f & ARCH_SWIGLU) != 0;
     size_t n = 0, D = d->embedding_dim, V = d->vocab_size, F = 4 * D;
     put_layout(out, cap, &n, DZ_KIND_EMBEDDING, V, D);
-    put_layout(out, cap, &n, DZ_KIND_PROJECTION, D, V);
+    if (!tied) put_layout(out, cap, &n, DZ_KIND_PROJECTION, D, V);
     put_layout(out, cap, &n, DZ_KIND_BIAS, 1, V);
     for (size_t l = 0; l < d->num_layers; l++) {
         for (int w = 0; w < 4; w++) put_layout(out, cap, &n, DZ_KIND_PROJECTION, D, D);
         put_layout(out, cap, &n, DZ_KIND_NORM, 1, D);
-        put_layout(out, cap, &n, DZ_KIND_NORM, 1, D);
+        if (!rms) put_layout(out, cap, &n, DZ_KIND_NORM, 1, D);
         put_layout(out, cap, &n, DZ_KIND_PROJECTION, D, F);
         put_layout(out, cap, &n, DZ_KIND_BIAS, 1, F);
+        if (swiglu) {
+            put_layout(out, cap, &n, DZ_KIND_PROJECTION, D, F);
+            put_layout(out, cap, &n, DZ_KIND_BIAS, 1, F);
+        }
         put_layout(out, cap, &n, DZ_KIND_PROJECTION, F, D);
         put_layout(out, cap, &n, DZ_KIND_BIAS, 1, D);
         put_layout(out, cap, &n, DZ_KIND_NORM, 1, D);
-        put_layout(out, cap, &n, DZ_KIND_NORM, 1, D);
+        if (!rms) put_layout(out, cap, &n, DZ_KIND_NORM, 1, D);
     }
     return n;
 }
@@ -499,9 +519,11 @@ static int add_ok(uint64_t a, uint64_t b, uint64_t *out) {
 static int shape_valid(const uint64_t dims[6], uint32_t flags) {
     uint64_t V = dims[0], D = dims[1], H = dims[2], Lr = dims[3], T = dims[4], total = dims[5];
     uint64_t d2, ve, g, sq, lin, lp, all, comp, tt, att, lim;
-    if (flags != 0 || V == 0 || D == 0 || H == 0 || Lr == 0 || T == 0 || D % H != 0) return 0;
-    if (!mul_ok(D, D, &d2) || !mul_ok(V, D, &ve) || !mul_ok(ve, 2, &g) || !add_ok(g, V, &g) ||
-        !mul_ok(d2, 12, &sq) || !mul_ok(D, 9, &lin) || !add_ok(sq, lin, &lp) ||
+    if (!arch_valid(flags) || V == 0 || D == 0 || H == 0 || Lr == 0 || T == 0 || D % H != 0) return 0;
+    const uint64_t tied = (flags & ARCH_TIED) ? 1 : 2, sqm = (flags & ARCH_SWIGLU) ? 16 : 12;
+    const uint64_t linm = ((flags & ARCH_RMSNORM) ? 7 : 9) + ((flags & ARCH_SWIGLU) ? 4 : 0);
+    if (!mul_ok(D, D, &d2) || !mul_ok(V, D, &ve) || !mul_ok(ve, tied, &g) || !add_ok(g, V, &g) ||
+        !mul_ok(d2, sqm, &sq) || !mul_ok(D, linm, &lin) || !add_ok(sq, lin, &lp) ||
         !mul_ok(Lr, lp, &all) || !add_ok(g, all, &comp) || comp != total ||
         !mul_ok(T, T, &tt) || !mul_ok(H, tt, &att) || !mul_ok(total, 64, &lim) || att > lim)
         return 0;
@@ -572,7 +594,7 @@ int dz_bundle_open(const char *path, dz_bundle_t **out) {
     uint64_t weight_sum = get_u64(map + 136), tok_sum = get_u64(map + 144);
     uint32_t arch = is_v3 ? get_u32(map + 184) : 0;
     if (is_v3 && (arch == 0 || get_u32(map + 188) != 0)) goto fail;
-    if (arch != 0) { rc = DZ_E_UNSUPPORTED; goto fail; }
+    if (!arch_valid(arch)) { rc = DZ_E_UNSUPPORTED; goto fail; }
     if (!shape_valid(dims, arch) || tok_bytes < 24 || train_window == 0 ||
         train_window > dims[4] || (is_float && weight_bytes != dims[5] * 4)) goto fail;
 
@@ -768,11 +790,15 @@ int dz_bundle_save_quantized(const char *path, const dz_model_desc_t *desc, cons
                              int bits, int granularity, const dz_bundle_meta_t *meta,
                              const uint8_t *tokenizer, size_t tokenizer_size) {
     if (!path || !desc || !params || !meta || !tokenizer || tokenizer_size < 24 || bits < 2 ||
-        bits > 16 || !valid_granularity(granularity) || desc->architecture_flags != 0)
+        bits > 16 || !valid_granularity(granularity) || !arch_valid(desc->architecture_flags))
         return DZ_E_INVALID;
+    /* v2 for the reference architecture, v3 (192-byte header, flags at 184)
+     * for any other (src/core/bundle.c:357-360, 475-476) */
+    const uint32_t arch = desc->architecture_flags;
+    const uint32_t hdr = arch ? HDR_V3 : HDR_V2;
     uint64_t dims[6] = {desc->vocab_size, desc->embedding_dim, desc->num_heads, desc->num_layers,
                         desc->max_seq_len, dz_model_param_count(desc)};
-    if (!shape_valid(dims, 0) || meta->train_window == 0 || meta->train_window > desc->max_seq_len)
+    if (!shape_valid(dims, arch) || meta->train_window == 0 || meta->train_window > desc->max_seq_len)
         return DZ_E_INVALID;
     size_t nt = dz_model_tensor_layout(desc, NULL, 0);
     dz_tensor_blob_t *lay = calloc(nt, sizeof(*lay));
@@ -801,10 +827,10 @@ int dz_bundle_save_quantized(const char *path, const dz_model_desc_t *desc, cons
     snprintf(tmp, plen + 32, "%s.tmp.%ld", path, (long)getpid());
     FILE *f = fopen(tmp, "wb");
     if (!f) { free(lay); free(tmp); return DZ_E_IO; }
-    uint8_t header[HDR_V2];
+    uint8_t header[HDR_V3];
     memset(header, 0, sizeof(header));
     sink_t s = {f, DZ_FNV_OFFSET, 1};
-    if (fwrite(header, 1, HDR_V2, f) != HDR_V2) s.ok = 0;
+    if (fwrite(header, 1, hdr, f) != hdr) s.ok = 0;
     int rc = DZ_OK;
     const float *cursor = params;
     for (size_t t = 0; t < nt && s.ok; t++) {
@@ -867,10 +893,10 @@ int dz_bundle_save_quantized(const char *path, const dz_model_desc_t *desc, cons
                  fwrite("DRNZDONE", 1, 8, f) != 8)) s.ok = 0;
 
     memcpy(header, "DRNZBNDL", 8);
-    put_u32(header + 8, 2);
+    put_u32(header + 8, arch ? 3 : 2);
     put_u32(header + 12, 0x01020304u);
     put_u32(header + 16, 2);
-    put_u32(header + 20, HDR_V2);
+    put_u32(header + 20, hdr);
     for (int i = 0; i < 6; i++) put_u64(header + 24 + 8 * i, dims[i]);
     put_u32(header + 72, meta->training_steps);
     put_u32(header + 80, meta->loss_bits);
@@ -888,10 +914,11 @@ int dz_bundle_save_quantized(const char *path, const dz_model_desc_t *desc, cons
     put_u32(header + 164, (uint32_t)nt);
     put_u64(header + 168, values_q);
     put_u64(header + 176, scales_q);
-    uint64_t hs = dz_fnv1a(DZ_FNV_OFFSET, header, HDR_V2);
+    if (arch) put_u32(header + 184, arch);
+    uint64_t hs = dz_fnv1a(DZ_FNV_OFFSET, header, hdr);
     put_u32(header + 76, (uint32_t)hs);
     put_u32(header + 84, (uint32_t)(hs >> 32));
-    if (s.ok && (fseek(f, 0, SEEK_SET) != 0 || fwrite(header, 1, HDR_V2, f) != HDR_V2)) s.ok = 0;
+    if (s.ok && (fseek(f, 0, SEEK_SET) != 0 || fwrite(header, 1, hdr, f) != hdr)) s.ok = 0;
     if (fclose(f) != 0) s.ok = 0;
     if (!s.ok || rename(tmp, path) != 0) {
         remove(tmp);

@@ -311,6 +311,47 @@ static void or_layer_norm(const float *in, float *out, size_t n, const float *ga
     for (size_t i = 0; i < n; i++) out[i] = gamma[i] * ((in[i] - mean) / sd) + beta[i];
 }
 
+/* src/core/tensor_ops.c:173-179 */
+static void or_rms_norm(const float *in, float *out, size_t n, const float *gamma, float eps) {
+    float ms = 0.0f;
+    for (size_t i = 0; i < n; i++) ms += in[i] * in[i];
+    float rms = sqrtf(ms / (float)n + eps);
+    for (size_t i = 0; i < n; i++) out[i] = gamma[i] * in[i] / rms;
+}
+
+/* src/core/tensor_ops.c:17-20 */
+static float or_gelu(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752440f)); }
+
+/* src/core/tensor_ops.c:29-40 */
+static float or_silu(float x) {
+    float sg;
+    if (x >= 0.0f) {
+        float z = expf(-x);
+        sg = 1.0f / (1.0f + z);
+    } else {
+        float z = expf(x);
+        sg = z / (1.0f + z);
+    }
+    return x * sg;
+}
+
+/* src/core/transformer.c:24-54 (rope_rotate, forward): each head's pairs
+ * (2p, 2p + 1) rotated by position * 10000^(-2p / head_dim), the angle and
+ * its cosine and sine in double. */
+static void or_rope(float *v, size_t dim, size_t heads, size_t position) {
+    const size_t hd = dim / heads;
+    for (size_t h = 0; h < heads; h++) {
+        float *x = v + h * hd;
+        for (size_t p = 0; p < hd / 2; p++) {
+            const double angle = (double)position * pow(10000.0, -(double)(2 * p) / (double)hd);
+            const float c = (float)cos(angle), s = (float)sin(angle);
+            const float a = x[2 * p], b = x[2 * p + 1];
+            x[2 * p] = a * c - b * s;
+            x[2 * p + 1] = a * s + b * c;
+        }
+    }
+}
+
 /* C[n] = a[k] . B[k x n], fp32 fused accumulation in ascending k. */
 static void or_matvec(const float *a, const float *B, float *c, size_t k, size_t n) {
     for (size_t j = 0; j < n; j++) c[j] = 0.0f;
@@ -324,11 +365,18 @@ static void or_matvec(const float *a, const float *B, float *c, size_t k, size_t
 /* -------------------------------------------------------------- model */
 
 typedef struct {
-    const float *wq, *wk, *wv, *wo, *g1, *be1, *w1, *b1, *w2, *b2, *g2, *be2;
+    const float *wq, *wk, *wv, *wo, *g1, *be1, *w1, *b1, *wg, *bg, *w2, *b2, *g2, *be2;
 } or_layer_t;
+
+#define OR_TIED 1u
+#define OR_ROPE 2u
+#define OR_RMSNORM 4u
+#define OR_GELU 8u
+#define OR_SWIGLU 16u
 
 struct or_model {
     size_t vocab, dim, heads, layers, max_seq;
+    uint32_t flags;
     float *params;
     const float *emb, *out_proj, *out_bias;
     or_layer_t *layer;
@@ -339,31 +387,45 @@ struct or_cache {
     const or_model_t *m;
     size_t capacity, length, start, total;
     float *keys, *values; /* [layers][capacity][dim] */
-    float *hidden, *attn_norm, *query, *concat, *attn_raw, *ff, *ff_raw, *scores, *pe_row;
+    float *hidden, *attn_norm, *query, *concat, *attn_raw, *ff, *gate, *ff_raw, *scores, *pe_row;
 };
 
-/* src/core/model.c:107-116 parameter count (default architecture). */
+/* src/core/model.c:107-124 parameter count. */
+size_t or_model_param_count_arch(size_t vocab, size_t dim, size_t layers, uint32_t flags) {
+    const size_t per = ((flags & OR_SWIGLU) ? 16 : 12) * dim * dim +
+                       (((flags & OR_RMSNORM) ? 7 : 9) + ((flags & OR_SWIGLU) ? 4 : 0)) * dim;
+    return ((flags & OR_TIED) ? 1 : 2) * vocab * dim + vocab + layers * per;
+}
+
 size_t or_model_param_count(size_t vocab, size_t dim, size_t layers) {
-    return 2 * vocab * dim + vocab + layers * (12 * dim * dim + 9 * dim);
+    return or_model_param_count_arch(vocab, dim, layers, 0);
 }
 
 or_model_t *or_model_create(size_t vocab, size_t dim, size_t heads, size_t layers,
                             size_t max_seq, const float *params) {
+    return or_model_create_arch(vocab, dim, heads, layers, max_seq, 0, params);
+}
+
+or_model_t *or_model_create_arch(size_t vocab, size_t dim, size_t heads, size_t layers,
+                                 size_t max_seq, uint32_t flags, const float *params) {
     if (!params || vocab == 0 || dim == 0 || heads == 0 || dim % heads || layers == 0 ||
-        max_seq == 0) return NULL;
+        max_seq == 0 || (flags & ~31u) || ((flags & OR_GELU) && (flags & OR_SWIGLU)) ||
+        ((flags & OR_ROPE) && (dim / heads) % 2)) return NULL;
     or_model_t *m = calloc(1, sizeof(*m));
-    size_t count = or_model_param_count(vocab, dim, layers);
+    m->flags = flags;
+    size_t count = or_model_param_count_arch(vocab, dim, layers, flags);
     m->params = malloc(count * sizeof(float));
     m->layer = calloc(layers, sizeof(or_layer_t));
     m->pe = malloc(max_seq * dim * sizeof(float));
     if (!m->params || !m->layer || !m->pe) { or_model_free(m); return NULL; }
     memcpy(m->params, params, count * sizeof(float));
     m->vocab = vocab; m->dim = dim; m->heads = heads; m->layers = layers; m->max_seq = max_seq;
-    /* src/core/model.c:38-67,213-228 */
+    /* src/core/model.c:38-67,213-228; src/core/model_params.c:39-103 */
     const float *p = m->params;
     const size_t F = 4 * dim;
+    const int rms = (flags & OR_RMSNORM) != 0;
     m->emb = p; p += vocab * dim;
-    m->out_proj = p; p += dim * vocab;
+    if (!(flags & OR_TIED)) { m->out_proj = p; p += dim * vocab; }
     m->out_bias = p; p += vocab;
     for (size_t l = 0; l < layers; l++) {
         or_layer_t *L = &m->layer[l];
@@ -372,13 +434,17 @@ or_model_t *or_model_create(size_t vocab, size_t dim, size_t heads, size_t layer
         L->wv = p; p += dim * dim;
         L->wo = p; p += dim * dim;
         L->g1 = p; p += dim;
-        L->be1 = p; p += dim;
+        if (!rms) { L->be1 = p; p += dim; }
         L->w1 = p; p += dim * F;
         L->b1 = p; p += F;
+        if (flags & OR_SWIGLU) {
+            L->wg = p; p += dim * F;
+            L->bg = p; p += F;
+        }
         L->w2 = p; p += F * dim;
         L->b2 = p; p += dim;
         L->g2 = p; p += dim;
-        L->be2 = p; p += dim;
+        if (!rms) { L->be2 = p; p += dim; }
     }
     or_positional_encoding(m->pe, max_seq, dim);
     return m;
@@ -403,6 +469,7 @@ or_cache_t *or_cache_create(const or_model_t *m, size_t capacity) {
     c->concat = malloc(d * sizeof(float));
     c->attn_raw = malloc(d * sizeof(float));
     c->ff = malloc(4 * d * sizeof(float));
+    c->gate = malloc(4 * d * sizeof(float));
     c->ff_raw = malloc(d * sizeof(float));
     c->scores = malloc(m->heads * capacity * sizeof(float));
     c->pe_row = malloc(d * sizeof(float));
@@ -414,7 +481,7 @@ void or_cache_reset(or_cache_t *c) { c->length = 0; c->start = 0; c->total = 0; 
 void or_cache_free(or_cache_t *c) {
     if (!c) return;
     free(c->keys); free(c->values); free(c->hidden); free(c->attn_norm); free(c->query);
-    free(c->concat); free(c->attn_raw); free(c->ff); free(c->ff_raw); free(c->scores);
+    free(c->concat); free(c->attn_raw); free(c->ff); free(c->gate); free(c->ff_raw); free(c->scores);
     free(c->pe_row); free(c);
 }
 
@@ -432,15 +499,18 @@ int or_forward_token(const or_model_t *m, or_cache_t *c, uint32_t token, float *
         c->start = (c->start + 1) % cap;
         ctx = cap;
     }
-    const float *pe;
-    if (pos < m->max_seq) {
-        pe = m->pe + pos * d;
-    } else {
-        or_positional_encoding_at(c->pe_row, pos, d);
-        pe = c->pe_row;
+    const int rope = (m->flags & OR_ROPE) != 0, rms = (m->flags & OR_RMSNORM) != 0;
+    const float *pe = NULL;
+    if (!rope) {
+        if (pos < m->max_seq) {
+            pe = m->pe + pos * d;
+        } else {
+            or_positional_encoding_at(c->pe_row, pos, d);
+            pe = c->pe_row;
+        }
     }
     if (token >= m->vocab) token = 0;
-    for (size_t i = 0; i < d; i++) c->hidden[i] = m->emb[token * d + i] + pe[i];
+    for (size_t i = 0; i < d; i++) c->hidden[i] = m->emb[token * d + i] + (pe ? pe[i] : 0.0f);
 
     for (size_t l = 0; l < m->layers; l++) {
         const or_layer_t *L = &m->layer[l];
@@ -448,6 +518,10 @@ int or_forward_token(const or_model_t *m, or_cache_t *c, uint32_t token, float *
         or_matvec(c->hidden, L->wq, c->query, d, d);
         or_matvec(c->hidden, L->wk, K + slot * d, d, d);
         or_matvec(c->hidden, L->wv, V + slot * d, d, d);
+        if (rope) {
+            or_rope(c->query, d, H, pos);
+            or_rope(K + slot * d, d, H, pos);
+        }
         for (size_t h = 0; h < H; h++) {
             float *sc = c->scores + h * cap;
             for (size_t j = 0; j < ctx; j++) {
@@ -469,17 +543,31 @@ int or_forward_token(const or_model_t *m, or_cache_t *c, uint32_t token, float *
         }
         or_matvec(c->concat, L->wo, c->attn_raw, d, d);
         for (size_t i = 0; i < d; i++) c->attn_raw[i] += c->hidden[i];
-        or_layer_norm(c->attn_raw, c->attn_norm, d, L->g1, L->be1, eps);
+        if (rms) or_rms_norm(c->attn_raw, c->attn_norm, d, L->g1, eps);
+        else or_layer_norm(c->attn_raw, c->attn_norm, d, L->g1, L->be1, eps);
         or_matvec(c->attn_norm, L->w1, c->ff, d, F);
+        if (m->flags & OR_SWIGLU) or_matvec(c->attn_norm, L->wg, c->gate, d, F);
         for (size_t i = 0; i < F; i++) {
             float pre = c->ff[i] + L->b1[i];
-            c->ff[i] = pre > 0.0f ? pre : 0.0f;
+            if (m->flags & OR_SWIGLU) c->ff[i] = or_silu(pre) * (c->gate[i] + L->bg[i]);
+            else if (m->flags & OR_GELU) c->ff[i] = or_gelu(pre);
+            else c->ff[i] = pre > 0.0f ? pre : 0.0f;
         }
         or_matvec(c->ff, L->w2, c->ff_raw, F, d);
         for (size_t i = 0; i < d; i++) c->ff_raw[i] += L->b2[i] + c->attn_norm[i];
-        or_layer_norm(c->ff_raw, c->hidden, d, L->g2, L->be2, eps);
+        if (rms) or_rms_norm(c->ff_raw, c->hidden, d, L->g2, eps);
+        else or_layer_norm(c->ff_raw, c->hidden, d, L->g2, L->be2, eps);
     }
-    or_matvec(c->hidden, m->out_proj, logits, d, m->vocab);
+    if (m->flags & OR_TIED) {
+        /* src/core/lm_head.c:21-46: logits = hidden . token_embeddings^T */
+        for (size_t v = 0; v < m->vocab; v++) {
+            float s = 0.0f;
+            for (size_t i = 0; i < d; i++) s += c->hidden[i] * m->emb[v * d + i];
+            logits[v] = s;
+        }
+    } else {
+        or_matvec(c->hidden, m->out_proj, logits, d, m->vocab);
+    }
     for (size_t i = 0; i < m->vocab; i++) logits[i] += m->out_bias[i];
     if (c->length < cap) c->length++;
     c->total++;

@@ -59,6 +59,15 @@ typedef struct or_model or_model_t;
 typedef struct or_cache or_cache_t;
 
 size_t or_model_param_count(size_t vocab, size_t dim, size_t layers);
+/* With the architecture bits of src/include/core/model_types.h:26-36 (1 tied
+ * embeddings, 2 RoPE, 4 RMSNorm, 8 GELU, 16 SwiGLU): the tensors of
+ * src/core/model_params.c:39-103 for those bits, and the forward of
+ * src/core/transformer.c:755-858 with rope_rotate (:24-54), rms_normalize
+ * (src/core/tensor_ops.c:173-179), gelu / silu (:17-40) and the tied head
+ * (src/core/lm_head.c:21-46). */
+size_t or_model_param_count_arch(size_t vocab, size_t dim, size_t layers, uint32_t flags);
+or_model_t *or_model_create_arch(size_t vocab, size_t dim, size_t heads, size_t layers,
+                                 size_t max_seq, uint32_t flags, const float *params);
 or_model_t *or_model_create(size_t vocab, size_t dim, size_t heads, size_t layers,
                             size_t max_seq, const float *params);
 void or_model_free(or_model_t *m);

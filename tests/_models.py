@@ -21,6 +21,7 @@ class Spec:
     heads: int
     layers: int
     max_seq: int
+    architecture_flags: int = 0   # src/include/core/model_types.h:26-36
 
     @property
     def ffn(self):
@@ -30,18 +31,32 @@ class Spec:
 C1 = Spec(512, 128, 4, 4, 64)
 
 
+TIED, ROPE, RMSNORM, GELU, SWIGLU = 1, 2, 4, 8, 16
+
+
 def inventory(spec):
+    """model_param_tensors (src/core/model_params.c:39-103) for the spec's
+    architecture bits: no output projection with tied embeddings, no norm
+    betas with RMSNorm, the gate branch after b_ff1 with SwiGLU."""
     d, V, F = spec.dim, spec.vocab, spec.ffn
-    out = [("token_embeddings", V, d, KIND_EMBEDDING),
-           ("output_projection", d, V, KIND_PROJECTION),
-           ("output_bias", 1, V, KIND_BIAS)]
+    f = spec.architecture_flags
+    out = [("token_embeddings", V, d, KIND_EMBEDDING)]
+    if not f & TIED:
+        out.append(("output_projection", d, V, KIND_PROJECTION))
+    out.append(("output_bias", 1, V, KIND_BIAS))
     for l in range(spec.layers):
         out += [(f"layer{l}.W_q", d, d, KIND_PROJECTION), (f"layer{l}.W_k", d, d, KIND_PROJECTION),
                 (f"layer{l}.W_v", d, d, KIND_PROJECTION), (f"layer{l}.W_o", d, d, KIND_PROJECTION),
-                (f"layer{l}.ln_gamma_attn", 1, d, KIND_NORM), (f"layer{l}.ln_beta_attn", 1, d, KIND_NORM),
-                (f"layer{l}.W_ff1", d, F, KIND_PROJECTION), (f"layer{l}.b_ff1", 1, F, KIND_BIAS),
-                (f"layer{l}.W_ff2", F, d, KIND_PROJECTION), (f"layer{l}.b_ff2", 1, d, KIND_BIAS),
-                (f"layer{l}.ln_gamma_ffn", 1, d, KIND_NORM), (f"layer{l}.ln_beta_ffn", 1, d, KIND_NORM)]
+                (f"layer{l}.ln_gamma_attn", 1, d, KIND_NORM)]
+        if not f & RMSNORM:
+            out.append((f"layer{l}.ln_beta_attn", 1, d, KIND_NORM))
+        out += [(f"layer{l}.W_ff1", d, F, KIND_PROJECTION), (f"layer{l}.b_ff1", 1, F, KIND_BIAS)]
+        if f & SWIGLU:
+            out += [(f"layer{l}.W_ff_gate", d, F, KIND_PROJECTION), (f"layer{l}.b_ff_gate", 1, F, KIND_BIAS)]
+        out += [(f"layer{l}.W_ff2", F, d, KIND_PROJECTION), (f"layer{l}.b_ff2", 1, d, KIND_BIAS),
+                (f"layer{l}.ln_gamma_ffn", 1, d, KIND_NORM)]
+        if not f & RMSNORM:
+            out.append((f"layer{l}.ln_beta_ffn", 1, d, KIND_NORM))
     return out
 
 

@@ -69,6 +69,7 @@ class Oracle:
         _sig(L, "or_positional_encoding_at", None, P, SZ, SZ)
         _sig(L, "or_model_param_count", SZ, SZ, SZ, SZ)
         _sig(L, "or_model_create", P, SZ, SZ, SZ, SZ, SZ, P)
+        _sig(L, "or_model_create_arch", P, SZ, SZ, SZ, SZ, SZ, U32, P)
         _sig(L, "or_model_free", None, P)
         _sig(L, "or_cache_create", P, P, SZ)
         _sig(L, "or_cache_reset", None, P)
@@ -138,8 +139,9 @@ class Oracle:
 
     # --- model
     def model(self, spec, params):
-        h = self.L.or_model_create(spec.vocab, spec.dim, spec.heads, spec.layers, spec.max_seq,
-                                   _ptr(np.ascontiguousarray(params, np.float32)))
+        h = self.L.or_model_create_arch(spec.vocab, spec.dim, spec.heads, spec.layers, spec.max_seq,
+                                        getattr(spec, "architecture_flags", 0),
+                                        _ptr(np.ascontiguousarray(params, np.float32)))
         assert h
         return OracleModel(self, spec, h)
 
@@ -230,6 +232,7 @@ class RefHarness:
         _sig(L, "dranzer_rng_unit", F64, P)
         _sig(L, "rh_fill_gaussian", None, P, P, SZ, F64)
         _sig(L, "rh_build_bundle", I32, ctypes.c_char_p, SZ, SZ, SZ, SZ, SZ, U64, I32, I32)
+        _sig(L, "rh_build_bundle_arch", I32, ctypes.c_char_p, SZ, SZ, SZ, SZ, SZ, U64, I32, I32, U32)
         _sig(L, "rh_load", P, ctypes.c_char_p)
         _sig(L, "rh_free", None, P)
         _sig(L, "rh_reset", None, P)

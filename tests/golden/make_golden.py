@@ -166,9 +166,9 @@ def units_for(seeds, n_new):
 
 
 def gen_model(name, vocab, dim, heads, layers, max_seq, wseed, bits, prompt_seed, n_seq, plen,
-              n_new, strategy, temperature, top_k, top_p, seeds, logits_seqs, prompt_logits=True):
+              n_new, strategy, temperature, top_k, top_p, seeds, logits_seqs, prompt_logits=True, flags=0):
     path = f"/tmp/dz_golden_{name}.bin"
-    rc = L.rh_build_bundle(path.encode(), vocab, dim, heads, layers, max_seq, wseed, bits, 2)
+    rc = L.rh_build_bundle_arch(path.encode(), vocab, dim, heads, layers, max_seq, wseed, bits, 2, flags)
     assert rc == 0, rc
     h = L.rh_load(path.encode())
     st = np.array([rng_stream(prompt_seed, STREAM_TESTING)], np.uint64)
@@ -196,6 +196,7 @@ def gen_model(name, vocab, dim, heads, layers, max_seq, wseed, bits, prompt_seed
     os.remove(path)
     np.savez_compressed(os.path.join(HERE, f"{name}.npz"),
                         spec=np.array([vocab, dim, heads, layers, max_seq, wseed, bits], np.int64),
+                        architecture_flags=np.array([flags], np.int64),
                         prompts=prompts, tokens=toks, logits=lg[:logits_seqs], margins=margins,
                         prompt_logits=pl, bundle_fnv=np.array([fnv(blob)], np.uint64),
                         bundle_size=np.array([blob.size], np.int64),
@@ -312,8 +313,18 @@ def gen_controls():
     np.savez_compressed(os.path.join(HERE, "controls.npz"), **out)
 
 
+def gen_arch():
+    # the architecture bits (src/include/core/model_types.h:26-36) on the
+    # reference's own forward: tied + RoPE + RMSNorm + SwiGLU; GELU; RoPE +
+    # RMSNorm with ring eviction (capacity 32, 24 + 24 tokens, positions past
+    # max_seq_len); greedy and top-k
+    gen_model("arch23", 512, 128, 4, 2, 64, 31, 8, 5, 3, 12, 20, GREEDY, 0.0, 0, 0.0, None, 3, flags=23)
+    gen_model("arch8", 512, 128, 4, 2, 64, 32, 4, 6, 3, 12, 20, TOPK, 0.8, 8, 0.0, [80, 81, 82], 3, flags=8)
+    gen_model("arch6", 400, 64, 2, 2, 32, 33, 8, 7, 2, 24, 24, TOPK, 0.8, 5, 0.0, [90, 91], 2, flags=6)
+
+
 GENERATORS = {"rng": gen_rng, "quant": gen_quant, "qmm": gen_qmm, "pe": gen_pe, "bundle": gen_bundle_small,
-              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "controls": gen_controls, "c4": gen_c4}
+              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "controls": gen_controls, "arch": gen_arch, "c4": gen_c4}
 
 if __name__ == "__main__":
     # no argument: every fixture except the config-4 sample (minutes of CPU)

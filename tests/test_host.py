@@ -84,12 +84,14 @@ def _flat_params(oracle, spec, seed):
     return np.concatenate([t.ravel() for t in synth_params(oracle, spec, seed)])
 
 
-@pytest.mark.parametrize("name", ["c1", "c2", "ring"])
+@pytest.mark.parametrize("name", ["c1", "c2", "ring", "arch23", "arch8", "arch6"])
 def test_bundle_writer_byte_identical(dz, oracle, tmp_path, name):
-    """dz_bundle_save_quantized writes the reference writer's exact bytes."""
+    """dz_bundle_save_quantized writes the reference writer's exact bytes (v2,
+    and v3 with the architecture bits for archNN)."""
     g = golden(f"{name}.npz")
     V, d, H, L, T, wseed, bits = (int(x) for x in g["spec"])
-    spec = Spec(V, d, H, L, T)
+    flags = int(g["architecture_flags"][0]) if "architecture_flags" in g.files else 0
+    spec = Spec(V, d, H, L, T, flags)
     params = _flat_params(oracle, spec, wseed)
     path = str(tmp_path / "b.bin")
     dz.save_quantized_bundle(path, spec, params, bits, dz.GRAN_COLUMN, train_window=T, seed=wseed)
@@ -151,10 +153,17 @@ def test_loader_rejects_corruption(dz, tmp_path):
     assert opened(code) in (-3, -4)
 
 
-def test_model_layout_matches_reference_inventory(dz):
-    spec = Spec(512, 128, 4, 4, 64)
+@pytest.mark.parametrize("flags", [0, 1, 4, 16, 23, 8, 22])
+def test_model_layout_matches_reference_inventory(dz, flags):
+    spec = Spec(512, 128, 4, 4, 64, flags)
     lay = dz.model_tensor_layout(spec)
     assert lay == [(k, r, c) for (_, r, c, k) in inventory(spec)]
+
+
+def test_layout_rejects_unsupported_architectures(dz):
+    # unknown bits, and GELU with SwiGLU (src/core/bundle.c:142-144)
+    for flags in (32, 8 | 16):
+        assert dz.model_tensor_layout(Spec(512, 128, 4, 1, 64, flags)) == []
 
 
 @pytest.mark.parametrize("bits", [8, 4, 3])

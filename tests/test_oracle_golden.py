@@ -115,11 +115,14 @@ def test_positional_encoding_golden(oracle):
     assert np.abs(pe - ref).max() <= 1.2e-7
 
 
-@pytest.mark.parametrize("name", ["c1", "c2", "ring"])
+@pytest.mark.parametrize("name", ["c1", "c2", "ring", "arch23", "arch8", "arch6"])
 def test_model_generation_golden(oracle, name):
+    """The oracle's forward and generation loop against the reference's
+    (archNN: the architecture bits NN, src/include/core/model_types.h:26-36)."""
     g = golden(f"{name}.npz")
     V, d, H, L, T, wseed, bits = (int(x) for x in g["spec"])
-    spec = Spec(V, d, H, L, T)
+    flags = int(g["architecture_flags"][0]) if "architecture_flags" in g.files else 0
+    spec = Spec(V, d, H, L, T, flags)
     recs, flat = quantize_params(oracle, spec, synth_params(oracle, spec, wseed), bits)
     m = oracle.model(spec, flat)
     strategy, top_k = (int(x) for x in g["sampling"])
