@@ -1584,11 +1584,7 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
         const size_t ss = seq_smem_for(m, c->cap);
         if (ss <= (size_t)SEQ_SMEM_LIMIT) {
             // the attribute is an upper bound shared by every cache: raise it to the limit
-            cudaError_t e = m->seq_bits == 8
-                ? cudaFuncSetAttribute(dz_seqgen_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SEQ_SMEM_LIMIT)
-                : cudaFuncSetAttribute(dz_seqgen_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SEQ_SMEM_LIMIT);
+            cudaError_t e = dz_seqgen_set_smem(m->seq_bits, SEQ_SMEM_LIMIT);
             if (e != cudaSuccess) rc = fail(DZ_E_DEVICE, "fused kernel shared memory: %s", cudaGetErrorString(e));
         }
     }
@@ -1718,7 +1714,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         launches++;
         QmvEpilogue e1 = plain_epilogue(L.w1, c->ff, F);
         e1.bias = L.b1;
-        e1.relu = 1;
+        e1.act = DZ_ACT_RELU;
         launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st, c->xs_scratch, c->status);
         QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
         if (m->tp_rank == 0) {   // bias and residual once, before the sum over ranks
@@ -1953,8 +1949,7 @@ static int launch_seqgen(dz_cuda_cache_t* c, const uint32_t* prompts, size_t ple
     ProfScope prof(DZ_KERNEL_SEQGEN, (double)m->step_bytes * c->B * ((double)plen + (double)n_new - 1.0), 0,
                    c->stream);
     // the dynamic shared-memory attribute was raised at cache creation (outside any capture)
-    if (m->seq_bits == 8) dz_seqgen_kernel<8><<<c->B, SEQ_THREADS, smem, c->stream>>>(p);
-    else dz_seqgen_kernel<4><<<c->B, SEQ_THREADS, smem, c->stream>>>(p);
+    (void)dz_seqgen_launch(p, m->seq_bits, c->B, smem, c->stream);
     return 1;
 }
 
@@ -2111,7 +2106,7 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
             launches++;
             QmvEpilogue e1 = plain_epilogue(L.w1, c->pf_ff, F);
             e1.bias = L.b1;
-            e1.relu = 1;
+            e1.act = DZ_ACT_RELU;
             launches += launch_qmv(L.w1, c->pf_attn_norm, D, R, e1, st, c->pf_scratch, c->status);
             QmvEpilogue e2 = plain_epilogue(L.w2, c->pf_ff_raw, D);
             if (m->tp_rank == 0) {

@@ -193,7 +193,7 @@ __device__ __forceinline__ int dz_ilogb(float v) {
 // [2^14, 2^15). Zero, inf and NaN rows take s = 0.
 __device__ __forceinline__ int dz_row_shift(float amax) {
     if (!(amax > 0.0f) || !(amax <= 3.402823466e38f)) return 0;
-    return 14 - dz_ilogb(amax);
+    return 14 - ilogbf(amax);
 }
 
 // v * 2^e, exact unless the result is subnormal (e in [-300, 300]).

@@ -17,7 +17,7 @@ struct QmvEpilogue {
     const float* bias;        // [N] or nullptr
     const float* residual;    // [M][ld_res] or nullptr, added after bias
     long long ld_res;
-    int relu;                 // apply max(0, .) last
+    int act;                  // activation applied last: DZ_ACT_NONE / RELU / GELU
     // Output column segments: columns [seg_start[i], seg_start[i+1]) go to
     // seg_ptr[i] + row*seg_ld[i] + (seg_row_off ? seg_row_off[row] : 0) + (n - seg_start[i]).
     int nseg;
@@ -26,6 +26,16 @@ struct QmvEpilogue {
     long long seg_ld[3];
     const int* seg_row_off[3];
 };
+
+// FFN activations (src/core/tensor_ops.c:17-20 gelu, src/core/transformer.c:
+// 485 relu), in the reference's operation order without contraction.
+enum { DZ_ACT_NONE = 0, DZ_ACT_RELU = 1, DZ_ACT_GELU = 2 };
+__device__ __forceinline__ float dz_act(float y, int act) {
+    if (act == DZ_ACT_RELU) return y > 0.0f ? y : 0.0f;
+    if (act == DZ_ACT_GELU)
+        return __fmul_rn(__fmul_rn(0.5f, y), __fadd_rn(1.0f, erff(__fmul_rn(y, 0.70710678118654752440f))));
+    return y;
+}
 
 __device__ __forceinline__ void dz_qmv_store_row(const QmvEpilogue& e, int M, int N, int m, int n, float acc) {
     if (m >= M || n >= N) return;
@@ -41,7 +51,7 @@ __device__ __forceinline__ void dz_qmv_store_row(const QmvEpilogue& e, int M, in
     float y = e.col_scale ? acc * e.col_scale[n] : acc;
     if (e.bias) y = y + e.bias[n];
     if (e.residual) y = y + e.residual[(long long)m * e.ld_res + n];
-    if (e.relu) y = y > 0.0f ? y : 0.0f;
+    if (e.act) y = dz_act(y, e.act);
     int s = 0;
     while (s + 1 < e.nseg && n >= e.seg_start[s + 1]) s++;
     long long off = (long long)m * e.seg_ld[s] + (n - e.seg_start[s]);

@@ -16,6 +16,10 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#ifndef DZ_KERNEL_LINKAGE
+#define DZ_KERNEL_LINKAGE
+#endif
+
 namespace dz {
 
 constexpr int SEL_THREADS = 512;
@@ -86,7 +90,7 @@ __device__ __forceinline__ float dz_key_value(uint64_t key) {
     return __uint_as_float(u);
 }
 
-__device__ void dz_bitonic_sort(uint64_t* a, int n) {  // n power of two, ascending
+static __device__ void dz_bitonic_sort(uint64_t* a, int n) {  // n power of two, ascending
     for (int size = 2; size <= n; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
             for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
@@ -122,7 +126,7 @@ __device__ __forceinline__ float dz_masked_logit(const SelectArgs& a, const SelR
 
 // One block per sequence. Dynamic shared memory: 8 * max(pow2(V), 2*TOPK) + 4*V bytes
 // (sort path) - see dz_select_smem_bytes.
-__global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
+DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
     extern __shared__ unsigned char sel_smem[];
     __shared__ uint64_t best_key[SEL_THREADS / 32];
     __shared__ uint32_t sel_result;
@@ -304,7 +308,7 @@ __global__ void __launch_bounds__(SEL_THREADS) dz_select_kernel(SelectArgs a) {
 }
 
 // Fresh loop state for every sequence of a generation.
-__global__ void dz_gen_init_kernel(uint32_t* __restrict__ state, int B) {
+DZ_KERNEL_LINKAGE __global__ void dz_gen_init_kernel(uint32_t* __restrict__ state, int B) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     uint32_t* s = state + (long long)b * DZ_GEN_WORDS;
@@ -314,7 +318,7 @@ __global__ void dz_gen_init_kernel(uint32_t* __restrict__ state, int B) {
 
 // Clears the token history of the sequences whose mask byte is set (all
 // when mask is null): grid (ceil(words / 256), B).
-__global__ void dz_seen_clear_kernel(uint32_t* __restrict__ seen, int words, const uint8_t* __restrict__ mask) {
+DZ_KERNEL_LINKAGE __global__ void dz_seen_clear_kernel(uint32_t* __restrict__ seen, int words, const uint8_t* __restrict__ mask) {
     const int b = blockIdx.y;
     const int w = blockIdx.x * blockDim.x + threadIdx.x;
     if (w < words && (!mask || mask[b])) seen[(long long)b * words + w] = 0u;
@@ -344,7 +348,7 @@ __device__ __forceinline__ uint64_t dz_splitmix64(uint64_t x) {
     return x ^ (x >> 31);
 }
 
-__global__ void dz_seed_kernel(const uint64_t* __restrict__ seeds, uint64_t* __restrict__ states, int B,
+DZ_KERNEL_LINKAGE __global__ void dz_seed_kernel(const uint64_t* __restrict__ seeds, uint64_t* __restrict__ states, int B,
                                uint64_t stream) {
     const int b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;

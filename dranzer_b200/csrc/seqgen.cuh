@@ -531,7 +531,7 @@ __device__ __forceinline__ void seq_layernorm(const float* in, float* out, const
 // are exchanged by warp shuffles, partners up to SEQ_THREADS / 2 apart through
 // a[] (two barriers per stage), the partner SEQ_THREADS away sits in the same
 // thread. Larger n go to dz_bitonic_sort.
-__device__ void seq_sort_keys(uint64_t* a, int n) {
+static __device__ void seq_sort_keys(uint64_t* a, int n) {
     if (n > 2 * SEQ_THREADS) {
         dz_bitonic_sort(a, n);
         return;
@@ -589,7 +589,7 @@ __device__ void seq_sort_keys(uint64_t* a, int n) {
 }
 
 // Selection over the logits in shared memory; returns the token on every thread.
-__device__ uint32_t seq_select(const SeqParams& p, SeqSmem& s, uint64_t* rng) {
+static __device__ uint32_t seq_select(const SeqParams& p, SeqSmem& s, uint64_t* rng) {
     const int V = p.V;
     float* lg = s.logits;
     for (int m = threadIdx.x; m < p.n_masked; m += SEQ_THREADS) {
@@ -984,5 +984,9 @@ __global__ void __launch_bounds__(SEQ_THREADS, 1) dz_seqgen_kernel(SeqParams p) 
         p.total[b] = total;
     }
 }
+
+// Host side (seqgen.cu): the dynamic shared-memory limit and one launch.
+cudaError_t dz_seqgen_set_smem(int bits, int bytes);
+cudaError_t dz_seqgen_launch(const SeqParams& p, int bits, int blocks, size_t smem, cudaStream_t st);
 
 }  // namespace dz

@@ -435,9 +435,9 @@ __device__ __forceinline__ void ug_store_tile(const UgArgs& a, const float* tile
             for (int j = 0; j < 4; j++)
                 if (j < nv) y[j] = y[j] + rp[j];
         }
-        if (e.relu) {
+        if (e.act) {
 #pragma unroll
-            for (int j = 0; j < 4; j++) y[j] = y[j] > 0.0f ? y[j] : 0.0f;
+            for (int j = 0; j < 4; j++) y[j] = dz_act(y[j], e.act);
         }
         if (one_seg) {
             long long off = (long long)row * e.seg_ld[sg] + (n - e.seg_start[sg]);
@@ -793,7 +793,7 @@ __device__ __forceinline__ void dz_qmv_store_col(const QmvEpilogue& e, int M, in
         float y = e.col_scale ? acc[m] * cs : acc[m];
         if (e.bias) y = y + bi;
         if (e.residual) y = y + res[m];
-        if (e.relu) y = y > 0.0f ? y : 0.0f;
+        if (e.act) y = dz_act(y, e.act);
         e.seg_ptr[s][(long long)m * e.seg_ld[s] + (n - e.seg_start[s]) + roff[m]] = y;
     }
 }
