@@ -402,6 +402,22 @@ class KVCache:
         check(lib().dz_cuda_prefill(self.handle, _p(ids), _p(ln), ids.shape[1], _p(out)), "prefill")
         return out
 
+    def forward_masked(self, ids, padding=None, attention=None):
+        """model_forward_masked for every sequence (dz_cuda_forward_masked):
+        ids [batch, seq_len], padding [batch, seq_len] (0 = padding) or None,
+        attention [batch, seq_len, seq_len] or None; returns the logits of each
+        sequence's last real position [batch, V]. The rings are left empty."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        assert ids.ndim == 2 and ids.shape[0] == self.batch
+        T = ids.shape[1]
+        pad = None if padding is None else np.ascontiguousarray(padding, np.uint8)
+        att = None if attention is None else np.ascontiguousarray(attention, np.uint8)
+        assert pad is None or pad.shape == (self.batch, T)
+        assert att is None or att.shape == (self.batch, T, T)
+        out = np.empty((self.batch, self.vocab), np.float32)
+        check(lib().dz_cuda_forward_masked(self.handle, _p(ids), T, _p(pad), _p(att), _p(out)), "forward_masked")
+        return out
+
     def uses_fused(self, sampling=None):
         return bool(lib().dz_cuda_cache_uses_fused(self.handle, ctypes.byref(sampling.c) if sampling else None))
 

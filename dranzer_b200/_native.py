@@ -128,6 +128,7 @@ SIGNATURES = {
     "dz_cuda_tp_unique_id": (I32, [P]),
     "dz_cuda_model_create_tp": (I32, [P, P, SZ, I32, I32, I32, P, P]),
     "dz_cuda_prefill": (I32, [P, P, P, SZ, P]),
+    "dz_cuda_forward_masked": (I32, [P, P, SZ, P, P, P]),
     "dz_cuda_cache_uses_fused": (I32, [P, P]),
     "dz_cuda_generate_ex": (I32, [P, P, SZ, SZ, P, P, P, P, P]),
     "dz_cuda_select_ex": (I32, [P, P, P, P, P]),

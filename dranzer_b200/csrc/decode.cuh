@@ -47,7 +47,9 @@ __global__ void dz_step_begin_kernel(RingState rs, const uint32_t* __restrict__ 
         rs.seen[(long long)b * rs.seen_words + (tok >> 5)] |= 1u << (tok & 31);
     const float* e = emb + (long long)tok * dim;
     float* h = hidden + (long long)b * dim;
-    if (pos < pe_rows) {
+    if (!pe) {   // rotary positions: no additive encoding (src/core/transformer.c:780-799)
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) h[i] = __fadd_rn(e[i], 0.0f);
+    } else if (pos < pe_rows) {
         const float* p = pe + pos * dim;
         for (int i = threadIdx.x; i < dim; i += blockDim.x) h[i] = e[i] + p[i];
     } else {

@@ -28,6 +28,7 @@
 #include "seqgen.cuh"
 #include "umma.cuh"
 #include "qmvi.cuh"
+#include "arch.cuh"
 
 using namespace dz;
 
@@ -986,9 +987,14 @@ extern "C" int dz_cuda_matmul_quantized(const float* A, const dz_cuda_qmatrix_t*
 
 struct DevLayer {
     bool fused_qkv = false;
-    DevQMat qkv, q, k, v, wo, w1, w2;
+    // with SwiGLU, w1 is [W_ff1 | W_ff_gate] (2F columns), or W_ff1 alone and
+    // wg the gate for ROW-granularity scales; b1 is then [b_ff1 | b_ff_gate]
+    DevQMat qkv, q, k, v, wo, w1, wg, w2;
     float *g1 = nullptr, *be1 = nullptr, *b1 = nullptr, *b2 = nullptr, *g2 = nullptr, *be2 = nullptr;
 };
+
+// Architecture bits (src/include/core/model_types.h:26-36).
+enum : uint32_t { ARCH_TIED = 1, ARCH_ROPE = 2, ARCH_RMSNORM = 4, ARCH_GELU = 8, ARCH_SWIGLU = 16 };
 
 struct dz_cuda_model {
     int device = 0;
@@ -999,7 +1005,11 @@ struct dz_cuda_model {
     float* pe = nullptr;
     long long pe_rows = 0;
     std::vector<DevLayer> layers;
-    DevQMat head;
+    DevQMat head;                 // empty with tied embeddings (the head is emb^T, fp32)
+    uint32_t flags = 0;
+    bool tied = false, rope = false, rms = false, swiglu = false;
+    int act = DZ_ACT_RELU;        // FFN activation (without SwiGLU)
+    float* rope_tab = nullptr;    // [pe_rows][hd / 2][cos, sin]
     size_t step_bytes = 0;
     std::vector<void*> f32_allocs;
     // fused one-CTA-per-sequence generation (seqgen.cuh), when the model fits it
@@ -1047,7 +1057,7 @@ static void model_release(dz_cuda_model_t* m) {
     if (m->comm && nccl_api()) nccl_api()->comm_destroy(m->comm);
     for (auto& L : m->layers) {
         free_qmat(L.qkv); free_qmat(L.q); free_qmat(L.k); free_qmat(L.v);
-        free_qmat(L.wo); free_qmat(L.w1); free_qmat(L.w2);
+        free_qmat(L.wo); free_qmat(L.w1); free_qmat(L.wg); free_qmat(L.w2);
     }
     free_qmat(m->head);
     for (void* p : m->f32_allocs) cudaFree(p);
@@ -1135,6 +1145,7 @@ static size_t seq_smem_for(const dz_cuda_model_t* m, int cap) {
 // layer table.
 static void prepare_seqgen(dz_cuda_model_t* m) {
     m->seq_ok = false;
+    if (m->flags) return;   // the fused kernel runs the default architecture
     if (m->layers.empty() || m->desc.embedding_dim % 4 != 0) return;  // 16-byte aligned activations
     // the fused attention keeps a head's output in four registers per lane
     if (m->desc.num_heads == 0 || m->desc.embedding_dim / m->desc.num_heads > 128) return;
@@ -1261,12 +1272,14 @@ static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tens
     if (!out) return fail(DZ_E_INVALID, "null output handle");
     *out = nullptr;
     if (!desc || !tensors) return fail(DZ_E_INVALID, "null argument");
-    if (desc->architecture_flags != 0)
-        return fail(DZ_E_UNSUPPORTED, "architecture flags 0x%x not supported on the device path",
-                    desc->architecture_flags);
+    const uint32_t flags = desc->architecture_flags;
     const size_t D = desc->embedding_dim, V = desc->vocab_size, H = desc->num_heads, F = 4 * D;
     if (D == 0 || H == 0 || D % H || V == 0 || desc->num_layers == 0 || desc->max_seq_len == 0)
         return fail(DZ_E_INVALID, "bad model shape");
+    if (flags && tp_world > 1)
+        return fail(DZ_E_UNSUPPORTED, "tensor parallelism runs the default architecture only (flags 0x%x)", flags);
+    if ((flags & ARCH_ROPE) && ((D / H) % 2))
+        return fail(DZ_E_INVALID, "RoPE needs an even head dimension");
     if (n != dz_model_tensor_layout(desc, nullptr, 0))
         return fail(DZ_E_INVALID, "tensor count %zu does not match the model", n);
     std::vector<dz_tensor_blob_t> lay(n);
@@ -1290,6 +1303,12 @@ static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tens
     m->Hl = (int)(H / tp_world);
     m->dl = (int)(D / tp_world);
     m->Fl = (int)(F / tp_world);
+    m->flags = flags;
+    m->tied = (flags & ARCH_TIED) != 0;
+    m->rope = (flags & ARCH_ROPE) != 0;
+    m->rms = (flags & ARCH_RMSNORM) != 0;
+    m->swiglu = (flags & ARCH_SWIGLU) != 0;
+    m->act = (flags & ARCH_GELU) ? DZ_ACT_GELU : DZ_ACT_RELU;
     cudaStream_t st;
     if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) {
         delete m;
@@ -1298,17 +1317,26 @@ static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tens
     int rc = DZ_OK;
     size_t step = 0;
     do {
+        // tensors in model_param_tensors order for the architecture bits
+        // (src/core/model_params.c:39-103)
         const dz_tensor_blob_t* t = tensors;
-        if ((rc = upload_f32(m, t[0], V * D, &m->emb, st))) break;
-        if ((rc = make_qmat({&t[1]}, st, &m->head))) break;
-        if ((rc = upload_f32(m, t[2], V, &m->out_bias, st))) break;
-        step += m->head.code_bytes + m->head.scale_bytes + V * 4 + D * 4;
+        size_t ti = 0;
+        if ((rc = upload_f32(m, t[ti++], V * D, &m->emb, st))) break;
+        if (!m->tied && (rc = make_qmat({&t[ti++]}, st, &m->head))) break;
+        if ((rc = upload_f32(m, t[ti++], V, &m->out_bias, st))) break;
+        step += (m->tied ? V * D * 4 : m->head.code_bytes + m->head.scale_bytes) + V * 4 + D * 4;
         m->layers.resize(desc->num_layers);
-        size_t ti = 3;
-        for (size_t l = 0; l < desc->num_layers && !rc; l++, ti += 12) {
+        for (size_t l = 0; l < desc->num_layers && !rc; l++) {
             DevLayer& L = m->layers[l];
-            const dz_tensor_blob_t *tq = &t[ti], *tk = &t[ti + 1], *tv = &t[ti + 2];
-            const dz_tensor_blob_t *two = &t[ti + 3], *tw1 = &t[ti + 6], *tw2 = &t[ti + 8];
+            const dz_tensor_blob_t *tq = &t[ti], *tk = &t[ti + 1], *tv = &t[ti + 2], *two = &t[ti + 3];
+            ti += 4;
+            const dz_tensor_blob_t* tg1 = &t[ti++];
+            const dz_tensor_blob_t* tbe1 = m->rms ? nullptr : &t[ti++];
+            const dz_tensor_blob_t *tw1 = &t[ti++], *tb1 = &t[ti++];
+            const dz_tensor_blob_t* twg = m->swiglu ? &t[ti++] : nullptr;
+            const dz_tensor_blob_t* tbg = m->swiglu ? &t[ti++] : nullptr;
+            const dz_tensor_blob_t *tw2 = &t[ti++], *tb2 = &t[ti++], *tg2 = &t[ti++];
+            const dz_tensor_blob_t* tbe2 = m->rms ? nullptr : &t[ti++];
             SliceBlob sq, sk, sv, swo, sw1, sw2;
             if (tp_world > 1) {
                 // this rank's heads (columns of Q, K, V; rows of W_o) and FFN columns (W1) / rows (W2)
@@ -1331,17 +1359,39 @@ static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tens
                 step += 3 * (L.q.code_bytes + L.q.scale_bytes);
             }
             if ((rc = make_qmat({two}, st, &L.wo))) break;
-            if ((rc = upload_f32(m, t[ti + 4], D, &L.g1, st)) || (rc = upload_f32(m, t[ti + 5], D, &L.be1, st)))
+            if ((rc = upload_f32(m, *tg1, D, &L.g1, st)) || (tbe1 && (rc = upload_f32(m, *tbe1, D, &L.be1, st))))
                 break;
-            if ((rc = make_qmat({tw1}, st, &L.w1))) break;
-            if ((rc = upload_f32(m, t[ti + 7], F, &L.b1, st))) break;
-            if (tp_world > 1) L.b1 += (size_t)tp_rank * m->Fl;   // this rank's FFN columns
+            if (m->swiglu) {
+                // one 2F-column product [x W_ff1 + b_ff1 | x W_ff_gate + b_ff_gate]
+                // (two for ROW-granularity scales, which two matrices cannot share)
+                if (tw1->granularity == DZ_GRAN_ROW) {
+                    if ((rc = make_qmat({tw1}, st, &L.w1)) || (rc = make_qmat({twg}, st, &L.wg))) break;
+                } else if ((rc = make_qmat({tw1, twg}, st, &L.w1))) {
+                    break;
+                }
+                if (tb1->bits != 0 || tbg->bits != 0 || !tb1->f32 || !tbg->f32 || tb1->rows * tb1->cols != F ||
+                    tbg->rows * tbg->cols != F) {
+                    rc = fail(DZ_E_UNSUPPORTED, "FFN biases expected as float32");
+                    break;
+                }
+                float* d = nullptr;
+                if (cudaMalloc(&d, 2 * F * 4) != cudaSuccess) { rc = fail(DZ_E_NOMEM, "bias"); break; }
+                m->f32_allocs.push_back(d);
+                cudaMemcpyAsync(d, tb1->f32, F * 4, cudaMemcpyHostToDevice, st);
+                cudaMemcpyAsync(d + F, tbg->f32, F * 4, cudaMemcpyHostToDevice, st);
+                L.b1 = d;
+            } else {
+                if ((rc = make_qmat({tw1}, st, &L.w1))) break;
+                if ((rc = upload_f32(m, *tb1, F, &L.b1, st))) break;
+                if (tp_world > 1) L.b1 += (size_t)tp_rank * m->Fl;   // this rank's FFN columns
+            }
             if ((rc = make_qmat({tw2}, st, &L.w2))) break;
-            if ((rc = upload_f32(m, t[ti + 9], D, &L.b2, st)) || (rc = upload_f32(m, t[ti + 10], D, &L.g2, st)) ||
-                (rc = upload_f32(m, t[ti + 11], D, &L.be2, st)))
+            if ((rc = upload_f32(m, *tb2, D, &L.b2, st)) || (rc = upload_f32(m, *tg2, D, &L.g2, st)) ||
+                (tbe2 && (rc = upload_f32(m, *tbe2, D, &L.be2, st))))
                 break;
-            step += L.wo.code_bytes + L.wo.scale_bytes + L.w1.code_bytes + L.w1.scale_bytes + L.w2.code_bytes +
-                    L.w2.scale_bytes + (6 * D + F) * 4;
+            step += L.wo.code_bytes + L.wo.scale_bytes + L.w1.code_bytes + L.w1.scale_bytes + L.wg.code_bytes +
+                    L.wg.scale_bytes + L.w2.code_bytes +
+                    L.w2.scale_bytes + ((m->rms ? 4 : 6) * D + (m->swiglu ? 2 : 1) * F) * 4;
         }
         if (rc) break;
         // sinusoid table for positions [0, max_seq_len + 4096), computed on the
@@ -1357,6 +1407,28 @@ static int build_model(const dz_model_desc_t* desc, const dz_tensor_blob_t* tens
             cudaStreamSynchronize(st) != cudaSuccess) {
             rc = fail(DZ_E_DEVICE, "pe upload");
             break;
+        }
+        if (m->rope) {
+            // cos / sin of position * 10000^(-2p / head_dim) for the same
+            // positions, in double as rope_rotate computes them
+            // (src/core/transformer.c:33-38), rounded to float
+            const size_t hd = D / H, half = hd / 2;
+            std::vector<float> rt((size_t)m->pe_rows * half * 2);
+            for (size_t pos = 0; pos < (size_t)m->pe_rows; pos++)
+                for (size_t pp = 0; pp < half; pp++) {
+                    const double angle = (double)pos * pow(10000.0, -(double)(2 * pp) / (double)hd);
+                    rt[(pos * half + pp) * 2] = (float)cos(angle);
+                    rt[(pos * half + pp) * 2 + 1] = (float)sin(angle);
+                }
+            float* drt = nullptr;
+            if (cudaMalloc(&drt, rt.size() * 4) != cudaSuccess) { rc = fail(DZ_E_NOMEM, "rope table"); break; }
+            m->f32_allocs.push_back(drt);
+            m->rope_tab = drt;
+            if (cudaMemcpyAsync(drt, rt.data(), rt.size() * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                cudaStreamSynchronize(st) != cudaSuccess) {
+                rc = fail(DZ_E_DEVICE, "rope table upload");
+                break;
+            }
         }
     } while (0);
     cudaStreamSynchronize(st);
@@ -1461,13 +1533,17 @@ struct dz_cuda_cache {
     uint32_t* pf_ids = nullptr;   // dz_cuda_prefill's device copies
     int* pf_lens = nullptr;
     size_t pf_ids_cap = 0;
+    uint8_t* mk_buf = nullptr;    // dz_cuda_forward_masked's padding + attention masks
+    size_t mk_cap = 0;
 };
 
 static void free_prefill(dz_cuda_cache_t* c) {
     for (void* p : {(void*)c->pf_hidden, (void*)c->pf_q, (void*)c->pf_concat, (void*)c->pf_attn_raw,
                     (void*)c->pf_attn_norm, (void*)c->pf_ff, (void*)c->pf_ff_raw, (void*)c->pf_rowoff,
-                    c->pf_scratch, (void*)c->pf_ids, (void*)c->pf_lens})
+                    c->pf_scratch, (void*)c->pf_ids, (void*)c->pf_lens, (void*)c->mk_buf})
         cudaFree(p);
+    c->mk_buf = nullptr;
+    c->mk_cap = 0;
     c->pf_hidden = c->pf_q = c->pf_concat = c->pf_attn_raw = c->pf_attn_norm = c->pf_ff = c->pf_ff_raw = nullptr;
     c->pf_rowoff = nullptr;
     c->pf_scratch = nullptr;
@@ -1547,7 +1623,7 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     if (!rc) rc = cache_alloc(c, (void**)&c->concat, B * dl * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->attn_raw, B * D * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->attn_norm, B * D * 4);
-    if (!rc) rc = cache_alloc(c, (void**)&c->ff, B * Fl * 4);
+    if (!rc) rc = cache_alloc(c, (void**)&c->ff, B * Fl * (m->swiglu ? 2 : 1) * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->ff_raw, B * D * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->logits, B * V * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->tok, B * 4);
@@ -1561,9 +1637,9 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     if (!rc) {
         size_t xs = 0;
         for (const auto& L : m->layers)
-            for (const DevQMat* q : {&L.qkv, &L.q, &L.k, &L.v, &L.wo, &L.w1, &L.w2})
+            for (const DevQMat* q : {&L.qkv, &L.q, &L.k, &L.v, &L.wo, &L.w1, &L.wg, &L.w2})
                 if (q->codes) xs = std::max(xs, qmv_scratch_bytes(*q, (int)B));
-        xs = std::max(xs, qmv_scratch_bytes(m->head, (int)B));
+        if (m->head.codes) xs = std::max(xs, qmv_scratch_bytes(m->head, (int)B));
         rc = cache_alloc(c, (void**)&c->xs_scratch, xs);
         if (!rc && cudaMemset(c->xs_scratch, 0, xs) != cudaSuccess) rc = fail(DZ_E_DEVICE, "scratch memset");
     }
@@ -1650,6 +1726,62 @@ static void tp_allreduce(dz_cuda_model_t* m, float* buf, size_t count, cudaStrea
     if (m->tp_world > 1) nccl_api()->all_reduce(buf, buf, count, ncclFloat32, ncclSum, m->comm, st);
 }
 
+// Launches of one layer pass over R rows and of the output head.
+static int layer_launches(const dz_cuda_model_t* m, const DevLayer& L, int R) {
+    int n = L.fused_qkv ? qmv_launches(L.qkv, R) : qmv_launches(L.q, R) + qmv_launches(L.k, R) + qmv_launches(L.v, R);
+    n += qmv_launches(L.wo, R) + qmv_launches(L.w1, R) + qmv_launches(L.w2, R);
+    if (L.wg.codes) n += qmv_launches(L.wg, R);
+    return n + 3 + (m->rope ? 1 : 0) + (m->swiglu ? 1 : 0);   // attention, two norms, RoPE, SwiGLU
+}
+static int head_launches(const dz_cuda_model_t* m, int B) { return m->tied ? 1 : qmv_launches(m->head, B); }
+
+// The attention-out and FFN-out norms: LayerNorm (src/core/tensor_ops.c:
+// 148-171) or RMSNorm (:173-179), eps 1e-6, `res` added to x first.
+static void launch_norm(const dz_cuda_model_t* m, const float* x, const float* res, const float* g, const float* be,
+                        float* y, int rows, int D, cudaStream_t st) {
+    if (m->rms)
+        dz_rmsnorm_kernel<<<rows, RMS_THREADS, 0, st>>>(x, res, g, y, D, 1e-6f);
+    else
+        dz_layernorm_kernel<<<rows, LN_THREADS, 0, st>>>(x, res, g, be, y, D, 1e-6f);
+}
+
+// FFN up-projection of R rows of x into ff (row stride ldf): bias and ReLU /
+// GELU in the product's epilogue, or both SwiGLU halves then the gate
+// (src/core/transformer.c:819-832). Returns the launches.
+static int launch_ffn_up(const dz_cuda_model_t* m, const DevLayer& L, const float* x, int D, int R, float* ff,
+                         long long ldf, int F, cudaStream_t st, void* scratch, int* status) {
+    QmvEpilogue e1 = plain_epilogue(L.w1, ff, ldf);
+    e1.bias = L.b1;
+    e1.act = m->swiglu ? DZ_ACT_NONE : m->act;
+    int n = launch_qmv(L.w1, x, D, R, e1, st, scratch, status);
+    if (L.wg.codes) {
+        QmvEpilogue eg = plain_epilogue(L.wg, ff + F, ldf);
+        eg.bias = L.b1 + F;
+        n += launch_qmv(L.wg, x, D, R, eg, st, scratch, status);
+    }
+    if (m->swiglu) {
+        dz_swiglu_kernel<<<dim3((unsigned)((F + 255) / 256), (unsigned)std::min(R, 65535)), 256, 0, st>>>(ff, R, F,
+                                                                                                        ldf);
+        n++;
+    }
+    return n;
+}
+
+// Output head over B hidden rows into c->logits: the quantized W_out, or the
+// token embeddings transposed when tied (src/core/lm_head.c:21-46).
+static int launch_head(dz_cuda_cache_t* c, cudaStream_t st) {
+    dz_cuda_model_t* m = c->model;
+    const int D = (int)m->desc.embedding_dim, V = (int)m->desc.vocab_size, B = c->B;
+    if (m->tied) {
+        dz_tied_head_kernel<<<(V + TIED_ROWS - 1) / TIED_ROWS, TIED_ROWS * 32, 0, st>>>(c->hidden, B, m->emb,
+                                                                                       m->out_bias, c->logits, V, D);
+        return 1;
+    }
+    QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
+    eh.bias = m->out_bias;
+    return launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status);
+}
+
 static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long tok_stride) {
     dz_cuda_model_t* m = c->model;
     const int D = (int)m->desc.embedding_dim, V = (int)m->desc.vocab_size;
@@ -1660,8 +1792,8 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
     RingState rs{c->start, c->length, c->total, c->slot, c->ctx, c->row_off, c->seen, c->seen_words};
     {
         ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)B * D * 12, 0, st);
-        dz_step_begin_kernel<<<B, 128, 0, st>>>(rs, tokens, tok_stride, m->emb, m->pe, m->pe_rows, c->hidden, D,
-                                                dl, V, cap);
+        dz_step_begin_kernel<<<B, 128, 0, st>>>(rs, tokens, tok_stride, m->emb, m->rope ? nullptr : m->pe,
+                                                m->pe_rows, c->hidden, D, dl, V, cap);
     }
     launches++;
     const size_t att_smem = (size_t)(cap + hd + ATT_THREADS) * 4;
@@ -1686,6 +1818,11 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             ev.seg_row_off[0] = c->row_off;
             launches += launch_qmv(L.v, c->hidden, D, B, ev, st, c->xs_scratch, c->status);
         }
+        if (m->rope) {
+            dz_rope_decode_kernel<<<B, 128, 0, st>>>(c->q, Kl, (long long)cap * dl, c->row_off, c->total, dl, hd,
+                                                     m->rope_tab, m->pe_rows);
+            launches++;
+        }
         {
             // bytes: the K and V rows of every sequence's context (ctx <= cap; the
             // exact per-step context is device state, so the capacity bound is used
@@ -1708,31 +1845,26 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         tp_allreduce(m, c->attn_raw, (size_t)B * D, st);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D, 0, st);
-            dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, D,
-                                                          1e-6f);
+            launch_norm(m, c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, B, D, st);
         }
         launches++;
-        QmvEpilogue e1 = plain_epilogue(L.w1, c->ff, F);
-        e1.bias = L.b1;
-        e1.act = DZ_ACT_RELU;
-        launches += launch_qmv(L.w1, c->attn_norm, D, B, e1, st, c->xs_scratch, c->status);
+        const long long ldf = m->swiglu ? 2LL * F : F;
+        launches += launch_ffn_up(m, L, c->attn_norm, D, B, c->ff, ldf, F, st, c->xs_scratch, c->status);
         QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
         if (m->tp_rank == 0) {   // bias and residual once, before the sum over ranks
             e2.bias = L.b2;
             e2.residual = c->attn_norm;
             e2.ld_res = D;
         }
-        launches += launch_qmv(L.w2, c->ff, F, B, e2, st, c->xs_scratch, c->status);
+        launches += launch_qmv(L.w2, c->ff, ldf, B, e2, st, c->xs_scratch, c->status);
         tp_allreduce(m, c->ff_raw, (size_t)B * D, st);
         {
             ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D, 0, st);
-            dz_layernorm_kernel<<<B, LN_THREADS, 0, st>>>(c->ff_raw, nullptr, L.g2, L.be2, c->hidden, D, 1e-6f);
+            launch_norm(m, c->ff_raw, nullptr, L.g2, L.be2, c->hidden, B, D, st);
         }
         launches++;
     }
-    QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
-    eh.bias = m->out_bias;
-    launches += launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status);
+    launches += launch_head(c, st);
     return launches;
 }
 
@@ -1993,11 +2125,11 @@ static int ensure_prefill(dz_cuda_cache_t* c, size_t T) {
     auto al = [&](void** p, size_t bytes) { return cudaMalloc(p, bytes) == cudaSuccess; };
     size_t scratch = 0;
     for (const DevLayer& L : m->layers)
-        for (const DevQMat* q : {&L.qkv, &L.q, &L.k, &L.v, &L.wo, &L.w1, &L.w2})
+        for (const DevQMat* q : {&L.qkv, &L.q, &L.k, &L.v, &L.wo, &L.w1, &L.wg, &L.w2})
             if (q->codes) scratch = std::max(scratch, qmv_scratch_bytes(*q, (int)rows));
     bool ok = al((void**)&c->pf_hidden, rows * D * 4) && al((void**)&c->pf_q, rows * D * 4) &&
               al((void**)&c->pf_concat, rows * D * 4) && al((void**)&c->pf_attn_raw, rows * D * 4) &&
-              al((void**)&c->pf_attn_norm, rows * D * 4) && al((void**)&c->pf_ff, rows * F * 4) &&
+              al((void**)&c->pf_attn_norm, rows * D * 4) && al((void**)&c->pf_ff, rows * F * (m->swiglu ? 2 : 1) * 4) &&
               al((void**)&c->pf_ff_raw, rows * D * 4) && al((void**)&c->pf_rowoff, rows * 4) &&
               al(&c->pf_scratch, scratch);
     if (!ok) {
@@ -2010,6 +2142,10 @@ static int ensure_prefill(dz_cuda_cache_t* c, size_t T) {
                                  (int)dz_prefill_att_smem(128)));
     DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)dz_prefill_att_smem(64)));
+    DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)dz_prefill_att_smem(128)));
+    DZ_CUDA(cudaFuncSetAttribute(dz_attention_prefill_kernel<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)dz_prefill_att_smem(64)));
     return DZ_OK;
 }
 
@@ -2017,24 +2153,34 @@ static int ensure_prefill(dz_cuda_cache_t* c, size_t T) {
 static size_t prefill_launches(const dz_cuda_cache_t* c, size_t T) {
     const dz_cuda_model_t* m = c->model;
     const size_t S = prefill_group(c, T), groups = ((size_t)c->B + S - 1) / S;
-    size_t n = 2 + (size_t)qmv_launches(m->head, c->B);   // row offsets, ring state, head
+    size_t n = 2 + (size_t)head_launches(m, c->B);   // row offsets, ring state, head
     for (size_t g = 0; g < groups; g++) {
         const int R = (int)(std::min((size_t)c->B, (g + 1) * S) - g * S) * (int)T;
         n += 2;   // embedding, gather
-        for (const auto& L : m->layers) {
-            n += L.fused_qkv ? qmv_launches(L.qkv, R)
-                             : qmv_launches(L.q, R) + qmv_launches(L.k, R) + qmv_launches(L.v, R);
-            n += qmv_launches(L.wo, R) + qmv_launches(L.w1, R) + qmv_launches(L.w2, R) + 3;   // attention, 2 LN
-        }
+        for (const auto& L : m->layers) n += layer_launches(m, L, R);
     }
     return n;
 }
 
+// The masked full-prefix forward (model_forward_masked, src/core/
+// transformer.c:527-576) on the prefill kernels: device copies of the padding
+// mask [B][T] and attention mask [B][T][T] (either null) and each sequence's
+// last real position + 1 [B].
+struct PrefillMask {
+    const uint8_t* pad = nullptr;
+    const uint8_t* att = nullptr;
+    const int* last = nullptr;
+};
+
 // Prefill of T positions of every sequence (ids_dev [B][ld], lens_dev [B]
 // positions per sequence or null for all T) into empty rings: all positions
 // of a group of sequences per layer pass, then the head on each sequence's
-// last position into c->logits. Returns the launches.
-static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long long ld, int T, const int* lens_dev) {
+// last position into c->logits. With `mk`, the masked forward instead: padded
+// rows zeroed after the embedding and after each norm (model_forward_hidden_
+// masked, :392-519), the masked attention, the head on the last real
+// position, and the rings left for the caller to reset. Returns the launches.
+static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long long ld, int T, const int* lens_dev,
+                           const PrefillMask* mk = nullptr) {
     dz_cuda_model_t* m = c->model;
     const int D = (int)m->desc.embedding_dim, V = (int)m->desc.vocab_size;
     const int H = m->Hl, dl = m->dl, F = m->Fl;   // this rank's heads, attention width, FFN width
@@ -2050,13 +2196,22 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
     for (int s0 = 0; s0 < B; s0 += S) {
         const int ns = std::min(S, B - s0), R = ns * T;
         const int* lens = lens_dev ? lens_dev + s0 : nullptr;
+        const uint8_t* pad = (mk && mk->pad) ? mk->pad + (long long)s0 * T : nullptr;
+        const uint8_t* att = (mk && mk->att) ? mk->att + (long long)s0 * T * T : nullptr;
+        auto zero_padded = [&](float* x) {
+            if (!pad) return;
+            dz_zero_padded_rows_kernel<<<R, 128, 0, st>>>(x, pad, D);
+            launches++;
+        };
         {
             ProfScope prof(DZ_KERNEL_STEP_BEGIN, (double)R * D * 12, 0, st);
-            dz_prefill_embed_kernel<<<R, 128, 0, st>>>(ids_dev + (long long)s0 * ld, ld, T, m->emb, m->pe,
-                                                       m->pe_rows, c->pf_hidden, D, V, lens,
-                                                       c->seen + (long long)s0 * c->seen_words, c->seen_words);
+            dz_prefill_embed_kernel<<<R, 128, 0, st>>>(ids_dev + (long long)s0 * ld, ld, T, m->emb,
+                                                       m->rope ? nullptr : m->pe, m->pe_rows, c->pf_hidden, D, V, lens,
+                                                       mk ? nullptr : c->seen + (long long)s0 * c->seen_words,
+                                                       c->seen_words);
         }
         launches++;
+        zero_padded(c->pf_hidden);
         for (size_t l = 0; l < m->layers.size(); l++) {
             DevLayer& L = m->layers[l];
             float* Kl = c->keys + l * (size_t)B * cap * dl + (size_t)s0 * cap * dl;
@@ -2078,13 +2233,28 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
                 ev.seg_row_off[0] = c->pf_rowoff;
                 launches += launch_qmv(L.v, c->pf_hidden, D, R, ev, st, c->pf_scratch, c->status);
             }
+            if (m->rope) {
+                dz_rope_prefill_kernel<<<R, 128, 0, st>>>(c->pf_q, Kl, (long long)cap * dl, T, dl, hd, m->rope_tab,
+                                                          m->pe_rows);
+                launches++;
+            }
             {
                 const double ctx_pairs = (double)ns * H * T * (T + 1) / 2.0;
                 ProfScope prof(DZ_KERNEL_ATTENTION, 8.0 * (double)R * dl + 8.0 * (double)ns * T * dl,
                                4.0 * ctx_pairs * hd, st);
                 const dim3 grid((unsigned)((T + PF_QT - 1) / PF_QT), (unsigned)H, (unsigned)ns);
                 const size_t smem = dz_prefill_att_smem(hd);
-                if (hd == 128)
+                if (mk) {
+                    if (hd == 128)
+                        dz_attention_prefill_kernel<4, true><<<grid, PF_THREADS, smem, st>>>(
+                            c->pf_q, Kl, Vl, nullptr, c->pf_concat, T, dl, cap, pad, att);
+                    else if (hd == 64)
+                        dz_attention_prefill_kernel<2, true><<<grid, PF_THREADS, smem, st>>>(
+                            c->pf_q, Kl, Vl, nullptr, c->pf_concat, T, dl, cap, pad, att);
+                    else
+                        dz_attention_prefill_kernel<1, true><<<grid, PF_THREADS, smem, st>>>(
+                            c->pf_q, Kl, Vl, nullptr, c->pf_concat, T, dl, cap, pad, att);
+                } else if (hd == 128)
                     dz_attention_prefill_kernel<4><<<grid, PF_THREADS, smem, st>>>(c->pf_q, Kl, Vl, lens,
                                                                                   c->pf_concat, T, dl, cap);
                 else if (hd == 64)
@@ -2100,37 +2270,36 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
             tp_allreduce(m, c->pf_attn_raw, (size_t)R * D, st);
             {
                 ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * R * D + 8.0 * D, 0, st);
-                dz_layernorm_kernel<<<R, LN_THREADS, 0, st>>>(c->pf_attn_raw, c->pf_hidden, L.g1, L.be1,
-                                                              c->pf_attn_norm, D, 1e-6f);
+                launch_norm(m, c->pf_attn_raw, c->pf_hidden, L.g1, L.be1, c->pf_attn_norm, R, D, st);
             }
             launches++;
-            QmvEpilogue e1 = plain_epilogue(L.w1, c->pf_ff, F);
-            e1.bias = L.b1;
-            e1.act = DZ_ACT_RELU;
-            launches += launch_qmv(L.w1, c->pf_attn_norm, D, R, e1, st, c->pf_scratch, c->status);
+            zero_padded(c->pf_attn_norm);
+            const long long ldf = m->swiglu ? 2LL * F : F;
+            launches += launch_ffn_up(m, L, c->pf_attn_norm, D, R, c->pf_ff, ldf, F, st, c->pf_scratch, c->status);
             QmvEpilogue e2 = plain_epilogue(L.w2, c->pf_ff_raw, D);
             if (m->tp_rank == 0) {
                 e2.bias = L.b2;
                 e2.residual = c->pf_attn_norm;
                 e2.ld_res = D;
             }
-            launches += launch_qmv(L.w2, c->pf_ff, F, R, e2, st, c->pf_scratch, c->status);
+            launches += launch_qmv(L.w2, c->pf_ff, ldf, R, e2, st, c->pf_scratch, c->status);
             tp_allreduce(m, c->pf_ff_raw, (size_t)R * D, st);
             {
                 ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * R * D + 8.0 * D, 0, st);
-                dz_layernorm_kernel<<<R, LN_THREADS, 0, st>>>(c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, D,
-                                                              1e-6f);
+                launch_norm(m, c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, R, D, st);
             }
             launches++;
+            zero_padded(c->pf_hidden);
         }
-        dz_prefill_gather_kernel<<<ns, 256, 0, st>>>(c->pf_hidden, lens, T, D, c->hidden + (size_t)s0 * D);
+        dz_prefill_gather_kernel<<<ns, 256, 0, st>>>(c->pf_hidden, mk ? mk->last + s0 : lens, T, D,
+                                                     c->hidden + (size_t)s0 * D);
         launches++;
     }
-    dz_prefill_ring_kernel<<<(B + 255) / 256, 256, 0, st>>>(c->start, c->length, c->total, lens_dev, T, B);
-    launches++;
-    QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
-    eh.bias = m->out_bias;
-    launches += launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status);
+    if (!mk) {
+        dz_prefill_ring_kernel<<<(B + 255) / 256, 256, 0, st>>>(c->start, c->length, c->total, lens_dev, T, B);
+        launches++;
+    }
+    launches += launch_head(c, st);
     return launches;
 }
 
@@ -2183,12 +2352,8 @@ extern "C" size_t dz_cuda_generate_launches(const dz_cuda_cache_t* c, size_t ple
     const dz_cuda_model_t* m = c->model;
     if (use_seqgen(c, s)) return 2;
     const int B = (int)c->B;
-    size_t step = 1 + (size_t)qmv_launches(m->head, B);   // step begin, head
-    for (const auto& L : m->layers) {
-        step += L.fused_qkv ? qmv_launches(L.qkv, B)
-                            : qmv_launches(L.q, B) + qmv_launches(L.k, B) + qmv_launches(L.v, B);
-        step += qmv_launches(L.wo, B) + qmv_launches(L.w1, B) + qmv_launches(L.w2, B) + 3;   // + attention, 2 LN
-    }
+    size_t step = 1 + (size_t)head_launches(m, B);   // step begin, head
+    for (const auto& L : m->layers) step += layer_launches(m, L, B);
     const size_t seeded = (s && s->strategy != 0 && s->temperature > 0.0f) ? 1 : 0;
     const size_t prefill = use_batched_prefill(c, plen) ? prefill_launches(c, plen) : plen * step;
     return seeded + 2 + prefill + n_new + (n_new ? n_new - 1 : 0) * step;   // + ring reset, history clear
@@ -2416,6 +2581,76 @@ extern "C" int dz_cuda_prefill(dz_cuda_cache_t* c, const uint32_t* ids, const ui
     if (logits_out)
         DZ_CUDA(cudaMemcpyAsync(logits_out, c->logits, B * c->model->desc.vocab_size * 4, cudaMemcpyDeviceToHost,
                                 c->stream));
+    DZ_CUDA(cudaStreamSynchronize(c->stream));
+    return DZ_OK;
+}
+
+extern "C" int dz_cuda_forward_masked(dz_cuda_cache_t* c, const uint32_t* ids, size_t seq_len,
+                                      const uint8_t* padding_mask, const uint8_t* attention_mask,
+                                      float* logits_out) {
+    if (!c || !ids || !logits_out || seq_len == 0)
+        return fail(DZ_E_INVALID, "forward_masked: null ids or logits, or seq_len 0");
+    const dz_cuda_model_t* m = c->model;
+    if (seq_len > m->desc.max_seq_len) return fail(DZ_E_INVALID, "forward_masked: seq_len above max_seq_len");
+    if (seq_len > (size_t)c->cap) return fail(DZ_E_INVALID, "forward_masked: seq_len above the cache capacity");
+    if (!prefill_eligible(c))
+        return fail(DZ_E_UNSUPPORTED, "the masked forward needs a head dimension of 32, 64 or 128");
+    const size_t B = c->B, T = seq_len;
+    // the last real position of each sequence (model_forward_masked,
+    // src/core/transformer.c:535-545): a padding mask with none is rejected
+    std::vector<int> last(B, (int)T);
+    if (padding_mask) {
+        for (size_t b = 0; b < B; b++) {
+            int l = 0;
+            for (size_t i = 0; i < T; i++)
+                if (padding_mask[b * T + i]) l = (int)i + 1;
+            if (l == 0) return fail(DZ_E_INVALID, "forward_masked: sequence %zu has no real position", b);
+            last[b] = l;
+        }
+    }
+    DeviceGuard g(m->device);
+    int rc = ensure_prefill(c, T);
+    if (rc) return rc;
+    if (B * T > c->pf_ids_cap) {
+        cudaFree(c->pf_ids);
+        cudaFree(c->pf_lens);
+        c->pf_ids = nullptr;
+        c->pf_lens = nullptr;
+        c->pf_ids_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->pf_ids, B * T * 4));
+        DZ_CUDA(cudaMalloc(&c->pf_lens, B * 4));
+        c->pf_ids_cap = B * T;
+    }
+    const size_t pad_bytes = padding_mask ? B * T : 0, att_bytes = attention_mask ? B * T * T : 0;
+    const size_t mk_bytes = ((pad_bytes + 15) & ~(size_t)15) + att_bytes;
+    if (mk_bytes > c->mk_cap) {
+        cudaFree(c->mk_buf);
+        c->mk_buf = nullptr;
+        c->mk_cap = 0;
+        DZ_CUDA(cudaMalloc(&c->mk_buf, mk_bytes));
+        c->mk_cap = mk_bytes;
+    }
+    PrefillMask mk;
+    DZ_CUDA(cudaMemcpyAsync(c->pf_ids, ids, B * T * 4, cudaMemcpyHostToDevice, c->stream));
+    DZ_CUDA(cudaMemcpyAsync(c->pf_lens, last.data(), B * 4, cudaMemcpyHostToDevice, c->stream));
+    mk.last = c->pf_lens;
+    if (padding_mask) {
+        DZ_CUDA(cudaMemcpyAsync(c->mk_buf, padding_mask, pad_bytes, cudaMemcpyHostToDevice, c->stream));
+        mk.pad = c->mk_buf;
+    }
+    if (attention_mask) {
+        uint8_t* d = c->mk_buf + ((pad_bytes + 15) & ~(size_t)15);
+        DZ_CUDA(cudaMemcpyAsync(d, attention_mask, att_bytes, cudaMemcpyHostToDevice, c->stream));
+        mk.att = d;
+    }
+    enqueue_prefill(c, c->pf_ids, (long long)T, (int)T, nullptr, &mk);
+    // the rings served as working storage: leave every sequence empty
+    dz_reset_kernel<<<(c->B + 255) / 256, 256, 0, c->stream>>>(c->start, c->length, c->total, nullptr, c->B);
+    dz_seen_clear_kernel<<<dim3((unsigned)((c->seen_words + 255) / 256), (unsigned)c->B), 256, 0, c->stream>>>(
+        c->seen, c->seen_words, nullptr);
+    c->seen_valid = true;
+    DZ_CUDA(cudaGetLastError());
+    DZ_CUDA(cudaMemcpyAsync(logits_out, c->logits, B * m->desc.vocab_size * 4, cudaMemcpyDeviceToHost, c->stream));
     DZ_CUDA(cudaStreamSynchronize(c->stream));
     return DZ_OK;
 }

@@ -28,7 +28,9 @@ __global__ void dz_prefill_embed_kernel(const uint32_t* __restrict__ tokens, lon
         atomicOr(&seen[(long long)s * seen_words + (tok >> 5)], 1u << (tok & 31));
     const float* e = emb + (long long)tok * dim;
     float* h = hidden + r * dim;
-    if (t < pe_rows) {
+    if (!pe) {   // rotary positions: no additive encoding (src/core/transformer.c:780-799)
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) h[i] = __fadd_rn(e[i], 0.0f);
+    } else if (t < pe_rows) {
         const float* p = pe + (long long)t * dim;
         for (int i = threadIdx.x; i < dim; i += blockDim.x) h[i] = e[i] + p[i];
     } else {
@@ -81,10 +83,17 @@ __device__ __forceinline__ void pf_cp_wait_all() { asm volatile("cp.async.wait_g
 // elements per thread), and the softmax runs online over the tiles (running
 // max and sum, rescaled), so its rounding differs from the reference's
 // two-pass form within fp32 noise.
-template <int HDW>   // head_dim / 32
+//
+// MASKED: the allowed edges of prepare_attention_mask (src/core/transformer.c:
+// 366-390) instead of the prefix lengths: key j is scored for query t when
+// j <= t, both positions are real (pad [S][T], null = all) and the custom
+// mask allows it (att [S][T][T], null = all); a query with no allowed key
+// gets a zero output (attention_head_forward, :80-131).
+template <int HDW, bool MASKED = false>   // head_dim / 32
 __global__ void __launch_bounds__(PF_THREADS) dz_attention_prefill_kernel(
     const float* __restrict__ q, const float* __restrict__ keys, const float* __restrict__ values,
-    const int* __restrict__ lens, float* __restrict__ out, int T, int dim, int capacity) {
+    const int* __restrict__ lens, float* __restrict__ out, int T, int dim, int capacity,
+    const uint8_t* __restrict__ pad = nullptr, const uint8_t* __restrict__ att = nullptr) {
     constexpr int HD = HDW * 32;
     constexpr int LD = HD + 4;               // row stride of the Q / K / V tiles (floats)
     constexpr int CH = HD / 4;               // 16-byte chunks per row
@@ -97,8 +106,18 @@ __global__ void __launch_bounds__(PF_THREADS) dz_attention_prefill_kernel(
     float* m_s = corr_s + PF_QT;             // [PF_QT]
     float* l_s = m_s + PF_QT;                // [PF_QT]
     const int q0 = blockIdx.x * PF_QT, h = blockIdx.y, s = blockIdx.z;
-    const int len = lens ? lens[s] : T;
+    const int len = (!MASKED && lens) ? lens[s] : T;
     if (q0 >= len) return;
+    const uint8_t* pad_s = (MASKED && pad) ? pad + (long long)s * T : nullptr;
+    const uint8_t* att_s = (MASKED && att) ? att + (long long)s * T * T : nullptr;
+    auto allowed = [&](int t, int j) -> bool {
+        if (!(j <= t && t < len)) return false;
+        if (MASKED) {
+            if (pad_s && !(pad_s[t] && pad_s[j])) return false;
+            if (att_s && !att_s[(long long)t * T + j]) return false;
+        }
+        return true;
+    };
     const int tid = threadIdx.x;
     const float* K = keys + (long long)s * capacity * dim + h * HD;
     const float* Vv = values + (long long)s * capacity * dim + h * HD;
@@ -177,7 +196,7 @@ __global__ void __launch_bounds__(PF_THREADS) dz_attention_prefill_kernel(
             for (int kk = 0; kk < 2; kk++) {
                 const int j = j0 + skg * 2 + kk;
                 sc[i][kk] = sc[i][kk] / denom;
-                if (j <= t && t < len) tmax = fmaxf(tmax, sc[i][kk]);
+                if (allowed(t, j)) tmax = fmaxf(tmax, sc[i][kk]);
             }
 #pragma unroll
             for (int off = 8; off >= 1; off >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
@@ -187,7 +206,7 @@ __global__ void __launch_bounds__(PF_THREADS) dz_attention_prefill_kernel(
 #pragma unroll
             for (int kk = 0; kk < 2; kk++) {
                 const int j = j0 + skg * 2 + kk;
-                const float p = (j <= t && t < len) ? expf(sc[i][kk] - mnew) : 0.0f;
+                const float p = allowed(t, j) ? expf(sc[i][kk] - mnew) : 0.0f;
                 pt[(skg * 2 + kk) * PF_PLD + qi] = p;
                 ps += p;
             }
@@ -229,11 +248,24 @@ __global__ void __launch_bounds__(PF_THREADS) dz_attention_prefill_kernel(
         const int qi = oqg * 8 + i;
         const int t = q0 + qi;
         if (t >= len) continue;
-        const float inv = 1.0f / l_s[qi];
         float* orow = out + (row0 + t) * dim + h * HD;
+        if (MASKED && l_s[qi] == 0.0f) {   // no allowed key: the row stays zero
+#pragma unroll
+            for (int c = 0; c < HDW; c++) orow[oe + c] = 0.0f;
+            continue;
+        }
+        const float inv = 1.0f / l_s[qi];
 #pragma unroll
         for (int c = 0; c < HDW; c++) orow[oe + c] = o[i][c] * inv;
     }
+}
+
+// zero_padded_rows (src/core/transformer.c:355-363): rows r of [R][dim] whose
+// padding entry pad[r] is 0 are set to zero. One block per row.
+__global__ void dz_zero_padded_rows_kernel(float* __restrict__ x, const uint8_t* __restrict__ pad, int dim) {
+    const long long r = blockIdx.x;
+    if (pad[r]) return;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) x[r * dim + i] = 0.0f;
 }
 
 // hidden rows of each sequence's last prompt position -> [S][dim].

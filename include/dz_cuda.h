@@ -277,6 +277,25 @@ int dz_cuda_cache_set_prefill(dz_cuda_cache_t *cache, int mode);
 int dz_cuda_prefill(dz_cuda_cache_t *cache, const uint32_t *ids, const uint32_t *lens, size_t prompt_len,
                     float *logits_out);
 
+/* The masked full-prefix forward of model_forward_masked
+ * (src/core/transformer.c:527-576, mask semantics of model_attention_mask_t,
+ * src/include/core/transformer.h:43-58) for every sequence of the cache:
+ * ids [batch x seq_len] (host); padding_mask [batch x seq_len] (0 = padding)
+ * or NULL; attention_mask [batch x seq_len x seq_len] (row = query, 0 removes
+ * the edge; causality always holds) or NULL; logits_out [batch x V] (host) of
+ * each sequence's last real position. Padded rows are zeroed after the
+ * embedding and after each norm, a query with no allowed key attends to
+ * nothing, as in the reference. The reference's call is one sequence with
+ * its own activation buffers; this one runs `batch` sequences through the
+ * batched-prefill kernels and uses the cache's rings as working storage,
+ * leaving every sequence empty (as after dz_cuda_cache_reset). DZ_E_INVALID
+ * for seq_len 0, seq_len above max_seq_len or the cache capacity, or a
+ * padding mask without a real position (MODEL_INVALID_INPUT in the
+ * reference); DZ_E_UNSUPPORTED for a head dimension other than 32, 64 or
+ * 128. Synchronous. */
+int dz_cuda_forward_masked(dz_cuda_cache_t *cache, const uint32_t *ids, size_t seq_len,
+                           const uint8_t *padding_mask, const uint8_t *attention_mask, float *logits_out);
+
 /* Runs one dz_cuda_generate_async loop eagerly (no graph) with CUDA events
  * around every launch on the cache's stream, synchronises, and fills
  * stats[kind] for kind < n_stats. No counterpart in the reference (its

@@ -574,6 +574,182 @@ int or_forward_token(const or_model_t *m, or_cache_t *c, uint32_t token, float *
     return 0;
 }
 
+/* src/core/tensor_ops.c:113-141 (layer_norm_forward_cached) for one row. */
+static void or_layer_norm_rows(const float *in, float *out, size_t n, const float *gamma,
+                               const float *beta, float eps) {
+    float mean = 0.0f;
+    for (size_t i = 0; i < n; i++) mean += in[i];
+    mean /= (float)n;
+    float var = 0.0f;
+    for (size_t i = 0; i < n; i++) { float d = in[i] - mean; var += d * d; }
+    var /= (float)n;
+    float sd = sqrtf(var + eps);
+    for (size_t i = 0; i < n; i++) out[i] = gamma[i] * ((in[i] - mean) / sd) + beta[i];
+}
+
+/* src/core/tensor_ops.c:181-200 (rms_norm_forward_cached) for one row:
+ * gamma * (x / rms), the decode step's rms_normalize order differs. */
+static void or_rms_norm_rows(const float *in, float *out, size_t n, const float *gamma, float eps) {
+    float ms = 0.0f;
+    for (size_t i = 0; i < n; i++) ms += in[i] * in[i];
+    float rms = sqrtf(ms / (float)n + eps);
+    for (size_t i = 0; i < n; i++) out[i] = gamma[i] * (in[i] / rms);
+}
+
+/* The masked full-prefix forward: model_forward_masked (src/core/
+ * transformer.c:527-576) over model_forward_hidden_masked (:392-519),
+ * prepare_attention_mask (:366-390), zero_padded_rows (:355-363),
+ * multihead_attention_forward (:192-235) and attention_head_forward
+ * (:73-190). One sequence of T ids, padding [T] and attention [T][T] either
+ * NULL; logits of the last real position into `logits` [V]. Returns 0, or -1
+ * for T == 0, T > max_seq_len or a padding mask without a real position. */
+int or_forward_masked(const or_model_t *m, const uint32_t *ids, size_t T, const uint8_t *padding,
+                      const uint8_t *attention, float *logits) {
+    if (!m || !ids || !logits || T == 0 || T > m->max_seq) return -1;
+    const size_t d = m->dim, H = m->heads, hd = d / H, F = 4 * d;
+    const float eps = 1e-6f;
+    size_t last = T - 1;
+    if (padding) {
+        int found = 0;
+        for (size_t i = 0; i < T; i++) if (padding[i]) { last = i; found = 1; }
+        if (!found) return -1;
+    }
+    const int rope = (m->flags & OR_ROPE) != 0, rms = (m->flags & OR_RMSNORM) != 0;
+    const int masked = padding || attention;
+    uint8_t *allowed = masked ? malloc(T * T) : NULL;
+    float *h = malloc(T * d * sizeof(float)), *q = malloc(T * d * sizeof(float));
+    float *k = malloc(T * d * sizeof(float)), *v = malloc(T * d * sizeof(float));
+    float *concat = malloc(T * d * sizeof(float)), *raw = malloc(T * d * sizeof(float));
+    float *x1 = malloc(T * d * sizeof(float)), *ff = malloc(T * F * sizeof(float));
+    float *gate = malloc(T * F * sizeof(float)), *row = malloc(T * sizeof(float));
+    int rc = 0;
+    if ((masked && !allowed) || !h || !q || !k || !v || !concat || !raw || !x1 || !ff || !gate || !row) {
+        rc = -1;
+        goto done;
+    }
+    if (masked) {
+        for (size_t i = 0; i < T; i++)
+            for (size_t j = 0; j < T; j++) {
+                const int qv = !padding || padding[i], kv = !padding || padding[j];
+                const int custom = !attention || attention[i * T + j];
+                allowed[i * T + j] = (uint8_t)(j <= i && qv && kv && custom);
+            }
+    }
+    for (size_t i = 0; i < T; i++) {
+        float *hr = h + i * d;
+        if (padding && !padding[i]) { memset(hr, 0, d * sizeof(float)); continue; }
+        uint32_t tok = ids[i] < m->vocab ? ids[i] : 0;
+        for (size_t e = 0; e < d; e++) hr[e] = m->emb[tok * d + e] + (rope ? 0.0f : m->pe[i * d + e]);
+    }
+    const float denom = sqrtf((float)hd);
+    for (size_t l = 0; l < m->layers; l++) {
+        const or_layer_t *L = &m->layer[l];
+        for (size_t i = 0; i < T; i++) {
+            or_matvec(h + i * d, L->wq, q + i * d, d, d);
+            or_matvec(h + i * d, L->wk, k + i * d, d, d);
+            or_matvec(h + i * d, L->wv, v + i * d, d, d);
+            if (rope) {
+                or_rope(q + i * d, d, H, i);
+                or_rope(k + i * d, d, H, i);
+            }
+        }
+        memset(concat, 0, T * d * sizeof(float));
+        for (size_t hh = 0; hh < H; hh++) {
+            for (size_t i = 0; i < T; i++) {
+                const float *qi = q + i * d + hh * hd;
+                if (masked) {
+                    /* scores on allowed edges only; a row with none stays zero */
+                    size_t count = 0;
+                    float mx = 0.0f;
+                    for (size_t j = 0; j < T; j++) {
+                        row[j] = 0.0f;
+                        if (!allowed[i * T + j]) continue;
+                        float sc = 0.0f;
+                        for (size_t e = 0; e < hd; e++) sc += qi[e] * k[j * d + hh * hd + e];
+                        row[j] = sc / denom;
+                        if (count == 0 || row[j] > mx) mx = row[j];
+                        count++;
+                    }
+                    if (count == 0) continue;
+                    float sum = 0.0f;
+                    for (size_t j = 0; j < T; j++) {
+                        if (!allowed[i * T + j]) continue;
+                        row[j] = expf(row[j] - mx);
+                        sum += row[j];
+                    }
+                    if (sum > 0.0f) {
+                        const float inv = 1.0f / sum;
+                        for (size_t j = 0; j < T; j++) if (allowed[i * T + j]) row[j] *= inv;
+                    }
+                    for (size_t e = 0; e < hd; e++) {
+                        float acc = 0.0f;
+                        for (size_t j = 0; j < T; j++) {
+                            if (!allowed[i * T + j]) continue;
+                            acc += row[j] * v[j * d + hh * hd + e];
+                        }
+                        concat[i * d + hh * hd + e] = acc;
+                    }
+                } else {
+                    for (size_t j = 0; j <= i; j++) {
+                        float sc = 0.0f;
+                        for (size_t e = 0; e < hd; e++) sc += qi[e] * k[j * d + hh * hd + e];
+                        row[j] = sc / denom;
+                    }
+                    or_softmax(row, i + 1);
+                    for (size_t e = 0; e < hd; e++) {
+                        float acc = 0.0f;
+                        for (size_t j = 0; j <= i; j++) acc += row[j] * v[j * d + hh * hd + e];
+                        concat[i * d + hh * hd + e] = acc;
+                    }
+                }
+            }
+        }
+        for (size_t i = 0; i < T; i++) {
+            float *r = raw + i * d;
+            or_matvec(concat + i * d, L->wo, r, d, d);
+            for (size_t e = 0; e < d; e++) r[e] += h[i * d + e];
+            if (rms) or_rms_norm_rows(r, x1 + i * d, d, L->g1, eps);
+            else or_layer_norm_rows(r, x1 + i * d, d, L->g1, L->be1, eps);
+            if (padding && !padding[i]) memset(x1 + i * d, 0, d * sizeof(float));
+        }
+        for (size_t i = 0; i < T; i++) {
+            float *fr = ff + i * F, *gr = gate + i * F;
+            or_matvec(x1 + i * d, L->w1, fr, d, F);
+            if (m->flags & OR_SWIGLU) or_matvec(x1 + i * d, L->wg, gr, d, F);
+            for (size_t e = 0; e < F; e++) {
+                const float pre = fr[e] + L->b1[e];
+                if (m->flags & OR_SWIGLU) fr[e] = or_silu(pre) * (gr[e] + L->bg[e]);
+                else if (m->flags & OR_GELU) fr[e] = or_gelu(pre);
+                else fr[e] = pre > 0.0f ? pre : 0.0f;
+            }
+            float *r = raw + i * d;
+            or_matvec(fr, L->w2, r, F, d);
+            for (size_t e = 0; e < d; e++) r[e] += L->b2[e];
+            for (size_t e = 0; e < d; e++) r[e] += x1[i * d + e];
+            if (rms) or_rms_norm_rows(r, h + i * d, d, L->g2, eps);
+            else or_layer_norm_rows(r, h + i * d, d, L->g2, L->be2, eps);
+            if (padding && !padding[i]) memset(h + i * d, 0, d * sizeof(float));
+        }
+    }
+    {
+        const float *hl = h + last * d;
+        if (m->flags & OR_TIED) {
+            for (size_t t = 0; t < m->vocab; t++) {
+                float sc = 0.0f;
+                for (size_t e = 0; e < d; e++) sc += hl[e] * m->emb[t * d + e];
+                logits[t] = sc;
+            }
+        } else {
+            or_matvec(hl, m->out_proj, logits, d, m->vocab);
+        }
+        for (size_t t = 0; t < m->vocab; t++) logits[t] += m->out_bias[t];
+    }
+done:
+    free(allowed); free(h); free(q); free(k); free(v); free(concat); free(raw); free(x1);
+    free(ff); free(gate); free(row);
+    return rc;
+}
+
 /* ----------------------------------------------------------- sampling */
 
 typedef struct { float prob; uint32_t idx; } or_pair_t;

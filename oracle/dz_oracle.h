@@ -76,6 +76,8 @@ void or_cache_reset(or_cache_t *c);
 void or_cache_free(or_cache_t *c);
 /* src/core/transformer.c:755-858 */
 int or_forward_token(const or_model_t *m, or_cache_t *c, uint32_t token, float *logits);
+int or_forward_masked(const or_model_t *m, const uint32_t *ids, size_t T, const uint8_t *padding,
+                      const uint8_t *attention, float *logits);
 
 /* src/cli/sampling.c:38-207. strategy: 0 greedy, 1 top-k, 2 top-p. */
 uint32_t or_sample_next_token(float *logits, size_t vocab, int strategy, float temperature,

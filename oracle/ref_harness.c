@@ -213,6 +213,24 @@ int rh_forward_token(void *handle, uint32_t token, float *logits) {
     return model_forward_token(&s->model, &s->cache, token, logits) == MODEL_SUCCESS ? 0 : -1;
 }
 
+/* model_forward_masked (src/core/transformer.c:527-576) on the loaded model:
+ * the full-prefix forward of one sequence of seq_len ids with an optional
+ * padding mask [seq_len] and attention mask [seq_len][seq_len] (either may be
+ * NULL), logits of the last real position into `logits` [V]. Returns the
+ * reference's model_errors_t. */
+int rh_forward_masked(void *handle, const uint32_t *ids, size_t seq_len, const uint8_t *padding,
+                      const uint8_t *attention, float *logits) {
+    rh_session_t *s = handle;
+    uint32_t *copy = malloc(seq_len * sizeof(*copy));
+    if (!copy) return -1;
+    memcpy(copy, ids, seq_len * sizeof(*copy));
+    model_attention_mask_t mask = {padding, attention};
+    const int rc = (int)model_forward_masked(&s->model, copy, seq_len,
+                                             (padding || attention) ? &mask : NULL, logits);
+    free(copy);
+    return rc;
+}
+
 /* The decode loop of generation_decode_with_options (src/cli/generation.c:
  * 231-295) with the tokenizer treated as fully trained (vocab_size == V):
  * control ids `masked` are set to -FLT_MAX before each draw, repetition

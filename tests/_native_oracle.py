@@ -75,6 +75,7 @@ class Oracle:
         _sig(L, "or_cache_reset", None, P)
         _sig(L, "or_cache_free", None, P)
         _sig(L, "or_forward_token", I32, P, P, U32, P)
+        _sig(L, "or_forward_masked", I32, P, P, SZ, P, P, P)
         _sig(L, "or_sample_next_token", U32, P, SZ, I32, F32, SZ, F32, P)
         _sig(L, "or_generate", I32, P, P, P, SZ, SZ, SZ, I32, F32, SZ, F32, P, P, SZ, P, P)
         _sig(L, "or_fnv1a", U64, U64, P, SZ)
@@ -158,6 +159,16 @@ class OracleModel:
         out = np.empty(self.spec.vocab, np.float32)
         self.o.L.or_forward_token(self.h, self.cache, int(token), _ptr(out))
         return out
+
+    def forward_masked(self, ids, padding=None, attention=None):
+        """or_forward_masked: logits of the last real position, or None when
+        the input is rejected."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        pad = None if padding is None else np.ascontiguousarray(padding, np.uint8)
+        att = None if attention is None else np.ascontiguousarray(attention, np.uint8)
+        out = np.empty(self.spec.vocab, np.float32)
+        rc = self.o.L.or_forward_masked(self.h, _ptr(ids), ids.size, _ptr(pad), _ptr(att), _ptr(out))
+        return out if rc == 0 else None
 
     def generate(self, prompts, n_new, strategy=GREEDY, temperature=0.0, top_k=0, top_p=0.0,
                  seeds=None, masked=(256, 257, 258, 259), want_logits=False):
@@ -252,6 +263,7 @@ class RefHarness:
         _sig(L, "compute_positional_encoding", I32, P, SZ, SZ)
         _sig(L, "rh_generate_ex", I32, P, P, SZ, SZ, SZ, I32, F32, SZ, F32, P, F32, SZ, P, P, SZ, P, P)
         _sig(L, "rh_tokenizer_vocab", SZ, P)
+        _sig(L, "rh_forward_masked", I32, P, P, SZ, P, P, P)
 
     def quantize_pack(self, w, bits, gran):
         w = np.ascontiguousarray(w, np.float32)

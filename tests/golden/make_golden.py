@@ -323,8 +323,74 @@ def gen_arch():
     gen_model("arch6", 400, 64, 2, 2, 32, 33, 8, 7, 2, 24, 24, TOPK, 0.8, 5, 0.0, [90, 91], 2, flags=6)
 
 
+def masked_cases(seed):
+    """Inputs of the masked full-prefix forward: (ids, padding or None,
+    attention or None) per case; T <= 64."""
+    rng = np.random.RandomState(seed)
+    st = np.array([rng_stream(seed, STREAM_TESTING)], np.uint64)
+    cases = []
+
+    def ids(T):
+        return prompt_ids(st, T, 512)
+
+    cases.append((ids(20), None, None))                                   # plain causal
+    pad = np.ones(24, np.uint8); pad[-5:] = 0
+    cases.append((ids(24), pad, None))                                    # right padding
+    pad = np.ones(24, np.uint8); pad[:6] = 0
+    cases.append((ids(24), pad, None))                                    # left padding
+    pad = (rng.rand(32) > 0.25).astype(np.uint8); pad[3] = 1
+    cases.append((ids(32), pad, None))                                    # holes
+    pad = (rng.rand(32) > 0.25).astype(np.uint8); pad[10] = 1; pad[-1] = 1
+    att = (rng.rand(32, 32) > 0.3).astype(np.uint8)
+    att[10, :] = 0                                                        # a real query with no key
+    cases.append((ids(32), pad, att))                                     # padding + custom mask
+    cases.append((ids(64), None, None))                                   # T = max_seq_len
+    att = (rng.rand(64, 64) > 0.5).astype(np.uint8)
+    att[63, :] = 0                                                        # the last position attends to nothing
+    cases.append((ids(64), None, att))                                    # custom mask only
+    return cases
+
+
+def gen_masked():
+    # model_forward_masked (src/core/transformer.c:527-576) on the reference's
+    # build: the default architecture (INT8) and tied + RoPE + RMSNorm +
+    # SwiGLU (INT4), seven mask cases each, plus a padding mask with no real
+    # position (rejected)
+    out = {}
+    for mi, (wseed, bits, flags) in enumerate([(51, 8, 0), (52, 4, 23)]):
+        V, d, H, Ly, T = 512, 128, 4, 2, 64
+        path = f"/tmp/dz_golden_masked{mi}.bin"
+        assert L.rh_build_bundle_arch(path.encode(), V, d, H, Ly, T, wseed, bits, 2, flags) == 0
+        h = L.rh_load(path.encode())
+        with open(path, "rb") as f:
+            blob = np.frombuffer(f.read(), np.uint8)
+        os.remove(path)
+        out[f"m{mi}_spec"] = np.array([V, d, H, Ly, T, wseed, bits], np.int64)
+        out[f"m{mi}_flags"] = np.array([flags], np.int64)
+        out[f"m{mi}_bundle_fnv"] = np.array([fnv(blob)], np.uint64)
+        cases = masked_cases(60 + mi)
+        for ci, (ids, pad, att) in enumerate(cases):
+            lg = np.empty(V, np.float32)
+            rc = L.rh_forward_masked(h, ids.ctypes.data, ids.size, pad.ctypes.data if pad is not None else None,
+                                     att.ctypes.data if att is not None else None, lg.ctypes.data)
+            assert rc == 0, rc
+            out[f"m{mi}_c{ci}_ids"] = ids
+            out[f"m{mi}_c{ci}_pad"] = pad if pad is not None else np.zeros(0, np.uint8)
+            out[f"m{mi}_c{ci}_att"] = att if att is not None else np.zeros(0, np.uint8)
+            out[f"m{mi}_c{ci}_logits"] = lg
+        bad = np.zeros(16, np.uint8)
+        lg = np.empty(V, np.float32)
+        out[f"m{mi}_rejected_rc"] = np.array([L.rh_forward_masked(h, cases[0][0].ctypes.data, 16, bad.ctypes.data,
+                                                                  None, lg.ctypes.data)], np.int64)
+        out[f"m{mi}_count"] = np.array([len(cases)], np.int64)
+        L.rh_free(h)
+    np.savez_compressed(os.path.join(HERE, "masked.npz"), **out)
+
+
 GENERATORS = {"rng": gen_rng, "quant": gen_quant, "qmm": gen_qmm, "pe": gen_pe, "bundle": gen_bundle_small,
-              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "controls": gen_controls, "arch": gen_arch, "c4": gen_c4}
+              "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "controls": gen_controls, "arch": gen_arch,
+              "masked": gen_masked,
+              "c4": gen_c4}
 
 if __name__ == "__main__":
     # no argument: every fixture except the config-4 sample (minutes of CPU)

@@ -167,3 +167,36 @@ def test_generation_controls_match_reference(oracle):
         np.testing.assert_array_equal(toks, g[f"c{i}_tokens"], err_msg=f"case {i}")
         np.testing.assert_array_equal(res, g[f"c{i}_results"], err_msg=f"case {i}")
     om.close()
+
+
+def masked_golden_cases(g, mi):
+    """(ids, padding or None, attention or None, reference logits) of model mi
+    in tests/golden/masked.npz."""
+    for ci in range(int(g[f"m{mi}_count"][0])):
+        ids = g[f"m{mi}_c{ci}_ids"]
+        pad, att = g[f"m{mi}_c{ci}_pad"], g[f"m{mi}_c{ci}_att"]
+        T = ids.size
+        yield (ids, pad if pad.size else None, att.reshape(T, T) if att.size else None,
+               g[f"m{mi}_c{ci}_logits"])
+
+
+@pytest.mark.parametrize("mi", [0, 1])
+def test_masked_forward_matches_reference(oracle, mi):
+    """or_forward_masked against model_forward_masked of the reference's build
+    (tests/golden/masked.npz): plain causal, right / left / scattered
+    padding, a custom attention mask with a real query that attends to
+    nothing, T = max_seq_len; the default architecture (INT8) and tied + RoPE +
+    RMSNorm + SwiGLU (INT4). A padding mask without a real position is
+    rejected by both."""
+    g = golden("masked.npz")
+    V, d, H, L, T, wseed, bits = (int(x) for x in g[f"m{mi}_spec"])
+    spec = Spec(V, d, H, L, T, int(g[f"m{mi}_flags"][0]))
+    _, flat = quantize_params(oracle, spec, synth_params(oracle, spec, wseed), bits)
+    m = oracle.model(spec, flat)
+    for ci, (ids, pad, att, ref) in enumerate(masked_golden_cases(g, mi)):
+        got = m.forward_masked(ids, pad, att)
+        err = np.abs(got - ref).max() / np.abs(ref).max()
+        assert err <= 1e-4, (ci, err)
+    assert int(g[f"m{mi}_rejected_rc"][0]) != 0
+    assert m.forward_masked(g[f"m{mi}_c0_ids"][:16], np.zeros(16, np.uint8)) is None
+    m.close()
