@@ -128,6 +128,22 @@ def quantize_unpack(scales, packed, rows, cols, bits, granularity=GRAN_COLUMN):
     return out
 
 
+def quantize_dequantize(values, bits, granularity=GRAN_COLUMN):
+    """quantize_dequantize_into (dz_quantize_dequantize_into): the simulated
+    grid of a [rows, cols] float32 matrix; returns (reconstruction, error
+    fields as a dict)."""
+    from ._native import DzQuantError
+    v = np.ascontiguousarray(values, np.float32)
+    if v.ndim != 2:
+        raise ValueError("quantize_dequantize: a 2-D matrix")
+    out = np.empty_like(v)
+    e = DzQuantError()
+    if lib().dz_quantize_dequantize_into(_p(v), _p(out), v.shape[0], v.shape[1], bits, granularity,
+                                         ctypes.addressof(e)) != 0:
+        raise ValueError("quantize_dequantize: bad arguments")
+    return out, {f: getattr(e, f) for f, _ in DzQuantError._fields_}
+
+
 def positional_encoding(rows, dim):
     out = np.empty((rows, dim), np.float32)
     check(lib().dz_positional_encoding(_p(out), rows, dim), "positional_encoding")

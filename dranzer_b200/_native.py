@@ -56,6 +56,12 @@ KERNEL_CLASSES = ["step_begin", "qmv", "attention", "layernorm", "select", "seqg
 FUSED_PHASES = ["embed", "weight_wait", "qmv", "attention", "layernorm", "select"]
 
 
+class DzQuantError(ctypes.Structure):
+    _fields_ = [("count", ctypes.c_size_t), ("max_abs_error", ctypes.c_float), ("rms_error", ctypes.c_double),
+                ("rms_relative", ctypes.c_double), ("original_rms", ctypes.c_double),
+                ("clipped", ctypes.c_size_t), ("levels_used", ctypes.c_size_t)]
+
+
 class DzSampling(ctypes.Structure):
     _fields_ = [("strategy", I32), ("temperature", F32), ("top_k", U32), ("top_p", F32),
                 ("masked_ids", ctypes.POINTER(U32)), ("n_masked", SZ)]
@@ -84,6 +90,8 @@ SIGNATURES = {
     "dz_quantized_packed_size": (I32, [SZ, I32, P]),
     "dz_quantize_pack": (I32, [P, SZ, SZ, I32, I32, P, SZ, P, SZ]),
     "dz_quantize_unpack": (I32, [P, SZ, P, SZ, SZ, SZ, I32, I32, P]),
+    "dz_quantize_dequantize_into": (I32, [P, P, SZ, SZ, I32, I32, P]),
+    "dz_quantize_dequantize": (I32, [P, SZ, SZ, I32, I32, P]),
     "dz_positional_encoding": (I32, [P, SZ, SZ]),
     "dz_fnv1a": (U64, [U64, P, SZ]),
     "dz_bundle_open": (I32, [CP, P]),

@@ -190,13 +190,14 @@ static inline float round_half_away(float v) {
 
 /* level = clamp(round_half_away(w * (qmax / peak)), +-qmax), code = level + qmax
  * (src/core/quantize.c:257-264). When the peak is subnormal, qmax / peak
- * overflows to +inf and a zero weight gives NaN; the reference build resolves
- * that NaN to +qmax, and so does this. */
+ * overflows to +inf and a zero weight gives NaN, which passes both clamps; the
+ * reference's (int) conversion of it yields INT_MIN on x86, whose low `bits`
+ * bits after + qmax are qmax, i.e. the zero level, and so does this. */
 static inline uint32_t quant_code(float w, float peak, int qmax) {
     float level = 0.0f;
     if (peak > 0.0f) {
         const float scaled = w * ((float)qmax / peak);
-        level = (scaled != scaled) ? (float)qmax : round_half_away(scaled);
+        level = (scaled != scaled) ? 0.0f : round_half_away(scaled);
     }
     if (level > (float)qmax) level = (float)qmax;
     if (level < -(float)qmax) level = -(float)qmax;
@@ -262,14 +263,87 @@ int dz_quantize_pack(const float *src, size_t rows, size_t cols, int bits, int g
         }
     }
 
-    /* scale = peak * fl(1/qmax): the reference source divides by qmax
-     * (src/core/quantize.c:265-267); its -O3 -ffast-math build turns that
-     * division by a constant into a multiply by the rounded reciprocal, and the
-     * artifacts it writes carry that result. */
-    const float reciprocal = 1.0f / (float)qmax;
+    /* scale = peak / qmax, a true division (src/core/quantize.c:265-267; the
+     * reference compiles its quantizer without -ffast-math, src/Makefile:
+     * 259-268) */
     for (size_t g = 0; g < scales_count; g++)
-        if (scales[g] > 0.0f) scales[g] = scales[g] * reciprocal;
+        if (scales[g] > 0.0f) scales[g] = scales[g] / (float)qmax;
     return 0;
+}
+
+/* One group of quantize_dequantize_into (quantize_group, src/core/
+ * quantize.c:54-116): values src[i * stride], i < count. The original is read
+ * before the store so the in-place form measures against it. */
+static void qdq_group(const float *src, float *dst, size_t count, size_t stride, int qmax, double *sse,
+                      double *sso, float *max_abs, size_t *clipped, unsigned char *seen) {
+    float peak = 0.0f;
+    for (size_t i = 0; i < count; i++) {
+        const float m = fabsf(src[i * stride]);
+        if (m > peak) peak = m;
+    }
+    if (!(peak > 0.0f)) {   /* nothing to scale: copied through, the zero level used */
+        for (size_t i = 0; i < count; i++) dst[i * stride] = src[i * stride];
+        seen[qmax] = 1;
+        return;
+    }
+    const float scale = peak / (float)qmax;
+    const float inverse = (float)qmax / peak;
+    for (size_t i = 0; i < count; i++) {
+        const float original = src[i * stride];
+        float level = round_half_away(original * inverse);
+        if (level > (float)qmax) level = (float)qmax;
+        if (level < -(float)qmax) level = -(float)qmax;
+        const int index = (int)level;
+        if (index == qmax || index == -qmax) (*clipped)++;
+        seen[index + qmax] = 1;
+        const float rec = scale * level;
+        dst[i * stride] = rec;
+        const double diff = (double)original - (double)rec;
+        *sse += diff * diff;
+        *sso += (double)original * (double)original;
+        const float a = fabsf((float)diff);
+        if (a > *max_abs) *max_abs = a;
+    }
+}
+
+int dz_quantize_dequantize_into(const float *src, float *dst, size_t rows, size_t cols, int bits,
+                                int granularity, dz_quant_error_t *error_out) {
+    if (!src || !dst || rows == 0 || cols == 0 || bits < 2 || bits > 16 || !valid_granularity(granularity))
+        return -1;
+    const int qmax = (1 << (bits - 1)) - 1;
+    const size_t total = rows * cols, levels = (size_t)(2 * qmax + 1);
+    unsigned char seen[1 << 16];
+    memset(seen, 0, levels);
+    double sse = 0.0, sso = 0.0;
+    float max_abs = 0.0f;
+    size_t clipped = 0;
+    if (granularity == DZ_GRAN_TENSOR) {
+        qdq_group(src, dst, total, 1, qmax, &sse, &sso, &max_abs, &clipped, seen);
+    } else if (granularity == DZ_GRAN_ROW) {
+        for (size_t r = 0; r < rows; r++)
+            qdq_group(src + r * cols, dst + r * cols, cols, 1, qmax, &sse, &sso, &max_abs, &clipped, seen);
+    } else {
+        for (size_t c = 0; c < cols; c++)
+            qdq_group(src + c, dst + c, rows, cols, qmax, &sse, &sso, &max_abs, &clipped, seen);
+    }
+    if (error_out) {
+        memset(error_out, 0, sizeof(*error_out));
+        error_out->count = total;
+        error_out->max_abs_error = max_abs;
+        error_out->rms_error = sqrt(sse / (double)total);
+        error_out->original_rms = sqrt(sso / (double)total);
+        error_out->rms_relative = error_out->original_rms > 0.0 ? error_out->rms_error / error_out->original_rms : 0.0;
+        error_out->clipped = clipped;
+        size_t used = 0;
+        for (size_t i = 0; i < levels; i++) used += seen[i] ? 1u : 0u;
+        error_out->levels_used = used;
+    }
+    return 0;
+}
+
+int dz_quantize_dequantize(float *values, size_t rows, size_t cols, int bits, int granularity,
+                           dz_quant_error_t *error_out) {
+    return dz_quantize_dequantize_into(values, values, rows, cols, bits, granularity, error_out);
 }
 
 static uint32_t code_at(const uint8_t *packed, size_t idx, int bits) {

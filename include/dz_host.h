@@ -42,6 +42,31 @@ int dz_quantize_unpack(const float *scales, size_t scales_count, const uint8_t *
                        size_t packed_size, size_t rows, size_t cols, int bits, int granularity,
                        float *dst);
 
+/* Error of one simulated quantization, quant_error_t
+ * (src/include/core/quantize.h:58-80): the same fields in the same order. */
+typedef struct {
+    size_t count;
+    float max_abs_error;
+    double rms_error;
+    double rms_relative;
+    double original_rms;
+    size_t clipped;
+    size_t levels_used;
+} dz_quant_error_t;
+
+/* quantize_dequantize_into / quantize_dequantize (src/core/quantize.c:
+ * 54-174, src/include/core/quantize.h:88-115): the symmetric grid applied
+ * and mapped straight back, dst = scale * clamp(round_half_away(x * inverse),
+ * +-qmax) per group with scale = peak / qmax and inverse = qmax / peak; an
+ * all-zero group is copied through. Small negatives become -0.0, as in the
+ * reference (round_half_away is ceilf there). Same -1 returns (null
+ * pointers, empty tensor, bits outside 2..16, bad granularity). The error
+ * statistics accumulate in double in the reference's order. */
+int dz_quantize_dequantize_into(const float *src, float *dst, size_t rows, size_t cols, int bits,
+                                int granularity, dz_quant_error_t *error_out);
+int dz_quantize_dequantize(float *values, size_t rows, size_t cols, int bits, int granularity,
+                           dz_quant_error_t *error_out);
+
 /* Rows [start, start + count) (axis 0) or columns (axis 1) of a quantized
  * rows x cols matrix as a quantized matrix of its own: the same codes (the
  * reference's layout, INT4 nibbles LSB-first with a zero pad nibble) and the

@@ -169,10 +169,11 @@ int or_quantize_pack(const float *src, size_t rows, size_t cols, int bits, int g
             const float inverse = (float)qmax / peak;
             const float scaled = src[i] * inverse;
             /* A subnormal peak makes qmax/peak overflow to +inf and a zero
-             * weight then gives 0 * inf = NaN. The reference build
-             * (-ffinite-math-only) resolves that NaN to +qmax through its
-             * clamp; restated explicitly (pinned by tests/golden/quant.npz). */
-            level = (scaled != scaled) ? (float)qmax : or_round_half_away(scaled);
+             * weight then gives 0 * inf = NaN, which passes both clamps; the
+             * reference's (int)level of it is INT_MIN on x86, whose low `bits`
+             * bits after + qmax are qmax: the zero level. Restated explicitly
+             * (pinned by tests/golden/quant.npz). */
+            level = (scaled != scaled) ? 0.0f : or_round_half_away(scaled);
         }
         if (level > (float)qmax) level = (float)qmax;
         if (level < -(float)qmax) level = -(float)qmax;
@@ -185,15 +186,10 @@ int or_quantize_pack(const float *src, size_t rows, size_t cols, int bits, int g
             }
         }
     }
-    /* quantize.c:265-267 writes `scales[g] /= (float)qmax`. The reference is
-     * built with -O3 -ffast-math (src/Makefile:46), whose -freciprocal-math
-     * compiles that division by a constant to a multiply by the rounded
-     * reciprocal; the shipped quantizer therefore stores peak * fl(1/qmax),
-     * which differs from peak / qmax by one ulp in some groups. The golden
-     * vectors in tests/golden/ pin this against the reference's own build. */
-    const float reciprocal = 1.0f / (float)qmax;
+    /* quantize.c:265-267: scales[g] /= qmax, a true division (the reference
+     * compiles quantize.c without -ffast-math, src/Makefile:259-268). */
     for (size_t g = 0; g < ns; g++) {
-        if (scales[g] > 0.0f) scales[g] = scales[g] * reciprocal;
+        if (scales[g] > 0.0f) scales[g] = scales[g] / (float)qmax;
     }
     return 0;
 }

@@ -8,6 +8,7 @@ generators described in tests/_models.py and the fill patterns of the
 reference's tests (src/tests/core/test_quantize.c:81-90,
 src/tests/core/test_quantized_matmul.c:25-29), restated here.
 """
+import ctypes
 import os
 import sys
 
@@ -323,6 +324,55 @@ def gen_arch():
     gen_model("arch6", 400, 64, 2, 2, 32, 33, 8, 7, 2, 24, 24, TOPK, 0.8, 5, 0.0, [90, 91], 2, flags=6)
 
 
+class QuantError(ctypes.Structure):
+    # quant_error_t (src/include/core/quantize.h:58-80)
+    _fields_ = [("count", ctypes.c_size_t), ("max_abs_error", ctypes.c_float), ("rms_error", ctypes.c_double),
+                ("rms_relative", ctypes.c_double), ("original_rms", ctypes.c_double),
+                ("clipped", ctypes.c_size_t), ("levels_used", ctypes.c_size_t)]
+
+
+def qdq_inputs():
+    """Inputs of the simulated grid: the reference test's fill pattern, and
+    Gaussian values with near-zero entries (-0.0 reconstructions) and an
+    all-zero group."""
+    out = []
+    for si, (rows, cols) in enumerate([(3, 5), (8, 32), (64, 48), (1, 100), (17, 1)]):
+        out.append(fill_quantize_test(rows * cols, si + 1).reshape(rows, cols))
+    st = np.array([rng_stream(77, STREAM_TESTING)], np.uint64)
+    g = gaussian(st, 40 * 24, 1.0).reshape(40, 24)
+    g[::7, :] *= np.float32(1e-4)
+    g[:, 5] = 0.0
+    out.append(g)
+    return out
+
+
+def gen_qdq():
+    # quantize_dequantize_into (src/core/quantize.c:118-174) of the
+    # reference's build: reconstructions (bit patterns) and error fields
+    fn = L.quantize_dequantize_into
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int, ctypes.c_int,
+                   ctypes.c_void_p]
+    out = {}
+    n = 0
+    for x in qdq_inputs():
+        for gran in (0, 1, 2):
+            for bits in (2, 3, 4, 8, 12, 16):
+                dst = np.empty_like(x)
+                e = QuantError()
+                assert fn(x.ctypes.data, dst.ctypes.data, x.shape[0], x.shape[1], bits, gran,
+                          ctypes.addressof(e)) == 0
+                out[f"q{n}_src"] = x
+                out[f"q{n}_args"] = np.array([gran, bits], np.int64)
+                out[f"q{n}_dst_bits"] = dst.view(np.uint32)
+                out[f"q{n}_counts"] = np.array([e.count, e.clipped, e.levels_used], np.int64)
+                out[f"q{n}_stats"] = np.array([e.max_abs_error, e.rms_error, e.rms_relative, e.original_rms],
+                                              np.float64)
+                n += 1
+    out["count"] = np.array([n], np.int64)
+    np.savez_compressed(os.path.join(HERE, "qdq.npz"), **out)
+
+
 def masked_cases(seed):
     """Inputs of the masked full-prefix forward: (ids, padding or None,
     attention or None) per case; T <= 64."""
@@ -389,7 +439,7 @@ def gen_masked():
 
 GENERATORS = {"rng": gen_rng, "quant": gen_quant, "qmm": gen_qmm, "pe": gen_pe, "bundle": gen_bundle_small,
               "c1": gen_c1, "c2": gen_c2, "ring": gen_ring, "controls": gen_controls, "arch": gen_arch,
-              "masked": gen_masked,
+              "masked": gen_masked, "qdq": gen_qdq,
               "c4": gen_c4}
 
 if __name__ == "__main__":

@@ -23,6 +23,34 @@ def test_quantize_pack_bit_exact(dz):
         assert deq.shape == (r, c)
 
 
+def test_quantize_dequantize_bit_exact(dz):
+    """dz_quantize_dequantize_into against quantize_dequantize_into of the
+    reference's build (tests/golden/qdq.npz): every reconstruction bit pattern
+    (signed zeros included), the counts exact, the double statistics to 1e-12
+    (test_quantize.c:124-140 allows that much between its two call forms)."""
+    g = golden("qdq.npz")
+    for n in range(int(g["count"][0])):
+        gran, bits = (int(x) for x in g[f"q{n}_args"])
+        out, e = dz.quantize_dequantize(g[f"q{n}_src"], bits, gran)
+        np.testing.assert_array_equal(out.view(np.uint32), g[f"q{n}_dst_bits"], err_msg=f"case {n}")
+        assert [e["count"], e["clipped"], e["levels_used"]] == g[f"q{n}_counts"].tolist(), n
+        ref = g[f"q{n}_stats"]
+        assert np.float32(e["max_abs_error"]) == np.float32(ref[0]), n
+        np.testing.assert_allclose([e["rms_error"], e["rms_relative"], e["original_rms"]], ref[1:], rtol=1e-12,
+                                   atol=0)
+    # the reconstruction is what unpacking the packed codes gives, up to the sign of zero
+    x = g["q7_src"]
+    for gran in (0, 1, 2):
+        for bits in (4, 8):
+            out, _ = dz.quantize_dequantize(x, bits, gran)
+            s, p = dz.quantize_pack(x, bits, gran)
+            np.testing.assert_array_equal(out + np.float32(0), dz.quantize_unpack(s, p, *x.shape, bits, gran))
+    with pytest.raises(ValueError):
+        dz.quantize_dequantize(x, 1, 2)
+    with pytest.raises(ValueError):
+        dz.quantize_dequantize(x, 8, 3)
+
+
 @pytest.mark.parametrize("N", [4096, 11008, 32000])
 def test_c3_weights_bit_exact(dz, N):
     """Full-size C3 matrices (K=4096), generator and quantizer of the product."""
