@@ -535,10 +535,25 @@ def run_job(args, wl, torch, dz, _native, W, world, rank, local, hbm, bf16, peak
             classes[name]["launches"] = max(1, int(round(classes[name]["launches"])))
         note = (f"kernel classes of the job: the eager prefill plus {P} decode steps at the full batch, the decode "
                 f"steps scaled to the job's {wl.n_new - 1}")
+        # the two phases on their own: the prefill, and one decode step (the
+        # mean of the P profiled steps)
+        step = {}
+        for name in set(c1) | set(c2):
+            a, b = c1.get(name, zero), c2.get(name, zero)
+            d = {k: (b[k] - a[k]) / P for k in ("launches", "total_ms", "bytes", "flops")}
+            if d["total_ms"] > 0:
+                d["launches"] = max(1, int(round(d["launches"])))
+                step[name] = d
+        phase_classes = {}
+        for pname, cl in (("prefill", c1), ("decode_step", step)):
+            _, per = roofline_of(cl, wl.name, hbm, bf16, peak_src, "")
+            phase_classes[pname] = {k: {f: v[f] for f in ("bound", "frac", "ms", "launches", "share")}
+                                    for k, v in per.items()}
     else:
         classes, ph = _profile(L, _native, cache, pd.data_ptr(), wl.prompt_len, wl.n_new, samp, seeds_ptr,
                                od.data_ptr())
         note = "kernel classes of one eagerly launched job"
+        phase_classes = None
     note += ("; bytes = weight codes + scales + fp32 tensors once per batch step, KV rows read and written, "
              "activations in and out; flops = 2*M*K*N of the quantized products (useful work; the integer tensor "
              "cores run three 8-bit limb passes) plus attention")
@@ -590,6 +605,8 @@ def run_job(args, wl, torch, dz, _native, W, world, rank, local, hbm, bf16, peak
         }
         if ph:
             out["fused_phases_ms"] = ph
+        if phase_classes:
+            out["phase_kernel_classes"] = phase_classes
     os.remove(path)
     return out, (cache, model, bundle, prompts, seeds, samp)
 

@@ -29,6 +29,7 @@
 #include "umma.cuh"
 #include "qmvi.cuh"
 #include "arch.cuh"
+#include "attn.cuh"
 
 using namespace dz;
 
@@ -395,6 +396,7 @@ static int qms_prepare(int device) {
     DZ_QMV1_ATTR(4, false); DZ_QMV1_ATTR(4, true); DZ_QMV1_ATTR(8, false); DZ_QMV1_ATTR(8, true);
 #undef DZ_QMV1_ATTR
     DZ_CUDA(dz_qmv1i_set_smem(optin));
+    DZ_CUDA(dz_attn_decode_set_smem());
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UG_SMEM_BYTES));
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UV_SMEM_BYTES));
     // the split runs right before the GEMV (and may share SMs with it): the
@@ -443,6 +445,18 @@ static bool matvec_int_kernel() {
     static const bool v = [] {
         const char* e = getenv("DZ_MATVEC_KERNEL");
         return !(e && strcmp(e, "mma") == 0);
+    }();
+    return v;
+}
+
+// Which decode attention runs for head dimensions 64 and 128: the streamed
+// kernel (attn.cuh, the default) or the register-blocked one
+// (dz_attention_decode2_kernel). DZ_ATTN_KERNEL=regs in the environment
+// selects the latter, for comparison; both compute the same attention.
+static bool attn_streamed_kernel() {
+    static const bool v = [] {
+        const char* e = getenv("DZ_ATTN_KERNEL");
+        return !(e && strcmp(e, "regs") == 0);
     }();
     return v;
 }
@@ -1829,7 +1843,10 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             // only when the profiler cannot read it) + q + output
             ProfScope prof(DZ_KERNEL_ATTENTION, c->prof_ctx_bytes_per_layer + 8.0 * B * dl,
                            c->prof_ctx_flops_per_layer, st);
-            if (hd == 128)
+            AdArgs aa{c->q, Kl, Vl, c->start, c->ctx, c->concat, dl, cap, c->status};
+            if ((hd == 128 || hd == 64) && attn_streamed_kernel())
+                dz_attn_decode_launch(aa, hd, H, B, st);
+            else if (hd == 128)
                 dz_attention_decode2_kernel<4><<<dim3(H, B), ATT2_THREADS, 0, st>>>(c->q, Kl, Vl, c->start, c->ctx,
                                                                                    c->concat, dl, cap);
             else if (hd == 64)

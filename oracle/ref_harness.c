@@ -205,6 +205,7 @@ void rh_free(void *handle) {
 }
 
 size_t rh_param_count(void *handle) { return ((rh_session_t *)handle)->model.total_param_count; }
+const void *rh_model(void *handle) { return &((rh_session_t *)handle)->model; }
 const float *rh_params(void *handle) { return ((rh_session_t *)handle)->model.params; }
 void rh_reset(void *handle) { model_kv_cache_reset(&((rh_session_t *)handle)->cache); }
 

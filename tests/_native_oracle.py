@@ -15,6 +15,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 ORACLE_DIR = os.path.join(ROOT, "oracle")
 ORACLE_SO = os.path.join(ORACLE_DIR, "liboracle.so")
 REF_SO = os.path.join(ORACLE_DIR, "_ref", "libdzref.so")
+BRIDGE_SO = os.path.join(ORACLE_DIR, "_ref", "libdzref_bridge.so")
 
 P = ctypes.c_void_p
 SZ = ctypes.c_size_t
@@ -233,11 +234,17 @@ class Controls:
 class RefHarness:
     """The reference's own sources (oracle/_ref/libdzref.so)."""
 
-    def __init__(self):
-        if not os.path.exists(REF_SO):
-            raise FileNotFoundError(REF_SO)
-        L = ctypes.CDLL(REF_SO)
+    def __init__(self, path=REF_SO):
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        L = ctypes.CDLL(path)
         self.L = L
+        if path == BRIDGE_SO:
+            # the reference-side binding (oracle/dz_bridge.c)
+            _sig(L, "br_attach", I32, P, ctypes.c_char_p, I32)
+            _sig(L, "br_detach", None, P)
+            _sig(L, "br_device_forwards", SZ)
+        _sig(L, "rh_model", P, P)
         _sig(L, "dranzer_rng_stream", U64, U64, U64)
         _sig(L, "dranzer_rng_next", U64, P)
         _sig(L, "dranzer_rng_unit", F64, P)

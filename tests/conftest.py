@@ -56,3 +56,17 @@ def ref():
         else:
             pytest.skip("reference build not present (tests/golden pins the oracle instead)")
     return RefHarness()
+
+
+@pytest.fixture(scope="session")
+def bridge(dz):
+    """The reference's objects with the reference-side binding of the device
+    path linked in (oracle/dz_bridge.c, oracle/_ref/libdzref_bridge.so)."""
+    from _native_oracle import BRIDGE_SO, RefHarness
+    if not os.path.exists(BRIDGE_SO):
+        if os.path.isdir(os.path.join(REF_TREE, "src")):
+            subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), "ref", "bridge", f"REF={REF_TREE}"],
+                           check=True)
+        else:
+            pytest.skip("reference build not present")
+    return RefHarness(BRIDGE_SO)
