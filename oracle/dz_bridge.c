@@ -79,18 +79,29 @@ void br_detach(const neural_model_t *model) {
 
 size_t br_device_forwards(void) { return br_forwards; }
 
-model_errors_t __wrap_model_kv_cache_init(model_kv_cache_t *cache, const neural_model_t *model) {
-    model_errors_t rc = __real_model_kv_cache_init(cache, model);
-    dz_cuda_model_t *dz = rc == MODEL_SUCCESS ? br_model_of(model) : NULL;
-    if (!dz) return rc;
+/* The device cache of a host cache of an attached model, made on first use
+ * while the host cache is empty (a cache initialised before the model was
+ * attached gets one at its next sequence); NULL: the CPU path. */
+static dz_cuda_cache_t **br_cache_for(const neural_model_t *model, model_kv_cache_t *cache) {
+    dz_cuda_cache_t **slot = br_cache_slot(cache);
+    if (slot) return slot;
+    dz_cuda_model_t *dz = br_model_of(model);
+    if (!dz || cache->total_tokens != 0) return NULL;
     for (int i = 0; i < BR_MAX; i++)
         if (!br_caches[i].dz) {
-            if (dz_cuda_cache_create(dz, 1, cache->capacity, &br_caches[i].dz) == DZ_OK)
-                br_caches[i].cache = cache;
-            else
+            if (dz_cuda_cache_create(dz, 1, cache->capacity, &br_caches[i].dz) != DZ_OK) {
                 br_caches[i].dz = NULL;   /* never fatal: this cache stays on the CPU */
-            break;
+                return NULL;
+            }
+            br_caches[i].cache = cache;
+            return &br_caches[i].dz;
         }
+    return NULL;
+}
+
+model_errors_t __wrap_model_kv_cache_init(model_kv_cache_t *cache, const neural_model_t *model) {
+    model_errors_t rc = __real_model_kv_cache_init(cache, model);
+    if (rc == MODEL_SUCCESS) (void)br_cache_for(model, cache);
     return rc;
 }
 
@@ -113,7 +124,7 @@ void __wrap_model_kv_cache_free(model_kv_cache_t *cache) {
 
 model_errors_t __wrap_model_forward_token(neural_model_t *model, model_kv_cache_t *cache, uint32_t token_id,
                                           float *output_logits) {
-    dz_cuda_cache_t **slot = cache ? br_cache_slot(cache) : NULL;
+    dz_cuda_cache_t **slot = cache ? br_cache_for(model, cache) : NULL;
     if (slot && output_logits) {
         if (dz_cuda_forward_tokens(*slot, &token_id, output_logits) != DZ_OK) {
             /* before the first token the CPU path takes over (never fatal);
