@@ -709,6 +709,7 @@ def main():
     ap.add_argument("--probe", choices=["qmv", "decode"],
                     help="run only the C3 quantized-matmul rows, or a few config-4 decode steps (profiling targets)")
     ap.add_argument("--probe-n", type=int, default=0, help="with --probe: one N instead of all three")
+    ap.add_argument("--probe-batch", type=int, default=64, help="with --probe decode: sequences")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -724,7 +725,7 @@ def main():
         import torch
         import dranzer_b200 as dz
         hbm, _, _ = peaks()
-        out = decode_probe(dz, torch, hbm)
+        out = decode_probe(dz, torch, hbm, batch=args.probe_batch)
     else:
         from dranzer_b200 import workloads as W
         out = run_dz(args, W.WORKLOADS[args.workload])

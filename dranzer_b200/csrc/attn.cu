@@ -14,12 +14,13 @@ cudaError_t dz_attn_decode_set_smem() {
     return e;
 }
 
-cudaError_t dz_attn_decode_launch(const AdArgs& a, int head_dim, int heads, int batch, cudaStream_t st) {
+cudaError_t dz_attn_decode_launch(const CUtensorMap& tmK, const CUtensorMap& tmV, const AdArgs& a, int head_dim,
+                                  int heads, int batch, cudaStream_t st) {
     const dim3 grid((unsigned)heads, (unsigned)batch);
     if (head_dim == 128)
-        dz_attn_decode_kernel<4><<<grid, AD_THREADS, AdCfg<4>::SMEM, st>>>(a);
+        dz_attn_decode_kernel<4><<<grid, AD_THREADS, AdCfg<4>::SMEM, st>>>(tmK, tmV, a);
     else if (head_dim == 64)
-        dz_attn_decode_kernel<2><<<grid, AD_THREADS, AdCfg<2>::SMEM, st>>>(a);
+        dz_attn_decode_kernel<2><<<grid, AD_THREADS, AdCfg<2>::SMEM, st>>>(tmK, tmV, a);
     else
         return cudaErrorNotSupported;
     return cudaGetLastError();

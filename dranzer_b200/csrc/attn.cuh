@@ -7,16 +7,18 @@
 // The step reads every context row of K and V once (the KV ring is the
 // step's dominant HBM traffic), so the kernel is built to keep many bytes in
 // flight: per block, tiles of 32 keys (the head's 32 K rows and 32 V rows,
-// hd * 4 bytes each) land in a ring of shared-memory stages through
-// cp.async.bulk copies (one K and one V row per lane of warp 0, completion
-// counted on the stage's mbarrier); 8 consumer warps take 4 keys each per
-// tile. The softmax runs online per warp (running max and sum, rescaled) and
+// hd * 4 bytes each) land in a ring of shared-memory stages, each tile by two
+// 2-D tensor copies (one for K, one for V: a box of hd floats x 32 ring
+// rows, completion counted on the stage's mbarrier; a tile that wraps round
+// the ring goes as one bulk copy per row instead); 8 consumer warps take 4
+// keys each per tile. The softmax runs online per warp (running max and sum, rescaled) and
 // the warps' partial results merge at the end, so its rounding differs from
 // the reference's two-pass form within fp32 noise. Waits are bounded (about
 // one second, %globaltimer); on a timeout the block records status 1, waits
 // for its copies in flight and returns.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace dz {
@@ -44,6 +46,7 @@ struct AdArgs {
     float* out;            // [B][dim]
     int dim, capacity;
     int* status;
+    int layer_row0;        // this layer's first row in the tensor maps' [rows][dim] view
 };
 
 static __device__ __forceinline__ uint32_t ad_smem_addr(const void* p) {
@@ -76,8 +79,20 @@ static __device__ __forceinline__ bool ad_mbar_wait(uint64_t* bar, uint32_t pari
     }
 }
 
+static __device__ __forceinline__ void ad_tma_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            ad_smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(ad_smem_addr(bar))
+        : "memory");
+}
+
+// tmK / tmV: every layer's K (V) ring as one [layers * B * capacity][dim]
+// fp32 tensor, box {hd, 32}.
 template <int HDW>
-__global__ void __launch_bounds__(AD_THREADS, 2) dz_attn_decode_kernel(AdArgs a) {
+__global__ void __launch_bounds__(AD_THREADS, 2) dz_attn_decode_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                                       const __grid_constant__ CUtensorMap tmV,
+                                                                       AdArgs a) {
     using C = AdCfg<HDW>;
     extern __shared__ __align__(128) uint8_t ad_smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(ad_smem + C::STAGES * C::STAGE);
@@ -94,20 +109,36 @@ __global__ void __launch_bounds__(AD_THREADS, 2) dz_attn_decode_kernel(AdArgs a)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    // warp 0: tile t's rows into stage t % STAGES, one K and one V row per lane
+    // warp 0: tile t's rows into stage t % STAGES: two tensor copies, or one
+    // K and one V row per lane for a tile that wraps round the ring
+    const int row_b = a.layer_row0 + b * a.capacity;
     auto issue = [&](int t) {
         const int s = t % C::STAGES;
         const int j0 = t * AD_KT;
         const int n = min(AD_KT, ctx - j0);
         uint8_t* ks = ad_smem + s * C::STAGE;
         uint8_t* vs = ks + AD_KT * C::ROW;
+        int p0 = start + j0;   // start < capacity and j0 < ctx <= capacity
+        if (p0 >= a.capacity) p0 -= a.capacity;
+        if (p0 + n <= a.capacity) {
+            // the box's rows past n (another sequence's rows, or past the
+            // tensor: zero-filled) are never used
+            if (lane == 0) {
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ad_smem_addr(&full[s])),
+                             "r"((uint32_t)(2 * AD_KT * C::ROW))
+                             : "memory");
+                ad_tma_2d(ks, &tmK, h * C::HD, row_b + p0, &full[s]);
+                ad_tma_2d(vs, &tmV, h * C::HD, row_b + p0, &full[s]);
+            }
+            return;
+        }
         if (lane == 0)
             asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(ad_smem_addr(&full[s])),
                          "r"((uint32_t)(2 * n * C::ROW))
                          : "memory");
         __syncwarp();
         if (lane < n) {
-            int phys = start + j0 + lane;   // start < capacity and j < ctx <= capacity
+            int phys = p0 + lane;
             if (phys >= a.capacity) phys -= a.capacity;
             asm volatile(
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -248,6 +279,7 @@ __global__ void __launch_bounds__(AD_THREADS, 2) dz_attn_decode_kernel(AdArgs a)
 // Host side (attn.cu): set the kernels' shared-memory limits once; launch
 // for head dimension 64 or 128 (cudaErrorNotSupported otherwise).
 cudaError_t dz_attn_decode_set_smem();
-cudaError_t dz_attn_decode_launch(const AdArgs& a, int head_dim, int heads, int batch, cudaStream_t st);
+cudaError_t dz_attn_decode_launch(const CUtensorMap& tmK, const CUtensorMap& tmV, const AdArgs& a, int head_dim,
+                                  int heads, int batch, cudaStream_t st);
 
 }  // namespace dz

@@ -187,9 +187,20 @@ __global__ void __launch_bounds__(ATT2_THREADS) dz_attention_decode2_kernel(
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const float* K = keys + (long long)b * capacity * dim + h * HD + lane * HDW;
     const float* V = values + (long long)b * capacity * dim + h * HD + lane * HDW;
+    // a lane's HDW elements of a row are one 16-byte (hd 128) or 8-byte
+    // (hd 64) load: rows start on 16-byte boundaries (dim and hd are
+    // multiples of 64)
+    auto load_row = [&](const float* p, float* v) {
+        if (HDW == 4) {
+            const float4 x = *reinterpret_cast<const float4*>(p);
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+        } else {
+            const float2 x = *reinterpret_cast<const float2*>(p);
+            v[0] = x.x; v[1] = x.y;
+        }
+    };
     float qv[HDW];
-#pragma unroll
-    for (int c = 0; c < HDW; c++) qv[c] = q[(long long)b * dim + h * HD + lane * HDW + c];
+    load_row(q + (long long)b * dim + h * HD + lane * HDW, qv);
     const float denom = sqrtf((float)HD);
     float m = -3.402823466e38f, l = 0.0f, o[HDW];
 #pragma unroll
@@ -201,9 +212,12 @@ __global__ void __launch_bounds__(ATT2_THREADS) dz_attention_decode2_kernel(
             const int j = j0 + u;
             int phys = start + j;
             if (phys >= capacity) phys -= capacity;
-            const float* kr = K + (long long)phys * dim;
+            if (j < ctx) {
+                load_row(K + (long long)phys * dim, kv[u]);
+            } else {
 #pragma unroll
-            for (int c = 0; c < HDW; c++) kv[u][c] = j < ctx ? kr[c] : 0.0f;
+                for (int c = 0; c < HDW; c++) kv[u][c] = 0.0f;
+            }
         }
 #pragma unroll
         for (int u = 0; u < ATT2_KEYS; u++) {
@@ -235,9 +249,10 @@ __global__ void __launch_bounds__(ATT2_THREADS) dz_attention_decode2_kernel(
             l += p;
             int phys = start + j;
             if (phys >= capacity) phys -= capacity;
-            const float* vr = V + (long long)phys * dim;
+            float vv[HDW];
+            load_row(V + (long long)phys * dim, vv);
 #pragma unroll
-            for (int c = 0; c < HDW; c++) o[c] = fmaf(p, vr[c], o[c]);
+            for (int c = 0; c < HDW; c++) o[c] = fmaf(p, vv[c], o[c]);
         }
     }
     if (lane == 0) {

@@ -1502,6 +1502,10 @@ struct dz_cuda_cache {
     cudaStream_t stream = nullptr;
     bool own_stream = false;
     float *keys = nullptr, *values = nullptr;  // [L][B][cap][D]
+    // the K / V rings as [L * B * cap][D] fp32 tensors, box {head dim, 32}
+    // (the streamed decode attention); kv_maps false: not available
+    CUtensorMap tm_keys, tm_values;
+    bool kv_maps = false;
     int *start = nullptr, *length = nullptr, *slot = nullptr, *ctx = nullptr, *row_off = nullptr;
     long long* total = nullptr;
     float *hidden = nullptr, *q = nullptr, *concat = nullptr, *attn_raw = nullptr, *attn_norm = nullptr;
@@ -1626,6 +1630,23 @@ extern "C" int dz_cuda_cache_create(dz_cuda_model_t* m, size_t batch, size_t cap
     const size_t dl = m->dl, Fl = m->Fl;   // this rank's attention and FFN widths
     if (!rc) rc = cache_alloc(c, (void**)&c->keys, Lr * B * capacity * dl * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->values, Lr * B * capacity * dl * 4);
+    if (!rc) {
+        const size_t hd = D / m->desc.num_heads, rows = Lr * B * capacity;
+        TensorMapEncodeFn enc = tensor_map_encoder();
+        c->kv_maps = false;
+        if (enc && (hd == 64 || hd == 128) && rows < (size_t)INT32_MAX) {
+            const cuuint64_t dims[2] = {(cuuint64_t)dl, (cuuint64_t)rows};
+            const cuuint64_t strides[1] = {(cuuint64_t)dl * 4};
+            const cuuint32_t box[2] = {(cuuint32_t)hd, (cuuint32_t)AD_KT};
+            const cuuint32_t es[2] = {1, 1};
+            c->kv_maps = true;
+            for (auto pr : {std::make_pair(&c->tm_keys, c->keys), std::make_pair(&c->tm_values, c->values)})
+                c->kv_maps = c->kv_maps &&
+                             enc(pr.first, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, pr.second, dims, strides, box, es,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }
+    }
     if (!rc) rc = cache_alloc(c, (void**)&c->start, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->length, B * 4);
     if (!rc) rc = cache_alloc(c, (void**)&c->slot, B * 4);
@@ -1843,9 +1864,9 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             // only when the profiler cannot read it) + q + output
             ProfScope prof(DZ_KERNEL_ATTENTION, c->prof_ctx_bytes_per_layer + 8.0 * B * dl,
                            c->prof_ctx_flops_per_layer, st);
-            AdArgs aa{c->q, Kl, Vl, c->start, c->ctx, c->concat, dl, cap, c->status};
-            if ((hd == 128 || hd == 64) && attn_streamed_kernel())
-                dz_attn_decode_launch(aa, hd, H, B, st);
+            AdArgs aa{c->q, Kl, Vl, c->start, c->ctx, c->concat, dl, cap, c->status, (int)(l * B * cap)};
+            if ((hd == 128 || hd == 64) && c->kv_maps && attn_streamed_kernel())
+                dz_attn_decode_launch(c->tm_keys, c->tm_values, aa, hd, H, B, st);
             else if (hd == 128)
                 dz_attention_decode2_kernel<4><<<dim3(H, B), ATT2_THREADS, 0, st>>>(c->q, Kl, Vl, c->start, c->ctx,
                                                                                    c->concat, dl, cap);

@@ -34,9 +34,29 @@ static struct { const neural_model_t *model; dz_cuda_model_t *dz; } br_models[BR
 static struct { const model_kv_cache_t *cache; dz_cuda_cache_t *dz; } br_caches[BR_MAX];
 static size_t br_forwards;   /* decode steps served by the device */
 
+/* a device model waiting for the next model that starts a sequence
+ * (br_attach_next: for handles whose neural_model_t the caller cannot name,
+ * such as the public API's opaque dranzer_model_t) */
+static dz_cuda_model_t *br_pending;
+
+static int br_bind(const neural_model_t *model, dz_cuda_model_t *dz) {
+    for (int i = 0; i < BR_MAX; i++)
+        if (!br_models[i].model) {
+            br_models[i].model = model;
+            br_models[i].dz = dz;
+            return 0;
+        }
+    return DZ_E_NOMEM;
+}
+
 static dz_cuda_model_t *br_model_of(const neural_model_t *model) {
     for (int i = 0; i < BR_MAX; i++)
         if (br_models[i].model == model) return br_models[i].dz;
+    if (br_pending && br_bind(model, br_pending) == 0) {
+        dz_cuda_model_t *dz = br_pending;
+        br_pending = NULL;
+        return dz;
+    }
     return NULL;
 }
 
@@ -46,26 +66,33 @@ static dz_cuda_cache_t **br_cache_slot(const model_kv_cache_t *cache) {
     return NULL;
 }
 
-/* Attach: the model's bundle reopened with its codes kept
- * (dz_bundle_open) and uploaded to `device`. Returns 0 or a DZ_E_* code. */
-int br_attach(const neural_model_t *model, const char *bundle_path, int device) {
+/* The model's bundle reopened with its codes kept (dz_bundle_open) and
+ * uploaded to `device`. */
+static int br_upload(const char *bundle_path, int device, dz_cuda_model_t **out) {
     dz_bundle_t *b = NULL;
     dz_model_desc_t desc;
     int rc = dz_bundle_open(bundle_path, &b);
     if (rc) return rc;
     rc = dz_bundle_desc(b, &desc);
-    dz_cuda_model_t *dz = NULL;
-    if (!rc) rc = dz_cuda_model_create(&desc, dz_bundle_tensors(b), dz_bundle_tensor_count(b), device, &dz);
+    if (!rc) rc = dz_cuda_model_create(&desc, dz_bundle_tensors(b), dz_bundle_tensor_count(b), device, out);
     dz_bundle_close(b);
+    return rc;
+}
+
+/* Attach the device copy of `bundle_path` to `model`. Returns 0 or a DZ_E_*
+ * code. */
+int br_attach(const neural_model_t *model, const char *bundle_path, int device) {
+    dz_cuda_model_t *dz = NULL;
+    int rc = br_upload(bundle_path, device, &dz);
     if (rc) return rc;
-    for (int i = 0; i < BR_MAX; i++)
-        if (!br_models[i].model) {
-            br_models[i].model = model;
-            br_models[i].dz = dz;
-            return 0;
-        }
-    dz_cuda_model_free(dz);
-    return DZ_E_NOMEM;
+    if ((rc = br_bind(model, dz))) dz_cuda_model_free(dz);
+    return rc;
+}
+
+/* Attach it to the next model that starts a sequence on an empty cache. */
+int br_attach_next(const char *bundle_path, int device) {
+    if (br_pending) return DZ_E_INVALID;
+    return br_upload(bundle_path, device, &br_pending);
 }
 
 void br_detach(const neural_model_t *model) {

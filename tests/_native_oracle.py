@@ -242,6 +242,19 @@ class RefHarness:
         if path == BRIDGE_SO:
             # the reference-side binding (oracle/dz_bridge.c)
             _sig(L, "br_attach", I32, P, ctypes.c_char_p, I32)
+            _sig(L, "br_attach_next", I32, ctypes.c_char_p, I32)
+            # the reference's public API (src/include/dranzer.h)
+            _sig(L, "dranzer_bundle_load", I32, ctypes.c_char_p, I32, P, P, P)
+            _sig(L, "dranzer_model_free", None, P)
+            _sig(L, "dranzer_tokenizer_free", None, P)
+            _sig(L, "dranzer_cache_create", I32, P, SZ, P)
+            _sig(L, "dranzer_cache_forward", I32, P, U32, P, SZ)
+            _sig(L, "dranzer_cache_reset", None, P)
+            _sig(L, "dranzer_cache_free", None, P)
+            _sig(L, "dranzer_generation_create", I32, P, P, SZ, P)
+            _sig(L, "dranzer_generation_reset", I32, P, ctypes.c_char_p, SZ)
+            _sig(L, "dranzer_generation_next_greedy", I32, P, P, P, P)
+            _sig(L, "dranzer_generation_free", None, P)
             _sig(L, "br_detach", None, P)
             _sig(L, "br_device_forwards", SZ)
         _sig(L, "rh_model", P, P)

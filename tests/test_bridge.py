@@ -93,3 +93,100 @@ def test_bridge_runs_the_reference_loop_on_the_device(gpu, bridge, tmp_path, nam
                                                                             if i not in MASKED]].max())
     bad = check_streams(toks, g["tokens"], g["margins"], max(err, 1e-6))
     print(f"{name}: bridged reference loop, {served} device steps, max-rel {rel[ok].max():.2e}, near-ties {bad}")
+
+
+# ------------------------------------------------ the reference's public API
+
+PROMPT = b"the quick brown fox jumps over"
+API_MASKED = [256, 257, 258]   # PAD, UNK, BOS (dranzer_generation_next_greedy, src/api/dranzer.c:374-384)
+
+
+def _api_load(bridge, path):
+    import ctypes
+    m, t = ctypes.c_void_p(), ctypes.c_void_p()
+    assert bridge.L.dranzer_bundle_load(path.encode(), 0, ctypes.byref(m), ctypes.byref(t), None) == 0
+    return m, t
+
+
+def _api_cache_logits(bridge, m, ids, V):
+    import ctypes
+    c = ctypes.c_void_p()
+    assert bridge.L.dranzer_cache_create(m, 0, ctypes.byref(c)) == 0
+    out = np.empty((len(ids), V), np.float32)
+    for i, t in enumerate(ids):
+        assert bridge.L.dranzer_cache_forward(c, int(t), out[i].ctypes.data, V) == 0
+    bridge.L.dranzer_cache_free(c)
+    return out
+
+
+def _api_greedy(bridge, m, t, n):
+    import ctypes
+    gen = ctypes.c_void_p()
+    assert bridge.L.dranzer_generation_create(m, t, 0, ctypes.byref(gen)) == 0
+    assert bridge.L.dranzer_generation_reset(gen, PROMPT, len(PROMPT)) == 0
+    toks = []
+    piece = ctypes.create_string_buffer(64)
+    for _ in range(n):
+        tid, size = ctypes.c_uint32(), ctypes.c_size_t(64)
+        rc = bridge.L.dranzer_generation_next_greedy(gen, ctypes.byref(tid), piece, ctypes.byref(size))
+        assert rc in (0, 9), rc   # DRANZER_OK, DRANZER_FINISHED
+        toks.append(tid.value)
+        if rc == 9:
+            break
+    bridge.L.dranzer_generation_free(gen)
+    return np.array(toks, np.uint32)
+
+
+def test_bridge_public_api_passes_through(bridge, tmp_path):
+    """dranzer_cache_forward over the c1 prompt through the bridge library,
+    no device model: the reference's prompt logits bit for bit."""
+    g = golden("c1.npz")
+    _, path = _load(bridge, g, tmp_path, "c1api")
+    m, t = _api_load(bridge, path)
+    lg = _api_cache_logits(bridge, m, g["prompts"][0], int(g["spec"][0]))
+    np.testing.assert_array_equal(lg.view(np.uint32), g["prompt_logits"].view(np.uint32))
+    bridge.L.dranzer_tokenizer_free(t)
+    bridge.L.dranzer_model_free(m)
+
+
+@pytest.mark.gpu
+def test_bridge_public_api_on_the_device(gpu, bridge, tmp_path):
+    """The public API (src/api/dranzer.c:228-414) on a device-attached model:
+    dranzer_cache_forward logits within 1e-3 of the same calls on the CPU,
+    and dranzer_generation_reset / _next_greedy giving the CPU's tokens (a
+    divergence only where the CPU's top-2 gap is below 10x the observed
+    logit error)."""
+    g = golden("c1.npz")
+    V = int(g["spec"][0])
+    _, path = _load(bridge, g, tmp_path, "c1api")
+    m, t = _api_load(bridge, path)
+    ids = np.concatenate([g["prompts"][0], g["tokens"][0][:16]])
+    cpu_lg = _api_cache_logits(bridge, m, ids, V)
+    cpu_toks = _api_greedy(bridge, m, t, 24)
+    # the CPU's greedy margins along its own stream (BOS, the prompt's bytes,
+    # the draws), masked as the API masks
+    feed = np.concatenate([[258], np.frombuffer(PROMPT, np.uint8).astype(np.uint32), cpu_toks[:-1]])
+    lg = _api_cache_logits(bridge, m, feed, V)[len(PROMPT):]   # the logits each draw was taken from
+    lg[:, API_MASKED] = -np.finfo(np.float32).max
+    lg[:, 260:] = -np.finfo(np.float32).max                  # ids past the tokenizer's 260
+    top2 = np.sort(lg, axis=-1)[:, -2:]
+    margins = top2[:, 1] - top2[:, 0]
+    assert bridge.L.br_attach_next(path.encode(), 0) == 0
+    before = bridge.L.br_device_forwards()
+    dev_lg = _api_cache_logits(bridge, m, ids, V)
+    assert bridge.L.br_device_forwards() - before == len(ids)
+    rel = np.abs(dev_lg - cpu_lg).max(axis=-1) / np.abs(cpu_lg).max(axis=-1)
+    assert rel.max() <= 1e-3, rel.max()
+    err = float(np.abs(dev_lg - cpu_lg).max())
+    dev_toks = _api_greedy(bridge, m, t, 24)
+    assert bridge.L.br_device_forwards() - before > len(ids) + len(PROMPT)
+    n = min(len(cpu_toks), len(dev_toks))
+    diff = np.nonzero(cpu_toks[:n] != dev_toks[:n])[0]
+    if diff.size:
+        i = int(diff[0])
+        assert margins[i] < 10 * err, (i, margins[i], err)
+    else:
+        assert len(cpu_toks) == len(dev_toks)
+    print(f"public API on the device: max-rel {rel.max():.2e}, tokens {dev_toks.tolist()}")
+    bridge.L.dranzer_tokenizer_free(t)
+    bridge.L.dranzer_model_free(m)
