@@ -288,14 +288,14 @@ def dist_init():
     return world, rank, local
 
 
-def quant_matvec_probe(dz, torch, stream, hbm, bf16=None, cpu=False, Ns=(4096, 11008, 32000)):
+def quant_matvec_probe(dz, torch, stream, hbm, bf16=None, cpu=False, Ns=(4096, 11008, 32000),
+                       Ms=(1, 8, 64, 512), K=4096):
     """C3 rows: K=4096, N in {4096, 11008, 32000}, M in {1, 8, 64, 512},
     INT8 and INT4; enough weight copies rotated per launch that the weights
     exceed L2 (126 MB). cpu: also time the reference's own
     matmul_quantized_weight (oracle/_ref, OpenMP over the host cores, median
     of 3) at M = 1 and 8, and M = 64 at N = 4096."""
     res = []
-    Ms = (1, 8, 64, 512)
     ref = None
     if cpu:
         no = _checker()
@@ -305,15 +305,15 @@ def quant_matvec_probe(dz, torch, stream, hbm, bf16=None, cpu=False, Ns=(4096, 1
             ref.L.rh_set_omp_threads(os.cpu_count() or 1)
     for N in Ns:
         st = np.array([dz.rng_stream(3, dz.STREAM_TESTING)], np.uint64)
-        x = dz.synth_gaussian(st, max(Ms) * 4096, 1.0).reshape(max(Ms), 4096)
-        w = dz.synth_gaussian(st, 4096 * N, 0.02).reshape(4096, N)
+        x = dz.synth_gaussian(st, max(Ms) * K, 1.0).reshape(max(Ms), K)
+        w = dz.synth_gaussian(st, K * N, 0.02).reshape(K, N)
         xd = torch.from_numpy(x).cuda()
         yd = torch.empty((max(Ms), N), dtype=torch.float32, device="cuda")
         for bits in (8, 4):
             s, p = dz.quantize_pack(w, bits)
-            wbytes = 4096 * N * bits // 8
+            wbytes = K * N * bits // 8
             copies = max(2, -(-(256 << 20) // wbytes))
-            mats = [dz.QuantizedWeightMatrix(s, p, 4096, N, bits) for _ in range(copies)]
+            mats = [dz.QuantizedWeightMatrix(s, p, K, N, bits) for _ in range(copies)]
             rh = ref.qmat(w, bits, 2) if ref is not None else None
             for M in Ms:
                 # every copy once first: a copy grows its scratch on its first call at a new M
@@ -346,10 +346,10 @@ def quant_matvec_probe(dz, torch, stream, hbm, bf16=None, cpu=False, Ns=(4096, 1
                 b1.record(stream)
                 torch.cuda.synchronize()
                 ms_stream = b0.elapsed_time(b1) / reps
-                nbytes = wbytes + N * 4 + M * 4096 * 4 + M * N * 4
+                nbytes = wbytes + N * 4 + M * K * 4 + M * N * 4
                 gbs = nbytes / (ms * 1e-3) / 1e9
-                tflops = 2.0 * M * 4096 * N / (ms * 1e-3) / 1e12
-                r = {"bits": bits, "M": M, "K": 4096, "N": N, "us": round(ms * 1e3, 2),
+                tflops = 2.0 * M * K * N / (ms * 1e-3) / 1e12
+                r = {"bits": bits, "M": M, "K": K, "N": N, "us": round(ms * 1e3, 2),
                      "GB/s": round(gbs, 1), "frac": round(gbs / hbm, 3), "TFLOP/s": round(tflops, 1),
                      "bytes": int(nbytes), "us_stream": round(ms_stream * 1e3, 2),
                      "frac_stream": round(nbytes / (ms_stream * 1e-3) / 1e9 / hbm, 3)}
@@ -710,6 +710,8 @@ def main():
                     help="run only the C3 quantized-matmul rows, or a few config-4 decode steps (profiling targets)")
     ap.add_argument("--probe-n", type=int, default=0, help="with --probe: one N instead of all three")
     ap.add_argument("--probe-batch", type=int, default=64, help="with --probe decode: sequences")
+    ap.add_argument("--probe-m", default="", help="with --probe qmv: comma-separated row counts")
+    ap.add_argument("--probe-k", type=int, default=4096, help="with --probe qmv: K")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
@@ -720,7 +722,8 @@ def main():
         stream = torch.cuda.Stream()
         hbm, bf16, _ = peaks()
         Ns = (args.probe_n,) if args.probe_n else (4096, 11008, 32000)
-        out = {"quant_matvec": quant_matvec_probe(dz, torch, stream, hbm, bf16, Ns=Ns)}
+        Ms = tuple(int(v) for v in args.probe_m.split(",")) if args.probe_m else (1, 8, 64, 512)
+        out = {"quant_matvec": quant_matvec_probe(dz, torch, stream, hbm, bf16, Ns=Ns, Ms=Ms, K=args.probe_k)}
     elif args.probe == "decode":
         import torch
         import dranzer_b200 as dz
