@@ -396,6 +396,9 @@ def _profile(L, _native, cache, pd, plen, n_new, samp, seeds_ptr, od):
     return _class_stats(_native, stats), phases
 
 
+NVLINK_GBS = 770.0   # measured peer copy per direction per GPU on this pool (900 nominal)
+
+
 def roofline_of(classes, wl_name, hbm, bf16, peak_src, note):
     """Per class: achieved bytes or flops over its time against the measured
     peak of its bound (flops per byte above the ridge = tensor); the class
@@ -405,6 +408,15 @@ def roofline_of(classes, wl_name, hbm, bf16, peak_src, note):
     for name, c in classes.items():
         t = c["total_ms"] * 1e-3
         if t <= 0:
+            continue
+        if name == "allreduce":
+            # bytes each rank sends over NVLink, against the measured peer copy
+            # of 770 GB/s per direction on this pool
+            ach = c["bytes"] / t / 1e9
+            per[name] = {"bound": "nvlink", "achieved": round(ach, 1), "peak": NVLINK_GBS, "unit": "GB/s",
+                         "frac": round(ach / NVLINK_GBS, 4), "ms": round(c["total_ms"], 3),
+                         "launches": c["launches"], "bytes_per_launch": int(c["bytes"] / c["launches"]),
+                         "flops_per_launch": 0.0}
             continue
         tensor = c["flops"] > 0 and c["flops"] / max(c["bytes"], 1.0) > ridge
         if tensor:
@@ -659,6 +671,100 @@ def run_dz(args, wl):
     return out
 
 
+def tp_probe(args):
+    """Tensor parallelism at the config-5 width (d 6144, 48 heads of 128,
+    F 24576, V 50257, INT4, weights seed 5) with args.probe_layers layers:
+    32 sequences, a 1024-token batched prefill, then 32 greedy steps, on every
+    rank of a torchrun job (heads and FFN columns split over the ranks, NCCL
+    all-reduces after attention-out and FFN-down). Reports the job, its
+    prefill and decode parts (max over ranks) and the share of each phase
+    spent in the all-reduce (eager launches bracketed by CUDA events)."""
+    import torch
+    import dranzer_b200 as dz
+    from dranzer_b200 import _native
+    from dranzer_b200 import workloads as W
+    world, rank, local = dist_init()
+    torch.cuda.set_device(local)
+    hbm, bf16, peak_src = peaks()
+    spec = W.Spec(50257, 6144, 48, args.probe_layers, 4096)
+    wl = W.Workload("c5-width-tp", spec, 4, 5, 5, 32, 1024, 33, capacity=1088)
+    path = f"/tmp/dz_tp_probe_{args.probe_layers}.bin"
+    if rank == 0:
+        W.write_bundle(wl, path)
+    if world > 1:
+        import torch.distributed as tdist
+        tdist.barrier()
+        uid = [dz.Model.tp_unique_id() if rank == 0 else None]
+        tdist.broadcast_object_list(uid, src=0)
+    bundle = dz.Bundle(path)
+    model = dz.Model.from_bundle(bundle, device=local, tp=(rank, world, uid[0]) if world > 1 else None)
+    cache = dz.KVCache(model, wl.batch, wl.capacity)
+    stream = torch.cuda.Stream()
+    cache.set_stream(stream.cuda_stream)
+    samp = wl.sampling()
+    pd = torch.from_numpy(W.prompts(wl).astype(np.int32)).cuda()
+    od = torch.zeros((wl.batch, wl.n_new), dtype=torch.int32, device="cuda")
+
+    def job(n_new):
+        cache.generate_async(pd.data_ptr(), wl.prompt_len, n_new, samp, None, od.data_ptr())
+
+    def timed(n_new, reps):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        if world > 1:
+            tdist.barrier()
+        torch.cuda.synchronize()
+        for k in range(reps):
+            with torch.cuda.stream(stream):
+                evs[k][0].record(stream)
+            job(n_new)
+            with torch.cuda.stream(stream):
+                evs[k][1].record(stream)
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / reps
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+            tdist.all_reduce(t, op=tdist.ReduceOp.MAX)
+            ms = float(t[0])
+        return ms
+
+    for n in (wl.n_new, 1):   # warm-up (and the graphs of both jobs)
+        job(n)
+    job_ms = timed(wl.n_new, args.steps)
+    pre_ms = timed(1, max(3, min(args.steps, 5)))
+    L = _native.lib()
+    c1, _ = _profile(L, _native, cache, pd.data_ptr(), wl.prompt_len, 1, samp, None, od.data_ptr())
+    c2, _ = _profile(L, _native, cache, pd.data_ptr(), wl.prompt_len, 9, samp, None, od.data_ptr())
+    toks = od.cpu().numpy()
+    out = None
+    if rank == 0:
+        def shares(cl):
+            tot = sum(v["total_ms"] for v in cl.values()) or 1.0
+            return {k: {"ms": round(v["total_ms"], 3), "share": round(v["total_ms"] / tot, 4)} for k, v in cl.items()}
+        step = {k: {f: (c2[k][f] - c1.get(k, {}).get(f, 0.0)) / 8 for f in ("total_ms", "launches", "bytes", "flops")}
+                for k in c2}
+        step = {k: v for k, v in step.items() if v["total_ms"] > 0}
+        ar = step.get("allreduce")
+        out = {"tp_probe": {
+            "world": world, "layers": args.probe_layers, "model": "d6144 h48 F24576 V50257 INT4 (config-5 width)",
+            "batch": wl.batch, "prompt_len": wl.prompt_len, "decode_steps": wl.n_new - 1,
+            "job_ms": round(job_ms, 3), "prefill_ms": round(pre_ms, 3),
+            "decode_step_ms": round((job_ms - pre_ms) / (wl.n_new - 1), 4),
+            "prefill_classes": shares(c1), "decode_step_classes": shares(step),
+            "decode_allreduce_gbs_per_rank": round(ar["bytes"] / (ar["total_ms"] * 1e-3) / 1e9, 1) if ar else None,
+            "how": "CUDA events on the launching stream, max over ranks; classes from eager launches each bracketed "
+                   "by events (prefill alone, and prefill + 8 steps, the difference per step)",
+            "first_tokens": toks[:2, :4].tolist()}}
+    cache.close()
+    model.close()
+    bundle.close()
+    if world > 1:
+        tdist.barrier()
+        tdist.destroy_process_group()
+    if rank == 0:
+        os.remove(path)
+    return out
+
+
 def decode_probe(dz, torch, hbm, layers=2, batch=64, steps=8):
     """The config-4 layer shapes (d 2048, 16 heads of 128, F 8192, V 32000,
     INT8) with a few layers and a smaller batch: a 512-token batched prefill,
@@ -706,7 +812,8 @@ def main():
     ap.add_argument("--no-secondary", action="store_true", help="skip the config-2 line after config 4")
     ap.add_argument("--no-probe", action="store_true", help="skip the config-3 quantized-matmul rows")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline and the CPU matmul column")
-    ap.add_argument("--probe", choices=["qmv", "decode"],
+    ap.add_argument("--probe-layers", type=int, default=2, help="with --probe tp: layers")
+    ap.add_argument("--probe", choices=["qmv", "decode", "tp"],
                     help="run only the C3 quantized-matmul rows, or a few config-4 decode steps (profiling targets)")
     ap.add_argument("--probe-n", type=int, default=0, help="with --probe: one N instead of all three")
     ap.add_argument("--probe-batch", type=int, default=64, help="with --probe decode: sequences")
@@ -724,6 +831,8 @@ def main():
         Ns = (args.probe_n,) if args.probe_n else (4096, 11008, 32000)
         Ms = tuple(int(v) for v in args.probe_m.split(",")) if args.probe_m else (1, 8, 64, 512)
         out = {"quant_matvec": quant_matvec_probe(dz, torch, stream, hbm, bf16, Ns=Ns, Ms=Ms, K=args.probe_k)}
+    elif args.probe == "tp":
+        out = tp_probe(args)
     elif args.probe == "decode":
         import torch
         import dranzer_b200 as dz

@@ -52,7 +52,7 @@ class DzKernelStat(ctypes.Structure):
     _fields_ = [("kind", U32), ("launches", U32), ("total_ms", F64), ("bytes", F64), ("flops", F64)]
 
 
-KERNEL_CLASSES = ["step_begin", "qmv", "attention", "layernorm", "select", "seqgen", "split"]
+KERNEL_CLASSES = ["step_begin", "qmv", "attention", "layernorm", "select", "seqgen", "split", "allreduce"]
 FUSED_PHASES = ["embed", "weight_wait", "qmv", "attention", "layernorm", "select"]
 
 

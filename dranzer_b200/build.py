@@ -20,7 +20,7 @@ NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", 
 CC_FLAGS = ["-O2", "-fPIC", "-std=c11", "-Wall", "-Wextra", "-fno-fast-math", "-ffp-contract=off",
             f"-I{INCLUDE}"]
 
-CUDA_SOURCES = ["dz_cuda.cu", "qmvi.cu", "seqgen.cu", "attn.cu"]
+CUDA_SOURCES = ["dz_cuda.cu", "qmvi.cu", "seqgen.cu", "attn.cu", "pfattn.cu"]
 C_SOURCES = ["dz_host.c"]
 
 

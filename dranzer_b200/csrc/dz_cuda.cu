@@ -30,6 +30,7 @@
 #include "qmvi.cuh"
 #include "arch.cuh"
 #include "attn.cuh"
+#include "pfattn.cuh"
 
 using namespace dz;
 
@@ -316,9 +317,27 @@ static size_t qmv_xf_bytes(const DevQMat& W, int M) {
 }
 // Bytes of scratch the tensor-core GEMM needs for M rows: three limb planes
 // of M x (K rounded up to 128) bytes and the row exponents.
+// Split-K parts of the tensor-core GEMM: a grid of fewer tiles than half the
+// SMs with a long k (32 or more k blocks) gets its k blocks cut into parts
+// (at least eight k blocks each, at most eight parts) so that about one CTA
+// per SM runs; below that k a part's main loop is too short to pay for
+// storing and adding the int64 partial tiles. Off while g_no_split_k is set
+// (callers with a fixed scratch budget).
+static thread_local bool g_no_split_k = false;
+static int ugemm_kparts(const DevQMat& W, int M) {
+    if (g_no_split_k) return 1;
+    const int tiles = ((W.N + UG_BN - 1) / UG_BN) * ((M + UG_BM - 1) / UG_BM);
+    const int nkb = round_up(W.K, UG_BK) / UG_BK;
+    if (2 * tiles > g_num_sms || nkb < 32) return 1;
+    return std::max(1, std::min({g_num_sms / tiles, nkb / 8, 8}));
+}
 static size_t ugemm_scratch_bytes(const DevQMat& W, int M) {
     const size_t kp = (size_t)round_up(W.K, UG_BK);
-    return r256(3 * (size_t)M * kp) + r256((size_t)M * 4);
+    size_t b = r256(3 * (size_t)M * kp) + r256((size_t)M * 4);
+    const int parts = ugemm_kparts(W, M);
+    if (parts > 1)
+        b += (size_t)((W.N + UG_BN - 1) / UG_BN) * ((M + UG_BM - 1) / UG_BM) * parts * UG_BM * UG_BN * 8;
+    return b;
 }
 // Every scratch buffer starts with the GEMV's per-tile counters, shared by
 // all matrices that use the buffer (each launch leaves the counters it used
@@ -397,6 +416,7 @@ static int qms_prepare(int device) {
 #undef DZ_QMV1_ATTR
     DZ_CUDA(dz_qmv1i_set_smem(optin));
     DZ_CUDA(dz_attn_decode_set_smem());
+    DZ_CUDA(dz_pfattn_set_smem());
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UG_SMEM_BYTES));
     DZ_CUDA(cudaFuncSetAttribute(dz_ugemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)UV_SMEM_BYTES));
     // the split runs right before the GEMV (and may share SMs with it): the
@@ -457,6 +477,18 @@ static bool attn_streamed_kernel() {
     static const bool v = [] {
         const char* e = getenv("DZ_ATTN_KERNEL");
         return !(e && strcmp(e, "regs") == 0);
+    }();
+    return v;
+}
+
+// Which causal prefill attention runs for head dimensions 64 and 128: the
+// tensor-core kernel (pfattn.cuh, the default) or the CUDA-core one
+// (dz_attention_prefill_kernel). DZ_PREFILL_ATTN=simt in the environment
+// selects the latter, for comparison; both compute the same attention.
+static bool prefill_attn_tensor_cores() {
+    static const bool v = [] {
+        const char* e = getenv("DZ_PREFILL_ATTN");
+        return !(e && strcmp(e, "simt") == 0);
     }();
     return v;
 }
@@ -598,10 +630,14 @@ constexpr size_t UGEMM_MIN_WEIGHTS = (size_t)1 << 20;
 // The tensor-core GEMM (umma.cuh): limb split, then one CTA per 128 x 128
 // output tile. Returns the launches (2), or 0 when its TMA map cannot be made.
 static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
-                        cudaStream_t st, void* scratch, int* status) {
+                        cudaStream_t st, void* scratch, int* counters, int* status) {
     const int Kp = round_up(W.K, UG_BK);
     int8_t* L = static_cast<int8_t*>(scratch);
     int* shift = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + r256(3 * (size_t)M * Kp));
+    const int parts = ugemm_kparts(W, M);
+    long long* partial = parts > 1 ? reinterpret_cast<long long*>(static_cast<uint8_t*>(scratch) +
+                                                                   r256(3 * (size_t)M * Kp) + r256((size_t)M * 4))
+                                   : nullptr;
     CUtensorMap tmA;
     const cuuint64_t dims[3] = {(cuuint64_t)Kp, (cuuint64_t)M, (cuuint64_t)UG_LIMBS};
     const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)Kp * M};
@@ -626,7 +662,10 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     a.status = status;
     a.ep = ep_in;
     a.ep.row_shift = nullptr;
-    const dim3 grid((unsigned)((W.N + UG_BN - 1) / UG_BN), (unsigned)((M + UG_BM - 1) / UG_BM));
+    a.kparts = parts;
+    a.partial = partial;
+    a.counters = counters;
+    const dim3 grid((unsigned)((W.N + UG_BN - 1) / UG_BN), (unsigned)((M + UG_BM - 1) / UG_BM), (unsigned)parts);
     ProfScope prof(DZ_KERNEL_QMV,
                    (double)W.K * W.N + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N,
                    2.0 * M * W.K * W.N, st);
@@ -720,7 +759,7 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     // small matrices stay on the register-blocked kernel: the GEMM's fixed
     // cost per tile (pipeline fill, tensor-memory drain) would dominate
     if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) {
-        const int n = launch_ugemm(W, X, ldx, M, ep_in, st, scratch, status);
+        const int n = launch_ugemm(W, X, ldx, M, ep_in, st, scratch, counters, status);
         if (n) return n;
     }
     const int KG = W.bits == 8 ? 32 : 64;
@@ -1758,7 +1797,10 @@ extern "C" int dz_cuda_cache_reset(dz_cuda_cache_t* c, const uint8_t* seq_mask) 
 // One decode step for all sequences; returns the number of kernel launches.
 // Sum of every rank's partial [rows x D] product, in place (tensor parallelism).
 static void tp_allreduce(dz_cuda_model_t* m, float* buf, size_t count, cudaStream_t st) {
-    if (m->tp_world > 1) nccl_api()->all_reduce(buf, buf, count, ncclFloat32, ncclSum, m->comm, st);
+    if (m->tp_world <= 1) return;
+    // bytes: what each rank sends over NVLink in a ring all-reduce, 2 (w - 1) / w of the buffer
+    ProfScope prof(DZ_KERNEL_ALLREDUCE, 8.0 * count * (m->tp_world - 1) / m->tp_world, 0, st);
+    nccl_api()->all_reduce(buf, buf, count, ncclFloat32, ncclSum, m->comm, st);
 }
 
 // Launches of one layer pass over R rows and of the output head.
@@ -2282,7 +2324,9 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
                                4.0 * ctx_pairs * hd, st);
                 const dim3 grid((unsigned)((T + PF_QT - 1) / PF_QT), (unsigned)H, (unsigned)ns);
                 const size_t smem = dz_prefill_att_smem(hd);
-                if (mk) {
+                if ((!mk || (!pad && !att)) && (hd == 128 || hd == 64) && prefill_attn_tensor_cores()) {
+                    dz_pfattn_launch(c->pf_q, Kl, Vl, lens, c->pf_concat, T, dl, cap, hd, H, ns, st);
+                } else if (mk) {
                     if (hd == 128)
                         dz_attention_prefill_kernel<4, true><<<grid, PF_THREADS, smem, st>>>(
                             c->pf_q, Kl, Vl, nullptr, c->pf_concat, T, dl, cap, pad, att);
@@ -2804,6 +2848,11 @@ extern "C" int dz_cuda_matmul_quantized_noalloc(const float* A, const dz_cuda_qm
                                                 size_t k, void* stream) {
     if (!q || !A || !C || m == 0 || k != (size_t)q->m.K || m > (1u << 24))
         return fail(DZ_E_INVALID, "matmul_quantized_noalloc: bad arguments (k must equal the matrix rows)");
+    // a fixed budget: no split-K partials (sizing and launch alike)
+    struct NoSplit {
+        NoSplit() { g_no_split_k = true; }
+        ~NoSplit() { g_no_split_k = false; }
+    } no_split;
     const size_t need = qmv_scratch_bytes(q->m, (int)m);
     if (need > (size_t)DZ_NOALLOC_SCRATCH_BYTES)
         return fail(DZ_E_INVALID,

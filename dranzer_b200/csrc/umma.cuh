@@ -45,6 +45,7 @@ constexpr uint32_t UG_TMEM_COLS = 512;           // three 128-column int32 accum
 constexpr size_t UG_SMEM_BYTES = (size_t)UG_STAGES * UG_STAGE_BYTES + 1024 + 256;
 constexpr int UG_ROW_NONFINITE = -0x40000000;    // row exponent marking a non-finite input row
 constexpr int UG_TILE_LD = UG_BN + 4;            // staging tile row stride (floats): 16-byte rows, spread banks
+constexpr int UG_PART_LD = UG_BN + 2;            // split-K int64 staging row stride: 65 16-byte units
 // Largest K for which the int32 limb sums are exact: |q| <= 127, |limb| <=
 // 128, and 131072 * 128 * 127 < 2^31.
 constexpr int UG_MAX_K = 131072;
@@ -55,6 +56,14 @@ struct UgArgs {
     const int* shift;             // [M] -s, or UG_ROW_NONFINITE
     int* status;                  // set to 1 when a wait gave up (may be null)
     QmvEpilogue ep;               // col_scale etc.; row_shift unused
+    // split-K (kparts > 1, grid z = kparts): CTA z takes k blocks
+    // [z nkb / kparts, (z + 1) nkb / kparts) of its tile and stores the
+    // tile's int64 totals as partial[tile][z][UG_BM][UG_BN]; the per-tile
+    // counter (zero between launches) finds the last part, which adds the
+    // parts, finishes the tile and resets the counter
+    int kparts;
+    long long* partial;
+    int* counters;
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -400,10 +409,13 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_warp_kern
     if (lane == 0) shift[r] = bad ? UG_ROW_NONFINITE : -s;
 }
 
-// Columns [n0, n0 + UG_BN) of rows [m0, m0 + UG_BM) from the staging tile
-// through the epilogue (column scale, bias, residual, ReLU, segment routing),
-// four columns per thread with float4 accesses where the addresses allow.
-__device__ __forceinline__ void ug_store_tile(const UgArgs& a, const float* tile, int m0, int n0, bool failed) {
+// Columns [n0, n0 + UG_BN) of rows [m0, m0 + UG_BM) through the epilogue
+// (column scale, bias, residual, activation, segment routing), a warp per
+// row and four columns per lane, float4 accesses where the addresses allow.
+// get4(r0, y) gives this lane's four values of tile rows r0 .. r0 + 3 (a
+// warp takes four rows at a time, so their loads can be in flight together).
+template <typename Get4>
+__device__ __forceinline__ void ug_store_rows(const UgArgs& a, int m0, int n0, Get4 get4) {
     const QmvEpilogue& e = a.ep;
     const int c4 = (threadIdx.x & 31) * 4;   // fixed per thread: blockDim.x is a multiple of 32
     const int n = n0 + c4;
@@ -418,47 +430,63 @@ __device__ __forceinline__ void ug_store_tile(const UgArgs& a, const float* tile
     int sg = 0;
     while (sg + 1 < e.nseg && n >= e.seg_start[sg + 1]) sg++;
     const bool one_seg = nv == 4 && (sg + 1 >= e.nseg || n + 3 < e.seg_start[sg + 1]);
-    for (int r = threadIdx.x >> 5; r < UG_BM; r += UG_THREADS / 32) {
-        const int row = m0 + r;
-        if (row >= a.M) break;
-        float4 t = *reinterpret_cast<const float4*>(tile + r * UG_TILE_LD + c4);
-        if (failed) t.x = t.y = t.z = t.w = __int_as_float(0x7fc00000);   // a failed tile reads NaN
-        float y[4] = {t.x, t.y, t.z, t.w};
+    for (int r0 = (threadIdx.x >> 5) * 4; r0 < UG_BM && m0 + r0 < a.M; r0 += (UG_THREADS / 32) * 4) {
+        float yy[4][4];
+        get4(r0, yy);
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            y[j] = (e.col_scale ? y[j] * sc[j] : y[j]);
-            if (e.bias) y[j] = y[j] + bi[j];
-        }
-        if (e.residual) {
-            const float* rp = e.residual + (long long)row * e.ld_res + n;
+        for (int i = 0; i < 4; i++) {
+            const int row = m0 + r0 + i;
+            if (row >= a.M) break;
+            float* y = yy[i];
 #pragma unroll
-            for (int j = 0; j < 4; j++)
-                if (j < nv) y[j] = y[j] + rp[j];
-        }
-        if (e.act) {
+            for (int j = 0; j < 4; j++) {
+                y[j] = (e.col_scale ? y[j] * sc[j] : y[j]);
+                if (e.bias) y[j] = y[j] + bi[j];
+            }
+            if (e.residual) {
+                const float* rp = e.residual + (long long)row * e.ld_res + n;
 #pragma unroll
-            for (int j = 0; j < 4; j++) y[j] = dz_act(y[j], e.act);
-        }
-        if (one_seg) {
-            long long off = (long long)row * e.seg_ld[sg] + (n - e.seg_start[sg]);
-            if (e.seg_row_off[sg]) off += e.seg_row_off[sg][row];
-            float* dst = e.seg_ptr[sg] + off;
-            if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-                *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+                for (int j = 0; j < 4; j++)
+                    if (j < nv) y[j] = y[j] + rp[j];
+            }
+            if (e.act) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) y[j] = dz_act(y[j], e.act);
+            }
+            if (one_seg) {
+                long long off = (long long)row * e.seg_ld[sg] + (n - e.seg_start[sg]);
+                if (e.seg_row_off[sg]) off += e.seg_row_off[sg][row];
+                float* dst = e.seg_ptr[sg] + off;
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    *reinterpret_cast<float4*>(dst) = make_float4(y[0], y[1], y[2], y[3]);
+                    continue;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) dst[j] = y[j];
                 continue;
             }
-#pragma unroll
-            for (int j = 0; j < 4; j++) dst[j] = y[j];
-            continue;
-        }
-        for (int j = 0; j < nv; j++) {
-            int s2 = 0;
-            while (s2 + 1 < e.nseg && n + j >= e.seg_start[s2 + 1]) s2++;
-            long long off = (long long)row * e.seg_ld[s2] + (n + j - e.seg_start[s2]);
-            if (e.seg_row_off[s2]) off += e.seg_row_off[s2][row];
-            e.seg_ptr[s2][off] = y[j];
+            for (int j = 0; j < nv; j++) {
+                int s2 = 0;
+                while (s2 + 1 < e.nseg && n + j >= e.seg_start[s2 + 1]) s2++;
+                long long off = (long long)row * e.seg_ld[s2] + (n + j - e.seg_start[s2]);
+                if (e.seg_row_off[s2]) off += e.seg_row_off[s2][row];
+                e.seg_ptr[s2][off] = y[j];
+            }
         }
     }
+}
+
+// The same from the fp32 staging tile ([UG_BM][UG_TILE_LD]); a failed tile reads NaN.
+__device__ __forceinline__ void ug_store_tile(const UgArgs& a, const float* tile, int m0, int n0, bool failed) {
+    const int c4 = (threadIdx.x & 31) * 4;
+    ug_store_rows(a, m0, n0, [&](int r0, float (*y)[4]) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float4 t = *reinterpret_cast<const float4*>(tile + (r0 + i) * UG_TILE_LD + c4);
+            if (failed) t.x = t.y = t.z = t.w = __int_as_float(0x7fc00000);
+            y[i][0] = t.x; y[i][1] = t.y; y[i][2] = t.z; y[i][3] = t.w;
+        }
+    });
 }
 
 constexpr int UG_SPLIT_CHUNK = 1024;   // k per block of dz_limb_split_chunk_kernel
@@ -571,9 +599,13 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
     uint64_t* empty = full + UG_STAGES;
     uint64_t* accum = empty + UG_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
-    int* progress = reinterpret_cast<int*>(tmem_slot + 1);   // [0] stages issued, [1] stages consumed, [2] failed
+    // [0] stages issued, [1] stages consumed, [2] failed, [3] last split-K part
+    int* progress = reinterpret_cast<int*>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * UG_BN, m0 = blockIdx.y * UG_BM;
+    // this CTA's k blocks (all of them unless split-K)
+    const int kb0 = (int)(((long long)a.nkb * blockIdx.z) / a.kparts);
+    const int nkb = (int)(((long long)a.nkb * (blockIdx.z + 1)) / a.kparts) - kb0;
     auto stage_a = [&](int s, int limb) { return sm + (size_t)s * UG_STAGE_BYTES + (size_t)limb * UG_A_BYTES; };
     auto stage_b = [&](int s) { return sm + (size_t)s * UG_STAGE_BYTES + (size_t)UG_LIMBS * UG_A_BYTES; };
 
@@ -601,15 +633,16 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
       if (lane == 0) {
         // producer: TMA loads of the three limb tiles and the code tile per k block
         int kb = 0;
-        for (; kb < a.nkb; kb++) {
+        for (; kb < nkb; kb++) {
             const int s = kb % UG_STAGES;
             if (kb >= UG_STAGES && !dz_mbar_wait(&empty[s], (uint32_t)(((kb / UG_STAGES) - 1) & 1))) {
                 progress[2] = 1;
                 break;
             }
             dz_mbar_expect_tx(&full[s], UG_STAGE_BYTES);
-            for (int limb = 0; limb < UG_LIMBS; limb++) ug_tma_3d(stage_a(s, limb), &tmA, kb * UG_BK, m0, limb, &full[s]);
-            ug_tma_4d(stage_b(s), &tmB, 0, 0, kb, blockIdx.x, &full[s]);
+            for (int limb = 0; limb < UG_LIMBS; limb++)
+                ug_tma_3d(stage_a(s, limb), &tmA, (kb0 + kb) * UG_BK, m0, limb, &full[s]);
+            ug_tma_4d(stage_b(s), &tmB, 0, 0, kb0 + kb, blockIdx.x, &full[s]);
         }
         progress[0] = kb;
       }
@@ -619,7 +652,7 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
         // MMA issuer: 3 limbs x 4 k-steps of 32 per stage
         int kb = 0;
         const uint32_t idesc = ug_idesc();
-        for (; kb < a.nkb; kb++) {
+        for (; kb < nkb; kb++) {
             const int s = kb % UG_STAGES;
             if (!dz_mbar_wait(&full[s], (uint32_t)((kb / UG_STAGES) & 1))) {
                 progress[2] = 1;
@@ -645,27 +678,38 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
       __syncwarp();
     } else if (warp >= 4) {
         // epilogue, part 1: thread = row; drain the three accumulators into a
-        // [128][UG_TILE_LD] fp32 staging tile in the pipeline buffers (free
-        // once the accumulator barrier completes)
+        // staging tile in the pipeline buffers (free once the accumulator
+        // barrier completes): fp32 [128][UG_TILE_LD], or with split-K the
+        // int64 totals [128][UG_PART_LD] (exact, so the parts add in any order)
         const int ew = warp - 4;
         bool ok = dz_mbar_wait(accum, 0);
         ug_fence_after();
         const int rl = ew * 32 + lane;
         const int row = m0 + rl;
         const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-        const bool live = row < a.M;
-        const int e = live ? a.shift[row] : 0;
+        const int e = row < a.M ? a.shift[row] : 0;
         if (!ok || progress[2]) {
             if (a.status && lane == 0) atomicExch(a.status, 1);
             ok = false;
             progress[2] = 1;
         }
         float* tile = reinterpret_cast<float*>(sm);
+        long long* srow = reinterpret_cast<long long*>(sm) + (size_t)rl * UG_PART_LD;
         for (int c0 = 0; c0 < UG_BN; c0 += 32) {
             int32_t top[32], mid[32], low[32];
             ug_tmem_ld32(tmem + lane_base + (uint32_t)c0, top);
             ug_tmem_ld32(tmem + lane_base + (uint32_t)(UG_BN + c0), mid);
             ug_tmem_ld32(tmem + lane_base + (uint32_t)(2 * UG_BN + c0), low);
+            if (a.kparts > 1) {
+#pragma unroll
+                for (int c = 0; c < 32; c += 2) {
+                    longlong2 v;
+                    v.x = (long long)top[c] * 65536 + (long long)mid[c] * 256 + (long long)low[c];
+                    v.y = (long long)top[c + 1] * 65536 + (long long)mid[c + 1] * 256 + (long long)low[c + 1];
+                    *reinterpret_cast<longlong2*>(srow + c0 + c) = v;
+                }
+                continue;
+            }
 #pragma unroll
             for (int q = 0; q < 8; q++) {
                 float y[4];
@@ -683,9 +727,78 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
 
     ug_fence_before();
     __syncthreads();
+    bool finish = true;
+    if (a.kparts > 1) {
+        // split-K: every part stores its totals (all warps, a warp per row,
+        // 32 bytes per lane: 1 KB contiguous per store pair); the part that
+        // arrives last adds the parts and finishes
+        int* last = progress + 3;
+        const int tile_id = blockIdx.y * gridDim.x + blockIdx.x;
+        const int c4 = lane * 4;
+        long long* part = a.partial + ((size_t)tile_id * a.kparts + blockIdx.z) * UG_BM * UG_BN;
+        const long long* stile = reinterpret_cast<const long long*>(sm);
+        for (int r = warp; r < UG_BM; r += UG_THREADS / 32) {
+            const longlong2 u0 = *reinterpret_cast<const longlong2*>(stile + (size_t)r * UG_PART_LD + c4);
+            const longlong2 u1 = *reinterpret_cast<const longlong2*>(stile + (size_t)r * UG_PART_LD + c4 + 2);
+            *reinterpret_cast<longlong2*>(part + (size_t)r * UG_BN + c4) = u0;
+            *reinterpret_cast<longlong2*>(part + (size_t)r * UG_BN + c4 + 2) = u1;
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int old = atomicAdd(&a.counters[tile_id], 1);
+            *last = old == a.kparts - 1;
+            if (*last) a.counters[tile_id] = 0;   // zero again for the next launch
+        }
+        __syncthreads();
+        finish = *last != 0;
+        if (finish) {
+            __threadfence();
+            // the parts' totals added (this part's from shared memory, the
+            // others' from global), converted to fp32 once and 2^-s applied,
+            // straight into the epilogue: a warp per row, four rows at a time
+            const long long* base = a.partial + (size_t)tile_id * a.kparts * UG_BM * UG_BN;
+            const int own = (int)blockIdx.z;
+            ug_store_rows(a, m0, n0, [&](int r0, float (*y)[4]) {
+                long long v[4][4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const longlong2 u0 = *reinterpret_cast<const longlong2*>(stile + (size_t)(r0 + i) * UG_PART_LD + c4);
+                    const longlong2 u1 =
+                        *reinterpret_cast<const longlong2*>(stile + (size_t)(r0 + i) * UG_PART_LD + c4 + 2);
+                    v[i][0] = u0.x; v[i][1] = u0.y; v[i][2] = u1.x; v[i][3] = u1.y;
+                }
+                for (int z = 0; z < a.kparts; z++) {
+                    if (z == own) continue;
+                    const long long* pz = base + (size_t)z * UG_BM * UG_BN + c4;
+                    longlong2 w[4][2];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        w[i][0] = *reinterpret_cast<const longlong2*>(pz + (size_t)(r0 + i) * UG_BN);
+                        w[i][1] = *reinterpret_cast<const longlong2*>(pz + (size_t)(r0 + i) * UG_BN + 2);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        v[i][0] += w[i][0].x; v[i][1] += w[i][0].y; v[i][2] += w[i][1].x; v[i][3] += w[i][1].y;
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const int row = m0 + r0 + i;
+                    const int e = row < a.M ? a.shift[row] : 0;
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        y[i][j] = dz_mul_pow2(__ll2float_rn(v[i][j]), e);
+                        if (e == UG_ROW_NONFINITE || progress[2]) y[i][j] = __int_as_float(0x7fc00000);
+                    }
+                }
+            });
+            finish = false;   // stored
+        }
+    }
     // epilogue, part 2, all warps: one warp per output row, lane = 4 columns,
     // so each store instruction writes 512 contiguous bytes
-    ug_store_tile(a, reinterpret_cast<const float*>(sm), m0, n0, progress[2] != 0);
+    if (finish) ug_store_tile(a, reinterpret_cast<const float*>(sm), m0, n0, progress[2] != 0);
 
     // teardown: copies and MMAs in flight finish before the shared memory and
     // the tensor memory are released

@@ -215,12 +215,13 @@ enum {
     DZ_KERNEL_LAYERNORM = 3,
     DZ_KERNEL_SELECT = 4,     /* greedy / top-k / top-p selection */
     DZ_KERNEL_SEQGEN = 5,     /* fused whole-generation kernel */
-    DZ_KERNEL_SPLIT = 6,      /* activation rows -> bf16 hi/mid/lo MMA operands */
-    DZ_KERNEL_CLASSES = 7,
+    DZ_KERNEL_SPLIT = 6,      /* activation rows -> integer limbs / fp16 parts, the MMA operands */
+    DZ_KERNEL_ALLREDUCE = 7,  /* tensor parallelism: NCCL sum of the ranks' partial products */
+    DZ_KERNEL_CLASSES = 8,
     /* Phases inside the fused kernel, timed on its first thread block with the
      * device's global timer (launches = 0, total_ms = time in the phase). */
-    DZ_PHASE_EMBED = 7, DZ_PHASE_WAIT = 8, DZ_PHASE_QMV = 9, DZ_PHASE_ATTENTION = 10,
-    DZ_PHASE_NORM = 11, DZ_PHASE_SELECT = 12, DZ_PROFILE_SLOTS = 13
+    DZ_PHASE_EMBED = 8, DZ_PHASE_WAIT = 9, DZ_PHASE_QMV = 10, DZ_PHASE_ATTENTION = 11,
+    DZ_PHASE_NORM = 12, DZ_PHASE_SELECT = 13, DZ_PROFILE_SLOTS = 14
 };
 
 typedef struct {

@@ -94,10 +94,12 @@ def test_masked_forward_properties(gpu, oracle):
     cache = gpu.KVCache(model, B)
     cache.set_prefill(gpu.PREFILL_BATCHED)
     want = cache.prefill(ids)
-    # no masks: the batched prefill's arithmetic, bit for bit; all-ones masks too
+    # no masks: the batched prefill's arithmetic, bit for bit; all-ones masks
+    # (the masked attention kernel) within fp32 noise of it
     np.testing.assert_array_equal(cache.forward_masked(ids), want)
-    np.testing.assert_array_equal(cache.forward_masked(ids, np.ones((B, T), np.uint8)), want)
-    np.testing.assert_array_equal(cache.forward_masked(ids, None, np.ones((B, T, T), np.uint8)), want)
+    for p, a in ((np.ones((B, T), np.uint8), None), (None, np.ones((B, T, T), np.uint8))):
+        got = cache.forward_masked(ids, p, a)
+        assert np.abs(got - want).max() <= 1e-5 * np.abs(want).max()
     # the rings are left empty: the next step is position 0
     first = cache.forward_tokens(ids[:, 0])
     fresh = gpu.KVCache(model, B)

@@ -211,3 +211,37 @@ def test_matmul_tensor_core_gemv_dynamic_range_and_nonfinite(gpu, oracle):
         assert np.isnan(c[9]).all() and not np.isfinite(c[3]).any()
         assert np.isfinite(np.delete(c, [3, 9], axis=0)).all()
         q.close()
+
+
+@pytest.mark.parametrize("shape", [(256, 2048, 2048), (96, 8192, 2048), (64, 4096, 4096), (64, 4096, 1000)])
+@pytest.mark.parametrize("bits", [8, 4])
+def test_split_k_gemm_is_bit_identical(gpu, oracle, shape, bits):
+    """Grids of fewer 128 x 128 tiles than half the SMs run split-K (the
+    tile's k blocks in parts, int64 partial totals added by the last part).
+    The totals are exact integers, so the result equals the unsplit GEMM's
+    (the allocation-free entry point never splits) bit for bit, and the
+    reference's tolerance against the oracle."""
+    import torch
+    from dranzer_b200 import _native
+    L = _native.lib()
+    m, k, n = shape
+    rng = np.random.RandomState(m + k + n + bits)
+    w = (rng.randn(k, n) * 0.02).astype(np.float32)
+    a = rng.randn(m, k).astype(np.float32)
+    q = gpu.QuantizedWeightMatrix.encode(w, bits)
+    ad = torch.from_numpy(a).cuda()
+    c_split = torch.zeros((m, n), dtype=torch.float32, device="cuda")
+    c_plain = torch.full((m, n), float("nan"), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    for _ in range(2):   # the per-tile counters are zero again after a launch
+        _native.check(L.dz_cuda_matmul_quantized_async(ad.data_ptr(), q.handle, c_split.data_ptr(), m, k,
+                                                       stream.cuda_stream), "async")
+        _native.check(L.dz_cuda_matmul_quantized_noalloc(ad.data_ptr(), q.handle, c_plain.data_ptr(), m, k,
+                                                         stream.cuda_stream), "noalloc")
+        stream.synchronize()
+        np.testing.assert_array_equal(c_split.cpu().numpy().view(np.uint32), c_plain.cpu().numpy().view(np.uint32))
+    s, p = oracle.quantize_pack(w, bits, 2)
+    ref = oracle.matmul_quantized(a, k, n, s, p, bits, 2)
+    ok, err = _tol_ok(c_split.cpu().numpy(), ref)
+    assert ok, err
+    q.close()
