@@ -643,14 +643,32 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     const cuuint64_t strides[2] = {(cuuint64_t)Kp, (cuuint64_t)Kp * M};
     const cuuint32_t box[3] = {UG_BK, UG_BM, 1};
     if (!encode_u8_map(&tmA, L, 3, dims, strides, box)) return 0;
+    // the split and the GEMM are programmatic dependents of the kernels
+    // before them (each waits, griddepcontrol.wait, before it reads what they
+    // wrote or writes what they read), so launch latency and the GEMM's
+    // prologue and first weight loads overlap the kernel ahead
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
     {
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 3.0 * M * Kp, 0, st);
         // a warp per row from one wave of rows on (fewer block barriers per byte)
-        if (M >= 2 * g_num_sms)
-            dz_limb_split_warp_kernel<<<(unsigned)((M + UG_SPLIT_WARP_ROWS - 1) / UG_SPLIT_WARP_ROWS), 256, 0, st>>>(
-                X, ldx, W.k_scale, M, W.K, Kp, L, shift);
-        else
-            dz_limb_split_kernel<<<(unsigned)M, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
+        const bool warp_rows = M >= 2 * g_num_sms;
+        cudaLaunchConfig_t sc;
+        memset(&sc, 0, sizeof(sc));
+        sc.gridDim = dim3(warp_rows ? (unsigned)((M + UG_SPLIT_WARP_ROWS - 1) / UG_SPLIT_WARP_ROWS) : (unsigned)M);
+        sc.blockDim = dim3(256);
+        sc.stream = st;
+        sc.attrs = pdl;
+        sc.numAttrs = 1;
+        if (cudaLaunchKernelEx(&sc, warp_rows ? dz_limb_split_warp_kernel : dz_limb_split_kernel, X, ldx, W.k_scale,
+                               M, W.K, Kp, L, shift) != cudaSuccess) {
+            (void)cudaGetLastError();
+            if (warp_rows)
+                dz_limb_split_warp_kernel<<<sc.gridDim, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
+            else
+                dz_limb_split_kernel<<<sc.gridDim, 256, 0, st>>>(X, ldx, W.k_scale, M, W.K, Kp, L, shift);
+        }
     }
     UgArgs a;
     memset(&a, 0, sizeof(a));
@@ -669,7 +687,18 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     ProfScope prof(DZ_KERNEL_QMV,
                    (double)W.K * W.N + (double)W.scale_bytes + 4.0 * M * W.K + 4.0 * M * W.N,
                    2.0 * M * W.K * W.N, st);
-    dz_ugemm_kernel<<<grid, UG_THREADS, UG_SMEM_BYTES, st>>>(tmA, W.tm_kn, a);
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(UG_THREADS);
+    cfg.dynamicSmemBytes = UG_SMEM_BYTES;
+    cfg.stream = st;
+    cfg.attrs = pdl;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, dz_ugemm_kernel, tmA, W.tm_kn, a) != cudaSuccess) {
+        (void)cudaGetLastError();
+        dz_ugemm_kernel<<<grid, UG_THREADS, UG_SMEM_BYTES, st>>>(tmA, W.tm_kn, a);
+    }
     return 2;
 }
 

@@ -276,6 +276,12 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_kernel(co
                                                             int8_t* __restrict__ L, int* __restrict__ shift) {
     __shared__ float wred[8];
     __shared__ int wbad[8];
+    // launched as a programmatic dependent of the previous kernel (a GEMM
+    // that may still read this scratch's limbs): the GEMM after this split
+    // may launch now, and nothing here is read or written before the
+    // previous kernel completed
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int r = blockIdx.x;
     const float* x = X + (long long)r * ldx;
     if (blockDim.x == 256 && K <= UG_SPLIT_REG_K && (K & 3) == 0 &&
@@ -344,6 +350,9 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_warp_kern
                                                                  const float* __restrict__ k_scale, int M, int K,
                                                                  int Kp, int8_t* __restrict__ L,
                                                                  int* __restrict__ shift) {
+    // a programmatic dependent, as dz_limb_split_kernel
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int lane = threadIdx.x & 31;
     const int r = blockIdx.x * UG_SPLIT_WARP_ROWS + (threadIdx.x >> 5);
     if (r >= M) return;
@@ -592,6 +601,12 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(256) dz_limb_split_chunk_ker
 
 DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
     dz_ugemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, UgArgs a) {
+    // launched as a programmatic dependent of its limb split: the weight
+    // tiles of the first stages load before the split grid completes; the
+    // limbs, row exponents and epilogue inputs are read only after
+    // griddepcontrol.wait. The next call's split may launch now (it waits for
+    // this grid before touching memory).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     extern __shared__ __align__(1024) uint8_t ug_raw[];
     const uint32_t raw = dz_smem_addr(ug_raw);
     uint8_t* sm = ug_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -632,6 +647,13 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
     if (warp == 0) {
       if (lane == 0) {
         // producer: TMA loads of the three limb tiles and the code tile per k block
+        // the first stages' weight tiles go out before the split is waited for
+        const int pre = nkb < UG_STAGES ? nkb : UG_STAGES;
+        for (int kb = 0; kb < pre; kb++) {
+            dz_mbar_expect_tx(&full[kb], UG_STAGE_BYTES);
+            ug_tma_4d(stage_b(kb), &tmB, 0, 0, kb0 + kb, blockIdx.x, &full[kb]);
+        }
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         int kb = 0;
         for (; kb < nkb; kb++) {
             const int s = kb % UG_STAGES;
@@ -639,10 +661,12 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
                 progress[2] = 1;
                 break;
             }
-            dz_mbar_expect_tx(&full[s], UG_STAGE_BYTES);
+            if (kb >= pre) {
+                dz_mbar_expect_tx(&full[s], UG_STAGE_BYTES);
+                ug_tma_4d(stage_b(s), &tmB, 0, 0, kb0 + kb, blockIdx.x, &full[s]);
+            }
             for (int limb = 0; limb < UG_LIMBS; limb++)
                 ug_tma_3d(stage_a(s, limb), &tmA, (kb0 + kb) * UG_BK, m0, limb, &full[s]);
-            ug_tma_4d(stage_b(s), &tmB, 0, 0, kb0 + kb, blockIdx.x, &full[s]);
         }
         progress[0] = kb;
       }
@@ -684,6 +708,7 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
         const int ew = warp - 4;
         bool ok = dz_mbar_wait(accum, 0);
         ug_fence_after();
+        asm volatile("griddepcontrol.wait;" ::: "memory");   // the split's exponents (and epilogue inputs)
         const int rl = ew * 32 + lane;
         const int row = m0 + rl;
         const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
@@ -725,6 +750,7 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
         }
     }
 
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // every thread: the split grid's writes are visible
     ug_fence_before();
     __syncthreads();
     bool finish = true;
