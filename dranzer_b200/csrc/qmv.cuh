@@ -37,6 +37,24 @@ __device__ __forceinline__ float dz_act(float y, int act) {
     return y;
 }
 
+// The output segment holding column n. Only constant indices into the
+// epilogue's arrays: a kernel parameter indexed with a run-time value has to
+// be addressable, and every access through it then becomes a generic load.
+struct DzSeg {
+    float* ptr;
+    long long ld;
+    const int* row_off;
+    int start, end;
+};
+__device__ __forceinline__ DzSeg dz_seg_of(const QmvEpilogue& e, int n) {
+    DzSeg s{e.seg_ptr[0], e.seg_ld[0], e.seg_row_off[0], e.seg_start[0], e.nseg > 1 ? e.seg_start[1] : 0x7fffffff};
+    if (e.nseg > 1 && n >= e.seg_start[1])
+        s = DzSeg{e.seg_ptr[1], e.seg_ld[1], e.seg_row_off[1], e.seg_start[1], e.nseg > 2 ? e.seg_start[2] : 0x7fffffff};
+    if (e.nseg > 2 && n >= e.seg_start[2])
+        s = DzSeg{e.seg_ptr[2], e.seg_ld[2], e.seg_row_off[2], e.seg_start[2], 0x7fffffff};
+    return s;
+}
+
 __device__ __forceinline__ void dz_qmv_store_row(const QmvEpilogue& e, int M, int N, int m, int n, float acc) {
     if (m >= M || n >= N) return;
     if (e.row_shift) {   // acc * 2^row_shift[m], exact for normal results
@@ -52,11 +70,10 @@ __device__ __forceinline__ void dz_qmv_store_row(const QmvEpilogue& e, int M, in
     if (e.bias) y = y + e.bias[n];
     if (e.residual) y = y + e.residual[(long long)m * e.ld_res + n];
     if (e.act) y = dz_act(y, e.act);
-    int s = 0;
-    while (s + 1 < e.nseg && n >= e.seg_start[s + 1]) s++;
-    long long off = (long long)m * e.seg_ld[s] + (n - e.seg_start[s]);
-    if (e.seg_row_off[s]) off += e.seg_row_off[s][m];
-    e.seg_ptr[s][off] = y;
+    const DzSeg sg = dz_seg_of(e, n);
+    long long off = (long long)m * sg.ld + (n - sg.start);
+    if (sg.row_off) off += sg.row_off[m];
+    sg.ptr[off] = y;
 }
 
 }  // namespace dz
