@@ -513,10 +513,11 @@ static bool qmv1i_plan(const DevQMat& W, int M, Qmv1iPlan* p) {
     const long long per_min = (long long)(W.ntiles / p->G) * W.nkg / WP;
     p->max_parts =
         per_min >= 1 ? (int)std::min<long long>(WP, std::max<long long>(1, (W.nkg - 2) / per_min + 2)) : WP;
-    const size_t fixed = dz_qmv1i_smem_bytes(0, WP, p->tab_bytes, p->max_tiles, p->max_parts);
+    if ((long long)p->max_tiles * W.nkg * WP >= (1LL << 31)) return false;   // the kernel's 32-bit range arithmetic
+    const size_t fixed = dz_qmv1i_smem_bytes(0, WP, p->tab_bytes, p->max_tiles, p->max_parts, M);
     if (fixed + (size_t)WP * QMS_STAGES * 512 > (size_t)g_smem_optin) return false;
     p->pk = (int)std::min<size_t>(16, ((size_t)g_smem_optin - fixed) / ((size_t)WP * QMS_STAGES * 512));
-    p->smem = dz_qmv1i_smem_bytes(p->pk, WP, p->tab_bytes, p->max_tiles, p->max_parts);
+    p->smem = dz_qmv1i_smem_bytes(p->pk, WP, p->tab_bytes, p->max_tiles, p->max_parts, M);
     return true;
 }
 

@@ -59,16 +59,24 @@ struct Qmv1iArgs {
 // Largest K for which the int32 limb sums of biased codes are exact.
 constexpr int QI_MAX_K = 65536;
 
-// The B-fragment table: per pair of k-tiles, 32 lanes x two words.
+// The B-fragment table: per pair of k-tiles, 32 lanes x two words, pairs
+// QI_PAIR_WORDS apart. The 8 words of padding put the four pairs that one
+// warp's stores meet (8 k-tiles) on different banks when the table is built.
+constexpr int QI_PAIR_WORDS = 72;
 __host__ __device__ constexpr unsigned dz_qmv1i_tab_bytes(int nkg, int KT) {
-    return (unsigned)nkg * KT / 2 * 256;
+    return (unsigned)nkg * KT / 2 * QI_PAIR_WORDS * 4;
 }
 
+// Shared memory: rings, table, tile slots and counters, barriers, row
+// shifts and sums, reduction scratch, a copy of the epilogue's parameters,
+// then its column scales, biases and M rows of residuals for the CTA's
+// columns (max_tiles * 16 each) and the output segments' row offsets
+// (3 segments x 2 rows).
 __host__ __device__ constexpr size_t dz_qmv1i_smem_bytes(int pk, int W, unsigned tab_bytes, int max_tiles,
-                                                         int max_parts) {
+                                                         int max_parts, int M) {
     return (size_t)W * QMS_STAGES * pk * 512 + tab_bytes + (size_t)max_tiles * max_parts * 32 * 8 +
            (size_t)((max_tiles + 3) & ~3) * 4 + (size_t)W * QMS_STAGES * 8 + 16 * 4 + 2 * 8 + 32 * 4 + 32 * 4 +
-           32 * 8;
+           32 * 8 + sizeof(QmvEpilogue) + (size_t)(2 + M) * max_tiles * 16 * 4 + 6 * 4;
 }
 
 // D += A (16 x 32, u8 codes, row) . B (32 x 8, s8 limbs, col), int32.
@@ -81,77 +89,182 @@ __device__ __forceinline__ void dz_imma(int (&d)[4], uint32_t a0, uint32_t a1, u
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b.x), "r"(b.y));
 }
 
-// Limbs of row r of M into the B-fragment table: for k-tile kt and t, the
-// limb words of k = 16 kt + (2t, 2t+8, 2t+1, 2t+9) (zero past K) go to lanes
-// g = 3r + limb, word kt & 1 of pair kt / 2; the last row also zeroes lanes
-// g >= 3M. Sets rsh[r] (-s, or UG_ROW_NONFINITE) and sumx[r] = sum_k X.
-__device__ __forceinline__ void dz_qmv1i_split_row(const float* __restrict__ x, const float* __restrict__ k_scale,
-                                                   int K, int nkt, int r, int M, uint32_t* __restrict__ tab,
-                                                   int* __restrict__ rsh, long long* __restrict__ sumx, float* wred,
-                                                   int* wbad, long long* wsum) {
-    float m = 0.0f;
-    int bad = 0;
-#pragma unroll 4
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        float v = x[k];
-        if (k_scale) v *= k_scale[k];
-        if (!(fabsf(v) <= 3.402823466e38f)) bad = 1;
-        else m = fmaxf(m, fabsf(v));
-    }
+// The activation split of the matvec, in two halves around the issue of the
+// weight ring's remaining copies.
+//
+// Entry e of a row covers k = k0, k0 + 8, k0 + 1, k0 + 9 with
+// k0 = 16 (e / 4) + 2 (e % 4): k-tile kt = e / 4 and t = e % 4 of the
+// B-fragment table. Thread i keeps entries i + j blockDim.x (j < QI_CE) of
+// every row in registers: the loads all go out at once, before the ring's
+// remaining copies, so that they do not wait in the memory queues behind
+// the weight stream, and both passes (row maximum, then digits) read the
+// registers. Entries past the cache (K above 4 QI_CE blockDim.x) are read
+// again in each pass.
+constexpr int QI_CE = 4;
+
+template <int MR>
+struct QiSplitRegs {
+    float v[MR][QI_CE][4];
+};
+
+__device__ __forceinline__ float dz_qmv1i_x(const Qmv1iArgs& a, int r, int k) {
+    float v = a.X[(long long)r * a.ldx + k];
+    if (a.k_scale) v *= a.k_scale[k];
+    return v;
+}
+
+// First half: the loads of the cached entries (zero past K and past M).
+template <int MR>
+__device__ __forceinline__ void dz_qmv1i_split_load(const Qmv1iArgs& a, int nent, QiSplitRegs<MR>& R) {
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        bad |= __shfl_xor_sync(0xffffffffu, bad, off);
-    }
-    __syncthreads();   // wred / wsum may still be read for the previous row
-    if ((threadIdx.x & 31) == 0) {
-        wred[threadIdx.x >> 5] = m;
-        wbad[threadIdx.x >> 5] = bad;
-    }
-    __syncthreads();
-    float amax = 0.0f;
-    for (int w = 0; w < (int)(blockDim.x >> 5); w++) {
-        amax = fmaxf(amax, wred[w]);
-        bad |= wbad[w];
-    }
-    const int s = amax > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(amax) : 0;
-    long long sx = 0;
-    for (int e = threadIdx.x; e < nkt * 4; e += blockDim.x) {
-        const int k0 = (e >> 2) * 16 + 2 * (e & 3);
-        const int ks[4] = {k0, k0 + 8, k0 + 1, k0 + 9};
-        uint32_t l4 = 0, m4 = 0, t4 = 0;
+    for (int r = 0; r < MR; r++)
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
-            int X = 0;
-            if (ks[b] < K) {
-                float v = x[ks[b]];
-                if (k_scale) v *= k_scale[ks[b]];
-                X = ug_fixed(v, s);
+        for (int j = 0; j < QI_CE; j++) {
+            const int e = threadIdx.x + j * blockDim.x;
+            const int k0 = (e >> 2) * 16 + 2 * (e & 3);
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int k = k0 + 8 * (b & 1) + (b >> 1);
+                R.v[r][j][b] = (r < a.M && e < nent && k < a.K) ? dz_qmv1i_x(a, r, k) : 0.0f;
             }
-            sx += X;
-            uint32_t dt, dm, dl;
-            ug_digits(X, dt, dm, dl);
-            l4 |= dl << (8 * b);
-            m4 |= dm << (8 * b);
-            t4 |= dt << (8 * b);
         }
-        const int kt = e >> 2, t = e & 3;
-        uint32_t* base = tab + (size_t)(kt >> 1) * 64 + t * 2 + (kt & 1);
-        base[(3 * r + 0) * 8] = l4;
-        base[(3 * r + 1) * 8] = m4;
-        base[(3 * r + 2) * 8] = t4;
-        if (r == M - 1)
-            for (int g = 3 * M; g < 8; g++) base[g * 8] = 0u;
+}
+
+// Second half: per row the largest magnitude (block-wide), the shift s with
+// max |x 2^s| in [2^21, 2^22), the digits X = 65536 top + 256 mid + low of
+// every k into the table (lanes g = 3r + limb, word kt & 1 of pair kt / 2;
+// lanes g >= 3M zero), rsh[r] (-s, or UG_ROW_NONFINITE) and
+// sumx[r] = sum_k X. Ends with the table, rsh and sumx written (block
+// barrier).
+template <int MR, int W>
+__device__ __forceinline__ void dz_qmv1i_split_finish(const Qmv1iArgs& a, int nent, const QiSplitRegs<MR>& R,
+                                                      uint32_t* __restrict__ tab, int* __restrict__ rsh,
+                                                      long long* __restrict__ sumx, float* wred, int* wbad,
+                                                      long long* wsum) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float m[MR];
+    int bad[MR];
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+        m[r] = 0.0f;
+        bad[r] = 0;
+#pragma unroll
+        for (int j = 0; j < QI_CE; j++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const float v = R.v[r][j][b];
+                if (!(fabsf(v) <= 3.402823466e38f)) bad[r] = 1;
+                else m[r] = fmaxf(m[r], fabsf(v));
+            }
+    }
+    for (int e = threadIdx.x + QI_CE * blockDim.x; e < nent; e += blockDim.x) {
+        const int k0 = (e >> 2) * 16 + 2 * (e & 3);
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int k = k0 + 8 * (b & 1) + (b >> 1);
+                if (r >= a.M || k >= a.K) continue;
+                const float v = dz_qmv1i_x(a, r, k);
+                if (!(fabsf(v) <= 3.402823466e38f)) bad[r] = 1;
+                else m[r] = fmaxf(m[r], fabsf(v));
+            }
     }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) sx += __shfl_xor_sync(0xffffffffu, sx, off);
-    if ((threadIdx.x & 31) == 0) wsum[threadIdx.x >> 5] = sx;
+    for (int r = 0; r < MR; r++) {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            m[r] = fmaxf(m[r], __shfl_xor_sync(0xffffffffu, m[r], off));
+            bad[r] |= __shfl_xor_sync(0xffffffffu, bad[r], off);
+        }
+        if (lane == 0) {
+            wred[r * W + warp] = m[r];
+            wbad[r * W + warp] = bad[r];
+        }
+    }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    int sh[MR];
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+        float amax = 0.0f;
+        for (int w = 0; w < W; w++) {
+            amax = fmaxf(amax, wred[r * W + w]);
+            bad[r] |= wbad[r * W + w];
+        }
+        sh[r] = amax > 0.0f ? (UG_X_BITS - 1) - dz_ilogb(amax) : 0;
+    }
+    long long sx[MR];
+#pragma unroll
+    for (int r = 0; r < MR; r++) sx[r] = 0;
+    // digits of one entry of every row, and the zero lanes. X = rint(x 2^s)
+    // needs no clamp (|x 2^s| < 2^22 by the choice of s) and a non-finite x
+    // gives 0, as ug_fixed. With Y = X + 0x8080 the balanced base-256 digits
+    // of ug_digits are (byte 0 of Y) - 128, (byte 1 of Y) - 128 and Y >> 16,
+    // so the limbs of four k are byte permutes of the four Y.
+    auto put = [&](int e, const float (&v)[MR][4]) {
+        const int kt = e >> 2, t = e & 3;
+        uint32_t* base = tab + (size_t)(kt >> 1) * QI_PAIR_WORDS + t * 2 + (kt & 1);
+#pragma unroll
+        for (int r = 0; r < MR; r++) {
+            if (r >= a.M) break;
+            uint32_t Y[4];
+            int xs = 0;
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const float f = v[r][b];
+                const int X = fabsf(f) <= 3.402823466e38f ? __float2int_rn(dz_mul_pow2(f, sh[r])) : 0;
+                xs += X;
+                Y[b] = (uint32_t)(X + 0x8080);
+            }
+            sx[r] += xs;
+            const uint32_t l4 = __byte_perm(__byte_perm(Y[0], Y[1], 0x0040), __byte_perm(Y[2], Y[3], 0x0040), 0x5410) ^
+                                0x80808080u;
+            const uint32_t m4 = __byte_perm(__byte_perm(Y[0], Y[1], 0x0051), __byte_perm(Y[2], Y[3], 0x0051), 0x5410) ^
+                                0x80808080u;
+            const uint32_t t4 = __byte_perm(__byte_perm(Y[0], Y[1], 0x0062), __byte_perm(Y[2], Y[3], 0x0062), 0x5410);
+            base[(3 * r + 0) * 8] = l4;
+            base[(3 * r + 1) * 8] = m4;
+            base[(3 * r + 2) * 8] = t4;
+        }
+        for (int g = 3 * a.M; g < 8; g++) base[g * 8] = 0u;
+    };
+#pragma unroll
+    for (int j = 0; j < QI_CE; j++) {
+        const int e = threadIdx.x + j * blockDim.x;
+        if (e >= nent) break;
+        float v[MR][4];
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) v[r][b] = R.v[r][j][b];
+        put(e, v);
+    }
+    for (int e = threadIdx.x + QI_CE * blockDim.x; e < nent; e += blockDim.x) {
+        const int k0 = (e >> 2) * 16 + 2 * (e & 3);
+        float v[MR][4];
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+#pragma unroll
+            for (int b = 0; b < 4; b++) {
+                const int k = k0 + 8 * (b & 1) + (b >> 1);
+                v[r][b] = (r < a.M && k < a.K) ? dz_qmv1i_x(a, r, k) : 0.0f;
+            }
+        put(e, v);
+    }
+#pragma unroll
+    for (int r = 0; r < MR; r++) {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) sx[r] += __shfl_xor_sync(0xffffffffu, sx[r], off);
+        if (lane == 0) wsum[r * W + warp] = sx[r];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < MR; r++) {   // thread r, constant indices into bad / sh
+        if ((int)threadIdx.x != r || r >= a.M) continue;
         long long tot = 0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += wsum[w];
+        for (int w = 0; w < W; w++) tot += wsum[r * W + w];
         sumx[r] = tot;
-        rsh[r] = bad ? UG_ROW_NONFINITE : -s;
+        rsh[r] = bad[r] ? UG_ROW_NONFINITE : -sh[r];
     }
 }
 
@@ -184,7 +297,8 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
     const int G = gridDim.x;
     const int t0 = (int)((long long)blockIdx.x * a.ntiles / G), t1 = (int)(((long long)blockIdx.x + 1) * a.ntiles / G);
     const int C0 = t0 * a.nkg, L = (t1 - t0) * a.nkg;
-    auto wstart = [&](int w) { return C0 + (int)((long long)w * L / W); };
+    // 32-bit: the host keeps max_tiles * nkg * W below 2^31
+    auto wstart = [&](int w) { return C0 + (w * L) / W; };
     const int my0 = wstart(warp), my1 = wstart(warp + 1);
     struct Cursor {
         int pos, tile, kg;
@@ -230,18 +344,75 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
         issued++;
         istage = istage == QMS_STAGES - 1 ? 0 : istage + 1;
     };
-    if (lane == 0)
-        for (int i = 0; i < QMS_STAGES - 1 && ic.pos < my1; i++) issue();
+    // one piece per warp goes out before the wait; the activation loads go
+    // out right after it, ahead of the ring's other copies (a load queued
+    // behind the whole ring would wait for it to drain), and the ring fills
+    // while the limb table is built
+    if (lane == 0 && ic.pos < my1) issue();
     asm volatile("griddepcontrol.wait;" ::: "memory");
-
-    const int nkt = a.nkg * KT;
-    for (int r = 0; r < a.M; r++)
-        dz_qmv1i_split_row(a.X + (long long)r * a.ldx, a.k_scale, a.K, nkt, r, a.M, tab, rsh, sumx, wred, wbad,
-                           wsum);
-    __syncthreads();   // counters zeroed, limb table, shifts and sums written
+    const int nent = a.nkg * KT * 4;
+    QiSplitRegs<MR> xr;
+    dz_qmv1i_split_load<MR>(a, nent, xr);
+    // the epilogue's per-column inputs of this CTA's columns and the output
+    // segments' row offsets, loaded with the activations: the tile
+    // epilogues then read only shared memory, and the stores are the last
+    // global accesses of a warp
+    const int ncols = (t1 - t0) * 16, EC = a.max_tiles * 16;
+    QmvEpilogue* s_ep = reinterpret_cast<QmvEpilogue*>(wsum + 32);   // the epilogue's parameters
+    float* e_cs = reinterpret_cast<float*>(s_ep + 1);
+    float* e_bi = e_cs + EC;
+    float* e_res = e_bi + EC;                                   // [MR][EC]
+    int* e_roff = reinterpret_cast<int*>(e_res + MR * EC);      // [3 segments][2 rows]
+    auto epi_load = [&](int c, float& cs, float& bi, float (&res)[MR]) {
+        const int n = t0 * 16 + c;
+        const bool ok = c < ncols && n < a.N;
+        cs = (ok && a.ep.col_scale) ? a.ep.col_scale[n] : 0.0f;
+        bi = (ok && a.ep.bias) ? a.ep.bias[n] : 0.0f;
+#pragma unroll
+        for (int r = 0; r < MR; r++)
+            res[r] = (ok && a.ep.residual && r < a.M) ? a.ep.residual[(long long)r * a.ep.ld_res + n] : 0.0f;
+    };
+    float ecs, ebi, eres[MR];
+    epi_load(threadIdx.x, ecs, ebi, eres);
+    int eroff = 0;
+    if (threadIdx.x < 6) {
+        const int si = threadIdx.x >> 1, r = threadIdx.x & 1;
+        const int* ro = si == 0 ? a.ep.seg_row_off[0] : si == 1 ? a.ep.seg_row_off[1] : a.ep.seg_row_off[2];
+        if (si < a.ep.nseg && ro && r < a.M) eroff = ro[r];
+    }
+    if (lane == 0)
+        for (int i = 1; i < QMS_STAGES && ic.pos < my1; i++) issue();
+    dz_qmv1i_split_finish<MR, W>(a, nent, xr, tab, rsh, sumx, wred, wbad, wsum);
+    for (int c = threadIdx.x; c < ncols; c += blockDim.x) {
+        if (c >= (int)blockDim.x) epi_load(c, ecs, ebi, eres);
+        e_cs[c] = ecs;
+        e_bi[c] = ebi;
+#pragma unroll
+        for (int r = 0; r < MR; r++) e_res[r * EC + c] = eres[r];
+    }
+    if (threadIdx.x < 6) e_roff[threadIdx.x] = eroff;
+    if (threadIdx.x == 0) *s_ep = a.ep;
+    __syncthreads();   // counters zeroed, limb table, shifts, sums and epilogue inputs written
+    // the fused epilogue of one output value (dz_qmv_store_row's arithmetic)
+    // (parameters from the shared copy: the first tile end comes when the
+    // memory system is busiest, and a constant-cache miss then waits long)
+    auto store = [&](int r, int n, float v) {
+        if (r >= a.M || n >= a.N) return;
+        const QmvEpilogue& ep = *s_ep;
+        const int c = n - t0 * 16;
+        float y = ep.col_scale ? v * e_cs[c] : v;
+        if (ep.bias) y = y + e_bi[c];
+        if (ep.residual) y = y + e_res[r * EC + c];
+        if (ep.act) y = dz_act(y, ep.act);
+        const int si = (ep.nseg > 1 && n >= ep.seg_start[1]) + (ep.nseg > 2 && n >= ep.seg_start[2]);
+        const DzSeg sg = dz_seg_of(ep, n);
+        long long off = (long long)r * sg.ld + (n - sg.start);
+        if (sg.row_off) off += e_roff[si * 2 + r];
+        sg.ptr[off] = y;
+    };
 
     auto owner_of = [&](int x) {
-        int w = (int)(((long long)(x - C0) * W) / (L > 0 ? L : 1));
+        int w = ((x - C0) * W) / (L > 0 ? L : 1);
         if (w > W - 1) w = W - 1;
         while (w < W - 1 && wstart(w + 1) <= x) w++;
         while (w > 0 && wstart(w) > x) w--;
@@ -267,7 +438,6 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
         for (int q = 0; q < 4; q++) acc[c][q] = 0;
     while (cc.pos < my1) {
         const int n = piece_len(cc);
-        if (!failed && lane == 0 && ic.pos < my1) issue();
         const int stage = cstage;
         if (!failed) {
             int ok = 1;
@@ -284,15 +454,15 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
         if (!failed) {
             const uint4* w4 = reinterpret_cast<const uint4*>(ring + stage * stage_bytes) + lane;
             // B fragments of this lane: one uint2 per pair of k-tiles
-            const uint2* tb = reinterpret_cast<const uint2*>(tab) + (size_t)kg0 * (KT / 2) * 32 + lane;
+            const uint2* tb = reinterpret_cast<const uint2*>(tab) + (size_t)kg0 * (KT / 2) * (QI_PAIR_WORDS / 2) + lane;
 #pragma unroll 2
-            for (int c = 0; c < n; c++, tb += (KT / 2) * 32) {
+            for (int c = 0; c < n; c++, tb += (KT / 2) * (QI_PAIR_WORDS / 2)) {
                 const uint4 w = w4[c * 32];
                 if (BITS == 4) {
                     dz_imma(acc[0], w.x & 0x0F0F0F0Fu, w.x & 0xF0F0F0F0u, w.y & 0x0F0F0F0Fu, w.y & 0xF0F0F0F0u,
                             tb[0]);
                     dz_imma(acc[1], w.z & 0x0F0F0F0Fu, w.z & 0xF0F0F0F0u, w.w & 0x0F0F0F0Fu, w.w & 0xF0F0F0F0u,
-                            tb[32]);
+                            tb[QI_PAIR_WORDS / 2]);
                 } else {
                     const uint32_t a0 = __byte_perm(w.x, w.y, 0x5140), a1 = __byte_perm(w.x, w.y, 0x7362);
                     const uint32_t a2 = __byte_perm(w.z, w.w, 0x5140), a3 = __byte_perm(w.z, w.w, 0x7362);
@@ -301,7 +471,8 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
                 }
             }
         }
-        __syncwarp();   // the stage is free for lane 0 to refill
+        __syncwarp();   // the stage is free: lane 0 refills it with the next piece
+        if (!failed && lane == 0 && ic.pos < my1) issue();
         consumed++;
         if (++cstage == QMS_STAGES) {
             cstage = 0;
@@ -350,8 +521,8 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
                     if (r >= a.M) continue;
                     const float v0 = failed ? __int_as_float(0x7fc00000) : finish(tot[r][0], r);
                     const float v1 = failed ? __int_as_float(0x7fc00000) : finish(tot[r][1], r);
-                    dz_qmv_store_row(a.ep, a.M, a.N, r, n0, v0);
-                    dz_qmv_store_row(a.ep, a.M, a.N, r, n0 + 8, v1);
+                    store(r, n0, v0);
+                    store(r, n0 + 8, v1);
                 }
             }
             continue;
@@ -401,8 +572,8 @@ __global__ void __launch_bounds__(W * 32, 1) dz_qmv1i_kernel(Qmv1iArgs a) {
                     }
                     const float v0 = any_failed ? __int_as_float(0x7fc00000) : finish(s0, r);
                     const float v1 = any_failed ? __int_as_float(0x7fc00000) : finish(s1, r);
-                    dz_qmv_store_row(a.ep, a.M, a.N, r, n0, v0);
-                    dz_qmv_store_row(a.ep, a.M, a.N, r, n0 + 8, v1);
+                    store(r, n0, v0);
+                    store(r, n0 + 8, v1);
                 }
             }
         }
