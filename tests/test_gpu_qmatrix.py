@@ -245,3 +245,19 @@ def test_split_k_gemm_is_bit_identical(gpu, oracle, shape, bits):
     ok, err = _tol_ok(c_split.cpu().numpy(), ref)
     assert ok, err
     q.close()
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_gemv_and_gemm_rows_bit_identical(gpu, bits):
+    """The tensor-core GEMV (16 rows) and the tensor-core GEMM (17 rows)
+    compute the same exact integer sums with one rounding: the 16 shared rows
+    agree bit for bit."""
+    st = np.array([gpu.rng_stream(9, gpu.STREAM_TESTING)], np.uint64)
+    K, N = 4096, 2000
+    x = gpu.synth_gaussian(st, 17 * K, 1.0).reshape(17, K)
+    w = gpu.synth_gaussian(st, K * N, 0.02).reshape(K, N)
+    q = gpu.QuantizedWeightMatrix.encode(w, bits)
+    gemv = q.matmul(x[:16])
+    gemm = q.matmul(x)
+    np.testing.assert_array_equal(gemv, gemm[:16])
+    q.close()
