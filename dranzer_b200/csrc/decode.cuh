@@ -286,17 +286,13 @@ constexpr int LN_THREADS = 256;
 // variance of (x - mean), sigma = sqrtf(var + eps), y = gamma*((x-mean)/sigma)+beta.
 // One block per row. `residual`, when given, is added to x first (the
 // attention sub-block's attn_raw += hidden, src/core/transformer.c:804-806).
-__global__ void __launch_bounds__(LN_THREADS) dz_layernorm_kernel(
-    const float* __restrict__ x, const float* __restrict__ residual, const float* __restrict__ gamma,
-    const float* __restrict__ beta, float* __restrict__ y, int dim, float eps) {
-    __shared__ float red[LN_THREADS / 32];
-    __shared__ float stat;
-    const int r = blockIdx.x;
-    const float* xr = x + (long long)r * dim;
-    const float* rr = residual ? residual + (long long)r * dim : nullptr;
-    float* yr = y + (long long)r * dim;
+//
+// The row statistics and the element formula are shared with the norm that
+// also writes the next product's limbs (umma.cuh), so both give the same y
+// bit for bit.
+__device__ __forceinline__ void dz_ln_stats(const float* __restrict__ xr, const float* __restrict__ rr, int dim,
+                                            float eps, float* red, float* stat, float& mean, float& sd) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
     float s = 0.0f;
     for (int i = threadIdx.x; i < dim; i += LN_THREADS) s += rr ? xr[i] + rr[i] : xr[i];
 #pragma unroll
@@ -306,10 +302,10 @@ __global__ void __launch_bounds__(LN_THREADS) dz_layernorm_kernel(
     if (threadIdx.x == 0) {
         float t = 0.0f;
         for (int w = 0; w < LN_THREADS / 32; w++) t += red[w];
-        stat = t / (float)dim;
+        *stat = t / (float)dim;
     }
     __syncthreads();
-    const float mean = stat;
+    mean = *stat;
     float v = 0.0f;
     for (int i = threadIdx.x; i < dim; i += LN_THREADS) {
         const float d = (rr ? xr[i] + rr[i] : xr[i]) - mean;
@@ -323,13 +319,29 @@ __global__ void __launch_bounds__(LN_THREADS) dz_layernorm_kernel(
     if (threadIdx.x == 0) {
         float t = 0.0f;
         for (int w = 0; w < LN_THREADS / 32; w++) t += red[w];
-        stat = sqrtf(t / (float)dim + eps);
+        *stat = sqrtf(t / (float)dim + eps);
     }
     __syncthreads();
-    const float sd = stat;
+    sd = *stat;
+}
+__device__ __forceinline__ float dz_ln_value(float xv, float mean, float sd, float g, float b) {
+    return g * ((xv - mean) / sd) + b;
+}
+
+__global__ void __launch_bounds__(LN_THREADS) dz_layernorm_kernel(
+    const float* __restrict__ x, const float* __restrict__ residual, const float* __restrict__ gamma,
+    const float* __restrict__ beta, float* __restrict__ y, int dim, float eps) {
+    __shared__ float red[LN_THREADS / 32];
+    __shared__ float stat;
+    const int r = blockIdx.x;
+    const float* xr = x + (long long)r * dim;
+    const float* rr = residual ? residual + (long long)r * dim : nullptr;
+    float* yr = y + (long long)r * dim;
+    float mean, sd;
+    dz_ln_stats(xr, rr, dim, eps, red, &stat, mean, sd);
     for (int i = threadIdx.x; i < dim; i += LN_THREADS) {
         const float xv = rr ? xr[i] + rr[i] : xr[i];
-        yr[i] = gamma[i] * ((xv - mean) / sd) + beta[i];
+        yr[i] = dz_ln_value(xv, mean, sd, gamma[i], beta[i]);
     }
 }
 

@@ -31,6 +31,7 @@
 #include "arch.cuh"
 #include "attn.cuh"
 #include "pfattn.cuh"
+#include "normlimbs.cuh"
 
 using namespace dz;
 
@@ -631,7 +632,7 @@ constexpr size_t UGEMM_MIN_WEIGHTS = (size_t)1 << 20;
 // The tensor-core GEMM (umma.cuh): limb split, then one CTA per 128 x 128
 // output tile. Returns the launches (2), or 0 when its TMA map cannot be made.
 static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
-                        cudaStream_t st, void* scratch, int* counters, int* status) {
+                        cudaStream_t st, void* scratch, int* counters, int* status, bool limbs_ready = false) {
     const int Kp = round_up(W.K, UG_BK);
     int8_t* L = static_cast<int8_t*>(scratch);
     int* shift = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + r256(3 * (size_t)M * Kp));
@@ -651,7 +652,7 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
     cudaLaunchAttribute pdl[1];
     pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
-    {
+    if (!limbs_ready) {   // (else the norm before wrote the limbs and shifts: dz_layernorm_limbs_kernel)
         ProfScope prof(DZ_KERNEL_SPLIT, 4.0 * M * W.K + 3.0 * M * Kp, 0, st);
         // a warp per row from one wave of rows on (fewer block barriers per byte)
         const bool warp_rows = M >= 2 * g_num_sms;
@@ -700,7 +701,7 @@ static int launch_ugemm(const DevQMat& W, const float* X, long long ldx, int M, 
         (void)cudaGetLastError();
         dz_ugemm_kernel<<<grid, UG_THREADS, UG_SMEM_BYTES, st>>>(tmA, W.tm_kn, a);
     }
-    return 2;
+    return limbs_ready ? 1 : 2;
 }
 
 // The tensor-core GEMV for M <= 16 (umma.cuh): chunked limb split, then the
@@ -778,8 +779,10 @@ static int launch_ugemv(const DevQMat& W, const float* X, long long ldx, int M, 
     return 2;
 }
 
+// limbs_ready: the norm before wrote this product's limbs and shifts into
+// the scratch (launch_norm_limbs), used when the product runs on the GEMM.
 static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, const QmvEpilogue& ep_in,
-                      cudaStream_t st, void* scratch, int* status) {
+                      cudaStream_t st, void* scratch, int* status, bool limbs_ready = false) {
     int* counters = static_cast<int*>(scratch);
     scratch = static_cast<uint8_t*>(scratch) + SCRATCH_COUNTERS;
     if (M <= UV_N && use_ugemv(W, M)) {
@@ -789,7 +792,7 @@ static int launch_qmv(const DevQMat& W, const float* X, long long ldx, int M, co
     // small matrices stay on the register-blocked kernel: the GEMM's fixed
     // cost per tile (pipeline fill, tensor-memory drain) would dominate
     if (M >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS) {
-        const int n = launch_ugemm(W, X, ldx, M, ep_in, st, scratch, counters, status);
+        const int n = launch_ugemm(W, X, ldx, M, ep_in, st, scratch, counters, status, limbs_ready);
         if (n) return n;
     }
     const int KG = W.bits == 8 ? 32 : 64;
@@ -1852,19 +1855,55 @@ static void launch_norm(const dz_cuda_model_t* m, const float* x, const float* r
         dz_layernorm_kernel<<<rows, LN_THREADS, 0, st>>>(x, res, g, be, y, D, 1e-6f);
 }
 
+// Whether DZ_NORM_LIMBS=0 in the environment turns the norm + split fusion
+// off (for comparison: both give the same bits).
+static bool norm_limbs_enabled() {
+    static const bool v = [] {
+        const char* e = getenv("DZ_NORM_LIMBS");
+        return !(e && strcmp(e, "0") == 0);
+    }();
+    return v;
+}
+
+// The norm can write the limbs of the product W that reads its `rows` x D
+// output when it is a LayerNorm of width <= LN_LIMBS_MAX_DIM, W has no row
+// scales (the split would fold them in) and W runs on the tensor-core GEMM.
+static bool norm_limbs_ok(const dz_cuda_model_t* m, const DevQMat& W, int rows, int D) {
+    return norm_limbs_enabled() && !m->rms && W.codes && !W.k_scale && W.K == D && D <= LN_LIMBS_MAX_DIM &&
+           D % 4 == 0 && rows >= UGEMM_MIN_M && W.kn && (size_t)W.K * W.N >= UGEMM_MIN_WEIGHTS;
+}
+// The fused norm's float4 element pass: every row and parameter 16-byte aligned.
+static bool norm_limbs_aligned(const float* x, const float* res, const float* g, const float* be, const float* y) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(res) |
+                        reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(be) | reinterpret_cast<uintptr_t>(y);
+    return (a & 15u) == 0;
+}
+
+// The norm (launch_norm) fused with the split of W's product: the limbs and
+// shifts go where launch_qmv's GEMM reads them in `scratch`. The caller checked
+// norm_limbs_ok.
+static void launch_norm_limbs(const float* x, const float* res, const float* g, const float* be, float* y, int rows,
+                              int D, const DevQMat& W, void* scratch, cudaStream_t st) {
+    const int Kp = round_up(W.K, UG_BK);
+    uint8_t* base = static_cast<uint8_t*>(scratch) + SCRATCH_COUNTERS;   // launch_qmv -> launch_ugemm layout
+    int8_t* L = reinterpret_cast<int8_t*>(base);
+    int* shift = reinterpret_cast<int*>(base + r256(3 * (size_t)rows * Kp));
+    dz_layernorm_limbs_kernel<<<rows, LN_THREADS, 0, st>>>(x, res, g, be, y, D, 1e-6f, rows, Kp, L, shift);
+}
+
 // FFN up-projection of R rows of x into ff (row stride ldf): bias and ReLU /
 // GELU in the product's epilogue, or both SwiGLU halves then the gate
 // (src/core/transformer.c:819-832). Returns the launches.
 static int launch_ffn_up(const dz_cuda_model_t* m, const DevLayer& L, const float* x, int D, int R, float* ff,
-                         long long ldf, int F, cudaStream_t st, void* scratch, int* status) {
+                         long long ldf, int F, cudaStream_t st, void* scratch, int* status, bool limbs_ready = false) {
     QmvEpilogue e1 = plain_epilogue(L.w1, ff, ldf);
     e1.bias = L.b1;
     e1.act = m->swiglu ? DZ_ACT_NONE : m->act;
-    int n = launch_qmv(L.w1, x, D, R, e1, st, scratch, status);
+    int n = launch_qmv(L.w1, x, D, R, e1, st, scratch, status, limbs_ready);
     if (L.wg.codes) {
         QmvEpilogue eg = plain_epilogue(L.wg, ff + F, ldf);
         eg.bias = L.b1 + F;
-        n += launch_qmv(L.wg, x, D, R, eg, st, scratch, status);
+        n += launch_qmv(L.wg, x, D, R, eg, st, scratch, status, limbs_ready);
     }
     if (m->swiglu) {
         dz_swiglu_kernel<<<dim3((unsigned)((F + 255) / 256), (unsigned)std::min(R, 65535)), 256, 0, st>>>(ff, R, F,
@@ -1876,7 +1915,7 @@ static int launch_ffn_up(const dz_cuda_model_t* m, const DevLayer& L, const floa
 
 // Output head over B hidden rows into c->logits: the quantized W_out, or the
 // token embeddings transposed when tied (src/core/lm_head.c:21-46).
-static int launch_head(dz_cuda_cache_t* c, cudaStream_t st) {
+static int launch_head(dz_cuda_cache_t* c, cudaStream_t st, bool limbs_ready = false) {
     dz_cuda_model_t* m = c->model;
     const int D = (int)m->desc.embedding_dim, V = (int)m->desc.vocab_size, B = c->B;
     if (m->tied) {
@@ -1886,7 +1925,7 @@ static int launch_head(dz_cuda_cache_t* c, cudaStream_t st) {
     }
     QmvEpilogue eh = plain_epilogue(m->head, c->logits, V);
     eh.bias = m->out_bias;
-    return launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status);
+    return launch_qmv(m->head, c->hidden, D, B, eh, st, c->xs_scratch, c->status, limbs_ready);
 }
 
 static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long tok_stride) {
@@ -1904,6 +1943,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
     }
     launches++;
     const size_t att_smem = (size_t)(cap + hd + ATT_THREADS) * 4;
+    bool hidden_limbs = false;   // the previous norm wrote the limbs of the product reading c->hidden
     for (size_t l = 0; l < m->layers.size(); l++) {
         DevLayer& L = m->layers[l];
         float* Kl = c->keys + l * (size_t)B * cap * dl;
@@ -1914,7 +1954,7 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
             ep.seg_start[0] = 0; ep.seg_start[1] = dl; ep.seg_start[2] = 2 * dl; ep.seg_start[3] = 3 * dl;
             ep.seg_ptr[1] = Kl; ep.seg_ld[1] = (long long)cap * dl; ep.seg_row_off[1] = c->row_off;
             ep.seg_ptr[2] = Vl; ep.seg_ld[2] = (long long)cap * dl; ep.seg_row_off[2] = c->row_off;
-            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st, c->xs_scratch, c->status);
+            launches += launch_qmv(L.qkv, c->hidden, D, B, ep, st, c->xs_scratch, c->status, hidden_limbs);
         } else {
             QmvEpilogue eq = plain_epilogue(L.q, c->q, dl);
             launches += launch_qmv(L.q, c->hidden, D, B, eq, st, c->xs_scratch, c->status);
@@ -1953,13 +1993,18 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         QmvEpilogue eo = plain_epilogue(L.wo, c->attn_raw, D);
         launches += launch_qmv(L.wo, c->concat, dl, B, eo, st, c->xs_scratch, c->status);
         tp_allreduce(m, c->attn_raw, (size_t)B * D, st);
+        const bool ffn_limbs = norm_limbs_ok(m, L.w1, B, D) && (!L.wg.codes || norm_limbs_ok(m, L.wg, B, D)) &&
+                               norm_limbs_aligned(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm);
         {
-            ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D, 0, st);
-            launch_norm(m, c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, B, D, st);
+            ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * B * D + 8.0 * D + (ffn_limbs ? 3.0 * B * D : 0.0), 0, st);
+            if (ffn_limbs)
+                launch_norm_limbs(c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, B, D, L.w1, c->xs_scratch, st);
+            else
+                launch_norm(m, c->attn_raw, c->hidden, L.g1, L.be1, c->attn_norm, B, D, st);
         }
         launches++;
         const long long ldf = m->swiglu ? 2LL * F : F;
-        launches += launch_ffn_up(m, L, c->attn_norm, D, B, c->ff, ldf, F, st, c->xs_scratch, c->status);
+        launches += launch_ffn_up(m, L, c->attn_norm, D, B, c->ff, ldf, F, st, c->xs_scratch, c->status, ffn_limbs);
         QmvEpilogue e2 = plain_epilogue(L.w2, c->ff_raw, D);
         if (m->tp_rank == 0) {   // bias and residual once, before the sum over ranks
             e2.bias = L.b2;
@@ -1968,13 +2013,21 @@ static int enqueue_step(dz_cuda_cache_t* c, const uint32_t* tokens, long long to
         }
         launches += launch_qmv(L.w2, c->ff, ldf, B, e2, st, c->xs_scratch, c->status);
         tp_allreduce(m, c->ff_raw, (size_t)B * D, st);
+        // the product reading c->hidden next: the next layer's fused QKV, or the head
+        const DevQMat* next = l + 1 < m->layers.size() ? (m->layers[l + 1].fused_qkv ? &m->layers[l + 1].qkv : nullptr)
+                                                       : (m->tied ? nullptr : &m->head);
+        hidden_limbs = next && norm_limbs_ok(m, *next, B, D) &&
+                       norm_limbs_aligned(c->ff_raw, nullptr, L.g2, L.be2, c->hidden);
         {
-            ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D, 0, st);
-            launch_norm(m, c->ff_raw, nullptr, L.g2, L.be2, c->hidden, B, D, st);
+            ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * B * D + 8.0 * D + (hidden_limbs ? 3.0 * B * D : 0.0), 0, st);
+            if (hidden_limbs)
+                launch_norm_limbs(c->ff_raw, nullptr, L.g2, L.be2, c->hidden, B, D, *next, c->xs_scratch, st);
+            else
+                launch_norm(m, c->ff_raw, nullptr, L.g2, L.be2, c->hidden, B, D, st);
         }
         launches++;
     }
-    launches += launch_head(c, st);
+    launches += launch_head(c, st, hidden_limbs);
     return launches;
 }
 
@@ -2322,6 +2375,7 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
         }
         launches++;
         zero_padded(c->pf_hidden);
+        bool hidden_limbs = false;   // the previous norm wrote the limbs of the product reading c->pf_hidden
         for (size_t l = 0; l < m->layers.size(); l++) {
             DevLayer& L = m->layers[l];
             float* Kl = c->keys + l * (size_t)B * cap * dl + (size_t)s0 * cap * dl;
@@ -2332,7 +2386,7 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
                 ep.seg_start[0] = 0; ep.seg_start[1] = dl; ep.seg_start[2] = 2 * dl; ep.seg_start[3] = 3 * dl;
                 ep.seg_ptr[1] = Kl; ep.seg_ld[1] = 0; ep.seg_row_off[1] = c->pf_rowoff;
                 ep.seg_ptr[2] = Vl; ep.seg_ld[2] = 0; ep.seg_row_off[2] = c->pf_rowoff;
-                launches += launch_qmv(L.qkv, c->pf_hidden, D, R, ep, st, c->pf_scratch, c->status);
+                launches += launch_qmv(L.qkv, c->pf_hidden, D, R, ep, st, c->pf_scratch, c->status, hidden_limbs);
             } else {
                 QmvEpilogue eq = plain_epilogue(L.q, c->pf_q, dl);
                 launches += launch_qmv(L.q, c->pf_hidden, D, R, eq, st, c->pf_scratch, c->status);
@@ -2380,14 +2434,23 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
             QmvEpilogue eo = plain_epilogue(L.wo, c->pf_attn_raw, D);
             launches += launch_qmv(L.wo, c->pf_concat, dl, R, eo, st, c->pf_scratch, c->status);
             tp_allreduce(m, c->pf_attn_raw, (size_t)R * D, st);
+            // (no fusion with padded rows: they are zeroed after the norm)
+            const bool ffn_limbs = !pad && norm_limbs_ok(m, L.w1, R, D) &&
+                                   (!L.wg.codes || norm_limbs_ok(m, L.wg, R, D)) &&
+                                   norm_limbs_aligned(c->pf_attn_raw, c->pf_hidden, L.g1, L.be1, c->pf_attn_norm);
             {
-                ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * R * D + 8.0 * D, 0, st);
-                launch_norm(m, c->pf_attn_raw, c->pf_hidden, L.g1, L.be1, c->pf_attn_norm, R, D, st);
+                ProfScope prof(DZ_KERNEL_LAYERNORM, 12.0 * R * D + 8.0 * D + (ffn_limbs ? 3.0 * R * D : 0.0), 0, st);
+                if (ffn_limbs)
+                    launch_norm_limbs(c->pf_attn_raw, c->pf_hidden, L.g1, L.be1, c->pf_attn_norm, R, D, L.w1,
+                                      c->pf_scratch, st);
+                else
+                    launch_norm(m, c->pf_attn_raw, c->pf_hidden, L.g1, L.be1, c->pf_attn_norm, R, D, st);
             }
             launches++;
             zero_padded(c->pf_attn_norm);
             const long long ldf = m->swiglu ? 2LL * F : F;
-            launches += launch_ffn_up(m, L, c->pf_attn_norm, D, R, c->pf_ff, ldf, F, st, c->pf_scratch, c->status);
+            launches += launch_ffn_up(m, L, c->pf_attn_norm, D, R, c->pf_ff, ldf, F, st, c->pf_scratch, c->status,
+                                      ffn_limbs);
             QmvEpilogue e2 = plain_epilogue(L.w2, c->pf_ff_raw, D);
             if (m->tp_rank == 0) {
                 e2.bias = L.b2;
@@ -2396,9 +2459,19 @@ static int enqueue_prefill(dz_cuda_cache_t* c, const uint32_t* ids_dev, long lon
             }
             launches += launch_qmv(L.w2, c->pf_ff, ldf, R, e2, st, c->pf_scratch, c->status);
             tp_allreduce(m, c->pf_ff_raw, (size_t)R * D, st);
+            // the next layer's fused QKV reads c->pf_hidden (the head reads
+            // the gathered last positions instead)
+            const DevQMat* next =
+                l + 1 < m->layers.size() && m->layers[l + 1].fused_qkv ? &m->layers[l + 1].qkv : nullptr;
+            hidden_limbs = !pad && next && norm_limbs_ok(m, *next, R, D) &&
+                           norm_limbs_aligned(c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden);
             {
-                ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * R * D + 8.0 * D, 0, st);
-                launch_norm(m, c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, R, D, st);
+                ProfScope prof(DZ_KERNEL_LAYERNORM, 8.0 * R * D + 8.0 * D + (hidden_limbs ? 3.0 * R * D : 0.0), 0, st);
+                if (hidden_limbs)
+                    launch_norm_limbs(c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, R, D, *next, c->pf_scratch,
+                                      st);
+                else
+                    launch_norm(m, c->pf_ff_raw, nullptr, L.g2, L.be2, c->pf_hidden, R, D, st);
             }
             launches++;
             zero_padded(c->pf_hidden);
