@@ -66,6 +66,15 @@ NCU_TRAFFIC = {
     # dz_seqgen_kernel, the whole config-2 job (64 x (32 + 32)) in one launch
     ("c2-int4-topp0.9-64x(32+32)", "seqgen"): 1025280 + 60672,
 }
+# Where the dominant kernel's launches are too many and too large to capture
+# each, one capture's DRAM bytes over its algorithmic bytes, applied to the
+# class's algorithmic bytes per launch (the launches scale with the context).
+NCU_TRAFFIC_RATIO = {
+    # dz_attn_decode_kernel<4>, one C4 decode step's layer at context 516-520
+    # (profiles/attn_decode_c4_b256.md): 2.284 GB read + 5.5 MB written for
+    # 256 x 518 x 2048 x 8 B of K/V rows + 4 MB of q and output
+    ("c4-int8-greedy-256x(512+128)", "attention"): (2.284e9 + 5.5e6) / (256 * 518 * 2048 * 8 + 4.0e6),
+}
 
 
 def peaks():
@@ -438,6 +447,11 @@ def roofline_of(classes, wl_name, hbm, bf16, peak_src, note):
     roof = {"bound": d["bound"], "kernel_class": dom, "achieved": d["achieved"], "peak": d["peak"],
             "unit": d["unit"], "frac": d["frac"], "peak_source": peak_src,
             "traffic": NCU_TRAFFIC.get((wl_name, dom)), "note": note}
+    ratio = NCU_TRAFFIC_RATIO.get((wl_name, dom))
+    if roof["traffic"] is None and ratio is not None:
+        roof["traffic"] = int(ratio * d["bytes_per_launch"])
+        roof["traffic_note"] = ("ncu DRAM bytes / algorithmic bytes of one captured launch "
+                                f"({ratio:.3f}) x the class's algorithmic bytes per launch")
     return roof, per
 
 
