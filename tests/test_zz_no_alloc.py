@@ -47,6 +47,43 @@ def test_noalloc_matches_allocating_entry_point(gpu, bits, shape):
     q.close()
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+def test_noalloc_first_call_gemm_and_no_growth(gpu, bits):
+    """A fresh matrix whose first product goes through the allocation-free
+    entry point, at 64 rows (the tensor-core GEMM, its limbs and TMA map in
+    the static array), then 1 row (the M <= 2 matvec); both against the
+    allocating entry point afterwards, and a repeated call leaves the
+    device's free memory unchanged."""
+    import torch
+    from dranzer_b200 import _native
+    L = _native.lib()
+    K, N = 4096, 8300
+    rng = np.random.RandomState(40 + bits)
+    w = (rng.randn(K, N) * 0.02).astype(np.float32)
+    q = gpu.QuantizedWeightMatrix.encode(w, bits)
+    stream = torch.cuda.Stream()
+    for m in (64, 1):
+        a = torch.from_numpy(rng.randn(m, K).astype(np.float32)).cuda()
+        c_new = torch.full((m, N), float("nan"), dtype=torch.float32, device="cuda")
+        c_ref = torch.zeros((m, N), dtype=torch.float32, device="cuda")
+        torch.cuda.synchronize()
+        _native.check(L.dz_cuda_matmul_quantized_noalloc(a.data_ptr(), q.handle, c_new.data_ptr(), m, K,
+                                                         stream.cuda_stream), "noalloc")
+        stream.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        _native.check(L.dz_cuda_matmul_quantized_noalloc(a.data_ptr(), q.handle, c_new.data_ptr(), m, K,
+                                                         stream.cuda_stream), "noalloc")
+        stream.synchronize()
+        assert torch.cuda.mem_get_info()[0] == free0, m
+        _native.check(L.dz_cuda_matmul_quantized_async(a.data_ptr(), q.handle, c_ref.data_ptr(), m, K,
+                                                       stream.cuda_stream), "async")
+        stream.synchronize()
+        ref, new = c_ref.cpu().numpy(), c_new.cpu().numpy()
+        assert np.isfinite(new).all(), m
+        assert _tol_ok(new, ref), (m, np.abs(new - ref).max())
+    q.close()
+
+
 def test_noalloc_rejects_oversized_calls(gpu):
     from dranzer_b200 import _native
     L = _native.lib()
