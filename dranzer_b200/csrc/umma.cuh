@@ -856,19 +856,34 @@ DZ_KERNEL_LINKAGE __global__ void __launch_bounds__(UG_THREADS, 1)
                         *reinterpret_cast<const longlong2*>(stile + (size_t)(r0 + i) * UG_PART_LD + c4 + 2);
                     v[i][0] = u0.x; v[i][1] = u0.y; v[i][2] = u1.x; v[i][3] = u1.y;
                 }
-                for (int z = 0; z < a.kparts; z++) {
-                    if (z == own) continue;
-                    const long long* pz = base + (size_t)z * UG_BM * UG_BN + c4;
-                    longlong2 w[4][2];
+                // the other parts three at a time, their loads issued together
+                // (one round trip to L2 per batch instead of one per part)
+                const int nother = a.kparts - 1;
+                for (int b0 = 0; b0 < nother; b0 += 3) {
+                    longlong2 w[3][4][2];
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        w[i][0] = *reinterpret_cast<const longlong2*>(pz + (size_t)(r0 + i) * UG_BN);
-                        w[i][1] = *reinterpret_cast<const longlong2*>(pz + (size_t)(r0 + i) * UG_BN + 2);
+                    for (int q = 0; q < 3; q++) {
+                        const int idx = b0 + q;
+                        const int z = idx < own ? idx : idx + 1;
+                        const long long* pz = base + (size_t)z * UG_BM * UG_BN + c4;
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            if (idx < nother) {
+                                w[q][i][0] = *reinterpret_cast<const longlong2*>(pz + (size_t)(r0 + i) * UG_BN);
+                                w[q][i][1] = *reinterpret_cast<const longlong2*>(pz + (size_t)(r0 + i) * UG_BN + 2);
+                            } else {
+                                w[q][i][0] = make_longlong2(0, 0);
+                                w[q][i][1] = make_longlong2(0, 0);
+                            }
+                        }
                     }
 #pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        v[i][0] += w[i][0].x; v[i][1] += w[i][0].y; v[i][2] += w[i][1].x; v[i][3] += w[i][1].y;
-                    }
+                    for (int q = 0; q < 3; q++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            v[i][0] += w[q][i][0].x; v[i][1] += w[q][i][0].y;
+                            v[i][2] += w[q][i][1].x; v[i][3] += w[q][i][1].y;
+                        }
                 }
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
