@@ -85,6 +85,10 @@ int dz_cuda_matmul_quantized_async(const float *A_dev, const dz_cuda_qmatrix_t *
  * call before any stream capture). All calls on a device share the array, so
  * calls whose work overlaps on the GPU (different streams, no ordering) race;
  * each call zeroes the counters it relies on before its kernels run.
+ * The address is kept per device ordinal for the life of the process: after
+ * cudaDeviceReset (or any other teardown of the device's primary context) the
+ * array can load at another address, so this entry point must not be called
+ * on that device again.
  * No counterpart in the reference. */
 #define DZ_NOALLOC_SCRATCH_BYTES (8u << 20)
 int dz_cuda_matmul_quantized_noalloc(const float *A_dev, const dz_cuda_qmatrix_t *weights, float *C_dev,
