@@ -86,3 +86,37 @@ def test_product_error_within_the_stated_bound():
         ref = (x.astype(np.float64)[:, None] * q).sum(axis=0)
         bound = np.ldexp(0.5, -s) * np.abs(q).sum(axis=0) + np.abs(ref) * 2.0 ** -23 + 1e-300
         assert np.all(np.abs(y - ref) <= bound * 1.0001), np.abs(y - ref).max()
+
+
+def _byte_perm(x, y, sel):
+    """PTX prmt (default mode) on uint32 arrays: byte i of the result is
+    byte (sel >> 4i) & 7 of the 8-byte value y:x."""
+    out = np.zeros_like(x)
+    for i in range(4):
+        b = (sel >> (4 * i)) & 7
+        src = x if b < 4 else y
+        out |= ((src >> np.uint32(8 * (b & 3))) & np.uint32(0xFF)) << np.uint32(8 * i)
+    return out
+
+
+def test_byte_permute_digits_equal_balanced_digits():
+    """The decode matvec (qmvi.cuh) builds the limb words of four k at once:
+    with Y = X + 0x8080 the balanced digits are byte 0 of Y - 128, byte 1 of
+    Y - 128 and Y >> 16, so the low / mid / top words are byte permutes of
+    the four Y (the first two with every byte's top bit flipped). Checked
+    against the digit arithmetic over random X and the range's edges."""
+    rng = np.random.RandomState(3)
+    edges = np.array([-(1 << 22), 1 << 22, 0, -1, 1, 127, 128, -128, -129, 255, 256, 32767, 32768, -32768,
+                      -32769, (1 << 22) - 1, -(1 << 22) + 1], np.int64)
+    xs = np.concatenate([rng.randint(-(1 << 22), (1 << 22) + 1, size=40000), np.tile(edges, 4)])
+    xs = xs[: len(xs) // 4 * 4].reshape(-1, 4)
+    Y = ((xs + 0x8080) & 0xFFFFFFFF).astype(np.uint32)
+    pair = lambda sel: _byte_perm(_byte_perm(Y[:, 0], Y[:, 1], sel), _byte_perm(Y[:, 2], Y[:, 3], sel), 0x5410)
+    l4 = pair(0x0040) ^ np.uint32(0x80808080)
+    m4 = pair(0x0051) ^ np.uint32(0x80808080)
+    t4 = pair(0x0062)
+    t, m, l = digits(xs)
+    pack = lambda d: sum(((d[:, b] & 0xFF).astype(np.uint32) << np.uint32(8 * b)) for b in range(4)).astype(np.uint32)
+    np.testing.assert_array_equal(l4, pack(l))
+    np.testing.assert_array_equal(m4, pack(m))
+    np.testing.assert_array_equal(t4, pack(t))
